@@ -1,0 +1,416 @@
+"""Decode benchmark: aggregate tok/s for tenants sharing Llama-2-7B Q4_K_M weights.
+
+python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Workload: Llama-2-7B shape (32 layers, hidden 4096,
+32 MHA heads x 128, FFN 11008, vocab 32000), random-init N(0, 0.02) weights
+quantised to Q4_K (attn_v and output Q6_K) on the device, 8 tenants per GPU
+with fp16 paged KV, prompts U[128, 512] tokens (seed 4), greedy decode. One
+step = one decode token for every tenant on the GPU (one rb_forward call).
+Under torchrun each rank drives one GPU with its own 8 tenants (weak scaling,
+no collective on the decode path; the barrier and the max-over-ranks time
+reduction are plumbing).
+
+`value` = tokens / device time of the K decode-step graphs (inputs resident);
+`e2e` = the same K steps timed on the device stream from the H2D copy of each
+step's token ids through the D2H copy of its greedy ids, via the C ABI with
+host buffers. The weights (3.9 GB) dwarf the 126 MB L2, so no flush is needed.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import subprocess
+import sys
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+CFG = dict(n_layers=32, hidden=4096, n_heads=32, n_kv_heads=32, head_dim=128, ffn=11008, vocab=32000,
+           max_seq=1024, rms_eps=1e-5, layer_eps=1e-5, rope_theta=10000.0)
+TENANTS_PER_GPU = 8
+METRIC = "aggregate decode tok/s, 8 tenants Llama-7B Q4_K; paged-KV attn HBM GB/s vs peak"
+Q4K_BPW, Q6K_BPW = 144 / 256, 210 / 256
+
+
+def peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        d = json.load(open(p))
+        return d["hbm_gbs"], "measured"
+    return 6650.0, "fallback"
+
+
+def weight_bytes(cfg):
+    H, Q, KV, F, V, L = (cfg["hidden"], cfg["n_heads"] * cfg["head_dim"], cfg["n_kv_heads"] * cfg["head_dim"],
+                         cfg["ffn"], cfg["vocab"], cfg["n_layers"])
+    layer = (Q * H + KV * H + Q * H + 3 * F * H) * Q4K_BPW + KV * H * Q6K_BPW
+    return L * layer + V * H * Q6K_BPW
+
+
+# ---------------------------------------------------------------------------
+# clocks sampled during the timed region
+# ---------------------------------------------------------------------------
+class Clocks:
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu: int):
+        self.gpu = gpu
+        self.p = None
+
+    def __enter__(self):
+        try:
+            self.p = subprocess.Popen(["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.Q}",
+                                       "--format=csv,noheader,nounits", "-lms", "200"],
+                                      stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.p = None
+        return self
+
+    def __exit__(self, *exc):
+        self.lines = []
+        if self.p:
+            self.p.terminate()
+            try:
+                out, _ = self.p.communicate(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.p.kill()
+                out, _ = self.p.communicate()
+            self.lines = [l for l in out.splitlines() if l.strip()]
+
+    def summary(self):
+        sm, mx, reasons = [], 0.0, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for l in getattr(self, "lines", []):
+            f = [x.strip() for x in l.split(",")]
+            try:
+                sm.append(float(f[1]))
+                mx = max(mx, float(f[2]))
+            except (ValueError, IndexError):
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        return {"sm_mhz": float(np.median(sm)) if sm else None, "sm_max_mhz": mx or None,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# ---------------------------------------------------------------------------
+# our arm
+# ---------------------------------------------------------------------------
+def build_model(rb, torch, ctx, dev, n_tenants, host_copy=None):
+    """Random-init Q4_K_M weights generated and quantised on the device. If
+    host_copy is a dict, the GGUF bytes of every tensor are also copied into it
+    (for the CPU baseline on identical weights)."""
+    cfg = dict(CFG, kv_dtype=rb.F16, max_tenants=n_tenants, kv_pages=n_tenants * (CFG["max_seq"] // 16))
+    m = rb.Model(ctx, cfg)
+    g = torch.Generator(device=dev)
+    H, Q, KV, F, V = CFG["hidden"], CFG["n_heads"] * CFG["head_dim"], CFG["n_kv_heads"] * CFG["head_dim"], \
+        CFG["ffn"], CFG["vocab"]
+    seed = [3]
+
+    def qt(dt, rows, cols):
+        g.manual_seed(seed[0])
+        seed[0] += 1
+        x = torch.randn(rows, cols, generator=g, device=dev, dtype=torch.float32).mul_(0.02)
+        be, bb = rb.BLOCK_ELEMS[dt], rb.BLOCK_BYTES[dt]
+        out = torch.empty(rows * cols // be * bb, dtype=torch.uint8, device=dev)
+        ctx.quantize(dt, x.view(-1), out)
+        return out
+
+    def put(which, layer, dt, t):
+        m.set_weight(which, layer, dt, t)
+        if host_copy is not None:
+            host_copy[(which, layer)] = (dt, t.cpu().numpy())
+
+    ones = torch.ones(H, dtype=torch.float32, device=dev)
+    put(rb.W_TOKEN_EMBD, -1, rb.Q4_K, qt(rb.Q4_K, V, H))
+    put(rb.W_OUTPUT_NORM, -1, rb.F32, ones)
+    put(rb.W_OUTPUT, -1, rb.Q6_K, qt(rb.Q6_K, V, H))
+    shapes = [(rb.W_Q, Q, H, rb.Q4_K), (rb.W_K, KV, H, rb.Q4_K), (rb.W_V, KV, H, rb.Q6_K), (rb.W_O, H, Q, rb.Q4_K),
+              (rb.W_GATE, F, H, rb.Q4_K), (rb.W_UP, F, H, rb.Q4_K), (rb.W_DOWN, H, F, rb.Q4_K)]
+    for l in range(CFG["n_layers"]):
+        put(rb.W_ATTN_NORM, l, rb.F32, ones)
+        put(rb.W_FFN_NORM, l, rb.F32, ones)
+        for which, r, c, dt in shapes:
+            put(which, l, dt, qt(dt, r, c))
+    m.finalize()
+    torch.cuda.synchronize(dev)
+    return m
+
+
+def gemv_roofline(rb, torch, ctx, dev, hbm_peak, peak_kind):
+    """Dominant kernel: the Q4_K gate|up GEMV (22016 x 4096, M = 8 tenants),
+    timed with CUDA events on the context stream over 48 back-to-back launches
+    rotating 4 weight copies (200 MB > L2)."""
+    n, k, m = 2 * CFG["ffn"], CFG["hidden"], TENANTS_PER_GPU
+    g = torch.Generator(device=dev)
+    ws = []
+    for i in range(4):
+        g.manual_seed(100 + i)
+        x = torch.randn(n, k, generator=g, device=dev).mul_(0.02)
+        blk = torch.empty(n * k // 256 * 144, dtype=torch.uint8, device=dev)
+        ctx.quantize(rb.Q4_K, x.view(-1), blk)
+        ws.append(rb.Weight(ctx, rb.Q4_K, n, k, blk))
+        del x
+    xin = torch.randn(m, k, device=dev)
+    yout = torch.empty(m, n, device=dev)
+    torch.cuda.synchronize(dev)  # raw C-ABI calls below run on the library's stream
+    stream = torch.cuda.ExternalStream(ctx.stream, device=dev)
+    lib = rb.lib()
+    import ctypes as C
+    flags = rb.PTR_DEVICE | 2  # device pointers, asynchronous
+    for i in range(8):
+        lib.rb_weight_matmul(ctx.handle, ws[i % 4].handle, C.c_void_p(xin.data_ptr()), C.c_void_p(yout.data_ptr()),
+                             m, flags)
+    ctx.sync()
+    n_launch = 48
+    evs = [torch.cuda.Event(enable_timing=True) for _ in range(n_launch + 1)]
+    for i in range(n_launch):
+        evs[i].record(stream)
+        rc = lib.rb_weight_matmul(ctx.handle, ws[i % 4].handle, C.c_void_p(xin.data_ptr()),
+                                  C.c_void_p(yout.data_ptr()), m, flags)
+        assert rc >= 0, rb.last_error()
+    evs[-1].record(stream)
+    ctx.sync()
+    ms = [evs[i].elapsed_time(evs[i + 1]) for i in range(n_launch)]
+    avg_ms = float(np.mean(ms))
+    alg_bytes = n * k * Q4K_BPW + m * k * 4 + m * n * 4
+    achieved = alg_bytes / (avg_ms * 1e-3) / 1e9
+    for w in ws:
+        w.free()
+    return {"kernel": "gemv_kernel<Q4_K, NT=1> (gate|up 22016x4096, M=8)", "bound": "hbm",
+            "achieved": round(achieved, 1), "peak": hbm_peak, "peak_kind": peak_kind, "unit": "GB/s",
+            "frac": round(achieved / hbm_peak, 4), "traffic": None, "algorithmic_bytes": int(alg_bytes),
+            "avg_launch_us": round(avg_ms * 1e3, 2)}
+
+
+def attention_roofline(rb, torch, ctx, dev, hbm_peak, peak_kind):
+    """Config 2: 16 tenants, 32 q / 8 kv heads, hd 128, fp16 K/V ~ N(0,1) (seed 2),
+    contexts U[512, 8192], 16-token pages from a permuted pool; one new token per
+    tenant appended then attended. Timed: the attention kernel (events)."""
+    rng = np.random.default_rng(2)
+    n_t, hq, hkv, hd = 16, 32, 8, 128
+    ctxs = rng.integers(512, 8193, n_t)
+    pool = ctx.kv_pool(1, hkv, hd, rb.F16, n_pages=int(sum((c + 17) // 16 for c in ctxs)) + 16,
+                       max_tenants=n_t, max_seq=8208)
+    pool.shuffle(2)
+    for t in range(n_t):
+        pool.create(t)
+        L = int(ctxs[t])
+        kk = torch.randn(L, hkv * hd, device=dev)
+        vv = torch.randn(L, hkv * hd, device=dev)
+        pool.append(t, 0, kk, vv)
+    q = torch.randn(n_t, hq * hd, device=dev)
+    kn = torch.randn(n_t, hkv * hd, device=dev)
+    vn = torch.randn(n_t, hkv * hd, device=dev)
+    out = torch.empty(n_t, hq * hd, device=dev)
+    tenants = list(range(n_t))
+    pos = [int(c) for c in ctxs]
+    pool.attention_forward(0, tenants, q, hq, 1 / np.sqrt(hd), positions=pos, k_new=kn, v_new=vn, out=out)
+    torch.cuda.synchronize(dev)
+    ms = []
+    for _ in range(20):
+        pool.attention_forward(0, tenants, q, hq, 1 / np.sqrt(hd), positions=[p for p in pos], out=out)
+        ms.append(ctx.last_forward_ms())
+    avg = float(np.mean(ms[3:]))
+    kv_bytes = sum((p + 1) * hkv * hd * 2 * 2 for p in pos)
+    pages = sum(p // 16 + 1 for p in pos)
+    alg = kv_bytes + pages * 4 + 2 * n_t * hq * hd * 4
+    achieved = alg / (avg * 1e-3) / 1e9
+    return {"kernel": "attn_kernel<HD=128, NREP=4, fp16> (config 2)", "bound": "hbm",
+            "achieved": round(achieved, 1), "peak": hbm_peak, "peak_kind": peak_kind, "unit": "GB/s",
+            "frac": round(achieved / hbm_peak, 4), "algorithmic_bytes": int(alg), "avg_launch_us": round(avg * 1e3, 2)}
+
+
+def cpu_baseline(weights, threads, max_s=20.0):
+    """The oracle (C++ restatement of the reference CPU path, all host threads)
+    on a bounded sample: single-token decode forwards of one tenant at context
+    length 448 (the workload's mean), timed until ~max_s seconds."""
+    from oracle import oracle as O
+    cfg = dict(CFG, kv_fp16=1)
+    om = O.Model(cfg, weights, threads=threads)
+    om.kv_fill(448, seed=0)
+    t0 = time.perf_counter()
+    n = 0
+    while True:
+        om.forward([1], 448 + n)
+        n += 1
+        if time.perf_counter() - t0 > max_s or n >= 8:
+            break
+    dt = time.perf_counter() - t0
+    return {"value": round(n / dt, 4), "unit": "tok/s", "cores": threads, "kind": "port",
+            "sample": f"{n} single-token decode forwards of one tenant at ctx 448 (Llama-2-7B Q4_K_M, "
+                      f"oracle dequant+fp32 GEMV path, {threads} threads); tenants are served one token at a time"}
+
+
+def run_ours(args):
+    import torch
+    import realm_b200 as rb
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    dist = None
+    if world > 1:
+        import torch.distributed as dist
+        dist.init_process_group("nccl", device_id=dev)
+    hbm_peak, peak_kind = peaks()
+    ctx = rb.Context(local)
+    nt = TENANTS_PER_GPU
+    host_w = {} if (world == 1 and not args.no_cpu) else None
+    m = build_model(rb, torch, ctx, dev, nt, host_w)
+    # prompts: U[128, 512] ids U[0, 32000) from seed 4 (per rank offset)
+    rng = np.random.default_rng(4 + rank)
+    lens = rng.integers(128, 513, nt)
+    last = []
+    for t in range(nt):
+        m.tenant_create(t)
+        ids = rng.integers(0, CFG["vocab"], int(lens[t])).astype(np.uint32)
+        for cs in range(0, len(ids), 64):
+            chunk = ids[cs:cs + 64]
+            _, am = m.forward_rows([t] * len(chunk), chunk, want_logits=False)
+        last.append(int(am[-1]))
+    tenants = np.arange(nt, dtype=np.uint32)
+    tok = np.array(last, np.uint32)
+    for _ in range(args.warmup):
+        _, tok = m.forward_rows(tenants, tok, want_logits=False)
+    stream = torch.cuda.ExternalStream(ctx.stream, device=dev)
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    if dist:
+        dist.barrier()
+    torch.cuda.synchronize(dev)
+    dev_ms = 0.0
+    launches = 0
+    with Clocks(local) as clk:
+        ev0.record(stream)
+        for _ in range(args.steps):
+            _, tok = m.forward_rows(tenants, tok, want_logits=False)
+            dev_ms += ctx.last_forward_ms()
+            launches += ctx.last_forward_launches()
+        ev1.record(stream)
+        torch.cuda.synchronize(dev)
+    e2e_ms = ev0.elapsed_time(ev1)
+    if dist:
+        t = torch.tensor([dev_ms, e2e_ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        dev_ms, e2e_ms = float(t[0]), float(t[1])
+        dist.barrier()
+    tokens = nt * world * args.steps
+    value = tokens / (dev_ms * 1e-3)
+    e2e = tokens / (e2e_ms * 1e-3)
+    if rank != 0:
+        if dist:
+            dist.destroy_process_group()
+        return
+    roof = gemv_roofline(rb, torch, ctx, dev, hbm_peak, peak_kind)
+    attn = attention_roofline(rb, torch, ctx, dev, hbm_peak, peak_kind)
+    # decode-step roofline: weights once + KV of every tenant per step
+    mean_ctx = float(np.mean(lens)) + args.warmup + args.steps / 2
+    step_bytes = weight_bytes(CFG) + nt * mean_ctx * CFG["n_layers"] * 2 * CFG["n_kv_heads"] * CFG["head_dim"] * 2
+    step_ms = dev_ms / args.steps
+    line = {
+        "metric": METRIC, "value": round(value, 1), "unit": "tok/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(step_ms, 4), "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f32 (Q4_K/Q6_K weights exact in fp16 tensor-core operands, fp16 hi/lo "
+                                      "activations, fp32 accumulate)",
+        "data": "synthetic: random-init N(0,0.02) weights quantised on device, prompts U[128,512] seed 4",
+        "config": {"workload": "Llama-2-7B Q4_K_M decode (configs[3]), 8 tenants per GPU, fp16 paged KV",
+                   "tenants": nt * world, "prompt_lens": [int(x) for x in lens], "parallelism": f"tenant-sharded x{world}",
+                   "l2": "weights 3.9 GB per step > 126 MB L2 (no flush needed)"},
+        "e2e": {"value": round(e2e, 1), "unit": "tok/s", "h2d_bytes_per_step": 4 * (2 + 3 * 64),
+                "d2h_bytes_per_step": 8 * nt},
+        "gpu_launches": launches,
+        "roofline": roof,
+        "attention": attn,
+        "decode_step": {"bytes_per_step": int(step_bytes), "achieved_GBps": round(step_bytes / (step_ms * 1e-3) / 1e9, 1),
+                        "frac": round(step_bytes / (step_ms * 1e-3) / 1e9 / hbm_peak, 4)},
+        "clocks": clk.summary(),
+    }
+    if host_w is not None:
+        try:
+            line["cpu_baseline"] = cpu_baseline(host_w, os.cpu_count() or 1)
+        except Exception as e:  # a baseline failure must not hide the GPU number
+            line["cpu_baseline"] = {"error": str(e)[:200]}
+    print(json.dumps(line), flush=True)
+    if dist:
+        dist.destroy_process_group()
+
+
+def run_reference(args):
+    """The reference arm: the oracle (C++ restatement of the reference's CPU
+    path; the Rust reference cannot be built here) on all host threads."""
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    from oracle import oracle as O
+    threads = os.cpu_count() or 1
+    rng = np.random.default_rng(3)
+    H, Q, KV, F, V = CFG["hidden"], CFG["n_heads"] * CFG["head_dim"], CFG["n_kv_heads"] * CFG["head_dim"], \
+        CFG["ffn"], CFG["vocab"]
+
+    def qt(dt, rows, cols):
+        x = rng.standard_normal((rows, cols), dtype=np.float32)
+        x *= 0.02
+        return dt, O.quantize(dt, x)
+
+    W = {(O.W_TOKEN_EMBD, -1): qt(O.Q4K, V, H), (O.W_OUTPUT_NORM, -1): (O.F32, np.ones(H, np.float32)),
+         (O.W_OUTPUT, -1): qt(O.Q6K, V, H)}
+    for l in range(CFG["n_layers"]):
+        W[(O.W_ATTN_NORM, l)] = (O.F32, np.ones(H, np.float32))
+        W[(O.W_FFN_NORM, l)] = (O.F32, np.ones(H, np.float32))
+        for which, r, c, dt in [(O.W_Q, Q, H, O.Q4K), (O.W_K, KV, H, O.Q4K), (O.W_V, KV, H, O.Q6K),
+                                (O.W_O, H, Q, O.Q4K), (O.W_GATE, F, H, O.Q4K), (O.W_UP, F, H, O.Q4K),
+                                (O.W_DOWN, H, F, O.Q4K)]:
+            W[(which, l)] = qt(dt, r, c)
+    om = O.Model(dict(CFG, kv_fp16=1), W, threads=threads)
+    om.kv_fill(448, seed=0)
+    pos = 448
+    for _ in range(min(args.warmup, 1)):
+        om.forward([1], pos)
+        pos += 1
+    k = max(1, min(args.steps, 4))
+    t0 = time.perf_counter()
+    for _ in range(k):
+        om.forward([1], pos)
+        pos += 1
+    dt = time.perf_counter() - t0
+    v = k / dt
+    sample = (f"{k} single-token decode forwards of one tenant at ctx ~448 (oracle restatement of the reference CPU "
+              f"path: dequant + fp32 GEMV, {threads} threads); the reference serves tenants one token at a time, so "
+              f"aggregate tok/s over tenants equals this rate")
+    print(json.dumps({"impl": "reference", "metric": METRIC, "value": round(v, 4), "unit": "tok/s",
+                      "n_gpus": int(os.environ.get("WORLD_SIZE", "1")), "steps": k, "warmup": min(args.warmup, 1),
+                      "ms_per_step": round(dt / k * 1e3, 2), "higher_is_better": True, "scaling": "weak",
+                      "vs_baseline": None, "dtype": "f32", "data": "synthetic (numpy N(0,0.02), seed 3)",
+                      "config": {"workload": "Llama-2-7B Q4_K_M decode (configs[3]), one tenant-token per sample"},
+                      "e2e": {"value": round(v, 4), "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+                      "cpu_baseline": {"value": round(v, 4), "unit": "tok/s", "cores": threads, "kind": "port",
+                                       "sample": sample}}), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=64)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--no-cpu", action="store_true", help="skip the CPU-baseline leg")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

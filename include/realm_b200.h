@@ -1,0 +1,235 @@
+/*
+ * realm_b200.h — C ABI of the B200-native decode engine for Realm.
+ *
+ * One shared library (librealm_b200.so) replaces, for the decode hot path, the
+ * reference's (Querent-ai/realm) host functions that WASM tenants call and the
+ * GPU backend trait behind them. Every entry point names the reference
+ * interface it stands in for (paths relative to the reference project root).
+ *
+ * Conventions
+ *  - Every function returns int32_t: >= 0 is a count (elements or bytes, the
+ *    same meaning as the host function it mirrors), < 0 is an error code.
+ *  - Codes -1..-8 keep the meanings of crates/realm-runtime/src/host_functions.rs:145-155;
+ *    codes from -20 on are specific to this library. rb_last_error() returns a
+ *    thread-local message for the last failure on the calling thread.
+ *  - Buffers passed with flags & RB_PTR_DEVICE are CUDA device pointers on the
+ *    context's device; otherwise they are host pointers and the call copies
+ *    in/out (pinned memory is fastest but not required).
+ *  - One rb_ctx per GPU. Calls on one context are serialised on its stream and
+ *    must come from one host thread at a time; contexts on different GPUs are
+ *    independent (no global locks).
+ *  - Weight bytes are GGUF block bytes exactly as stored in the reference's
+ *    QuantizedTensor (crates/realm-runtime/src/model_storage.rs:44-77).
+ */
+#ifndef REALM_B200_H
+#define REALM_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- status codes ---- */
+#define RB_OK 0
+#define RB_ERR_DISABLED (-1)        /* feature not available */
+#define RB_ERR_NOT_FOUND (-2)       /* layer / resource not found */
+#define RB_ERR_INVALID (-3)         /* buffer too small / validation failed */
+#define RB_ERR_IO (-4)              /* read / write failed */
+#define RB_ERR_NO_MEMORY (-5)       /* memory not available */
+#define RB_ERR_PTR_OVERFLOW (-6)
+#define RB_ERR_OUT_OF_BOUNDS (-7)
+#define RB_ERR_WRITE (-8)
+#define RB_ERR_BAD_HANDLE (-20)
+#define RB_ERR_KV_POOL_EXHAUSTED (-21)
+#define RB_ERR_KV_OVERFLOW (-22)    /* crates/realm-models/src/kv_cache.rs:48-53 */
+#define RB_ERR_UNSUPPORTED (-23)    /* dtype / shape, e.g. K % 256 != 0 (fused.rs:238-243) */
+#define RB_ERR_CUDA (-24)
+#define RB_ERR_TIMEOUT (-25)        /* a bounded device wait gave up */
+#define RB_ERR_OOM (-26)
+
+/* ---- pointer-space flags ---- */
+#define RB_PTR_HOST 0u
+#define RB_PTR_DEVICE 1u
+/* With RB_PTR_DEVICE: enqueue on the context stream and return without waiting
+ * (rb_weight_matmul, rb_attention_forward); device-side failures surface at the
+ * next rb_sync. Without RB_PTR_DEVICE the flag is ignored. */
+#define RB_ASYNC 2u
+
+/* ---- dtypes: GGML type ids (crates/realm-core/src/tensor.rs:7-40) ---- */
+#define RB_F32 0
+#define RB_F16 1
+#define RB_Q8_0 8
+#define RB_Q4_K 12
+#define RB_Q6_K 14
+
+typedef struct rb_ctx rb_ctx;
+
+typedef struct rb_config {
+  int32_t device;       /* CUDA device ordinal */
+  uint32_t max_rows;    /* largest batch of query rows per call (<= 64) */
+  uint32_t use_pdl;     /* programmatic dependent launch between kernels */
+  uint32_t use_graphs;  /* capture decode steps as CUDA graphs */
+} rb_config;
+
+/* ---- context ---- */
+int32_t rb_ctx_create(const rb_config* cfg, rb_ctx** out);
+int32_t rb_ctx_destroy(rb_ctx* ctx);
+int32_t rb_last_error(char* buf, size_t len);
+/* Waits for all work on the context's stream (bounded: RB_ERR_TIMEOUT after ~60 s). */
+int32_t rb_sync(rb_ctx* ctx);
+/* The context's cudaStream_t, for callers that enqueue their own copies. */
+void* rb_stream(rb_ctx* ctx);
+int32_t rb_num_sms(rb_ctx* ctx);
+
+/* ---- quantised blocks ----
+ * rb_dequantize: bit-exact dequantize_q4_k / q6_k / q8_0
+ * (crates/realm-core/src/quant.rs:127-187, 393-451, 371-387; dispatch :663-939).
+ * Returns elements written. */
+int32_t rb_dequantize(rb_ctx* ctx, int32_t dtype, const void* blocks, size_t nblocks, float* out, uint32_t flags);
+/* Quantiser (the reference has none; used to build the synthetic Q4_K_M weights).
+ * Returns blocks written. */
+int32_t rb_quantize(rb_ctx* ctx, int32_t dtype, const float* x, size_t n, void* out_blocks, uint32_t flags);
+
+/* ---- fused dequant matmul ----
+ * Mirrors fused_dequant_matmul_{q4k,q6k,q80}(blocks, input, output, batch_size, n, k)
+ * (crates/realm-compute-cpu/src/fused.rs:229, 1128, 2451) and
+ * GpuBackendTrait::fused_dequant_matmul_* (crates/realm-compute-gpu/src/gpu_backend_trait.rs:17-143):
+ * output[b, j] = sum_i input[b, i] * W[j, i]; W is [n][k] GGUF blocks.
+ * Validation as the reference: K % 256 for K-quants, block count, batch <= max_rows.
+ * Returns batch_size * n. The blocks are staged and re-tiled on every call; use
+ * rb_weight_upload + rb_weight_matmul to keep a weight resident. */
+int32_t rb_fused_dequant_matmul(rb_ctx* ctx, int32_t dtype, const void* blocks, size_t nblocks, const float* input,
+                                float* output, uint32_t batch_size, uint32_t n, uint32_t k, uint32_t flags);
+/* Uploads a [n][k] GGUF weight once (tiled for the tensor-core GEMV). */
+int32_t rb_weight_upload(rb_ctx* ctx, int32_t dtype, uint32_t n, uint32_t k, const void* blocks, size_t nbytes,
+                         uint32_t flags, int32_t* handle);
+int32_t rb_weight_free(rb_ctx* ctx, int32_t handle);
+int32_t rb_weight_matmul(rb_ctx* ctx, int32_t handle, const float* input, float* output, uint32_t batch_size,
+                         uint32_t flags);
+/* Test hook: the resident tiled bytes converted back to GGUF layout (Q4_K). */
+int32_t rb_weight_export(rb_ctx* ctx, int32_t handle, void* out_blocks, size_t nbytes, uint32_t flags);
+
+/* candle_matmul (crates/realm-runtime/src/memory64_host.rs:861-969): C[m,n] = A[m,k] . B[k,n], f32.
+ * candle_matmul_transposed (:975-1086): B given as [n,k]. Returns m*n. */
+int32_t rb_candle_matmul(rb_ctx* ctx, const float* a, const float* b, float* c, uint32_t m, uint32_t k, uint32_t n,
+                         uint32_t flags);
+int32_t rb_candle_matmul_transposed(rb_ctx* ctx, const float* a, const float* b, float* c, uint32_t m, uint32_t k,
+                                    uint32_t n, uint32_t flags);
+
+/* ---- paged KV cache ----
+ * The reference keeps one contiguous fp32 KVCache per layer
+ * (crates/realm-models/src/kv_cache.rs:7-80) in a global map keyed by (model, layer)
+ * (crates/realm-runtime/src/kv_cache_storage.rs:12-88). Here a pool holds
+ * 16-token pages for all layers of a model geometry; each tenant owns a page
+ * table and one length per layer. kv_dtype is RB_F32 (reference layout) or
+ * RB_F16 (K/V rounded to fp16, nearest-even, on append). */
+int32_t rb_kv_pool_create(rb_ctx* ctx, uint32_t n_layers, uint32_t n_kv_heads, uint32_t head_dim, int32_t kv_dtype,
+                          uint32_t n_pages, uint32_t max_tenants, uint32_t max_seq, int32_t* pool);
+int32_t rb_kv_pool_destroy(rb_ctx* ctx, int32_t pool);
+/* Permutes the order in which free pages are handed out (deterministic in seed). */
+int32_t rb_kv_pool_shuffle(rb_ctx* ctx, int32_t pool, uint64_t seed);
+int32_t rb_kv_pool_free_pages(rb_ctx* ctx, int32_t pool);
+/* KVCache::new (kv_cache.rs:24-34) for one tenant. */
+int32_t rb_kv_create(rb_ctx* ctx, int32_t pool, uint32_t tenant);
+int32_t rb_kv_destroy(rb_ctx* ctx, int32_t pool, uint32_t tenant);
+/* KVCache::clear (kv_cache.rs:36-40): length 0, pages returned to the pool. */
+int32_t rb_kv_clear(rb_ctx* ctx, int32_t pool, uint32_t tenant);
+/* KVCache::current_seq_len */
+int32_t rb_kv_len(rb_ctx* ctx, int32_t pool, uint32_t tenant, uint32_t layer);
+/* KVCache::append (kv_cache.rs:44-70): k, v are [seq_len][n_kv][hd] f32.
+ * Returns the new length, or RB_ERR_KV_OVERFLOW past max_seq. */
+int32_t rb_kv_append(rb_ctx* ctx, int32_t pool, uint32_t tenant, uint32_t layer, const float* k, const float* v,
+                     uint32_t seq_len, uint32_t flags);
+/* KVCache::current_data (kv_cache.rs:73-79): writes [len][n_kv][hd] f32 each; returns len. */
+int32_t rb_kv_gather(rb_ctx* ctx, int32_t pool, uint32_t tenant, uint32_t layer, float* k_out, float* v_out,
+                     uint32_t flags);
+
+/* ---- attention ----
+ * The north star's attention_forward; defined after the reference's
+ * Attention::forward trait (crates/realm-runtime/src/attention/mod.rs:34-45) and
+ * compute_attention (crates/realm-models/src/attention.rs:310-380), over the paged cache.
+ * Row r is a query of tenant tenants[r] at position positions[r]; it attends to
+ * cached positions [0, positions[r]] of `layer` (causal mask, GQA grouping
+ * n_heads / n_kv_heads). If k_new/v_new are given ([n_rows][n_kv][hd]) they are
+ * appended at positions[r] first (positions[r] must equal that tenant's length).
+ * q, out: [n_rows][n_heads][hd]. Returns n_rows * n_heads * hd. */
+int32_t rb_attention_forward(rb_ctx* ctx, int32_t pool, uint32_t layer, uint32_t n_rows, const uint32_t* tenants,
+                             const uint32_t* positions, const float* q, const float* k_new, const float* v_new,
+                             float* out, uint32_t n_heads, float scale, uint32_t flags);
+
+/* ---- model ---- */
+typedef struct rb_model_config {
+  uint32_t n_layers, hidden, n_heads, n_kv_heads, head_dim, ffn, vocab, max_seq;
+  float rms_eps;    /* final norm eps (crates/realm-models/src/model.rs:604-610) */
+  float layer_eps;  /* per-layer norm eps (memory64_host.rs:2069, 2337 use the config eps) */
+  float rope_theta;
+  int32_t kv_dtype; /* RB_F32 or RB_F16 */
+  uint32_t max_tenants;
+  uint32_t kv_pages; /* 0: max_tenants * ceil(max_seq / 16) */
+} rb_model_config;
+
+/* weight ids (layer = -1 for the global ones) */
+#define RB_W_TOKEN_EMBD 0
+#define RB_W_OUTPUT_NORM 1
+#define RB_W_OUTPUT 2
+#define RB_W_ATTN_NORM 10
+#define RB_W_Q 11
+#define RB_W_K 12
+#define RB_W_V 13
+#define RB_W_O 14
+#define RB_W_FFN_NORM 15
+#define RB_W_GATE 16
+#define RB_W_UP 17
+#define RB_W_DOWN 18
+
+int32_t rb_model_create(rb_ctx* ctx, const rb_model_config* cfg, int32_t* model);
+int32_t rb_model_destroy(rb_ctx* ctx, int32_t model);
+/* Stores one tensor (GGUF bytes, or f32 for norms). Returns bytes stored. */
+int32_t rb_model_set_weight(rb_ctx* ctx, int32_t model, int32_t which, int32_t layer, int32_t dtype, const void* data,
+                            size_t nbytes, uint32_t flags);
+/* Tiles and fuses the stored tensors (q|k, gate/up interleave); call once after set_weight. */
+int32_t rb_model_finalize(rb_ctx* ctx, int32_t model);
+/* The KV pool holding this model's tenants (usable with the rb_kv_* calls). */
+int32_t rb_model_kv_pool(rb_ctx* ctx, int32_t model);
+int32_t rb_tenant_create(rb_ctx* ctx, int32_t model, uint32_t tenant);
+int32_t rb_tenant_reset(rb_ctx* ctx, int32_t model, uint32_t tenant);
+
+/* Batched forward over query rows (decode: one row per tenant; prefill chunk:
+ * consecutive rows of one tenant). Row r feeds tokens[r] at positions[r]
+ * (NULL: the tenant's cache length, then +1 per further row of that tenant),
+ * which must equal the tenant's cache length plus the row's rank within the
+ * tenant. Follows Model::forward (crates/realm-models/src/model.rs:572-625) per
+ * row: embed, layers, final norm, LM head. logits: [n_rows][vocab] or NULL;
+ * argmax: [n_rows] greedy ids (sampling.rs:141-148, ties -> last) or NULL.
+ * Returns n_rows. */
+int32_t rb_forward(rb_ctx* ctx, int32_t model, uint32_t n_rows, const uint32_t* tenants, const uint32_t* tokens,
+                   const uint32_t* positions, float* logits, uint32_t* argmax, uint32_t flags);
+
+/* realm_embed_tokens (crates/realm-runtime/src/memory64_host.rs:2483-2613): out [n][hidden]. Returns bytes. */
+int32_t rb_embed_tokens(rb_ctx* ctx, int32_t model, const uint32_t* token_ids, uint32_t n, float* out,
+                        uint32_t flags);
+/* realm_forward_layer (memory64_host.rs:1918-2471): one transformer layer over
+ * hidden [hidden_len / hidden][hidden] for `tenant`, appending to its cache at
+ * `position` (must equal the layer's cache length). Returns bytes written. */
+int32_t rb_forward_layer(rb_ctx* ctx, int32_t model, uint32_t tenant, uint32_t layer, const float* hidden,
+                         uint32_t hidden_len, uint32_t position, float* out, uint32_t flags);
+/* realm_compute_logits (memory64_host.rs:2742-2896): final norm + LM head of one
+ * hidden row (hidden_len == hidden). Returns vocab * 4 bytes. */
+int32_t rb_compute_logits(rb_ctx* ctx, int32_t model, const float* hidden, uint32_t hidden_len, float* out,
+                          uint32_t flags);
+/* memory64_load_layer (memory64_host.rs:688-763): copies layer `layer_id`'s GGUF
+ * weight bytes (wq, wk, wv, wo, w_gate, w_up, w_down in that order) to dst.
+ * Returns bytes, RB_ERR_NOT_FOUND (no such layer) or RB_ERR_INVALID (max_size too small). */
+int32_t rb_memory64_load_layer(rb_ctx* ctx, int32_t model, uint32_t layer_id, void* dst, uint32_t max_size);
+
+/* Timing hook for benchmarks: device time (ms) of the last rb_forward. */
+float rb_last_forward_ms(rb_ctx* ctx);
+/* Kernel launches issued by the last rb_forward (graph replays count their kernels). */
+int32_t rb_last_forward_launches(rb_ctx* ctx);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* REALM_B200_H */

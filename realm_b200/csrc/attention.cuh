@@ -1,0 +1,37 @@
+// Paged KV cache kernels and paged GQA decode attention.
+#pragma once
+#include "gemv.cuh"
+
+namespace rb {
+
+struct AttnArgs {
+  int32_t n_rows = 0;              // query rows (tenant, position) pairs
+  const int32_t* row_tenant = nullptr;
+  const int32_t* row_pos = nullptr;  // row attends to positions [0, pos]
+  const float* q = nullptr;        // [n_rows][ldq], head h at h*hd
+  int32_t ldq = 0;
+  float* out = nullptr;            // [n_rows][ldo]
+  int32_t ldo = 0;
+  int32_t n_heads = 0;
+  int32_t layer = 0;
+  float scale = 0.f;
+  KvView kv;
+  float* partials = nullptr;       // split scratch
+  int32_t* counters = nullptr;     // [n_rows * n_kv]
+  int32_t max_splits = 0;          // partial slots per (row, kv head)
+  uint32_t* err = nullptr;
+};
+
+constexpr int kAttnPagesPerSplit = 16;  // 256 tokens per split
+
+size_t attn_partials_floats(int max_rows, int n_kv, int n_rep, int hd, int max_splits);
+cudaError_t attn_launch(const AttnArgs& a, int num_sms, cudaStream_t s, int pdl);
+
+// Standalone append of k/v rows ([n_rows][n_kv*hd] fp32) at (tenant, pos).
+cudaError_t kv_append_launch(const KvView& kv, int layer, int n_rows, const int32_t* row_tenant,
+                             const int32_t* row_pos, const float* k, const float* v, cudaStream_t s);
+// Gather one tenant/layer's first `len` positions into [len][n_kv][hd] fp32.
+cudaError_t kv_gather_launch(const KvView& kv, int layer, int tenant, int len, float* k_out, float* v_out,
+                             cudaStream_t s);
+
+}  // namespace rb

@@ -1,0 +1,1363 @@
+// Host runtime behind the C ABI: contexts, resident weights, paged KV pools,
+// models and the batched forward (decode step) with CUDA-graph replay.
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cmath>
+#include <cstdarg>
+#include <cstdio>
+#include <chrono>
+#include <cstring>
+#include <map>
+#include <memory>
+#include <random>
+#include <string>
+#include <vector>
+
+#include "../../include/realm_b200.h"
+#include "attention.cuh"
+#include "common.cuh"
+#include "gemv.cuh"
+#include "quant.cuh"
+
+namespace rb {
+
+// ---------------------------------------------------------------------------
+// errors
+// ---------------------------------------------------------------------------
+static thread_local std::string g_last_error;
+
+int fail(int code, const char* fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof buf, fmt, ap);
+  va_end(ap);
+  g_last_error = buf;
+  return code;
+}
+
+#define RB_CUDA(call)                                                                         \
+  do {                                                                                        \
+    cudaError_t e_ = (call);                                                                  \
+    if (e_ != cudaSuccess) return fail(RB_ERR_CUDA, "%s: %s (%s:%d)", #call, cudaGetErrorString(e_), __FILE__, __LINE__); \
+  } while (0)
+
+// ---------------------------------------------------------------------------
+// small kernels owned by the runtime
+// ---------------------------------------------------------------------------
+struct StepDesc {  // device view of one forward step (filled by one H2D copy)
+  int32_t n_rows;
+  int32_t n_updates;
+  int32_t* row_tenant;
+  int32_t* row_pos;
+  int32_t* tokens;
+  int32_t* upd;  // [n_updates][3] (tenant, page index, physical page)
+};
+
+// Embedding rows (bit-exact dequant of token_embd, model.rs:579-596 /
+// memory64_host.rs:2570-2583), page-table updates, argmax reset, and the
+// per-128-column sums of squares feeding the first fused RMSNorm.
+__global__ void embed_kernel(const uint8_t* embd, int dtype, int hidden, const int32_t* desc_i, int32_t* ptab,
+                             int ptab_stride, float* x, int ldx, float* ss, int ld_ss, unsigned long long* argmax) {
+  const int n_rows = desc_i[0], n_upd = desc_i[1];
+  const int32_t* row_tokens = desc_i + 2 + 2 * 64;
+  const int32_t* upd = desc_i + 2 + 3 * 64;
+  const int r = blockIdx.x;
+  if (r == 0) {
+    for (int i = threadIdx.x; i < n_upd; i += blockDim.x)
+      ptab[(size_t)upd[3 * i] * ptab_stride + upd[3 * i + 1]] = upd[3 * i + 2];
+  }
+  if (r >= n_rows) return;
+  if (threadIdx.x == 0 && argmax) argmax[r] = 0ull;
+  const int tok = row_tokens[r];
+  const int be = block_elems(dtype), bb = block_bytes(dtype);
+  const size_t row_bytes = (size_t)(hidden / be) * bb;
+  const uint8_t* src = embd + (size_t)tok * row_bytes;
+  __shared__ float red[8];
+  for (int g0 = 0; g0 < hidden; g0 += 128) {
+    float sq = 0.f;
+    if (threadIdx.x < 128) {
+      const int i = g0 + threadIdx.x;
+      float v = 0.f;
+      if (i < hidden) {
+        const uint8_t* blk = src + (size_t)(i / be) * bb;
+        const int e = i % be;
+        v = dtype == DT_Q4_K ? dequant_q4k_elem(blk, e)
+          : dtype == DT_Q6_K ? dequant_q6k_elem(blk, e)
+          : dtype == DT_Q8_0 ? dequant_q80_elem(blk, e)
+                             : reinterpret_cast<const float*>(embd)[(size_t)tok * hidden + i];
+        x[(size_t)r * ldx + i] = v;
+      }
+      sq = v * v;
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) sq += __shfl_xor_sync(0xffffffffu, sq, o);
+    if ((threadIdx.x & 31) == 0 && threadIdx.x < 128) red[threadIdx.x >> 5] = sq;
+    __syncthreads();
+    if (threadIdx.x == 0) ss[(size_t)(g0 / 128) * ld_ss + r] = (red[0] + red[1]) + (red[2] + red[3]);
+    __syncthreads();
+  }
+}
+
+// Per-128-column sums of squares of x rows (for forward_layer / compute_logits entry).
+__global__ void ss_kernel(const float* x, int ldx, int hidden, float* ss, int ld_ss) {
+  const int r = blockIdx.y, g = blockIdx.x;
+  const int i = g * 128 + threadIdx.x;
+  float v = i < hidden ? x[(size_t)r * ldx + i] : 0.f;
+  float sq = v * v;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) sq += __shfl_xor_sync(0xffffffffu, sq, o);
+  __shared__ float red[4];
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = sq;
+  __syncthreads();
+  if (threadIdx.x == 0) ss[(size_t)g * ld_ss + r] = (red[0] + red[1]) + (red[2] + red[3]);
+}
+
+__global__ void zero_u64_kernel(unsigned long long* p, int n) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < n) p[i] = 0ull;
+}
+
+// Plain tiled fp32 GEMM for the candle_matmul host functions (not on the decode path).
+__global__ void sgemm_kernel(const float* A, const float* B, float* Cm, int M, int K, int N, int b_trans) {
+  __shared__ float As[16][17], Bs[16][17];
+  const int tx = threadIdx.x, ty = threadIdx.y;
+  const int row = blockIdx.y * 16 + ty, col = blockIdx.x * 16 + tx;
+  float acc = 0.f;
+  for (int k0 = 0; k0 < K; k0 += 16) {
+    As[ty][tx] = (row < M && k0 + tx < K) ? A[(size_t)row * K + k0 + tx] : 0.f;
+    const int bk = k0 + ty;
+    Bs[ty][tx] = (bk < K && col < N) ? (b_trans ? B[(size_t)col * K + bk] : B[(size_t)bk * N + col]) : 0.f;
+    __syncthreads();
+#pragma unroll
+    for (int kk = 0; kk < 16; ++kk) acc = fmaf(As[ty][kk], Bs[kk][tx], acc);
+    __syncthreads();
+  }
+  if (row < M && col < N) Cm[(size_t)row * N + col] = acc;
+}
+
+// ---------------------------------------------------------------------------
+// resources
+// ---------------------------------------------------------------------------
+struct DevBuf {
+  void* p = nullptr;
+  size_t n = 0;
+  DevBuf() = default;
+  DevBuf(const DevBuf&) = delete;
+  DevBuf& operator=(const DevBuf&) = delete;
+  DevBuf(DevBuf&& o) noexcept : p(o.p), n(o.n) { o.p = nullptr; o.n = 0; }
+  DevBuf& operator=(DevBuf&& o) noexcept {
+    if (this != &o) { release(); p = o.p; n = o.n; o.p = nullptr; o.n = 0; }
+    return *this;
+  }
+  ~DevBuf() { release(); }
+  void release() {
+    if (p) cudaFree(p);
+    p = nullptr;
+    n = 0;
+  }
+  cudaError_t alloc(size_t bytes) {
+    release();
+    if (bytes == 0) return cudaSuccess;
+    cudaError_t e = cudaMalloc(&p, bytes);
+    if (e == cudaSuccess) n = bytes;
+    return e;
+  }
+  template <class T> T* as() const { return reinterpret_cast<T*>(p); }
+};
+
+struct Weight {
+  int dtype = 0, n = 0, k = 0, n_rg = 0;
+  DevBuf tiled;
+};
+
+struct KvTenant {
+  bool live = false;
+  std::vector<int> len;    // per layer
+  std::vector<int> pages;  // physical ids
+};
+
+struct KvPool {
+  int n_layers = 0, n_kv = 0, hd = 0, f16 = 1, max_tenants = 0, max_seq = 0, max_pages_per_tenant = 0;
+  int n_pages = 0;
+  DevBuf pool, ptab;
+  std::vector<int32_t> h_ptab;
+  std::vector<int> free_list;  // stack; back() is handed out next
+  std::vector<KvTenant> tenants;
+  KvView view() const {
+    KvView v;
+    v.pool = pool.p;
+    v.f16 = f16;
+    v.n_layers = n_layers;
+    v.n_kv = n_kv;
+    v.hd = hd;
+    v.ptab = ptab.as<int32_t>();
+    v.ptab_stride = max_pages_per_tenant;
+    return v;
+  }
+};
+
+struct RawTensor {
+  int dtype = -1;
+  size_t bytes = 0;
+  DevBuf d;
+};
+
+struct LayerW {
+  RawTensor raw[9];  // attn_norm, q, k, v, o, ffn_norm, gate, up, down
+  Weight qk, v, o, gu, down;
+  bool v_fused = false;
+};
+
+struct Model {
+  rb_model_config cfg{};
+  int pool = -1;
+  RawTensor embd, out_norm, out_raw;
+  Weight out;
+  std::vector<LayerW> layers;
+  bool finalized = false;
+  // step buffers
+  DevBuf x, q, att, h, ss, logits, argmax, desc;
+  int max_rows = 0;
+  std::map<int, cudaGraphExec_t> graphs;  // by row count
+  std::map<int, int> graph_launches;
+};
+
+struct Ctx {
+  int device = 0, num_sms = 148, max_rows = 64;
+  bool pdl = true, graphs = true;
+  cudaStream_t stream = nullptr;
+  cudaEvent_t ev0 = nullptr, ev1 = nullptr;
+  DevBuf gemv_partials, counters, attn_partials, err;
+  size_t attn_partials_cap = 0;
+  DevBuf stage_in, stage_out;  // generic device staging for host-pointer calls
+  void* pinned = nullptr;      // step descriptor staging
+  size_t pinned_bytes = 0;
+  cudaEvent_t pinned_ev = nullptr;  // last copy out of `pinned` (reuse waits on it)
+  std::vector<std::unique_ptr<Weight>> weights;
+  std::vector<std::unique_ptr<KvPool>> pools;
+  std::vector<std::unique_ptr<Model>> models;
+  float last_ms = 0.f;
+  int last_launches = 0;
+};
+
+constexpr int kMaxRowsAbi = 64;
+constexpr int kCounters = 1 << 16;
+
+int check_err(Ctx* c) {
+  uint32_t e = 0;
+  RB_CUDA(cudaMemcpyAsync(&e, c->err.p, 4, cudaMemcpyDeviceToHost, c->stream));
+  RB_CUDA(cudaStreamSynchronize(c->stream));
+  if (e) {
+    cudaMemsetAsync(c->err.p, 0, 4, c->stream);
+    cudaStreamSynchronize(c->stream);
+    return fail(RB_ERR_TIMEOUT, "device wait timed out (code %u)", e);
+  }
+  return RB_OK;
+}
+
+// Bounded host wait on the stream.
+int sync_ctx(Ctx* c, double timeout_s = 60.0) {
+  const auto t0 = std::chrono::steady_clock::now();
+  for (;;) {
+    cudaError_t e = cudaStreamQuery(c->stream);
+    if (e == cudaSuccess) break;
+    if (e != cudaErrorNotReady) return fail(RB_ERR_CUDA, "stream: %s", cudaGetErrorString(e));
+    if (std::chrono::duration<double>(std::chrono::steady_clock::now() - t0).count() > timeout_s)
+      return fail(RB_ERR_TIMEOUT, "stream did not finish within %.0f s", timeout_s);
+  }
+  return check_err(c);
+}
+
+// Stage a caller buffer on the device (copy if host). Returns device pointer.
+struct Staged {
+  DevBuf own;
+  const void* dptr = nullptr;
+};
+int stage(Ctx* c, const void* src, size_t bytes, uint32_t flags, Staged& out) {
+  if (flags & RB_PTR_DEVICE) {
+    out.dptr = src;
+    return RB_OK;
+  }
+  RB_CUDA(out.own.alloc(bytes ? bytes : 1));
+  if (bytes) RB_CUDA(cudaMemcpyAsync(out.own.p, src, bytes, cudaMemcpyHostToDevice, c->stream));
+  out.dptr = out.own.p;
+  return RB_OK;
+}
+
+int ensure_attn_partials(Ctx* c, size_t floats) {
+  if (floats <= c->attn_partials_cap) return RB_OK;
+  RB_CUDA(c->attn_partials.alloc(floats * 4));
+  c->attn_partials_cap = floats;
+  return RB_OK;
+}
+
+int upload_tiled(Ctx* c, Weight& w, int dtype, int n, int k, const uint8_t* a, int rows_a, const uint8_t* b,
+                 int rows_b, int mode) {
+  if (dtype != DT_Q4_K && dtype != DT_Q6_K && dtype != DT_Q8_0)
+    return fail(RB_ERR_UNSUPPORTED, "dtype %d has no tiled GEMV", dtype);
+  if (k % kSuperK) return fail(RB_ERR_UNSUPPORTED, "K=%d must be a multiple of 256", k);
+  w.dtype = dtype;
+  w.n = n;
+  w.k = k;
+  w.n_rg = (n + kRowGroup - 1) / kRowGroup;
+  RB_CUDA(w.tiled.alloc((size_t)w.n_rg * (k / kSuperK) * unit_bytes(dtype)));
+  RB_CUDA(repack_launch(a, rows_a, b, rows_b, mode, dtype, k, w.tiled.as<uint8_t>(), w.n_rg, c->stream));
+  return RB_OK;
+}
+
+GemvArgs base_args(Ctx* c, const Weight& w, int m) {
+  GemvArgs a;
+  a.w = w.tiled.as<uint8_t>();
+  a.dtype = w.dtype;
+  a.n = w.n;
+  a.n_rg = w.n_rg;
+  a.nsb = w.k / kSuperK;
+  a.m = m;
+  a.ldx = w.k;
+  a.partials = c->gemv_partials.as<float>();
+  a.counters = c->counters.as<int32_t>();
+  a.err = c->err.as<uint32_t>();
+  return a;
+}
+
+int launch_gemv(Ctx* c, const GemvArgs& a, int* launches) {
+  RB_CUDA(gemv_launch(a, c->num_sms, c->stream, c->pdl ? 1 : 0));
+  if (launches) ++*launches;
+  return RB_OK;
+}
+
+// ---------------------------------------------------------------------------
+// model forward (enqueue only)
+// ---------------------------------------------------------------------------
+int enqueue_layer(Ctx* c, Model& M, int l, int m, const int32_t* d_tenant, const int32_t* d_pos, int* launches) {
+  const rb_model_config& cf = M.cfg;
+  KvPool& P = *c->pools[M.pool];
+  LayerW& L = M.layers[l];
+  const int H = cf.hidden, hd = cf.head_dim, Hq = cf.n_heads, Hkv = cf.n_kv_heads;
+  const int n_ss = (H + 127) / 128;
+  float* x = M.x.as<float>();
+  float* ss = M.ss.as<float>();
+  // q|k (+v) with fused RMSNorm prologue, RoPE and KV append epilogue
+  GemvArgs a = base_args(c, L.qk, m);
+  a.x = x;
+  a.ldx = H;
+  a.norm_w = L.raw[0].d.as<float>();
+  a.ss_part = ss;
+  a.n_ss = n_ss;
+  a.ld_ss = kMaxRowsAbi;
+  a.norm_eps = cf.layer_eps;
+  a.norm_dim = H;
+  a.epi = EPI_QKV;
+  a.qkv_row0 = 0;
+  a.n_q_rows = Hq * hd;
+  a.n_k_rows = Hkv * hd;
+  a.q_out = M.q.as<float>();
+  a.ldq = Hq * hd;
+  a.rope_theta = cf.rope_theta;
+  a.head_dim = hd;
+  a.layer = l;
+  a.row_tenant = d_tenant;
+  a.row_pos = d_pos;
+  a.kv = P.view();
+  if (int rc = launch_gemv(c, a, launches)) return rc;
+  if (!L.v_fused) {
+    GemvArgs av = a;
+    av.w = L.v.tiled.as<uint8_t>();
+    av.dtype = L.v.dtype;
+    av.n = L.v.n;
+    av.n_rg = L.v.n_rg;
+    av.nsb = L.v.k / kSuperK;
+    av.qkv_row0 = (Hq + Hkv) * hd;
+    if (int rc = launch_gemv(c, av, launches)) return rc;
+  }
+  // paged GQA attention
+  AttnArgs at;
+  at.n_rows = m;
+  at.row_tenant = d_tenant;
+  at.row_pos = d_pos;
+  at.q = M.q.as<float>();
+  at.ldq = Hq * hd;
+  at.out = M.att.as<float>();
+  at.ldo = Hq * hd;
+  at.n_heads = Hq;
+  at.layer = l;
+  at.scale = 1.0f / sqrtf((float)hd);  // attention_stub/mod.rs:57
+  at.kv = P.view();
+  at.partials = c->attn_partials.as<float>();
+  at.counters = c->counters.as<int32_t>() + kCounters / 2;
+  at.max_splits = (cf.max_seq + 16 * kAttnPagesPerSplit - 1) / (16 * kAttnPagesPerSplit);
+  at.err = c->err.as<uint32_t>();
+  RB_CUDA(attn_launch(at, c->num_sms, c->stream, c->pdl ? 1 : 0));
+  if (launches) ++*launches;
+  // o-proj + residual
+  GemvArgs ao = base_args(c, L.o, m);
+  ao.x = M.att.as<float>();
+  ao.ldx = Hq * hd;
+  ao.epi = EPI_RESID;
+  ao.resid = x;
+  ao.ldr = H;
+  ao.ss_out = ss;
+  ao.ld_ss = kMaxRowsAbi;
+  if (int rc = launch_gemv(c, ao, launches)) return rc;
+  // gate/up (interleaved) with fused RMSNorm prologue and SwiGLU epilogue
+  GemvArgs ag = base_args(c, L.gu, m);
+  ag.x = x;
+  ag.ldx = H;
+  ag.norm_w = L.raw[5].d.as<float>();
+  ag.ss_part = ss;
+  ag.n_ss = n_ss;
+  ag.ld_ss = kMaxRowsAbi;
+  ag.norm_eps = cf.layer_eps;
+  ag.norm_dim = H;
+  ag.epi = EPI_SWIGLU;
+  ag.y = M.h.as<float>();
+  ag.ldy = cf.ffn;
+  if (int rc = launch_gemv(c, ag, launches)) return rc;
+  // down + residual
+  GemvArgs ad = base_args(c, L.down, m);
+  ad.x = M.h.as<float>();
+  ad.ldx = cf.ffn;
+  ad.epi = EPI_RESID;
+  ad.resid = x;
+  ad.ldr = H;
+  ad.ss_out = ss;
+  ad.ld_ss = kMaxRowsAbi;
+  return launch_gemv(c, ad, launches);
+}
+
+int enqueue_head(Ctx* c, Model& M, int m, bool want_logits, int* launches) {
+  const rb_model_config& cf = M.cfg;
+  GemvArgs a = base_args(c, M.out, m);
+  a.x = M.x.as<float>();
+  a.ldx = cf.hidden;
+  a.norm_w = M.out_norm.d.as<float>();
+  a.ss_part = M.ss.as<float>();
+  a.n_ss = (cf.hidden + 127) / 128;
+  a.ld_ss = kMaxRowsAbi;
+  a.norm_eps = cf.rms_eps;
+  a.norm_dim = cf.hidden;
+  a.epi = EPI_LOGITS;
+  a.y = want_logits ? M.logits.as<float>() : nullptr;
+  a.ldy = cf.vocab;
+  a.argmax = M.argmax.as<unsigned long long>();
+  return launch_gemv(c, a, launches);
+}
+
+// Descriptor layout in int32s: [n_rows, n_upd, tenant[64], pos[64], tokens[64], upd[...][3]]
+constexpr int kDescTenant = 2, kDescPos = 2 + 64, kDescTok = 2 + 128, kDescUpd = 2 + 192;
+
+int enqueue_step(Ctx* c, Model& M, int m, int* launches) {
+  const rb_model_config& cf = M.cfg;
+  KvPool& P = *c->pools[M.pool];
+  int32_t* desc = M.desc.as<int32_t>();
+  // the embed kernel expects tokens at +2+128 and updates at +2+192
+  embed_kernel<<<m, 128, 0, c->stream>>>(M.embd.d.as<uint8_t>(), M.embd.dtype, cf.hidden, desc, P.ptab.as<int32_t>(),
+                                         P.max_pages_per_tenant, M.x.as<float>(), cf.hidden, M.ss.as<float>(),
+                                         kMaxRowsAbi, M.argmax.as<unsigned long long>());
+  RB_CUDA(cudaGetLastError());
+  if (launches) ++*launches;
+  for (int l = 0; l < (int)cf.n_layers; ++l)
+    if (int rc = enqueue_layer(c, M, l, m, desc + kDescTenant, desc + kDescPos, launches)) return rc;
+  return enqueue_head(c, M, m, true, launches);
+}
+
+}  // namespace rb
+
+// ===========================================================================
+// C ABI
+// ===========================================================================
+using namespace rb;
+
+struct rb_ctx : Ctx {};
+
+namespace {
+
+__global__ void ptab_update_kernel(const int32_t* desc, int32_t* ptab, int stride) {
+  const int n_upd = desc[1];
+  const int32_t* upd = desc + kDescUpd;
+  for (int i = threadIdx.x; i < n_upd; i += blockDim.x) ptab[(size_t)upd[3 * i] * stride + upd[3 * i + 1]] = upd[3 * i + 2];
+}
+
+KvPool* get_pool(rb_ctx* c, int32_t pool) {
+  if (!c || pool < 0 || pool >= (int)c->pools.size() || !c->pools[pool]) return nullptr;
+  return c->pools[pool].get();
+}
+Model* get_model(rb_ctx* c, int32_t model) {
+  if (!c || model < 0 || model >= (int)c->models.size() || !c->models[model]) return nullptr;
+  return c->models[model].get();
+}
+
+// Rows for one step: validates positions, allocates pages, fills the pinned
+// descriptor. rank_layer < 0 checks all layers' lengths (model forward).
+struct RowPlan {
+  std::vector<int> tenant, pos, tok;
+  std::vector<int> upd;  // triples
+};
+
+int plan_rows(KvPool& P, int n, const uint32_t* tenants, const uint32_t* tokens, const uint32_t* positions,
+              int layer, RowPlan& rp) {
+  rp.tenant.assign(n, 0);
+  rp.pos.assign(n, 0);
+  rp.tok.assign(n, 0);
+  rp.upd.clear();
+  std::map<int, int> rank;
+  for (int r = 0; r < n; ++r) {
+    const uint32_t t = tenants[r];
+    if (t >= (uint32_t)P.max_tenants || !P.tenants[t].live) return fail(RB_ERR_NOT_FOUND, "tenant %u not created", t);
+    KvTenant& T = P.tenants[t];
+    const int base = T.len[layer < 0 ? 0 : layer];
+    if (layer < 0)
+      for (int l = 1; l < P.n_layers; ++l)
+        if (T.len[l] != base) return fail(RB_ERR_INVALID, "tenant %u layers out of step", t);
+    const int expect = base + rank[t]++;
+    const int pos = positions ? (int)positions[r] : expect;
+    if (pos != expect) return fail(RB_ERR_INVALID, "row %d: position %d != cache length %d", r, pos, expect);
+    if (pos >= P.max_seq)
+      return fail(RB_ERR_KV_OVERFLOW, "KV cache overflow: %d + 1 > %d", pos, P.max_seq);
+    rp.tenant[r] = (int)t;
+    rp.pos[r] = pos;
+    rp.tok[r] = tokens ? (int)tokens[r] : 0;
+  }
+  // page allocation (all-or-nothing)
+  std::vector<std::pair<int, int>> taken;
+  for (int r = 0; r < n; ++r) {
+    KvTenant& T = P.tenants[rp.tenant[r]];
+    const int idx = rp.pos[r] >> 4;
+    while ((int)T.pages.size() <= idx) {
+      if (P.free_list.empty()) {
+        for (auto it = taken.rbegin(); it != taken.rend(); ++it) {
+          P.tenants[it->first].pages.pop_back();
+          P.free_list.push_back(it->second);
+        }
+        return fail(RB_ERR_KV_POOL_EXHAUSTED, "KV page pool exhausted");
+      }
+      const int pg = P.free_list.back();
+      P.free_list.pop_back();
+      T.pages.push_back(pg);
+      taken.push_back({rp.tenant[r], pg});
+      const int pi = (int)T.pages.size() - 1;
+      P.h_ptab[(size_t)rp.tenant[r] * P.max_pages_per_tenant + pi] = pg;
+      rp.upd.insert(rp.upd.end(), {rp.tenant[r], pi, pg});
+    }
+  }
+  return RB_OK;
+}
+
+int upload_desc(rb_ctx* c, const RowPlan& rp, int32_t* d_desc) {
+  const int n = (int)rp.tenant.size(), nu = (int)rp.upd.size() / 3;
+  const size_t ints = kDescUpd + 3 * (size_t)nu;
+  if (ints * 4 > c->pinned_bytes) return fail(RB_ERR_INVALID, "descriptor too large");
+  // an earlier asynchronous call may still be copying out of the staging buffer
+  RB_CUDA(cudaEventSynchronize(c->pinned_ev));
+  int32_t* h = reinterpret_cast<int32_t*>(c->pinned);
+  h[0] = n;
+  h[1] = nu;
+  for (int r = 0; r < n; ++r) {
+    h[kDescTenant + r] = rp.tenant[r];
+    h[kDescPos + r] = rp.pos[r];
+    h[kDescTok + r] = rp.tok[r];
+  }
+  std::copy(rp.upd.begin(), rp.upd.end(), h + kDescUpd);
+  RB_CUDA(cudaMemcpyAsync(d_desc, h, ints * 4, cudaMemcpyHostToDevice, c->stream));
+  RB_CUDA(cudaEventRecord(c->pinned_ev, c->stream));
+  return RB_OK;
+}
+
+int copy_out(rb_ctx* c, void* dst, const void* src, size_t bytes, uint32_t flags) {
+  RB_CUDA(cudaMemcpyAsync(dst, src, bytes,
+                          (flags & RB_PTR_DEVICE) ? cudaMemcpyDeviceToDevice : cudaMemcpyDeviceToHost, c->stream));
+  return RB_OK;
+}
+
+int pool_create(rb_ctx* c, int n_layers, int n_kv, int hd, int kv_dtype, int n_pages, int max_tenants, int max_seq) {
+  if (n_layers < 1 || n_kv < 1 || (hd != 64 && hd != 128) || n_pages < 1 || max_tenants < 1 || max_seq < 1)
+    return fail(RB_ERR_UNSUPPORTED, "kv pool geometry (layers %d, kv %d, hd %d) unsupported", n_layers, n_kv, hd);
+  if (kv_dtype != RB_F16 && kv_dtype != RB_F32) return fail(RB_ERR_UNSUPPORTED, "kv dtype %d", kv_dtype);
+  auto P = std::make_unique<KvPool>();
+  P->n_layers = n_layers;
+  P->n_kv = n_kv;
+  P->hd = hd;
+  P->f16 = kv_dtype == RB_F16;
+  P->n_pages = n_pages;
+  P->max_tenants = max_tenants;
+  P->max_seq = max_seq;
+  P->max_pages_per_tenant = (max_seq + 15) / 16;
+  const size_t page_bytes = (size_t)n_layers * 2 * n_kv * 16 * hd * (P->f16 ? 2 : 4);
+  if (P->pool.alloc(page_bytes * n_pages) != cudaSuccess) return fail(RB_ERR_OOM, "kv pool of %zu bytes", page_bytes * n_pages);
+  RB_CUDA(cudaMemsetAsync(P->pool.p, 0, page_bytes * n_pages, c->stream));
+  P->h_ptab.assign((size_t)max_tenants * P->max_pages_per_tenant, 0);
+  RB_CUDA(P->ptab.alloc(P->h_ptab.size() * 4));
+  RB_CUDA(cudaMemsetAsync(P->ptab.p, 0, P->h_ptab.size() * 4, c->stream));
+  for (int i = n_pages - 1; i >= 0; --i) P->free_list.push_back(i);
+  P->tenants.resize(max_tenants);
+  const int n_rep_max = 8;
+  const int max_splits = (max_seq + 16 * kAttnPagesPerSplit - 1) / (16 * kAttnPagesPerSplit);
+  if (int rc = ensure_attn_partials(c, attn_partials_floats(kMaxRowsAbi, n_kv, n_rep_max, hd, max_splits))) return rc;
+  c->pools.push_back(std::move(P));
+  return (int)c->pools.size() - 1;
+}
+
+void tenant_release(KvPool& P, int t) {
+  KvTenant& T = P.tenants[t];
+  for (auto it = T.pages.rbegin(); it != T.pages.rend(); ++it) P.free_list.push_back(*it);
+  T.pages.clear();
+  std::fill(T.len.begin(), T.len.end(), 0);
+}
+
+int run_forward(rb_ctx* c, Model& M, int m, bool use_graph) {
+  int launches = 0;
+  RB_CUDA(cudaEventRecord(c->ev0, c->stream));
+  if (use_graph) {
+    auto it = M.graphs.find(m);
+    if (it == M.graphs.end()) {
+      cudaGraph_t g = nullptr;
+      RB_CUDA(cudaStreamBeginCapture(c->stream, cudaStreamCaptureModeThreadLocal));
+      int rc = enqueue_step(c, M, m, &launches);
+      cudaError_t e = cudaStreamEndCapture(c->stream, &g);
+      if (rc) {
+        if (g) cudaGraphDestroy(g);
+        return rc;
+      }
+      if (e != cudaSuccess) return fail(RB_ERR_CUDA, "graph capture: %s", cudaGetErrorString(e));
+      cudaGraphExec_t ex = nullptr;
+      e = cudaGraphInstantiate(&ex, g, 0);
+      cudaGraphDestroy(g);
+      if (e != cudaSuccess) return fail(RB_ERR_CUDA, "graph instantiate: %s", cudaGetErrorString(e));
+      it = M.graphs.emplace(m, ex).first;
+      M.graph_launches[m] = launches;
+    }
+    RB_CUDA(cudaGraphLaunch(it->second, c->stream));
+    launches = M.graph_launches[m];
+  } else {
+    if (int rc = enqueue_step(c, M, m, &launches)) return rc;
+  }
+  RB_CUDA(cudaEventRecord(c->ev1, c->stream));
+  c->last_launches = launches;
+  return RB_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int32_t rb_last_error(char* buf, size_t len) {
+  if (!buf || len == 0) return (int32_t)g_last_error.size();
+  const size_t n = std::min(len - 1, g_last_error.size());
+  std::memcpy(buf, g_last_error.data(), n);
+  buf[n] = 0;
+  return (int32_t)n;
+}
+
+int32_t rb_ctx_create(const rb_config* cfg, rb_ctx** out) {
+  if (!out) return fail(RB_ERR_INVALID, "out is NULL");
+  rb_config def{0, 64, 1, 1};
+  if (!cfg) cfg = &def;
+  int ndev = 0;
+  if (cudaGetDeviceCount(&ndev) != cudaSuccess || ndev == 0) return fail(RB_ERR_DISABLED, "no CUDA device");
+  if (cfg->device < 0 || cfg->device >= ndev) return fail(RB_ERR_NOT_FOUND, "device %d not present", cfg->device);
+  RB_CUDA(cudaSetDevice(cfg->device));
+  cudaDeviceProp prop;
+  RB_CUDA(cudaGetDeviceProperties(&prop, cfg->device));
+  if (prop.major != 10) return fail(RB_ERR_UNSUPPORTED, "device %s is sm_%d%d; this build targets sm_100a", prop.name, prop.major, prop.minor);
+  auto c = std::make_unique<rb_ctx>();
+  c->device = cfg->device;
+  c->num_sms = prop.multiProcessorCount;
+  c->max_rows = cfg->max_rows ? std::min<int>(cfg->max_rows, kMaxRowsAbi) : kMaxRowsAbi;
+  c->pdl = cfg->use_pdl != 0;
+  c->graphs = cfg->use_graphs != 0;
+  RB_CUDA(cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking));
+  RB_CUDA(cudaEventCreate(&c->ev0));
+  RB_CUDA(cudaEventCreate(&c->ev1));
+  RB_CUDA(cudaEventCreateWithFlags(&c->pinned_ev, cudaEventDisableTiming));
+  RB_CUDA(cudaEventRecord(c->pinned_ev, c->stream));
+  RB_CUDA(c->gemv_partials.alloc(gemv_partials_floats(c->num_sms, 8) * 4));
+  RB_CUDA(c->counters.alloc(kCounters * 4));
+  RB_CUDA(cudaMemsetAsync(c->counters.p, 0, kCounters * 4, c->stream));
+  RB_CUDA(c->err.alloc(16));
+  RB_CUDA(cudaMemsetAsync(c->err.p, 0, 16, c->stream));
+  c->pinned_bytes = 64 << 10;
+  RB_CUDA(cudaMallocHost(&c->pinned, c->pinned_bytes));
+  RB_CUDA(c->stage_in.alloc(c->pinned_bytes));
+  RB_CUDA(cudaStreamSynchronize(c->stream));
+  *out = c.release();
+  return RB_OK;
+}
+
+int32_t rb_ctx_destroy(rb_ctx* c) {
+  if (!c) return fail(RB_ERR_BAD_HANDLE, "null context");
+  cudaSetDevice(c->device);
+  cudaStreamSynchronize(c->stream);
+  for (auto& m : c->models)
+    if (m)
+      for (auto& g : m->graphs) cudaGraphExecDestroy(g.second);
+  c->models.clear();
+  c->pools.clear();
+  c->weights.clear();
+  if (c->pinned) cudaFreeHost(c->pinned);
+  cudaEventDestroy(c->ev0);
+  cudaEventDestroy(c->ev1);
+  cudaEventDestroy(c->pinned_ev);
+  cudaStreamDestroy(c->stream);
+  delete c;
+  return RB_OK;
+}
+
+int32_t rb_sync(rb_ctx* c) {
+  if (!c) return fail(RB_ERR_BAD_HANDLE, "null context");
+  return sync_ctx(c);
+}
+void* rb_stream(rb_ctx* c) { return c ? (void*)c->stream : nullptr; }
+int32_t rb_num_sms(rb_ctx* c) { return c ? c->num_sms : fail(RB_ERR_BAD_HANDLE, "null context"); }
+
+int32_t rb_dequantize(rb_ctx* c, int32_t dtype, const void* blocks, size_t nblocks, float* out, uint32_t flags) {
+  if (!c) return fail(RB_ERR_BAD_HANDLE, "null context");
+  if (dtype != DT_Q4_K && dtype != DT_Q6_K && dtype != DT_Q8_0) return fail(RB_ERR_UNSUPPORTED, "dtype %d", dtype);
+  const size_t n = nblocks * block_elems(dtype);
+  Staged in;
+  if (int rc = stage(c, blocks, nblocks * block_bytes(dtype), flags, in)) return rc;
+  DevBuf tmp;
+  float* dout = out;
+  if (!(flags & RB_PTR_DEVICE)) {
+    RB_CUDA(tmp.alloc(n * 4 + 4));
+    dout = tmp.as<float>();
+  }
+  RB_CUDA(dequant_launch(dtype, (const uint8_t*)in.dptr, nblocks, dout, c->stream));
+  if (!(flags & RB_PTR_DEVICE)) RB_CUDA(cudaMemcpyAsync(out, dout, n * 4, cudaMemcpyDeviceToHost, c->stream));
+  if (int rc = sync_ctx(c)) return rc;
+  return (int32_t)n;
+}
+
+int32_t rb_quantize(rb_ctx* c, int32_t dtype, const float* x, size_t n, void* out_blocks, uint32_t flags) {
+  if (!c) return fail(RB_ERR_BAD_HANDLE, "null context");
+  if (dtype != DT_Q4_K && dtype != DT_Q6_K && dtype != DT_Q8_0) return fail(RB_ERR_UNSUPPORTED, "dtype %d", dtype);
+  if (n % block_elems(dtype)) return fail(RB_ERR_INVALID, "n %% %d != 0", block_elems(dtype));
+  const size_t nb = n / block_elems(dtype), ob = nb * block_bytes(dtype);
+  Staged in;
+  if (int rc = stage(c, x, n * 4, flags, in)) return rc;
+  DevBuf tmp;
+  uint8_t* dout = (uint8_t*)out_blocks;
+  if (!(flags & RB_PTR_DEVICE)) {
+    RB_CUDA(tmp.alloc(ob + 16));
+    dout = tmp.as<uint8_t>();
+  }
+  RB_CUDA(quantize_launch(dtype, (const float*)in.dptr, n, dout, c->stream));
+  if (!(flags & RB_PTR_DEVICE)) RB_CUDA(cudaMemcpyAsync(out_blocks, dout, ob, cudaMemcpyDeviceToHost, c->stream));
+  if (int rc = sync_ctx(c)) return rc;
+  return (int32_t)nb;
+}
+
+int32_t rb_weight_upload(rb_ctx* c, int32_t dtype, uint32_t n, uint32_t k, const void* blocks, size_t nbytes,
+                         uint32_t flags, int32_t* handle) {
+  if (!c || !handle) return fail(RB_ERR_BAD_HANDLE, "null context/handle");
+  if (dtype != DT_Q4_K && dtype != DT_Q6_K && dtype != DT_Q8_0) return fail(RB_ERR_UNSUPPORTED, "dtype %d", dtype);
+  if (k % kSuperK) return fail(RB_ERR_UNSUPPORTED, "K dimension %u must be multiple of 256", k);
+  const size_t expect = (size_t)n * (k / block_elems(dtype)) * block_bytes(dtype);
+  if (nbytes != expect) return fail(RB_ERR_INVALID, "expected %zu bytes, got %zu", expect, nbytes);
+  Staged in;
+  if (int rc = stage(c, blocks, nbytes, flags, in)) return rc;
+  auto w = std::make_unique<Weight>();
+  if (int rc = upload_tiled(c, *w, dtype, n, k, (const uint8_t*)in.dptr, n, nullptr, 0, 0)) return rc;
+  if (int rc = sync_ctx(c)) return rc;
+  c->weights.push_back(std::move(w));
+  *handle = (int32_t)c->weights.size() - 1;
+  return RB_OK;
+}
+
+int32_t rb_weight_free(rb_ctx* c, int32_t h) {
+  if (!c || h < 0 || h >= (int)c->weights.size() || !c->weights[h]) return fail(RB_ERR_BAD_HANDLE, "weight %d", h);
+  cudaStreamSynchronize(c->stream);
+  c->weights[h].reset();
+  return RB_OK;
+}
+
+static int weight_matmul_dev(rb_ctx* c, const Weight& w, const float* din, float* dout, uint32_t batch) {
+  for (uint32_t b0 = 0; b0 < batch; b0 += kMaxRowsAbi) {
+    const int m = (int)std::min<uint32_t>(kMaxRowsAbi, batch - b0);
+    GemvArgs a = base_args(c, w, m);
+    a.x = din + (size_t)b0 * w.k;
+    a.ldx = w.k;
+    a.epi = EPI_STORE;
+    a.y = dout + (size_t)b0 * w.n;
+    a.ldy = w.n;
+    if (int rc = launch_gemv(c, a, nullptr)) return rc;
+  }
+  return RB_OK;
+}
+
+int32_t rb_weight_matmul(rb_ctx* c, int32_t h, const float* input, float* output, uint32_t batch, uint32_t flags) {
+  if (!c || h < 0 || h >= (int)c->weights.size() || !c->weights[h]) return fail(RB_ERR_BAD_HANDLE, "weight %d", h);
+  const Weight& w = *c->weights[h];
+  if (batch == 0) return 0;
+  Staged in;
+  if (int rc = stage(c, input, (size_t)batch * w.k * 4, flags, in)) return rc;
+  DevBuf tmp;
+  float* dout = output;
+  if (!(flags & RB_PTR_DEVICE)) {
+    RB_CUDA(tmp.alloc((size_t)batch * w.n * 4));
+    dout = tmp.as<float>();
+  }
+  if (int rc = weight_matmul_dev(c, w, (const float*)in.dptr, dout, batch)) return rc;
+  if (!(flags & RB_PTR_DEVICE)) RB_CUDA(cudaMemcpyAsync(output, dout, (size_t)batch * w.n * 4, cudaMemcpyDeviceToHost, c->stream));
+  if ((flags & RB_PTR_DEVICE) && (flags & RB_ASYNC)) return (int32_t)(batch * w.n);
+  if (int rc = sync_ctx(c)) return rc;
+  return (int32_t)(batch * w.n);
+}
+
+int32_t rb_weight_export(rb_ctx* c, int32_t h, void* out_blocks, size_t nbytes, uint32_t flags) {
+  if (!c || h < 0 || h >= (int)c->weights.size() || !c->weights[h]) return fail(RB_ERR_BAD_HANDLE, "weight %d", h);
+  const Weight& w = *c->weights[h];
+  if (w.dtype != DT_Q4_K) return fail(RB_ERR_UNSUPPORTED, "export supports Q4_K");
+  const size_t bytes = (size_t)w.n * (w.k / 256) * 144;
+  if (nbytes < bytes) return fail(RB_ERR_INVALID, "buffer too small");
+  DevBuf tmp;
+  uint8_t* d = (uint8_t*)out_blocks;
+  if (!(flags & RB_PTR_DEVICE)) {
+    RB_CUDA(tmp.alloc(bytes));
+    d = tmp.as<uint8_t>();
+  }
+  RB_CUDA(unpack_launch(w.tiled.as<uint8_t>(), w.dtype, w.n, w.k, d, c->stream));
+  if (!(flags & RB_PTR_DEVICE)) RB_CUDA(cudaMemcpyAsync(out_blocks, d, bytes, cudaMemcpyDeviceToHost, c->stream));
+  if (int rc = sync_ctx(c)) return rc;
+  return (int32_t)bytes;
+}
+
+int32_t rb_fused_dequant_matmul(rb_ctx* c, int32_t dtype, const void* blocks, size_t nblocks, const float* input,
+                                float* output, uint32_t batch, uint32_t n, uint32_t k, uint32_t flags) {
+  if (!c) return fail(RB_ERR_BAD_HANDLE, "null context");
+  if (dtype == DT_Q4_K || dtype == DT_Q6_K) {
+    if (k % 256) return fail(RB_ERR_UNSUPPORTED, "K dimension %u must be multiple of 256", k);
+    if (nblocks != (size_t)n * (k / 256)) return fail(RB_ERR_INVALID, "Expected %zu blocks, got %zu", (size_t)n * (k / 256), nblocks);
+  } else if (dtype == DT_Q8_0) {
+    if (nblocks != ((size_t)n * k + 31) / 32) return fail(RB_ERR_INVALID, "Wrong number of blocks: expected %zu, got %zu", ((size_t)n * k + 31) / 32, nblocks);
+    if (k % 256) return fail(RB_ERR_UNSUPPORTED, "Q8_0 GEMV needs K %% 256 == 0 (K=%u)", k);
+  } else {
+    return fail(RB_ERR_UNSUPPORTED, "dtype %d", dtype);
+  }
+  if (batch == 0) return 0;
+  Staged in;
+  if (int rc = stage(c, blocks, nblocks * block_bytes(dtype), flags, in)) return rc;
+  Weight w;
+  if (int rc = upload_tiled(c, w, dtype, n, k, (const uint8_t*)in.dptr, n, nullptr, 0, 0)) return rc;
+  Staged xin;
+  if (int rc = stage(c, input, (size_t)batch * k * 4, flags, xin)) return rc;
+  DevBuf tmp;
+  float* dout = output;
+  if (!(flags & RB_PTR_DEVICE)) {
+    RB_CUDA(tmp.alloc((size_t)batch * n * 4));
+    dout = tmp.as<float>();
+  }
+  if (int rc = weight_matmul_dev(c, w, (const float*)xin.dptr, dout, batch)) return rc;
+  if (!(flags & RB_PTR_DEVICE)) RB_CUDA(cudaMemcpyAsync(output, dout, (size_t)batch * n * 4, cudaMemcpyDeviceToHost, c->stream));
+  if (int rc = sync_ctx(c)) return rc;
+  return (int32_t)(batch * n);
+}
+
+static int32_t candle_mm(rb_ctx* c, const float* a, const float* b, float* cm, uint32_t m, uint32_t k, uint32_t n,
+                         uint32_t flags, int bt) {
+  if (!c) return fail(RB_ERR_BAD_HANDLE, "null context");
+  if (m == 0 || k == 0 || n == 0) return fail(RB_ERR_INVALID, "empty matmul");
+  Staged sa, sb;
+  if (int rc = stage(c, a, (size_t)m * k * 4, flags, sa)) return rc;
+  if (int rc = stage(c, b, (size_t)k * n * 4, flags, sb)) return rc;
+  DevBuf tmp;
+  float* d = cm;
+  if (!(flags & RB_PTR_DEVICE)) {
+    RB_CUDA(tmp.alloc((size_t)m * n * 4));
+    d = tmp.as<float>();
+  }
+  dim3 grid((n + 15) / 16, (m + 15) / 16), block(16, 16);
+  sgemm_kernel<<<grid, block, 0, c->stream>>>((const float*)sa.dptr, (const float*)sb.dptr, d, m, k, n, bt);
+  RB_CUDA(cudaGetLastError());
+  if (!(flags & RB_PTR_DEVICE)) RB_CUDA(cudaMemcpyAsync(cm, d, (size_t)m * n * 4, cudaMemcpyDeviceToHost, c->stream));
+  if (int rc = sync_ctx(c)) return rc;
+  return (int32_t)(m * n);
+}
+
+int32_t rb_candle_matmul(rb_ctx* c, const float* a, const float* b, float* cm, uint32_t m, uint32_t k, uint32_t n,
+                         uint32_t flags) {
+  return candle_mm(c, a, b, cm, m, k, n, flags, 0);
+}
+int32_t rb_candle_matmul_transposed(rb_ctx* c, const float* a, const float* b, float* cm, uint32_t m, uint32_t k,
+                                    uint32_t n, uint32_t flags) {
+  return candle_mm(c, a, b, cm, m, k, n, flags, 1);
+}
+
+// ---- KV ----
+int32_t rb_kv_pool_create(rb_ctx* c, uint32_t n_layers, uint32_t n_kv, uint32_t hd, int32_t kv_dtype,
+                          uint32_t n_pages, uint32_t max_tenants, uint32_t max_seq, int32_t* pool) {
+  if (!c || !pool) return fail(RB_ERR_BAD_HANDLE, "null context/pool");
+  int rc = pool_create(c, n_layers, n_kv, hd, kv_dtype, n_pages, max_tenants, max_seq);
+  if (rc < 0) return rc;
+  *pool = rc;
+  if (int e = sync_ctx(c)) return e;
+  return RB_OK;
+}
+
+int32_t rb_kv_pool_destroy(rb_ctx* c, int32_t pool) {
+  if (!get_pool(c, pool)) return fail(RB_ERR_BAD_HANDLE, "pool %d", pool);
+  cudaStreamSynchronize(c->stream);
+  c->pools[pool].reset();
+  return RB_OK;
+}
+
+int32_t rb_kv_pool_shuffle(rb_ctx* c, int32_t pool, uint64_t seed) {
+  KvPool* P = get_pool(c, pool);
+  if (!P) return fail(RB_ERR_BAD_HANDLE, "pool %d", pool);
+  std::mt19937_64 g(seed);
+  std::shuffle(P->free_list.begin(), P->free_list.end(), g);
+  return RB_OK;
+}
+
+int32_t rb_kv_pool_free_pages(rb_ctx* c, int32_t pool) {
+  KvPool* P = get_pool(c, pool);
+  if (!P) return fail(RB_ERR_BAD_HANDLE, "pool %d", pool);
+  return (int32_t)P->free_list.size();
+}
+
+int32_t rb_kv_create(rb_ctx* c, int32_t pool, uint32_t t) {
+  KvPool* P = get_pool(c, pool);
+  if (!P) return fail(RB_ERR_BAD_HANDLE, "pool %d", pool);
+  if (t >= (uint32_t)P->max_tenants) return fail(RB_ERR_OUT_OF_BOUNDS, "tenant %u >= %d", t, P->max_tenants);
+  if (P->tenants[t].live) tenant_release(*P, t);
+  P->tenants[t].live = true;
+  P->tenants[t].len.assign(P->n_layers, 0);
+  return RB_OK;
+}
+
+int32_t rb_kv_destroy(rb_ctx* c, int32_t pool, uint32_t t) {
+  KvPool* P = get_pool(c, pool);
+  if (!P) return fail(RB_ERR_BAD_HANDLE, "pool %d", pool);
+  if (t >= (uint32_t)P->max_tenants || !P->tenants[t].live) return fail(RB_ERR_NOT_FOUND, "tenant %u", t);
+  tenant_release(*P, t);
+  P->tenants[t].live = false;
+  return RB_OK;
+}
+
+int32_t rb_kv_clear(rb_ctx* c, int32_t pool, uint32_t t) {
+  KvPool* P = get_pool(c, pool);
+  if (!P) return fail(RB_ERR_BAD_HANDLE, "pool %d", pool);
+  if (t >= (uint32_t)P->max_tenants || !P->tenants[t].live) return fail(RB_ERR_NOT_FOUND, "tenant %u", t);
+  cudaStreamSynchronize(c->stream);
+  tenant_release(*P, t);
+  return RB_OK;
+}
+
+int32_t rb_kv_len(rb_ctx* c, int32_t pool, uint32_t t, uint32_t layer) {
+  KvPool* P = get_pool(c, pool);
+  if (!P) return fail(RB_ERR_BAD_HANDLE, "pool %d", pool);
+  if (t >= (uint32_t)P->max_tenants || !P->tenants[t].live) return fail(RB_ERR_NOT_FOUND, "tenant %u", t);
+  if (layer >= (uint32_t)P->n_layers) return fail(RB_ERR_NOT_FOUND, "layer %u", layer);
+  return P->tenants[t].len[layer];
+}
+
+static int kv_append_rows(rb_ctx* c, KvPool& P, int layer, int n, const uint32_t* tenants, const uint32_t* positions,
+                          const float* k, const float* v, uint32_t flags, RowPlan& rp) {
+  if (int rc = plan_rows(P, n, tenants, nullptr, positions, layer, rp)) return rc;
+  int32_t* d_desc = c->stage_in.as<int32_t>();
+  if (int rc = upload_desc(c, rp, d_desc)) return rc;
+  ptab_update_kernel<<<1, 128, 0, c->stream>>>(d_desc, P.ptab.as<int32_t>(), P.max_pages_per_tenant);
+  RB_CUDA(cudaGetLastError());
+  const size_t bytes = (size_t)n * P.n_kv * P.hd * 4;
+  Staged sk, sv;
+  if (int rc = stage(c, k, bytes, flags, sk)) return rc;
+  if (int rc = stage(c, v, bytes, flags, sv)) return rc;
+  RB_CUDA(kv_append_launch(P.view(), layer, n, d_desc + kDescTenant, d_desc + kDescPos, (const float*)sk.dptr,
+                           (const float*)sv.dptr, c->stream));
+  if (int rc = sync_ctx(c)) return rc;
+  for (int r = 0; r < n; ++r) P.tenants[rp.tenant[r]].len[layer] = std::max(P.tenants[rp.tenant[r]].len[layer], rp.pos[r] + 1);
+  return RB_OK;
+}
+
+int32_t rb_kv_append(rb_ctx* c, int32_t pool, uint32_t t, uint32_t layer, const float* k, const float* v,
+                     uint32_t seq_len, uint32_t flags) {
+  KvPool* P = get_pool(c, pool);
+  if (!P) return fail(RB_ERR_BAD_HANDLE, "pool %d", pool);
+  if (t >= (uint32_t)P->max_tenants || !P->tenants[t].live) return fail(RB_ERR_NOT_FOUND, "tenant %u", t);
+  if (layer >= (uint32_t)P->n_layers) return fail(RB_ERR_NOT_FOUND, "layer %u", layer);
+  if (P->tenants[t].len[layer] + (int)seq_len > P->max_seq)
+    return fail(RB_ERR_KV_OVERFLOW, "KV cache overflow: %d + %u > %d", P->tenants[t].len[layer], seq_len, P->max_seq);
+  for (uint32_t s0 = 0; s0 < seq_len; s0 += kMaxRowsAbi) {
+    const int n = (int)std::min<uint32_t>(kMaxRowsAbi, seq_len - s0);
+    std::vector<uint32_t> tv(n, t);
+    RowPlan rp;
+    const size_t off = (size_t)s0 * P->n_kv * P->hd;
+    if (int rc = kv_append_rows(c, *P, layer, n, tv.data(), nullptr, k + off, v + off, flags, rp)) return rc;
+  }
+  return P->tenants[t].len[layer];
+}
+
+int32_t rb_kv_gather(rb_ctx* c, int32_t pool, uint32_t t, uint32_t layer, float* k_out, float* v_out, uint32_t flags) {
+  KvPool* P = get_pool(c, pool);
+  if (!P) return fail(RB_ERR_BAD_HANDLE, "pool %d", pool);
+  if (t >= (uint32_t)P->max_tenants || !P->tenants[t].live) return fail(RB_ERR_NOT_FOUND, "tenant %u", t);
+  if (layer >= (uint32_t)P->n_layers) return fail(RB_ERR_NOT_FOUND, "layer %u", layer);
+  const int len = P->tenants[t].len[layer];
+  const size_t bytes = (size_t)len * P->n_kv * P->hd * 4;
+  if (len == 0) return 0;
+  DevBuf tk, tv;
+  float *dk = k_out, *dv = v_out;
+  if (!(flags & RB_PTR_DEVICE)) {
+    RB_CUDA(tk.alloc(bytes));
+    RB_CUDA(tv.alloc(bytes));
+    dk = tk.as<float>();
+    dv = tv.as<float>();
+  }
+  RB_CUDA(kv_gather_launch(P->view(), layer, t, len, dk, dv, c->stream));
+  if (!(flags & RB_PTR_DEVICE)) {
+    RB_CUDA(cudaMemcpyAsync(k_out, dk, bytes, cudaMemcpyDeviceToHost, c->stream));
+    RB_CUDA(cudaMemcpyAsync(v_out, dv, bytes, cudaMemcpyDeviceToHost, c->stream));
+  }
+  if (int rc = sync_ctx(c)) return rc;
+  return len;
+}
+
+int32_t rb_attention_forward(rb_ctx* c, int32_t pool, uint32_t layer, uint32_t n_rows, const uint32_t* tenants,
+                             const uint32_t* positions, const float* q, const float* k_new, const float* v_new,
+                             float* out, uint32_t n_heads, float scale, uint32_t flags) {
+  KvPool* P = get_pool(c, pool);
+  if (!P) return fail(RB_ERR_BAD_HANDLE, "pool %d", pool);
+  if (n_rows == 0 || n_rows > (uint32_t)kMaxRowsAbi) return fail(RB_ERR_INVALID, "n_rows %u not in [1, 64]", n_rows);
+  if (layer >= (uint32_t)P->n_layers) return fail(RB_ERR_NOT_FOUND, "layer %u", layer);
+  if (n_heads % P->n_kv) return fail(RB_ERR_UNSUPPORTED, "n_heads %u not a multiple of n_kv %d", n_heads, P->n_kv);
+  const int nrep = n_heads / P->n_kv;
+  if (nrep != 1 && nrep != 2 && nrep != 4 && nrep != 8) return fail(RB_ERR_UNSUPPORTED, "GQA group %d", nrep);
+  RowPlan rp;
+  int32_t* d_desc = c->stage_in.as<int32_t>();
+  if (k_new || v_new) {
+    if (!k_new || !v_new) return fail(RB_ERR_INVALID, "k_new and v_new go together");
+    if (int rc = kv_append_rows(c, *P, layer, n_rows, tenants, positions, k_new, v_new, flags, rp)) return rc;
+  } else {
+    rp.tenant.resize(n_rows);
+    rp.pos.resize(n_rows);
+    rp.tok.assign(n_rows, 0);
+    for (uint32_t r = 0; r < n_rows; ++r) {
+      const uint32_t t = tenants[r];
+      if (t >= (uint32_t)P->max_tenants || !P->tenants[t].live) return fail(RB_ERR_NOT_FOUND, "tenant %u", t);
+      const int len = P->tenants[t].len[layer];
+      const int pos = positions ? (int)positions[r] : len - 1;
+      if (pos < 0 || pos >= len) return fail(RB_ERR_OUT_OF_BOUNDS, "row %u position %d outside cache [0,%d)", r, pos, len);
+      rp.tenant[r] = (int)t;
+      rp.pos[r] = pos;
+    }
+    if (int rc = upload_desc(c, rp, d_desc)) return rc;
+  }
+  const size_t qbytes = (size_t)n_rows * n_heads * P->hd * 4;
+  Staged sq;
+  if (int rc = stage(c, q, qbytes, flags, sq)) return rc;
+  DevBuf tmp;
+  float* dout = out;
+  if (!(flags & RB_PTR_DEVICE)) {
+    RB_CUDA(tmp.alloc(qbytes));
+    dout = tmp.as<float>();
+  }
+  AttnArgs at;
+  at.n_rows = n_rows;
+  at.row_tenant = d_desc + kDescTenant;
+  at.row_pos = d_desc + kDescPos;
+  at.q = (const float*)sq.dptr;
+  at.ldq = n_heads * P->hd;
+  at.out = dout;
+  at.ldo = n_heads * P->hd;
+  at.n_heads = n_heads;
+  at.layer = layer;
+  at.scale = scale;
+  at.kv = P->view();
+  at.partials = c->attn_partials.as<float>();
+  at.counters = c->counters.as<int32_t>() + kCounters / 2;
+  at.max_splits = (P->max_seq + 16 * kAttnPagesPerSplit - 1) / (16 * kAttnPagesPerSplit);
+  at.err = c->err.as<uint32_t>();
+  RB_CUDA(cudaEventRecord(c->ev0, c->stream));
+  RB_CUDA(attn_launch(at, c->num_sms, c->stream, 0));
+  RB_CUDA(cudaEventRecord(c->ev1, c->stream));
+  if (!(flags & RB_PTR_DEVICE)) RB_CUDA(cudaMemcpyAsync(out, dout, qbytes, cudaMemcpyDeviceToHost, c->stream));
+  if ((flags & RB_PTR_DEVICE) && (flags & RB_ASYNC)) {
+    c->last_launches = 1;
+    return (int32_t)(n_rows * n_heads * P->hd);
+  }
+  if (int rc = sync_ctx(c)) return rc;
+  cudaEventElapsedTime(&c->last_ms, c->ev0, c->ev1);
+  c->last_launches = 1;
+  return (int32_t)(n_rows * n_heads * P->hd);
+}
+
+// ---- model ----
+int32_t rb_model_create(rb_ctx* c, const rb_model_config* cfg, int32_t* model) {
+  if (!c || !cfg || !model) return fail(RB_ERR_BAD_HANDLE, "null argument");
+  const rb_model_config& f = *cfg;
+  if (f.hidden % 256 || f.ffn % 256 || (f.n_heads * f.head_dim) % 256 || f.n_heads % f.n_kv_heads)
+    return fail(RB_ERR_UNSUPPORTED, "hidden/ffn/heads*head_dim must be multiples of 256");
+  const int nrep = f.n_heads / f.n_kv_heads;
+  if (nrep != 1 && nrep != 2 && nrep != 4 && nrep != 8) return fail(RB_ERR_UNSUPPORTED, "GQA group %d", nrep);
+  if (f.ffn % 8) return fail(RB_ERR_UNSUPPORTED, "ffn %% 8");
+  auto M = std::make_unique<Model>();
+  M->cfg = f;
+  if (M->cfg.max_tenants == 0) M->cfg.max_tenants = 64;
+  const int pages = f.kv_pages ? (int)f.kv_pages : (int)(M->cfg.max_tenants * ((f.max_seq + 15) / 16));
+  const int p = pool_create(c, f.n_layers, f.n_kv_heads, f.head_dim, f.kv_dtype, pages, M->cfg.max_tenants, f.max_seq);
+  if (p < 0) return p;
+  M->pool = p;
+  M->layers.resize(f.n_layers);
+  const int R = kMaxRowsAbi;
+  RB_CUDA(M->x.alloc((size_t)R * f.hidden * 4));
+  RB_CUDA(M->q.alloc((size_t)R * f.n_heads * f.head_dim * 4));
+  RB_CUDA(M->att.alloc((size_t)R * f.n_heads * f.head_dim * 4));
+  RB_CUDA(M->h.alloc((size_t)R * f.ffn * 4));
+  RB_CUDA(M->ss.alloc((size_t)((f.hidden + 127) / 128) * R * 4));
+  RB_CUDA(M->logits.alloc((size_t)R * f.vocab * 4));
+  RB_CUDA(M->argmax.alloc((size_t)R * 8));
+  RB_CUDA(M->desc.alloc((kDescUpd + 3 * R) * 4));
+  RB_CUDA(cudaMemsetAsync(M->x.p, 0, M->x.n, c->stream));
+  RB_CUDA(cudaMemsetAsync(M->att.p, 0, M->att.n, c->stream));
+  if (int rc = sync_ctx(c)) return rc;
+  c->models.push_back(std::move(M));
+  *model = (int32_t)c->models.size() - 1;
+  return RB_OK;
+}
+
+int32_t rb_model_destroy(rb_ctx* c, int32_t model) {
+  Model* M = get_model(c, model);
+  if (!M) return fail(RB_ERR_BAD_HANDLE, "model %d", model);
+  cudaStreamSynchronize(c->stream);
+  for (auto& g : M->graphs) cudaGraphExecDestroy(g.second);
+  const int p = M->pool;
+  c->models[model].reset();
+  if (p >= 0 && p < (int)c->pools.size()) c->pools[p].reset();
+  return RB_OK;
+}
+
+static bool tensor_shape(const rb_model_config& f, int which, size_t& rows, size_t& cols) {
+  const size_t H = f.hidden, Q = (size_t)f.n_heads * f.head_dim, KV = (size_t)f.n_kv_heads * f.head_dim;
+  switch (which) {
+    case RB_W_TOKEN_EMBD: rows = f.vocab; cols = H; return true;
+    case RB_W_OUTPUT_NORM: case RB_W_ATTN_NORM: case RB_W_FFN_NORM: rows = 1; cols = H; return true;
+    case RB_W_OUTPUT: rows = f.vocab; cols = H; return true;
+    case RB_W_Q: rows = Q; cols = H; return true;
+    case RB_W_K: case RB_W_V: rows = KV; cols = H; return true;
+    case RB_W_O: rows = H; cols = Q; return true;
+    case RB_W_GATE: case RB_W_UP: rows = f.ffn; cols = H; return true;
+    case RB_W_DOWN: rows = H; cols = f.ffn; return true;
+  }
+  return false;
+}
+
+int32_t rb_model_set_weight(rb_ctx* c, int32_t model, int32_t which, int32_t layer, int32_t dtype, const void* data,
+                            size_t nbytes, uint32_t flags) {
+  Model* M = get_model(c, model);
+  if (!M) return fail(RB_ERR_BAD_HANDLE, "model %d", model);
+  size_t rows, cols;
+  if (!tensor_shape(M->cfg, which, rows, cols)) return fail(RB_ERR_NOT_FOUND, "weight id %d", which);
+  const bool global = which < 10;
+  if (!global && (layer < 0 || layer >= (int)M->cfg.n_layers)) return fail(RB_ERR_NOT_FOUND, "layer %d", layer);
+  const bool is_norm = which == RB_W_OUTPUT_NORM || which == RB_W_ATTN_NORM || which == RB_W_FFN_NORM;
+  if (is_norm && dtype != RB_F32) return fail(RB_ERR_UNSUPPORTED, "norm weights are f32");
+  if (!is_norm && dtype != RB_Q4_K && dtype != RB_Q6_K && dtype != RB_Q8_0 && !(which == RB_W_TOKEN_EMBD && dtype == RB_F32))
+    return fail(RB_ERR_UNSUPPORTED, "dtype %d for weight %d", dtype, which);
+  const size_t expect = rows * (cols / block_elems(dtype)) * block_bytes(dtype);
+  if (cols % block_elems(dtype) || nbytes != expect)
+    return fail(RB_ERR_INVALID, "weight %d: expected %zu bytes, got %zu", which, expect, nbytes);
+  RawTensor* t = nullptr;
+  if (which == RB_W_TOKEN_EMBD) t = &M->embd;
+  else if (which == RB_W_OUTPUT_NORM) t = &M->out_norm;
+  else if (which == RB_W_OUTPUT) t = &M->out_raw;
+  else t = &M->layers[layer].raw[which - RB_W_ATTN_NORM];
+  t->dtype = dtype;
+  t->bytes = nbytes;
+  RB_CUDA(t->d.alloc(nbytes));
+  RB_CUDA(cudaMemcpyAsync(t->d.p, data, nbytes, (flags & RB_PTR_DEVICE) ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice, c->stream));
+  if (int rc = sync_ctx(c)) return rc;
+  M->finalized = false;
+  return (int32_t)nbytes;
+}
+
+int32_t rb_model_finalize(rb_ctx* c, int32_t model) {
+  Model* M = get_model(c, model);
+  if (!M) return fail(RB_ERR_BAD_HANDLE, "model %d", model);
+  const rb_model_config& f = M->cfg;
+  if (M->embd.dtype < 0 || M->out_norm.dtype < 0 || M->out_raw.dtype < 0) return fail(RB_ERR_NOT_FOUND, "global weights missing");
+  const int H = f.hidden, Q = f.n_heads * f.head_dim, KV = f.n_kv_heads * f.head_dim;
+  for (int l = 0; l < (int)f.n_layers; ++l) {
+    LayerW& L = M->layers[l];
+    for (int i = 0; i < 9; ++i)
+      if (L.raw[i].dtype < 0) return fail(RB_ERR_NOT_FOUND, "layer %d weight %d missing", l, RB_W_ATTN_NORM + i);
+    RawTensor &q = L.raw[1], &k = L.raw[2], &v = L.raw[3], &o = L.raw[4], &g = L.raw[6], &u = L.raw[7], &d = L.raw[8];
+    if (q.dtype != k.dtype) return fail(RB_ERR_UNSUPPORTED, "layer %d: wq and wk dtypes differ", l);
+    if (g.dtype != u.dtype) return fail(RB_ERR_UNSUPPORTED, "layer %d: gate and up dtypes differ", l);
+    if (int rc = upload_tiled(c, L.qk, q.dtype, Q + KV, H, q.d.as<uint8_t>(), Q, k.d.as<uint8_t>(), KV, 1)) return rc;
+    if (int rc = upload_tiled(c, L.v, v.dtype, KV, H, v.d.as<uint8_t>(), KV, nullptr, 0, 0)) return rc;
+    L.v_fused = false;
+    if (int rc = upload_tiled(c, L.o, o.dtype, H, Q, o.d.as<uint8_t>(), H, nullptr, 0, 0)) return rc;
+    if (int rc = upload_tiled(c, L.gu, g.dtype, 2 * f.ffn, H, g.d.as<uint8_t>(), f.ffn, u.d.as<uint8_t>(), f.ffn, 2)) return rc;
+    if (int rc = upload_tiled(c, L.down, d.dtype, H, f.ffn, d.d.as<uint8_t>(), H, nullptr, 0, 0)) return rc;
+  }
+  if (int rc = upload_tiled(c, M->out, M->out_raw.dtype, f.vocab, H, M->out_raw.d.as<uint8_t>(), f.vocab, nullptr, 0, 0)) return rc;
+  if (int rc = sync_ctx(c)) return rc;
+  for (auto& g : M->graphs) cudaGraphExecDestroy(g.second);
+  M->graphs.clear();
+  M->finalized = true;
+  return RB_OK;
+}
+
+int32_t rb_model_kv_pool(rb_ctx* c, int32_t model) {
+  Model* M = get_model(c, model);
+  if (!M) return fail(RB_ERR_BAD_HANDLE, "model %d", model);
+  return M->pool;
+}
+
+int32_t rb_tenant_create(rb_ctx* c, int32_t model, uint32_t t) {
+  Model* M = get_model(c, model);
+  if (!M) return fail(RB_ERR_BAD_HANDLE, "model %d", model);
+  return rb_kv_create(c, M->pool, t);
+}
+
+int32_t rb_tenant_reset(rb_ctx* c, int32_t model, uint32_t t) {
+  Model* M = get_model(c, model);
+  if (!M) return fail(RB_ERR_BAD_HANDLE, "model %d", model);
+  return rb_kv_clear(c, M->pool, t);
+}
+
+int32_t rb_forward(rb_ctx* c, int32_t model, uint32_t n_rows, const uint32_t* tenants, const uint32_t* tokens,
+                   const uint32_t* positions, float* logits, uint32_t* argmax, uint32_t flags) {
+  Model* M = get_model(c, model);
+  if (!M) return fail(RB_ERR_BAD_HANDLE, "model %d", model);
+  if (!M->finalized) return fail(RB_ERR_INVALID, "model not finalized");
+  if (n_rows == 0 || n_rows > (uint32_t)c->max_rows) return fail(RB_ERR_INVALID, "n_rows %u not in [1, %d]", n_rows, c->max_rows);
+  if (!tenants || !tokens) return fail(RB_ERR_INVALID, "tenants/tokens NULL");
+  for (uint32_t r = 0; r < n_rows; ++r)
+    if (tokens[r] >= M->cfg.vocab) return fail(RB_ERR_INVALID, "token %u >= vocab", tokens[r]);
+  KvPool& P = *c->pools[M->pool];
+  RowPlan rp;
+  if (int rc = plan_rows(P, n_rows, tenants, tokens, positions, -1, rp)) return rc;
+  if (int rc = upload_desc(c, rp, M->desc.as<int32_t>())) return rc;
+  if (int rc = run_forward(c, *M, n_rows, c->graphs)) return rc;
+  // outputs
+  std::vector<unsigned long long> keys(n_rows);
+  RB_CUDA(cudaMemcpyAsync(keys.data(), M->argmax.p, n_rows * 8, cudaMemcpyDeviceToHost, c->stream));
+  if (logits) {
+    if (int rc = copy_out(c, logits, M->logits.p, (size_t)n_rows * M->cfg.vocab * 4, flags)) return rc;
+  }
+  if (int rc = sync_ctx(c)) return rc;
+  cudaEventElapsedTime(&c->last_ms, c->ev0, c->ev1);
+  for (uint32_t r = 0; r < n_rows; ++r) {
+    KvTenant& T = P.tenants[rp.tenant[r]];
+    for (auto& l : T.len) l = std::max(l, rp.pos[r] + 1);
+  }
+  if (argmax) {
+    if (flags & RB_PTR_DEVICE) {
+      std::vector<uint32_t> ids(n_rows);
+      for (uint32_t r = 0; r < n_rows; ++r) ids[r] = (uint32_t)(keys[r] & 0xffffffffu);
+      RB_CUDA(cudaMemcpy(argmax, ids.data(), n_rows * 4, cudaMemcpyHostToDevice));
+    } else {
+      for (uint32_t r = 0; r < n_rows; ++r) argmax[r] = (uint32_t)(keys[r] & 0xffffffffu);
+    }
+  }
+  return (int32_t)n_rows;
+}
+
+int32_t rb_embed_tokens(rb_ctx* c, int32_t model, const uint32_t* ids, uint32_t n, float* out, uint32_t flags) {
+  Model* M = get_model(c, model);
+  if (!M) return fail(RB_ERR_BAD_HANDLE, "model %d", model);
+  if (M->embd.dtype < 0) return fail(RB_ERR_NOT_FOUND, "token_embd missing");
+  const int H = M->cfg.hidden;
+  for (uint32_t s0 = 0; s0 < n; s0 += kMaxRowsAbi) {
+    const int m = (int)std::min<uint32_t>(kMaxRowsAbi, n - s0);
+    RowPlan rp;
+    rp.tenant.assign(m, 0);
+    rp.pos.assign(m, 0);
+    rp.tok.resize(m);
+    for (int r = 0; r < m; ++r) {
+      if (ids[s0 + r] >= M->cfg.vocab) return fail(RB_ERR_INVALID, "token %u >= vocab", ids[s0 + r]);
+      rp.tok[r] = (int)ids[s0 + r];
+    }
+    int32_t* d = c->stage_in.as<int32_t>();
+    if (int rc = upload_desc(c, rp, d)) return rc;
+    KvPool& P = *c->pools[M->pool];
+    embed_kernel<<<m, 128, 0, c->stream>>>(M->embd.d.as<uint8_t>(), M->embd.dtype, H, d, P.ptab.as<int32_t>(),
+                                           P.max_pages_per_tenant, M->x.as<float>(), H, M->ss.as<float>(), kMaxRowsAbi,
+                                           nullptr);
+    RB_CUDA(cudaGetLastError());
+    if (int rc = copy_out(c, (uint8_t*)out + (size_t)s0 * H * 4, M->x.p, (size_t)m * H * 4, flags)) return rc;
+    if (int rc = sync_ctx(c)) return rc;
+  }
+  return (int32_t)((size_t)n * H * 4);
+}
+
+int32_t rb_forward_layer(rb_ctx* c, int32_t model, uint32_t t, uint32_t layer, const float* hidden,
+                         uint32_t hidden_len, uint32_t position, float* out, uint32_t flags) {
+  Model* M = get_model(c, model);
+  if (!M) return fail(RB_ERR_BAD_HANDLE, "model %d", model);
+  if (!M->finalized) return fail(RB_ERR_INVALID, "model not finalized");
+  const int H = M->cfg.hidden;
+  if (layer >= M->cfg.n_layers) return fail(RB_ERR_NOT_FOUND, "layer %u", layer);
+  if (hidden_len == 0 || hidden_len % H) return fail(RB_ERR_INVALID, "hidden_len %u not a multiple of %d", hidden_len, H);
+  const uint32_t S = hidden_len / H;
+  if (S > (uint32_t)kMaxRowsAbi) return fail(RB_ERR_INVALID, "%u rows > 64", S);
+  KvPool& P = *c->pools[M->pool];
+  std::vector<uint32_t> tv(S, t), pv(S);
+  for (uint32_t i = 0; i < S; ++i) pv[i] = position + i;
+  RowPlan rp;
+  if (int rc = plan_rows(P, S, tv.data(), nullptr, pv.data(), (int)layer, rp)) return rc;
+  if (int rc = upload_desc(c, rp, M->desc.as<int32_t>())) return rc;
+  ptab_update_kernel<<<1, 128, 0, c->stream>>>(M->desc.as<int32_t>(), P.ptab.as<int32_t>(), P.max_pages_per_tenant);
+  RB_CUDA(cudaMemcpyAsync(M->x.p, hidden, (size_t)S * H * 4,
+                          (flags & RB_PTR_DEVICE) ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice, c->stream));
+  ss_kernel<<<dim3((H + 127) / 128, S), 128, 0, c->stream>>>(M->x.as<float>(), H, H, M->ss.as<float>(), kMaxRowsAbi);
+  RB_CUDA(cudaGetLastError());
+  int launches = 2;
+  RB_CUDA(cudaEventRecord(c->ev0, c->stream));
+  const int32_t* d = M->desc.as<int32_t>();
+  if (int rc = enqueue_layer(c, *M, (int)layer, (int)S, d + kDescTenant, d + kDescPos, &launches)) return rc;
+  RB_CUDA(cudaEventRecord(c->ev1, c->stream));
+  if (int rc = copy_out(c, out, M->x.p, (size_t)S * H * 4, flags)) return rc;
+  if (int rc = sync_ctx(c)) return rc;
+  cudaEventElapsedTime(&c->last_ms, c->ev0, c->ev1);
+  c->last_launches = launches;
+  P.tenants[t].len[layer] = position + S;
+  return (int32_t)((size_t)S * H * 4);
+}
+
+int32_t rb_compute_logits(rb_ctx* c, int32_t model, const float* hidden, uint32_t hidden_len, float* out,
+                          uint32_t flags) {
+  Model* M = get_model(c, model);
+  if (!M) return fail(RB_ERR_BAD_HANDLE, "model %d", model);
+  if (!M->finalized) return fail(RB_ERR_INVALID, "model not finalized");
+  const int H = M->cfg.hidden;
+  if (hidden_len != (uint32_t)H) return fail(RB_ERR_INVALID, "hidden_len %u != %d", hidden_len, H);
+  RB_CUDA(cudaMemcpyAsync(M->x.p, hidden, (size_t)H * 4,
+                          (flags & RB_PTR_DEVICE) ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice, c->stream));
+  ss_kernel<<<dim3((H + 127) / 128, 1), 128, 0, c->stream>>>(M->x.as<float>(), H, H, M->ss.as<float>(), kMaxRowsAbi);
+  zero_u64_kernel<<<1, 64, 0, c->stream>>>(M->argmax.as<unsigned long long>(), 1);
+  RB_CUDA(cudaGetLastError());
+  if (int rc = enqueue_head(c, *M, 1, true, nullptr)) return rc;
+  if (int rc = copy_out(c, out, M->logits.p, (size_t)M->cfg.vocab * 4, flags)) return rc;
+  if (int rc = sync_ctx(c)) return rc;
+  return (int32_t)(M->cfg.vocab * 4);
+}
+
+int32_t rb_memory64_load_layer(rb_ctx* c, int32_t model, uint32_t layer_id, void* dst, uint32_t max_size) {
+  Model* M = get_model(c, model);
+  if (!M) return fail(RB_ERR_BAD_HANDLE, "model %d", model);
+  if (layer_id >= M->cfg.n_layers) return fail(RB_ERR_NOT_FOUND, "layer %u not found", layer_id);
+  LayerW& L = M->layers[layer_id];
+  const int order[7] = {1, 2, 3, 4, 6, 7, 8};
+  size_t total = 0;
+  for (int i : order) {
+    if (L.raw[i].dtype < 0) return fail(RB_ERR_NOT_FOUND, "layer %u incomplete", layer_id);
+    total += L.raw[i].bytes;
+  }
+  if (total > max_size) return fail(RB_ERR_INVALID, "buffer too small: %zu > %u", total, max_size);
+  if (total > 0x7fffffffu) return fail(RB_ERR_PTR_OVERFLOW, "layer larger than 2 GiB");
+  size_t off = 0;
+  for (int i : order) {
+    RB_CUDA(cudaMemcpyAsync((uint8_t*)dst + off, L.raw[i].d.p, L.raw[i].bytes, cudaMemcpyDeviceToHost, c->stream));
+    off += L.raw[i].bytes;
+  }
+  if (int rc = sync_ctx(c)) return rc;
+  return (int32_t)total;
+}
+
+float rb_last_forward_ms(rb_ctx* c) { return c ? c->last_ms : -1.f; }
+int32_t rb_last_forward_launches(rb_ctx* c) { return c ? c->last_launches : fail(RB_ERR_BAD_HANDLE, "null context"); }
+
+}  // extern "C"

@@ -1,0 +1,992 @@
+// Fused GGUF dequant GEMV/GEMM for decode: y[t, n] = sum_k x[t, k] * W[n, k].
+//
+// Replaces the reference's fused_dequant_matmul_{q4k,q6k,q80}
+// (crates/realm-compute-cpu/src/fused.rs:229-374, 1128-1259, 2451-2554) and the
+// CandleCpuBackend dequant+GEMM (candle_cpu_backend.rs:92-114) on the decode path.
+//
+// Design (B200, HBM-bound for M <= 64 tokens):
+//  * Persistent CTAs (one per SM) split the (row-group, super-block) unit space
+//    evenly (stream-K), so every SM streams the same number of weight bytes.
+//  * One producer lane streams 128-row x 256-column units (18-35 KB) with the
+//    bulk-copy engine (cp.async.bulk, no multicast) into a shared-memory ring.
+//  * Stager warps convert the fp32 activations of each unit's K range (times the
+//    RMSNorm weight when fused) into fp16 hi/lo B fragments, so x ~= hi + lo to
+//    ~22 bits and the tensor cores see exact integer weights.
+//  * Eight consumer warps (one 16-row tile each) turn the quantised values into
+//    exact fp16 A fragments (integer x sub-scale for Q4_K, q-32 for Q6_K, q for
+//    Q8_0) and run mma.sync m16n8k16 with fp32 accumulators; per-32/16-column
+//    scales need register accumulators, which is why this path uses mma.sync
+//    rather than TMEM-resident tcgen05 tiles.
+//  * Row groups split across CTAs are reduced by the last-arriving CTA in a
+//    fixed order (deterministic; no spin waits), then the fused epilogue runs.
+#include "gemv.cuh"
+#include "quant.cuh"
+
+namespace rb {
+
+namespace {
+
+constexpr int kConsumerWarps = kUnitTiles;  // one per 16-row tile
+constexpr int kProducerWarp = kConsumerWarps;
+constexpr int kXFragBytes = 16 * 32 * 16;   // per n-tile per super-block: [ks][lane] uint4
+constexpr int kXSumBytes = 32 * 8;          // per n-tile: [lane] uint2 (Q4_K min term)
+constexpr int kMaxTokens = 64;
+
+template <int NT>
+struct Cfg {
+  static constexpr int NX = (NT <= 2) ? 4 : 2;  // x buffers == stager warps
+  static constexpr int kThreads = 32 * (kConsumerWarps + 1 + NX);
+  static constexpr int kXBytes = NT * (kXFragBytes + kXSumBytes);
+};
+
+__host__ __device__ constexpr int ring_stages(int dtype, int nt) {
+  // keep the whole CTA under ~200 KB of shared memory
+  return dtype == DT_Q4_K ? (nt <= 2 ? 5 : (nt == 4 ? 3 : 2))
+       : dtype == DT_Q6_K ? (nt <= 2 ? 4 : 2)
+                          : (nt <= 2 ? 3 : 2);
+}
+
+struct SmemLayout {
+  int ring, xbuf, bars, inv_rms, red, total;
+};
+
+__host__ __device__ inline SmemLayout smem_layout(int dtype, int nt) {
+  SmemLayout L;
+  const int S = ring_stages(dtype, nt);
+  const int NX = (nt <= 2) ? 4 : 2;
+  L.ring = 0;
+  L.xbuf = L.ring + S * unit_bytes(dtype);
+  L.bars = L.xbuf + NX * nt * (kXFragBytes + kXSumBytes);
+  L.inv_rms = L.bars + 8 * (2 * S + 2 * NX);
+  L.red = L.inv_rms + 4 * kMaxTokens;
+  L.total = L.red + 4 * kConsumerWarps * kMaxTokens + 16;
+  return L;
+}
+
+__device__ __forceinline__ uint4 lds128(const uint8_t* p) { return *reinterpret_cast<const uint4*>(p); }
+__device__ __forceinline__ uint2 lds64(const uint8_t* p) { return *reinterpret_cast<const uint2*>(p); }
+
+__device__ __forceinline__ uint32_t pack_h2(__half lo, __half hi) {
+  return (uint32_t)__half_as_ushort(lo) | ((uint32_t)__half_as_ushort(hi) << 16);
+}
+
+// byte i (0..3) of w as half2(b, b), exact
+__device__ __forceinline__ uint32_t byte_h2(uint32_t w, int i) {
+  // bytes [b_i, 0x64, b_i, 0x64] = half2(1024 + b, 1024 + b); minus 1024 is exact
+  const uint32_t t = prmt(w, 0x64646464u, (uint32_t)i | (4u << 4) | ((uint32_t)i << 8) | (4u << 12));
+  return hsub2_u(t, 0x64006400u);
+}
+
+__device__ __forceinline__ void named_bar(int id, int threads) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
+}
+
+__device__ __forceinline__ float4 ldcg4(const float* p) { return __ldcg(reinterpret_cast<const float4*>(p)); }
+
+// ---------------------------------------------------------------------------
+// x staging: B fragments (hi, lo) for one super-block, plus Q4_K sub-block sums.
+// ---------------------------------------------------------------------------
+template <int NT>
+__device__ void stage_x(const GemvArgs& a, int sb, uint8_t* xb, int lane, bool need_sum) {
+  const int k_base = sb * kSuperK;
+  for (int nt = 0; nt < NT; ++nt) {
+    const int tok = nt * 8 + (lane >> 2);
+    const bool valid = tok < a.m;
+    const float* xr = a.x + (size_t)tok * a.ldx + k_base + 2 * (lane & 3);
+    const float* gr = a.norm_w ? a.norm_w + k_base + 2 * (lane & 3) : nullptr;
+    float jsum[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) jsum[j] = 0.f;
+#pragma unroll 4
+    for (int ks = 0; ks < 16; ++ks) {
+      float2 v0 = make_float2(0.f, 0.f), v1 = make_float2(0.f, 0.f);
+      if (valid) {
+        v0 = *reinterpret_cast<const float2*>(xr + 16 * ks);
+        v1 = *reinterpret_cast<const float2*>(xr + 16 * ks + 8);
+        if (gr) {
+          const float2 g0 = *reinterpret_cast<const float2*>(gr + 16 * ks);
+          const float2 g1 = *reinterpret_cast<const float2*>(gr + 16 * ks + 8);
+          v0.x *= g0.x; v0.y *= g0.y; v1.x *= g1.x; v1.y *= g1.y;
+        }
+      }
+      __half h0, l0, h1, l1, h2, l2, h3, l3;
+      split_hilo(v0.x, h0, l0);
+      split_hilo(v0.y, h1, l1);
+      split_hilo(v1.x, h2, l2);
+      split_hilo(v1.y, h3, l3);
+      uint4 o;
+      o.x = pack_h2(h0, h1);
+      o.y = pack_h2(h2, h3);
+      o.z = pack_h2(l0, l1);
+      o.w = pack_h2(l2, l3);
+      *reinterpret_cast<uint4*>(xb + nt * kXFragBytes + (ks * 32 + lane) * 16) = o;
+      jsum[ks >> 1] += (v0.x + v0.y) + (v1.x + v1.y);
+    }
+    if (need_sum) {
+      // the 4 lanes sharing a token hold the 32 values of each sub-block between them
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        jsum[j] += __shfl_xor_sync(0xffffffffu, jsum[j], 1);
+        jsum[j] += __shfl_xor_sync(0xffffffffu, jsum[j], 2);
+      }
+      const int j0 = 2 * (lane & 3);
+      float s0 = 0.f, s1 = 0.f;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        if (j == j0) s0 = jsum[j];
+        if (j == j0 + 1) s1 = jsum[j];
+      }
+      __half sh0, sl0, sh1, sl1;
+      split_hilo(s0, sh0, sl0);
+      split_hilo(s1, sh1, sl1);
+      uint2 o;
+      o.x = pack_h2(sh0, sh1);
+      o.y = pack_h2(sl0, sl1);
+      *reinterpret_cast<uint2*>(xb + NT * kXFragBytes + nt * kXSumBytes + lane * 8) = o;
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Consumers: one 16-row tile x one super-block, accumulated into acc[NT][4]
+// (C fragment: [0]=(g, 2c) [1]=(g, 2c+1) [2]=(g+8, 2c) [3]=(g+8, 2c+1)).
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ float guard_scale(float v, float repl) {
+  // fused.rs:276-285 / 1171-1175: NaN or Inf super-scales are replaced
+  return (isnan(v) || isinf(v)) ? repl : v;
+}
+
+template <int NT>
+__device__ __forceinline__ void tile_q4k(const uint8_t* tile, const uint8_t* xb, int lane, float acc[NT][4]) {
+  const int g = lane >> 2, c = lane & 3;
+  const uint4 hA = lds128(tile + g * 16);
+  const uint4 hB = lds128(tile + (g + 8) * 16);
+  const float dA = guard_scale(half_bits_to_float(hA.x), 0.00000006f);
+  const float mA = guard_scale(half_bits_to_float(hA.x >> 16), 0.00000024f);
+  const float dB = guard_scale(half_bits_to_float(hB.x), 0.00000006f);
+  const float mB = guard_scale(half_bits_to_float(hB.x >> 16), 0.00000024f);
+  // 6-bit sub-scales and mins (get_scale_min_k4, quant.rs:108-122), 4 per word
+  const uint32_t scA_lo = hA.y & 0x3F3F3F3Fu, scA_hi = (hA.w & 0x0F0F0F0Fu) | ((hA.y >> 2) & 0x30303030u);
+  const uint32_t mnA_lo = hA.z & 0x3F3F3F3Fu, mnA_hi = ((hA.w >> 4) & 0x0F0F0F0Fu) | ((hA.z >> 2) & 0x30303030u);
+  const uint32_t scB_lo = hB.y & 0x3F3F3F3Fu, scB_hi = (hB.w & 0x0F0F0F0Fu) | ((hB.y >> 2) & 0x30303030u);
+  const uint32_t mnB_lo = hB.z & 0x3F3F3F3Fu, mnB_hi = ((hB.w >> 4) & 0x0F0F0F0Fu) | ((hB.z >> 2) & 0x30303030u);
+  uint32_t scA[8], scB[8], offA[8], offB[8];
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    scA[j] = byte_h2(scA_lo, j);
+    scA[j + 4] = byte_h2(scA_hi, j);
+    scB[j] = byte_h2(scB_lo, j);
+    scB[j + 4] = byte_h2(scB_hi, j);
+  }
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    offA[j] = h2_as_u32(__hmul2(u32_as_h2(scA[j]), __half2half2(__float2half_rn(-1024.f))));
+    offB[j] = h2_as_u32(__hmul2(u32_as_h2(scB[j]), __half2half2(__float2half_rn(-1024.f))));
+  }
+  // min term operands: A_m = m_j of rows g / g+8 at j = 2c, 2c+1
+  const uint32_t mwA = (c < 2) ? mnA_lo : mnA_hi, mwB = (c < 2) ? mnB_lo : mnB_hi;
+  const int jb = (2 * c) & 3;
+  const uint32_t amA = prmt(mwA, 0x64646464u, (uint32_t)jb | (4u << 4) | ((uint32_t)(jb + 1) << 8) | (4u << 12));
+  const uint32_t amB = prmt(mwB, 0x64646464u, (uint32_t)jb | (4u << 4) | ((uint32_t)(jb + 1) << 8) | (4u << 12));
+  const uint32_t am0 = hsub2_u(amA, 0x64006400u), am1 = hsub2_u(amB, 0x64006400u);
+
+  float cs[NT][4];
+#pragma unroll
+  for (int nt = 0; nt < NT; ++nt) cs[nt][0] = cs[nt][1] = cs[nt][2] = cs[nt][3] = 0.f;
+  const uint8_t* qs = tile + 256;
+#pragma unroll
+  for (int ch = 0; ch < 4; ++ch) {
+    const uint4 q = lds128(qs + ch * 512 + lane * 16);
+    const uint32_t qw[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+    for (int w = 0; w < 4; ++w) {
+      const int ks = ch * 4 + w, j = ks >> 1;
+      const uint32_t word = qw[w];
+      uint32_t af[4];
+      af[0] = hfma2_u(lop3_and_or(word, 0x000F000Fu, 0x64006400u), scA[j], offA[j]);
+      af[1] = hfma2_u(lop3_and_or(word >> 4, 0x000F000Fu, 0x64006400u), scB[j], offB[j]);
+      af[2] = hfma2_u(lop3_and_or(word >> 8, 0x000F000Fu, 0x64006400u), scA[j], offA[j]);
+      af[3] = hfma2_u(lop3_and_or(word >> 12, 0x000F000Fu, 0x64006400u), scB[j], offB[j]);
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt) {
+        const uint4 b = lds128(xb + nt * kXFragBytes + (ks * 32 + lane) * 16);
+        mma_16816(cs[nt], af, b.x, b.y);
+        mma_16816(cs[nt], af, b.z, b.w);
+      }
+    }
+  }
+#pragma unroll
+  for (int nt = 0; nt < NT; ++nt) {
+    const uint2 bm = lds64(xb + NT * kXFragBytes + nt * kXSumBytes + lane * 8);
+    float cm[4] = {0.f, 0.f, 0.f, 0.f};
+    mma_1688(cm, am0, am1, bm.x);
+    mma_1688(cm, am0, am1, bm.y);
+    acc[nt][0] = fmaf(-mA, cm[0], fmaf(dA, cs[nt][0], acc[nt][0]));
+    acc[nt][1] = fmaf(-mA, cm[1], fmaf(dA, cs[nt][1], acc[nt][1]));
+    acc[nt][2] = fmaf(-mB, cm[2], fmaf(dB, cs[nt][2], acc[nt][2]));
+    acc[nt][3] = fmaf(-mB, cm[3], fmaf(dB, cs[nt][3], acc[nt][3]));
+  }
+}
+
+template <int NT>
+__device__ __forceinline__ void tile_q6k(const uint8_t* tile, const uint8_t* xb, int lane, float acc[NT][4]) {
+  const int g = lane >> 2;
+  const uint16_t* dd = reinterpret_cast<const uint16_t*>(tile);
+  const float dA = guard_scale(half_bits_to_float(dd[g]), 0.00000006f);
+  const float dB = guard_scale(half_bits_to_float(dd[g + 8]), 0.00000006f);
+  const uint4 sAw = lds128(tile + 32 + g * 16);
+  const uint4 sBw = lds128(tile + 32 + (g + 8) * 16);
+  const int8_t* sA = reinterpret_cast<const int8_t*>(&sAw);
+  const int8_t* sB = reinterpret_cast<const int8_t*>(&sBw);
+  const uint8_t* lo = tile + 288;
+  const uint8_t* hi = tile + 288 + 2048;
+#pragma unroll
+  for (int hc = 0; hc < 2; ++hc) {
+    const uint4 hw = lds128(hi + hc * 512 + lane * 16);
+    const uint32_t hws[4] = {hw.x, hw.y, hw.z, hw.w};
+#pragma unroll
+    for (int half_ch = 0; half_ch < 2; ++half_ch) {
+      const int ch = hc * 2 + half_ch;
+      const uint4 q = lds128(lo + ch * 512 + lane * 16);
+      const uint32_t qw[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+      for (int w = 0; w < 4; ++w) {
+        const int ks = ch * 4 + w;               // 0..15
+        const int hwi = (ks & 7) >> 1;           // word within the hi chunk
+        const uint32_t H = (ks & 1) ? (hws[hwi] >> 16) : (hws[hwi] & 0xffffu);
+        const uint32_t X = (H & 0xffu) | ((H & 0xff00u) << 8);
+        const uint32_t word = qw[w];
+        uint32_t af[4];
+        af[0] = hsub2_u(lop3_and_or(word, 0x000F000Fu, 0x64006400u) | ((X << 4) & 0x00300030u), 0x64206420u);
+        af[1] = hsub2_u(lop3_and_or(word >> 4, 0x000F000Fu, 0x64006400u) | ((X << 2) & 0x00300030u), 0x64206420u);
+        af[2] = hsub2_u(lop3_and_or(word >> 8, 0x000F000Fu, 0x64006400u) | (X & 0x00300030u), 0x64206420u);
+        af[3] = hsub2_u(lop3_and_or(word >> 12, 0x000F000Fu, 0x64006400u) | ((X >> 2) & 0x00300030u), 0x64206420u);
+        const float fa = dA * (float)sA[ks], fb = dB * (float)sB[ks];
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt) {
+          const uint4 b = lds128(xb + nt * kXFragBytes + (ks * 32 + lane) * 16);
+          float ct[4] = {0.f, 0.f, 0.f, 0.f};
+          mma_16816(ct, af, b.x, b.y);
+          mma_16816(ct, af, b.z, b.w);
+          acc[nt][0] = fmaf(fa, ct[0], acc[nt][0]);
+          acc[nt][1] = fmaf(fa, ct[1], acc[nt][1]);
+          acc[nt][2] = fmaf(fb, ct[2], acc[nt][2]);
+          acc[nt][3] = fmaf(fb, ct[3], acc[nt][3]);
+        }
+      }
+    }
+  }
+}
+
+template <int NT>
+__device__ __forceinline__ void tile_q80(const uint8_t* tile, const uint8_t* xb, int lane, float acc[NT][4]) {
+  const int g = lane >> 2;
+  const uint4 dAw = lds128(tile + g * 16);
+  const uint4 dBw = lds128(tile + (g + 8) * 16);
+  const uint32_t dAs[4] = {dAw.x, dAw.y, dAw.z, dAw.w};
+  const uint32_t dBs[4] = {dBw.x, dBw.y, dBw.z, dBw.w};
+  const uint8_t* qs = tile + 256;
+#pragma unroll
+  for (int ch = 0; ch < 8; ++ch) {  // one 32-column block per chunk
+    const uint4 q = lds128(qs + ch * 512 + lane * 16);
+    const float da = half_bits_to_float(dAs[ch >> 1] >> ((ch & 1) * 16));
+    const float db = half_bits_to_float(dBs[ch >> 1] >> ((ch & 1) * 16));
+    float ct[NT][4];
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt) ct[nt][0] = ct[nt][1] = ct[nt][2] = ct[nt][3] = 0.f;
+#pragma unroll
+    for (int s2 = 0; s2 < 2; ++s2) {
+      const int ks = ch * 2 + s2;
+      const uint32_t w0 = s2 ? q.z : q.x, w1 = s2 ? q.w : q.y;
+      uint32_t af[4];
+      af[0] = hsub2_u(prmt(w0, 0x64646464u, 0x4140u), 0x64806480u);
+      af[1] = hsub2_u(prmt(w0, 0x64646464u, 0x4342u), 0x64806480u);
+      af[2] = hsub2_u(prmt(w1, 0x64646464u, 0x4140u), 0x64806480u);
+      af[3] = hsub2_u(prmt(w1, 0x64646464u, 0x4342u), 0x64806480u);
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt) {
+        const uint4 b = lds128(xb + nt * kXFragBytes + (ks * 32 + lane) * 16);
+        mma_16816(ct[nt], af, b.x, b.y);
+        mma_16816(ct[nt], af, b.z, b.w);
+      }
+    }
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt) {
+      acc[nt][0] = fmaf(da, ct[nt][0], acc[nt][0]);
+      acc[nt][1] = fmaf(da, ct[nt][1], acc[nt][1]);
+      acc[nt][2] = fmaf(db, ct[nt][2], acc[nt][2]);
+      acc[nt][3] = fmaf(db, ct[nt][3], acc[nt][3]);
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Epilogues (run by the 8 consumer warps; warp = tile within the row group)
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void kv_store(const KvView& kv, int layer, int which, int tenant, int pos, int head,
+                                         int d, float v) {
+  const int page = kv.ptab[(size_t)tenant * kv.ptab_stride + (pos >> 4)];
+  const size_t off = ((((size_t)page * kv.n_layers + layer) * 2 + which) * kv.n_kv + head) * 16 * (size_t)kv.hd +
+                     (size_t)(pos & 15) * kv.hd + d;
+  if (kv.f16) reinterpret_cast<__half*>(kv.pool)[off] = __float2half_rn(v);
+  else reinterpret_cast<float*>(kv.pool)[off] = v;
+}
+
+template <int NT>
+__device__ void epilogue(const GemvArgs& a, int rg, int warp, int lane, float acc[NT][4], const float* inv_rms,
+                         float* red) {
+  const int g = lane >> 2, c = lane & 3;
+  const int row0 = rg * kRowGroup + warp * kTileRows + g;  // rows row0 and row0+8
+#pragma unroll
+  for (int nt = 0; nt < NT; ++nt) {
+    const int t0 = nt * 8 + 2 * c;
+    const float s0 = inv_rms ? inv_rms[t0] : 1.f, s1 = inv_rms ? inv_rms[t0 + 1] : 1.f;
+    acc[nt][0] *= s0;
+    acc[nt][1] *= s1;
+    acc[nt][2] *= s0;
+    acc[nt][3] *= s1;
+  }
+  if (a.epi == EPI_STORE) {
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt) {
+#pragma unroll
+      for (int r = 0; r < 4; ++r) {
+        const int t = nt * 8 + 2 * c + (r & 1), row = row0 + ((r & 2) ? 8 : 0);
+        if (t < a.m && row < a.n) a.y[(size_t)t * a.ldy + row] = acc[nt][r];
+      }
+    }
+  } else if (a.epi == EPI_SWIGLU) {
+    // tile rows 0-7 gate, 8-15 up, same output index (ffn.rs:98-103 order)
+    const int o = rg * (kRowGroup / 2) + warp * 8 + g;
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt) {
+#pragma unroll
+      for (int r = 0; r < 2; ++r) {
+        const int t = nt * 8 + 2 * c + r;
+        const float gt = acc[nt][r], up = acc[nt][r + 2];
+        const float sig = 1.0f / (1.0f + expf(-gt));
+        const float h = (gt * sig) * up;
+        if (t < a.m && 2 * o < a.n) a.y[(size_t)t * a.ldy + o] = h;
+      }
+    }
+  } else if (a.epi == EPI_RESID) {
+    float sq[NT][2];
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt) {
+      sq[nt][0] = sq[nt][1] = 0.f;
+#pragma unroll
+      for (int r = 0; r < 4; ++r) {
+        const int t = nt * 8 + 2 * c + (r & 1), row = row0 + ((r & 2) ? 8 : 0);
+        if (t < a.m && row < a.n) {
+          float* p = a.resid + (size_t)t * a.ldr + row;
+          const float v = *p + acc[nt][r];
+          *p = v;
+          sq[nt][r & 1] += v * v;
+        }
+      }
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        sq[nt][h] += __shfl_xor_sync(0xffffffffu, sq[nt][h], 4);
+        sq[nt][h] += __shfl_xor_sync(0xffffffffu, sq[nt][h], 8);
+        sq[nt][h] += __shfl_xor_sync(0xffffffffu, sq[nt][h], 16);
+      }
+      if (g == 0) {
+        red[warp * kMaxTokens + nt * 8 + 2 * c] = sq[nt][0];
+        red[warp * kMaxTokens + nt * 8 + 2 * c + 1] = sq[nt][1];
+      }
+    }
+    named_bar(2, 32 * kConsumerWarps);
+    const int tid = warp * 32 + lane;
+    if (tid < a.m) {
+      float s = 0.f;
+      for (int w = 0; w < kConsumerWarps; ++w) s += red[w * kMaxTokens + tid];
+      a.ss_out[(size_t)rg * a.ld_ss + tid] = s;
+    }
+    named_bar(2, 32 * kConsumerWarps);
+  } else if (a.epi == EPI_LOGITS) {
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt) {
+      unsigned long long best[2] = {0ull, 0ull};
+#pragma unroll
+      for (int r = 0; r < 4; ++r) {
+        const int t = nt * 8 + 2 * c + (r & 1), row = row0 + ((r & 2) ? 8 : 0);
+        if (t < a.m && row < a.n) {
+          if (a.y) a.y[(size_t)t * a.ldy + row] = acc[nt][r];
+          const unsigned long long key =
+              ((unsigned long long)float_order_key(acc[nt][r]) << 32) | (unsigned long long)row;
+          best[r & 1] = key > best[r & 1] ? key : best[r & 1];
+        }
+      }
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+#pragma unroll
+        for (int sh = 4; sh <= 16; sh <<= 1) {
+          const unsigned long long o = __shfl_xor_sync(0xffffffffu, best[h], sh);
+          best[h] = o > best[h] ? o : best[h];
+        }
+        const int t = nt * 8 + 2 * c + h;
+        if (g == 0 && t < a.m && best[h]) atomicMax(a.argmax + t, best[h]);
+      }
+    }
+  } else if (a.epi == EPI_QKV) {
+    // RoPE on adjacent pairs (attention.rs:171-240): rows 2i and 2i+1 live in
+    // lanes that differ by 4 (g and g^1).
+    const int hd = a.head_dim;
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt) {
+#pragma unroll
+      for (int r = 0; r < 4; ++r) {
+        const int t = nt * 8 + 2 * c + (r & 1);
+        const int row = row0 + ((r & 2) ? 8 : 0);
+        const int grow = a.qkv_row0 + row;
+        const bool is_v = grow >= a.n_q_rows + a.n_k_rows;
+        const float partner = __shfl_xor_sync(0xffffffffu, acc[nt][r], 4);
+        const bool valid = t < a.m && row < a.n;
+        if (!valid) continue;
+        const int pos = a.row_pos[t];
+        float v = acc[nt][r];
+        const int rr = grow < a.n_q_rows ? grow : (grow < a.n_q_rows + a.n_k_rows ? grow - a.n_q_rows
+                                                                                   : grow - a.n_q_rows - a.n_k_rows);
+        const int head = rr / hd, dim = rr % hd;
+        if (!is_v) {
+          const int i = dim & ~1;
+          const float freq = 1.0f / powf(a.rope_theta, (float)i / (float)hd);
+          const float ang = (float)pos * freq;
+          float sn, cs;
+          sincosf(ang, &sn, &cs);
+          if ((dim & 1) == 0) v = __fsub_rn(__fmul_rn(v, cs), __fmul_rn(partner, sn));
+          else v = __fadd_rn(__fmul_rn(partner, sn), __fmul_rn(v, cs));
+        }
+        if (grow < a.n_q_rows) {
+          a.q_out[(size_t)t * a.ldq + rr] = v;
+        } else {
+          kv_store(a.kv, a.layer, is_v ? 1 : 0, a.row_tenant[t], pos, head, dim, v);
+        }
+      }
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// The kernel
+// ---------------------------------------------------------------------------
+template <int DT, int NT>
+__global__ void __launch_bounds__(Cfg<NT>::kThreads, 1) gemv_kernel(const GemvArgs a) {
+  constexpr int NX = Cfg<NT>::NX;
+  constexpr int S = ring_stages(DT, NT);
+  constexpr int UB = unit_bytes(DT);
+  constexpr int TB = tile_bytes(DT);
+  extern __shared__ __align__(128) uint8_t smem[];
+  const SmemLayout L = smem_layout(DT, NT);
+  uint8_t* ring = smem + L.ring;
+  uint8_t* xbuf = smem + L.xbuf;
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + L.bars);
+  uint64_t* empty = full + S;
+  uint64_t* xfull = empty + S;
+  uint64_t* xempty = xfull + NX;
+  float* inv_rms = reinterpret_cast<float*>(smem + L.inv_rms);
+  float* red = reinterpret_cast<float*>(smem + L.red);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const long long U = (long long)a.n_rg * a.nsb;
+  const int G = gridDim.x;
+  const long long u0 = U * blockIdx.x / G, u1 = U * (blockIdx.x + 1) / G;
+  const int n_units = (int)(u1 - u0);
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < S; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], kConsumerWarps);
+    }
+    for (int b = 0; b < NX; ++b) {
+      mbar_init(&xfull[b], 1);
+      mbar_init(&xempty[b], kConsumerWarps);
+    }
+    fence_barrier_init();
+  }
+  __syncthreads();
+  pdl_launch_dependents();
+
+  if (warp == kProducerWarp) {
+    // Weights do not depend on the previous kernel: start streaming before the
+    // grid dependency resolves.
+    if (lane == 0) {
+      const uint64_t pol = policy_evict_first();
+      bool ok = true;
+      for (int i = 0; i < n_units && ok; ++i) {
+        const int s = i % S;
+        if (i >= S) ok = mbar_wait(&empty[s], ((i / S) - 1) & 1, a.err, DEV_TIMEOUT_EMPTY);
+        if (!ok) break;
+        mbar_arrive_expect_tx(&full[s], UB);
+        bulk_g2s_evict_first(ring + (size_t)s * UB, a.w + (u0 + i) * (long long)UB, UB, &full[s], pol);
+      }
+      // drain: every issued copy must land before this CTA may exit
+      const int issued = n_units;
+      for (int i = (issued > S ? issued - S : 0); i < issued; ++i)
+        mbar_wait(&full[i % S], (i / S) & 1, a.err, DEV_TIMEOUT_DRAIN);
+    }
+    return;
+  }
+
+  pdl_wait();
+
+  if (warp > kProducerWarp) {
+    // stager warp s fills x buffer s for units i = s, s + NX, ...
+    const int s = warp - kProducerWarp - 1;
+    uint8_t* xb = xbuf + s * Cfg<NT>::kXBytes;
+    for (int i = s; i < n_units; i += NX) {
+      if (i >= NX && !mbar_wait(&xempty[s], ((i / NX) - 1) & 1, a.err, DEV_TIMEOUT_EMPTY)) break;
+      const int sb = (int)((u0 + i) % a.nsb);
+      stage_x<NT>(a, sb, xb, lane, DT == DT_Q4_K);
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&xfull[s]);
+    }
+    return;
+  }
+
+  // ---- consumers ----
+  if (a.ss_part) {
+    const int tid = threadIdx.x;
+    if (tid < a.m) {
+      float ss = 0.f;
+      for (int j = 0; j < a.n_ss; ++j) ss += a.ss_part[(size_t)j * a.ld_ss + tid];
+      inv_rms[tid] = 1.0f / sqrtf(ss / (float)a.norm_dim + a.norm_eps);
+    }
+    named_bar(1, 32 * kConsumerWarps);
+  }
+  const float* irms = a.ss_part ? inv_rms : nullptr;
+
+  float acc[NT][4];
+#pragma unroll
+  for (int nt = 0; nt < NT; ++nt) acc[nt][0] = acc[nt][1] = acc[nt][2] = acc[nt][3] = 0.f;
+
+  const int first_rg = (int)(u0 / a.nsb);
+  bool alive = true;
+  for (int i = 0; i < n_units; ++i) {
+    const long long u = u0 + i;
+    const int rg = (int)(u / a.nsb), sb = (int)(u % a.nsb);
+    const int s = i % S, b = i % NX;
+    if (alive) alive = mbar_wait(&full[s], (i / S) & 1, a.err, DEV_TIMEOUT_FULL);
+    if (alive) alive = mbar_wait(&xfull[b], (i / NX) & 1, a.err, DEV_TIMEOUT_FULL);
+    if (alive) {
+      const uint8_t* tile = ring + (size_t)s * UB + warp * TB;
+      const uint8_t* xb = xbuf + b * Cfg<NT>::kXBytes;
+      if (DT == DT_Q4_K) tile_q4k<NT>(tile, xb, lane, acc);
+      else if (DT == DT_Q6_K) tile_q6k<NT>(tile, xb, lane, acc);
+      else tile_q80<NT>(tile, xb, lane, acc);
+    }
+    __syncwarp();
+    if (lane == 0) {
+      mbar_arrive(&empty[s]);
+      mbar_arrive(&xempty[b]);
+    }
+    const bool seg_end = (i + 1 == n_units) || (sb + 1 == a.nsb);
+    if (!seg_end) continue;
+    const long long seg_lo = (u0 > (long long)rg * a.nsb) ? u0 : (long long)rg * a.nsb;
+    const bool full_seg = (seg_lo == (long long)rg * a.nsb) && (sb + 1 == a.nsb);
+    if (!full_seg) {
+      // deposit this CTA's partial; slot 0 if rg is this CTA's first row group
+      const int slot = (rg == first_rg) ? 0 : 1;
+      float* dst = a.partials + ((((size_t)blockIdx.x * 2 + slot) * kConsumerWarps + warp) * NT) * 128;
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt)
+        __stcg(reinterpret_cast<float4*>(dst + nt * 128 + lane * 4),
+               make_float4(acc[nt][0], acc[nt][1], acc[nt][2], acc[nt][3]));
+      __threadfence();
+      named_bar(1, 32 * kConsumerWarps);
+      __shared__ int s_last;
+      // contributors: CTAs whose unit range intersects row group rg
+      const long long ua = (long long)rg * a.nsb, ub = ua + a.nsb - 1;
+      long long cf = ua * G / U, cl = ub * G / U;
+      while (cf + 1 < G && U * (cf + 1) / G <= ua) ++cf;
+      while (cf > 0 && U * cf / G > ua) --cf;
+      while (cl + 1 < G && U * (cl + 1) / G <= ub) ++cl;
+      while (cl > 0 && U * cl / G > ub) --cl;
+      const int ncontrib = (int)(cl - cf + 1);
+      if (threadIdx.x == 0) s_last = (atomicAdd(a.counters + rg, 1) == ncontrib - 1);
+      named_bar(1, 32 * kConsumerWarps);
+      if (s_last) {
+        __threadfence();
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt) acc[nt][0] = acc[nt][1] = acc[nt][2] = acc[nt][3] = 0.f;
+        for (long long cc = cf; cc <= cl; ++cc) {
+          const int first_of_c = (int)((U * cc / G) / a.nsb);
+          const int sl = (rg == first_of_c) ? 0 : 1;
+          const float* src = a.partials + ((((size_t)cc * 2 + sl) * kConsumerWarps + warp) * NT) * 128;
+#pragma unroll
+          for (int nt = 0; nt < NT; ++nt) {
+            const float4 p = ldcg4(src + nt * 128 + lane * 4);
+            acc[nt][0] += p.x;
+            acc[nt][1] += p.y;
+            acc[nt][2] += p.z;
+            acc[nt][3] += p.w;
+          }
+        }
+        if (alive) epilogue<NT>(a, rg, warp, lane, acc, irms, red);
+        if (threadIdx.x == 0) a.counters[rg] = 0;
+      }
+    } else if (alive) {
+      epilogue<NT>(a, rg, warp, lane, acc, irms, red);
+    }
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt) acc[nt][0] = acc[nt][1] = acc[nt][2] = acc[nt][3] = 0.f;
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Repack GGUF -> tiles (one CTA of 128 threads per tile).
+// ---------------------------------------------------------------------------
+struct RowSrc {
+  const uint8_t* p;
+  int row;
+};
+
+__device__ __forceinline__ RowSrc tiled_row_source(int R, const uint8_t* a, int rows_a, const uint8_t* b, int rows_b,
+                                                   int mode) {
+  if (mode == 0) return {R < rows_a ? a : nullptr, R};
+  if (mode == 1) {
+    if (R < rows_a) return {a, R};
+    return {(R - rows_a) < rows_b ? b : nullptr, R - rows_a};
+  }
+  // interleave-8: tile rows 0-7 from a, 8-15 from b, output index t*8 + r%8
+  const int t = R >> 4, r = R & 15, o = t * 8 + (r & 7);
+  if (r < 8) return {o < rows_a ? a : nullptr, o};
+  return {o < rows_b ? b : nullptr, o};
+}
+
+template <int DT>
+__global__ void repack_kernel(const uint8_t* a, int rows_a, const uint8_t* b, int rows_b, int mode, int k,
+                              uint8_t* out, int n_rg) {
+  constexpr int BB = block_bytes(DT);
+  constexpr int BPS = kSuperK / block_elems(DT);  // GGUF blocks per 256 columns
+  constexpr int TB = tile_bytes(DT);
+  __shared__ __align__(16) uint8_t src[16 * BB * BPS];
+  const int nsb = k / kSuperK;
+  const long long tile = blockIdx.x;  // ((rg * nsb + sb) * 8 + mt)
+  const int mt = (int)(tile % kUnitTiles);
+  const int sb = (int)((tile / kUnitTiles) % nsb);
+  const int rg = (int)(tile / kUnitTiles / nsb);
+  const size_t row_bytes = (size_t)(k / block_elems(DT)) * BB;
+  for (int i = threadIdx.x; i < 16 * BB * BPS; i += blockDim.x) {
+    const int r = i / (BB * BPS), off = i % (BB * BPS);
+    const RowSrc rs = tiled_row_source(rg * kRowGroup + mt * kTileRows + r, a, rows_a, b, rows_b, mode);
+    src[i] = rs.p ? rs.p[(size_t)rs.row * row_bytes + (size_t)sb * BB * BPS + off] : 0;
+  }
+  __syncthreads();
+  uint8_t* o = out + tile * TB;
+  const int t = threadIdx.x;
+  if (DT == DT_Q4_K) {
+    if (t < 16) {
+      for (int i = 0; i < 16; ++i) o[t * 16 + i] = src[t * BB + i];
+    }
+    // 4 chunks x 32 lanes x 4 words
+    for (int idx = t; idx < 4 * 32 * 4; idx += blockDim.x) {
+      const int ch = idx / 128, lane = (idx / 4) % 32, w = idx % 4;
+      const int ks = ch * 4 + w;
+      uint32_t word = 0;
+      for (int i = 0; i < 8; ++i) {
+        int row, col;
+        frag_pos(lane, i, row, col);
+        const int e = ks * 16 + col;
+        const uint32_t q = (uint32_t)q4k_quant(src + row * BB + 16, e);
+        word |= q << (4 * i);
+      }
+      *reinterpret_cast<uint32_t*>(o + 256 + (ch * 32 + lane) * 16 + w * 4) = word;
+    }
+  } else if (DT == DT_Q6_K) {
+    if (t < 16) {
+      o[t * 2] = src[t * BB + 208];
+      o[t * 2 + 1] = src[t * BB + 209];
+      for (int i = 0; i < 16; ++i) o[32 + t * 16 + i] = src[t * BB + 192 + i];
+    }
+    for (int idx = t; idx < 16 * 32; idx += blockDim.x) {  // (ks, lane)
+      const int ks = idx / 32, lane = idx % 32;
+      uint32_t word = 0, hbits = 0;
+      for (int i = 0; i < 8; ++i) {
+        int row, col;
+        frag_pos(lane, i, row, col);
+        const int e = ks * 16 + col;
+        const uint32_t q = (uint32_t)(q6k_quant(src + row * BB, e) + 32);  // 0..63
+        word |= (q & 0xF) << (4 * i);
+        hbits |= (q >> 4) << (i < 4 ? 2 * i : 8 + 2 * (i - 4));
+      }
+      const int ch = ks / 4, w = ks % 4;
+      *reinterpret_cast<uint32_t*>(o + 288 + (ch * 32 + lane) * 16 + w * 4) = word;
+      const int hc = ks / 8, hw = (ks & 7) >> 1;
+      uint16_t* hp = reinterpret_cast<uint16_t*>(o + 288 + 2048 + (hc * 32 + lane) * 16 + hw * 4);
+      hp[ks & 1] = (uint16_t)hbits;
+    }
+  } else {  // Q8_0
+    for (int idx = t; idx < 16 * 8; idx += blockDim.x) {
+      const int r = idx / 8, bk = idx % 8;
+      o[(r * 8 + bk) * 2] = src[(r * BPS + bk) * BB];
+      o[(r * 8 + bk) * 2 + 1] = src[(r * BPS + bk) * BB + 1];
+    }
+    for (int idx = t; idx < 16 * 32; idx += blockDim.x) {  // (ks, lane)
+      const int ks = idx / 32, lane = idx % 32;
+      uint8_t bytes[8];
+      for (int i = 0; i < 8; ++i) {
+        int row, col;
+        frag_pos(lane, i, row, col);
+        const int e = ks * 16 + col;
+        const int8_t q = (int8_t)src[(row * BPS + e / 32) * BB + 2 + (e % 32)];
+        bytes[i] = (uint8_t)((int)q + 128);
+      }
+      // [v0 v4 v1 v5 | v2 v6 v3 v7]
+      const uint8_t ord[8] = {bytes[0], bytes[4], bytes[1], bytes[5], bytes[2], bytes[6], bytes[3], bytes[7]};
+      const int ch = ks / 2;
+      uint8_t* dst = o + 256 + (ch * 32 + lane) * 16 + (ks & 1) * 8;
+      for (int i = 0; i < 8; ++i) dst[i] = ord[i];
+    }
+  }
+}
+
+// Inverse of repack for plain mode (test hook: tiled -> GGUF bytes).
+template <int DT>
+__global__ void unpack_kernel(const uint8_t* tiled, int n, int k, uint8_t* out) {
+  constexpr int BB = block_bytes(DT);
+  constexpr int BPS = kSuperK / block_elems(DT);
+  constexpr int TB = tile_bytes(DT);
+  const int nsb = k / kSuperK;
+  const long long tile = blockIdx.x;
+  const int mt = (int)(tile % kUnitTiles);
+  const int sb = (int)((tile / kUnitTiles) % nsb);
+  const int rg = (int)(tile / kUnitTiles / nsb);
+  const uint8_t* o = tiled + tile * TB;
+  const size_t row_bytes = (size_t)(k / block_elems(DT)) * BB;
+  __shared__ __align__(16) uint8_t dst[16 * BB * BPS];
+  for (int i = threadIdx.x; i < 16 * BB * BPS; i += blockDim.x) dst[i] = 0;
+  __syncthreads();
+  const int t = threadIdx.x;
+  if (DT == DT_Q4_K) {
+    if (t < 16)
+      for (int i = 0; i < 16; ++i) dst[t * BB + i] = o[t * 16 + i];
+    __syncthreads();
+    for (int idx = t; idx < 16 * 256; idx += blockDim.x) {
+      const int row = idx / 256, e = idx % 256;
+      const int ks = e / 16, col = e % 16;
+      // find lane/i holding (row, col)
+      const int g = row & 7, r1 = row >> 3, c8 = col >> 3, cc = col & 7, c = cc >> 1, hi = cc & 1;
+      const int lane = g * 4 + c, i = (r1 | (c8 << 1)) + 4 * hi;
+      const uint32_t word = *reinterpret_cast<const uint32_t*>(o + 256 + ((ks / 4) * 32 + lane) * 16 + (ks % 4) * 4);
+      const uint32_t q = (word >> (4 * i)) & 0xF;
+      const int grp = e >> 6, w = e & 63;
+      uint8_t* qb = dst + row * BB + 16 + 32 * grp + (w & 31);
+      if (w < 32) atomicOr(reinterpret_cast<unsigned int*>((size_t)qb & ~(size_t)3), q << (8 * ((size_t)qb & 3)));
+      else atomicOr(reinterpret_cast<unsigned int*>((size_t)qb & ~(size_t)3), (q << 4) << (8 * ((size_t)qb & 3)));
+    }
+  }
+  __syncthreads();
+  for (int i = t; i < 16 * BB * BPS; i += blockDim.x) {
+    const int r = i / (BB * BPS), off = i % (BB * BPS);
+    const int row = rg * kRowGroup + mt * kTileRows + r;
+    if (row < n) out[(size_t)row * row_bytes + (size_t)sb * BB * BPS + off] = dst[i];
+  }
+}
+
+__global__ void dequant_kernel(int dtype, const uint8_t* blocks, size_t nblocks, float* out) {
+  const size_t be = block_elems(dtype), bb = block_bytes(dtype);
+  const size_t total = nblocks * be;
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < total; i += (size_t)gridDim.x * blockDim.x) {
+    const uint8_t* blk = blocks + (i / be) * bb;
+    const int e = (int)(i % be);
+    out[i] = dtype == DT_Q4_K ? dequant_q4k_elem(blk, e) : dtype == DT_Q6_K ? dequant_q6k_elem(blk, e)
+                                                                           : dequant_q80_elem(blk, e);
+  }
+}
+
+// Quantisers (own design; the reference has none). Every step is an IEEE-rounded
+// operation, so a CPU implementation of the same steps reproduces the bytes.
+__device__ __forceinline__ int clampi(int v, int lo, int hi) { return v < lo ? lo : (v > hi ? hi : v); }
+__device__ __forceinline__ uint16_t f2h_bits(float f) { return __half_as_ushort(__float2half_rn(f)); }
+
+__global__ void quantize_kernel(int dtype, const float* x, size_t nblocks, uint8_t* out) {
+  const size_t bi = blockIdx.x * (size_t)blockDim.x + threadIdx.x;
+  if (bi >= nblocks) return;
+  if (dtype == DT_Q4_K) {
+    const float* v = x + bi * 256;
+    uint8_t* o = out + bi * 144;
+    float scale[8], minv[8], max_scale = 0.f, max_min = 0.f;
+    for (int j = 0; j < 8; ++j) {
+      float mn = v[32 * j], mx = v[32 * j];
+      for (int i = 1; i < 32; ++i) {
+        const float t = v[32 * j + i];
+        mn = (t < mn) ? t : mn;
+        mx = (mx < t) ? t : mx;
+      }
+      if (mn > 0.f) mn = 0.f;
+      scale[j] = __fdiv_rn(__fsub_rn(mx, mn), 15.0f);
+      minv[j] = -mn;
+      max_scale = (max_scale < scale[j]) ? scale[j] : max_scale;
+      max_min = (max_min < minv[j]) ? minv[j] : max_min;
+    }
+    const uint16_t dh = f2h_bits(__fdiv_rn(max_scale, 63.0f)), mh = f2h_bits(__fdiv_rn(max_min, 63.0f));
+    const float df = half_bits_to_float(dh), dmf = half_bits_to_float(mh);
+    int sc[8], m[8];
+    for (int j = 0; j < 8; ++j) {
+      sc[j] = df > 0.f ? clampi(__float2int_rn(__fdiv_rn(scale[j], df)), 0, 63) : 0;
+      m[j] = dmf > 0.f ? clampi(__float2int_rn(__fdiv_rn(minv[j], dmf)), 0, 63) : 0;
+    }
+    o[0] = dh & 0xff; o[1] = dh >> 8; o[2] = mh & 0xff; o[3] = mh >> 8;
+    for (int j = 0; j < 4; ++j) {
+      o[4 + j] = (uint8_t)(sc[j] | ((sc[j + 4] >> 4) << 6));
+      o[4 + j + 4] = (uint8_t)(m[j] | ((m[j + 4] >> 4) << 6));
+      o[4 + j + 8] = (uint8_t)((sc[j + 4] & 0xF) | ((m[j + 4] & 0xF) << 4));
+    }
+    for (int i = 0; i < 4; ++i)
+      for (int l = 0; l < 32; ++l) {
+        int qq[2];
+        for (int hh = 0; hh < 2; ++hh) {
+          const int j = 2 * i + hh, e = 64 * i + 32 * hh + l;
+          const float dd = __fmul_rn(df, (float)sc[j]), mm = __fmul_rn(dmf, (float)m[j]);
+          qq[hh] = dd > 0.f ? clampi(__float2int_rn(__fdiv_rn(__fadd_rn(v[e], mm), dd)), 0, 15) : 0;
+        }
+        o[16 + 32 * i + l] = (uint8_t)(qq[0] | (qq[1] << 4));
+      }
+  } else if (dtype == DT_Q6_K) {
+    const float* v = x + bi * 256;
+    uint8_t* o = out + bi * 210;
+    float s[16], smax = 0.f;
+    for (int g = 0; g < 16; ++g) {
+      float amax = 0.f;
+      for (int i = 0; i < 16; ++i) {
+        const float t = fabsf(v[16 * g + i]);
+        amax = (amax < t) ? t : amax;
+      }
+      s[g] = __fdiv_rn(amax, 31.0f);
+      smax = (smax < s[g]) ? s[g] : smax;
+    }
+    const uint16_t dh = f2h_bits(__fdiv_rn(smax, 127.0f));
+    const float df = half_bits_to_float(dh);
+    int8_t sc[16];
+    for (int g = 0; g < 16; ++g) sc[g] = (int8_t)(df > 0.f ? clampi(__float2int_rn(__fdiv_rn(s[g], df)), -128, 127) : 0);
+    uint8_t q[256];
+    for (int i = 0; i < 256; ++i) {
+      const float dd = __fmul_rn(df, (float)sc[i / 16]);
+      q[i] = (uint8_t)((dd != 0.f ? clampi(__float2int_rn(__fdiv_rn(v[i], dd)), -32, 31) : 0) + 32);
+    }
+    for (int h = 0; h < 2; ++h)
+      for (int l = 0; l < 32; ++l) {
+        const uint8_t* qq = q + 128 * h;
+        const uint8_t q1 = qq[l], q2 = qq[l + 32], q3 = qq[l + 64], q4 = qq[l + 96];
+        o[64 * h + l] = (uint8_t)((q1 & 0xF) | ((q3 & 0xF) << 4));
+        o[64 * h + l + 32] = (uint8_t)((q2 & 0xF) | ((q4 & 0xF) << 4));
+        o[128 + 32 * h + l] = (uint8_t)((q1 >> 4) | ((q2 >> 4) << 2) | ((q3 >> 4) << 4) | ((q4 >> 4) << 6));
+      }
+    for (int g = 0; g < 16; ++g) o[192 + g] = (uint8_t)sc[g];
+    o[208] = dh & 0xff;
+    o[209] = dh >> 8;
+  } else {  // Q8_0
+    const float* v = x + bi * 32;
+    uint8_t* o = out + bi * 34;
+    float amax = 0.f;
+    for (int i = 0; i < 32; ++i) {
+      const float t = fabsf(v[i]);
+      amax = (amax < t) ? t : amax;
+    }
+    const uint16_t dh = f2h_bits(__fdiv_rn(amax, 127.0f));
+    const float df = half_bits_to_float(dh);
+    o[0] = dh & 0xff;
+    o[1] = dh >> 8;
+    for (int i = 0; i < 32; ++i)
+      o[2 + i] = (uint8_t)(int8_t)(df > 0.f ? clampi(__float2int_rn(__fdiv_rn(v[i], df)), -128, 127) : 0);
+  }
+}
+
+template <int DT, int NT>
+cudaError_t launch_t(const GemvArgs& a, int num_sms, cudaStream_t s, int pdl) {
+  const int smem = smem_layout(DT, NT).total;
+  auto kern = gemv_kernel<DT, NT>;
+  static unsigned long long attr_set = 0;  // per instantiation, one bit per device
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (!(attr_set & (1ull << dev))) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    if (e != cudaSuccess) return e;
+    attr_set |= 1ull << dev;
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(gemv_ctas(num_sms, a.n_rg, a.nsb));
+  cfg.blockDim = dim3(Cfg<NT>::kThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, kern, a);
+}
+
+template <int DT>
+cudaError_t launch_dt(const GemvArgs& a, int num_sms, cudaStream_t s, int pdl) {
+  switch (gemv_nt_for(a.m)) {
+    case 1: return launch_t<DT, 1>(a, num_sms, s, pdl);
+    case 2: return launch_t<DT, 2>(a, num_sms, s, pdl);
+    case 4: return launch_t<DT, 4>(a, num_sms, s, pdl);
+    default: return launch_t<DT, 8>(a, num_sms, s, pdl);
+  }
+}
+
+}  // namespace
+
+int gemv_nt_for(int m) { return m <= 8 ? 1 : m <= 16 ? 2 : m <= 32 ? 4 : 8; }
+
+int gemv_ctas(int num_sms, int n_rg, int nsb) {
+  const long long U = (long long)n_rg * nsb;
+  return (int)(U < num_sms ? U : num_sms);
+}
+
+size_t gemv_partials_floats(int num_ctas, int nt) { return (size_t)num_ctas * 2 * kConsumerWarps * nt * 128; }
+
+int gemv_dynamic_smem(int dtype, int nt) { return smem_layout(dtype, nt).total; }
+
+cudaError_t gemv_launch(const GemvArgs& a, int num_sms, cudaStream_t s, int pdl) {
+  if (a.m < 1 || a.m > kMaxTokens) return cudaErrorInvalidValue;
+  switch (a.dtype) {
+    case DT_Q4_K: return launch_dt<DT_Q4_K>(a, num_sms, s, pdl);
+    case DT_Q6_K: return launch_dt<DT_Q6_K>(a, num_sms, s, pdl);
+    case DT_Q8_0: return launch_dt<DT_Q8_0>(a, num_sms, s, pdl);
+  }
+  return cudaErrorInvalidValue;
+}
+
+cudaError_t repack_launch(const uint8_t* a, int rows_a, const uint8_t* b, int rows_b, int mode, int dtype, int k,
+                          uint8_t* out, int n_rg, cudaStream_t s) {
+  const long long tiles = (long long)n_rg * (k / kSuperK) * kUnitTiles;
+  if (tiles == 0) return cudaSuccess;
+  switch (dtype) {
+    case DT_Q4_K: repack_kernel<DT_Q4_K><<<(unsigned)tiles, 128, 0, s>>>(a, rows_a, b, rows_b, mode, k, out, n_rg); break;
+    case DT_Q6_K: repack_kernel<DT_Q6_K><<<(unsigned)tiles, 128, 0, s>>>(a, rows_a, b, rows_b, mode, k, out, n_rg); break;
+    case DT_Q8_0: repack_kernel<DT_Q8_0><<<(unsigned)tiles, 128, 0, s>>>(a, rows_a, b, rows_b, mode, k, out, n_rg); break;
+    default: return cudaErrorInvalidValue;
+  }
+  return cudaGetLastError();
+}
+
+cudaError_t unpack_launch(const uint8_t* tiled, int dtype, int n, int k, uint8_t* out, cudaStream_t s) {
+  if (dtype != DT_Q4_K) return cudaErrorInvalidValue;
+  const int n_rg = (n + kRowGroup - 1) / kRowGroup;
+  const long long tiles = (long long)n_rg * (k / kSuperK) * kUnitTiles;
+  unpack_kernel<DT_Q4_K><<<(unsigned)tiles, 128, 0, s>>>(tiled, n, k, out);
+  return cudaGetLastError();
+}
+
+cudaError_t dequant_launch(int dtype, const uint8_t* blocks, size_t nblocks, float* out, cudaStream_t s) {
+  if (nblocks == 0) return cudaSuccess;
+  const size_t total = nblocks * block_elems(dtype);
+  const unsigned grid = (unsigned)((total + 255) / 256 < 65535 * 16 ? (total + 255) / 256 : 65535 * 16);
+  dequant_kernel<<<grid, 256, 0, s>>>(dtype, blocks, nblocks, out);
+  return cudaGetLastError();
+}
+
+cudaError_t quantize_launch(int dtype, const float* x, size_t n, uint8_t* out, cudaStream_t s) {
+  const size_t be = block_elems(dtype);
+  if (n % be) return cudaErrorInvalidValue;
+  const size_t nb = n / be;
+  if (nb == 0) return cudaSuccess;
+  quantize_kernel<<<(unsigned)((nb + 127) / 128), 128, 0, s>>>(dtype, x, nb, out);
+  return cudaGetLastError();
+}
+
+}  // namespace rb

@@ -1,0 +1,86 @@
+// Host/device interface of the fused dequant GEMV/GEMM (y = x . W^T).
+#pragma once
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace rb {
+
+enum Epilogue : int32_t {
+  EPI_STORE = 0,   // y[tok][row] = acc * inv_rms[tok]
+  EPI_QKV = 1,     // RoPE + q store + paged K/V append
+  EPI_RESID = 2,   // x[tok][row] += acc, plus per-row-group sum of squares of the new x
+  EPI_SWIGLU = 3,  // rows interleaved gate/up per 8: h = silu(g) * u
+  EPI_LOGITS = 4,  // optional logits store + greedy argmax (ties -> last index)
+};
+
+// Paged KV pool view (shared with the attention kernels).
+// Element (page, layer, kv, head, slot, d) lives at
+// ((((page * n_layers + layer) * 2 + kv) * n_kv + head) * 16 + slot) * hd + d.
+struct KvView {
+  void* pool = nullptr;
+  int32_t f16 = 1;  // 1: fp16 elements, 0: fp32
+  int32_t n_layers = 1, n_kv = 1, hd = 128;
+  const int32_t* ptab = nullptr;  // [tenant][ptab_stride] physical page ids
+  int32_t ptab_stride = 0;
+};
+
+struct GemvArgs {
+  // weights (tiled layout) and geometry
+  const uint8_t* w = nullptr;
+  int32_t dtype = 0;
+  int32_t n = 0;      // logical output rows
+  int32_t n_rg = 0;   // 128-row groups (padded rows = n_rg * 128)
+  int32_t nsb = 0;    // K / 256
+  int32_t m = 0;      // tokens (x rows)
+  // input
+  const float* x = nullptr;
+  int32_t ldx = 0;
+  const float* norm_w = nullptr;   // optional elementwise prologue weight [K]
+  const float* ss_part = nullptr;  // optional [n_ss][ld_ss] partial sums of squares
+  int32_t n_ss = 0, ld_ss = 64;
+  float norm_eps = 1e-5f;
+  int32_t norm_dim = 0;
+  // epilogue
+  int32_t epi = EPI_STORE;
+  float* y = nullptr;   // STORE / SWIGLU output, LOGITS logits (optional)
+  int32_t ldy = 0;
+  float* resid = nullptr;  // RESID: x stream (read-modify-write), ld = ldr
+  int32_t ldr = 0;
+  float* ss_out = nullptr;  // RESID: [n_rg][ld_ss]
+  unsigned long long* argmax = nullptr;  // LOGITS: per token key
+  // QKV
+  int32_t qkv_row0 = 0, n_q_rows = 0, n_k_rows = 0;
+  float* q_out = nullptr;
+  int32_t ldq = 0;
+  float rope_theta = 10000.f;
+  int32_t head_dim = 128;
+  int32_t layer = 0;
+  const int32_t* row_tenant = nullptr;
+  const int32_t* row_pos = nullptr;
+  KvView kv;
+  // scratch / status
+  float* partials = nullptr;
+  int32_t* counters = nullptr;
+  uint32_t* err = nullptr;
+};
+
+// Scratch needed by one GEMV launch (partials in floats, counters in ints).
+size_t gemv_partials_floats(int num_ctas, int nt);
+int gemv_ctas(int num_sms, int n_rg, int nsb);
+int gemv_nt_for(int m);
+// Launch with programmatic dependent launch enabled when pdl != 0.
+cudaError_t gemv_launch(const GemvArgs& a, int num_sms, cudaStream_t s, int pdl);
+int gemv_dynamic_smem(int dtype, int nt);
+
+// Repack GGUF blocks into the tiled layout. Source rows come from up to two
+// matrices: mode 0 plain (rows of a), 1 concat (a then b), 2 interleave-8
+// (tile rows 0-7 from a, 8-15 from b, same output index).
+cudaError_t repack_launch(const uint8_t* a, int rows_a, const uint8_t* b, int rows_b, int mode, int dtype,
+                          int k, uint8_t* out, int n_rg, cudaStream_t s);
+cudaError_t unpack_launch(const uint8_t* tiled, int dtype, int n, int k, uint8_t* out, cudaStream_t s);
+
+// Element-wise dequant (GGUF layout) and quantisers.
+cudaError_t dequant_launch(int dtype, const uint8_t* blocks, size_t nblocks, float* out, cudaStream_t s);
+cudaError_t quantize_launch(int dtype, const float* x, size_t n, uint8_t* out, cudaStream_t s);
+
+}  // namespace rb

@@ -1,0 +1,91 @@
+"""CPU tests of the product library boundary (no GPU needed): the C ABI loads
+and exports every symbol include/realm_b200.h declares, host-side failures
+return the documented status codes, and the product never touches the oracle."""
+import ctypes as C
+import os
+import re
+import subprocess
+import sys
+
+import pytest
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+HEADER = os.path.join(ROOT, "include", "realm_b200.h")
+
+
+def declared_symbols():
+    txt = open(HEADER).read()
+    txt = re.sub(r"/\*.*?\*/", "", txt, flags=re.S)
+    return sorted(set(re.findall(r"^\s*(?:int32_t|void\s*\*|float)\s+(rb_\w+)\s*\(", txt, flags=re.M)))
+
+
+def test_library_exports_every_declared_symbol():
+    import realm_b200 as rb
+    syms = declared_symbols()
+    assert len(syms) >= 40
+    lib = C.CDLL(rb.LIB_PATH)
+    missing = [s for s in syms if not hasattr(lib, s)]
+    assert not missing, missing
+
+
+def test_built_for_sm100a_only():
+    import realm_b200 as rb
+    out = subprocess.run(["/usr/local/cuda/bin/cuobjdump", "--list-elf", rb.LIB_PATH], capture_output=True, text=True)
+    if out.returncode != 0:
+        pytest.skip("cuobjdump unavailable")
+    arches = set(re.findall(r"sm_(\d+a?)", out.stdout))
+    assert arches == {"100a"}, arches
+
+
+def test_no_gpu_context_error_code():
+    import realm_b200 as rb
+    try:
+        import torch
+        if torch.cuda.is_available():
+            pytest.skip("a GPU is present")
+    except ImportError:
+        pass
+    with pytest.raises(rb.RealmError) as e:
+        rb.Context(0)
+    assert e.value.code == -1
+    assert "CUDA" in rb.last_error()
+
+
+def test_null_handles_rejected():
+    import realm_b200 as rb
+    lib = rb.lib()
+    assert lib.rb_sync(None) == -20
+    assert lib.rb_ctx_destroy(None) == -20
+    assert lib.rb_kv_len(None, 0, 0, 0) == -20
+    assert lib.rb_forward(None, 0, 1, None, None, None, None, None, 0) == -20
+    assert lib.rb_last_error(None, 0) > 0
+
+
+def test_error_codes_match_header():
+    import realm_b200 as rb
+    txt = open(HEADER).read()
+    codes = {int(v) for v in re.findall(r"#define RB_ERR_\w+ \((-\d+)\)", txt)}
+    assert codes == set(rb.ERRORS)
+
+
+def test_product_never_imports_oracle():
+    pkg = os.path.join(ROOT, "realm_b200")
+    for dirpath, _, files in os.walk(pkg):
+        for f in files:
+            if f.endswith((".py", ".cu", ".cuh", ".cpp", ".h")):
+                src = open(os.path.join(dirpath, f), errors="replace").read()
+                assert "oracle" not in src.lower(), f
+    # the shared library does not link the oracle either
+    out = subprocess.run(["ldd", os.path.join(pkg, "librealm_b200.so")], capture_output=True, text=True).stdout
+    assert "oracle" not in out
+
+
+def test_tenant_sharding():
+    from realm_b200.sharding import lpt_shard, tenant_shard
+    assert tenant_shard(64, 8, 3) == list(range(24, 32))
+    parts = [tenant_shard(10, 4, r) for r in range(4)]
+    assert sum(parts, []) == list(range(10)) and [len(p) for p in parts] == [3, 3, 2, 2]
+    bins = lpt_shard([500, 100, 400, 300, 200, 100], 2)
+    assert sorted(sum(bins, [])) == list(range(6))
+    loads = [sum([500, 100, 400, 300, 200, 100][t] for t in b) for b in bins]
+    assert abs(loads[0] - loads[1]) <= 100

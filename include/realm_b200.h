@@ -108,6 +108,13 @@ int32_t rb_weight_upload(rb_ctx* ctx, int32_t dtype, uint32_t n, uint32_t k, con
 int32_t rb_weight_free(rb_ctx* ctx, int32_t handle);
 int32_t rb_weight_matmul(rb_ctx* ctx, int32_t handle, const float* input, float* output, uint32_t batch_size,
                          uint32_t flags);
+/* Timing hook: device time (microseconds) per launch of the GEMV kernel alone,
+ * from a CUDA graph of `iters` back-to-back launches cycling over `n_handles`
+ * resident weights (same K) with a fixed device-resident batch of `batch` rows
+ * (activation fragments prepared once). The graph is replayed `reps` times and
+ * the mean is returned in *avg_us. */
+int32_t rb_weight_matmul_timing(rb_ctx* ctx, const int32_t* handles, uint32_t n_handles, uint32_t batch, uint32_t iters,
+                                uint32_t reps, float* avg_us);
 /* Test hook: the resident tiled bytes converted back to GGUF layout (Q4_K). */
 int32_t rb_weight_export(rb_ctx* ctx, int32_t handle, void* out_blocks, size_t nbytes, uint32_t flags);
 

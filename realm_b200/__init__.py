@@ -44,7 +44,7 @@ ERRORS = {
 }
 
 if not os.path.exists(LIB_PATH):
-    raise ImportError(f"{LIB_PATH} is missing: build it with `python -m realm_b200.build` "
+    raise ImportError(f"{LIB_PATH} is missing: build it with `python realm_b200/build.py` "
                       "(there is no CPU fallback)")
 
 _lib = C.CDLL(LIB_PATH)
@@ -84,6 +84,7 @@ _sig("rb_weight_upload", [_vp, _i32, _u32, _u32, _vp, _sz, _u32, _I32P])
 _sig("rb_weight_free", [_vp, _i32])
 _sig("rb_weight_matmul", [_vp, _i32, _vp, _vp, _u32, _u32])
 _sig("rb_weight_export", [_vp, _i32, _vp, _sz, _u32])
+_sig("rb_weight_matmul_timing", [_vp, _vp, _u32, _u32, _u32, _u32, C.POINTER(C.c_float)])
 _sig("rb_candle_matmul", [_vp, _vp, _vp, _vp, _u32, _u32, _u32, _u32])
 _sig("rb_candle_matmul_transposed", [_vp, _vp, _vp, _vp, _u32, _u32, _u32, _u32])
 _sig("rb_kv_pool_create", [_vp, _u32, _u32, _u32, _i32, _u32, _u32, _u32, _I32P])
@@ -194,9 +195,9 @@ class Context:
         _ORDER_CTX[0] = self
 
     def close(self):
-        if getattr(self, "_h", None):
+        if getattr(self, "_h", None) and _lib is not None:
             _lib.rb_ctx_destroy(self._h)
-            self._h = None
+        self._h = None
 
     def __del__(self):
         self.close()
@@ -266,6 +267,14 @@ class Context:
 
     def fused_dequant_matmul_q80(self, blocks, input, batch_size, n, k):
         return self.fused_dequant_matmul(Q8_0, blocks, input, batch_size, n, k)
+
+    def gemv_timing(self, weights, batch: int, iters: int = 32, reps: int = 5) -> float:
+        """Device microseconds per GEMV launch (graph of back-to-back launches)."""
+        h = np.array([w.handle for w in weights], np.int32)
+        out = C.c_float()
+        _check(_lib.rb_weight_matmul_timing(self._h, h.ctypes.data_as(C.c_void_p), len(h), batch, iters, reps,
+                                            C.byref(out)))
+        return float(out.value)
 
     def upload_weight(self, dtype: int, n: int, k: int, blocks) -> "Weight":
         return Weight(self, dtype, n, k, blocks)
@@ -425,9 +434,10 @@ class Model:
                          cfg["max_seq"], handle=pool)
 
     def set_weight(self, which: int, layer: int, dtype: int, data):
-        data = _u8(data) if dtype != F32 or not _is_dev(data) else data
-        if not _is_dev(data) and dtype == F32:
-            data = np.ascontiguousarray(data, np.float32).view(np.uint8).ravel()
+        if not _is_dev(data):
+            if dtype == F32:
+                data = np.ascontiguousarray(data, np.float32)
+            data = np.ascontiguousarray(data).view(np.uint8).ravel()
         nbytes = (data.numel() * data.element_size()) if _is_dev(data) else data.nbytes
         _check(_lib.rb_model_set_weight(self.ctx.handle, self.handle, which, layer, dtype, _ptr(data), nbytes,
                                         _flags(data)))

@@ -1,6 +1,6 @@
 """Builds realm_b200/librealm_b200.so (sm_100a) in-tree with nvcc.
 
-Usage: python -m realm_b200.build [--force]
+Usage: python realm_b200/build.py [--force]   (run by path: the package import needs the library)
 """
 from __future__ import annotations
 
@@ -14,7 +14,7 @@ CSRC = os.path.join(HERE, "csrc")
 BUILD = os.path.join(HERE, "_build")
 LIB = os.path.join(HERE, "librealm_b200.so")
 SOURCES = ["gemv.cu", "attention.cu", "engine.cu"]
-HEADERS = ["common.cuh", "quant.cuh", "gemv.cuh", "attention.cuh"]
+HEADERS = ["common.cuh", "quant.cuh", "gemv.cuh", "attention.cuh", "xfrag.cuh"]
 NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
 FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a", "-O3", "-std=c++17", "-lineinfo",
          "-Xcompiler", "-fPIC"]

@@ -14,6 +14,7 @@
 // in a fixed order (deterministic, no spin waits).
 #include "attention.cuh"
 #include "common.cuh"
+#include "xfrag.cuh"
 
 namespace rb {
 
@@ -280,20 +281,43 @@ __global__ void __launch_bounds__(kAttnWarps * 32) attn_kernel(const AttnArgs a)
     const int np_row = (a.row_pos[ui.row] >> 4) + 1;
     const int nsplit = (np_row + kAttnPagesPerSplit - 1) / kAttnPagesPerSplit;
     const size_t slot = ((size_t)ui.row * n_kv + ui.kvh) * a.max_splits + ui.split;
-    for (int i = threadIdx.x; i < NREP * HD; i += blockDim.x) {
+    // Final values go to shared memory (the q buffer is free now), then out to the
+    // fp32 output and / or the activation fragments of the o-proj GEMV.
+    float* ofin = qs;
+    auto finish = [&]() {
+      __syncthreads();
+      if (a.out)
+        for (int i = threadIdx.x; i < NREP * HD; i += blockDim.x)
+          a.out[(size_t)ui.row * a.ldo + (size_t)ui.kvh * NREP * HD + i] = ofin[i];
+      if (a.xout.xf)
+        frags_write(ofin, 1, 0, NREP * HD, 1, ui.kvh * NREP * HD, ui.row, nullptr, a.xout, a.xf_nt, threadIdx.x,
+                    blockDim.x);
+    };
+    auto merge_warps = [&](int i, float& M, float& Lsum, float& O) {
       const int r = i / HD, d = i % HD;
-      float M = -INFINITY;
+      M = -INFINITY;
       for (int w = 0; w < kAttnWarps; ++w) M = fmaxf(M, mrg[(w * NREP + r) * (HD + 2) + HD]);
-      float Lsum = 0.f, O = 0.f;
+      Lsum = 0.f;
+      O = 0.f;
       for (int w = 0; w < kAttnWarps; ++w) {
         const float* ww = mrg + (w * NREP + r) * (HD + 2);
         const float f = (ww[HD] == -INFINITY) ? 0.f : expf(ww[HD] - M);
         Lsum += ww[HD + 1] * f;
         O += ww[d] * f;
       }
-      if (nsplit == 1) {
-        a.out[(size_t)ui.row * a.ldo + ((size_t)ui.kvh * NREP + r) * HD + d] = Lsum > 0.f ? O / Lsum : 0.f;
-      } else {
+    };
+    if (nsplit == 1) {
+      for (int i = threadIdx.x; i < NREP * HD; i += blockDim.x) {
+        float M, Lsum, O;
+        merge_warps(i, M, Lsum, O);
+        ofin[i] = Lsum > 0.f ? O / Lsum : 0.f;
+      }
+      finish();
+    } else {
+      for (int i = threadIdx.x; i < NREP * HD; i += blockDim.x) {
+        const int r = i / HD, d = i % HD;
+        float M, Lsum, O;
+        merge_warps(i, M, Lsum, O);
         float* dst = a.partials + (slot * NREP + r) * (HD + 2);
         __stcg(dst + d, O);
         if (d == 0) {
@@ -301,8 +325,6 @@ __global__ void __launch_bounds__(kAttnWarps * 32) attn_kernel(const AttnArgs a)
           __stcg(dst + HD + 1, Lsum);
         }
       }
-    }
-    if (nsplit > 1) {
       __threadfence();
       __syncthreads();
       if (threadIdx.x == 0)
@@ -323,8 +345,9 @@ __global__ void __launch_bounds__(kAttnWarps * 32) attn_kernel(const AttnArgs a)
             Lsum += __ldcg(src + HD + 1) * f;
             O += __ldcg(src + d) * f;
           }
-          a.out[(size_t)ui.row * a.ldo + ((size_t)ui.kvh * NREP + r) * HD + d] = Lsum > 0.f ? O / Lsum : 0.f;
+          ofin[i] = Lsum > 0.f ? O / Lsum : 0.f;
         }
+        finish();
         if (threadIdx.x == 0) a.counters[ui.row * n_kv + ui.kvh] = 0;
       }
     }

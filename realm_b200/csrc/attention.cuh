@@ -10,8 +10,10 @@ struct AttnArgs {
   const int32_t* row_pos = nullptr;  // row attends to positions [0, pos]
   const float* q = nullptr;        // [n_rows][ldq], head h at h*hd
   int32_t ldq = 0;
-  float* out = nullptr;            // [n_rows][ldo]
+  float* out = nullptr;            // [n_rows][ldo] fp32 (optional)
   int32_t ldo = 0;
+  XFrags xout;                     // optional: output as activation fragments (xfrag.cuh)
+  int32_t xf_nt = 1;               //   for the next GEMV, with xf_nt n-tiles
   int32_t n_heads = 0;
   int32_t layer = 0;
   float scale = 0.f;

@@ -19,6 +19,7 @@
 #include "common.cuh"
 #include "gemv.cuh"
 #include "quant.cuh"
+#include "xfrag.cuh"
 
 namespace rb {
 
@@ -56,10 +57,12 @@ struct StepDesc {  // device view of one forward step (filled by one H2D copy)
 };
 
 // Embedding rows (bit-exact dequant of token_embd, model.rs:579-596 /
-// memory64_host.rs:2570-2583), page-table updates, argmax reset, and the
-// per-128-column sums of squares feeding the first fused RMSNorm.
+// memory64_host.rs:2570-2583), page-table updates, argmax reset, the
+// per-128-column sums of squares feeding the first fused RMSNorm, and the
+// activation fragments of x * attn_norm for layer 0's q|k|v GEMV.
 __global__ void embed_kernel(const uint8_t* embd, int dtype, int hidden, const int32_t* desc_i, int32_t* ptab,
-                             int ptab_stride, float* x, int ldx, float* ss, int ld_ss, unsigned long long* argmax) {
+                             int ptab_stride, float* x, int ldx, float* ss, int ld_ss, unsigned long long* argmax,
+                             const float* norm_w, int nt, XFrags frags) {
   const int n_rows = desc_i[0], n_upd = desc_i[1];
   const int32_t* row_tokens = desc_i + 2 + 2 * 64;
   const int32_t* upd = desc_i + 2 + 3 * 64;
@@ -74,6 +77,7 @@ __global__ void embed_kernel(const uint8_t* embd, int dtype, int hidden, const i
   const int be = block_elems(dtype), bb = block_bytes(dtype);
   const size_t row_bytes = (size_t)(hidden / be) * bb;
   const uint8_t* src = embd + (size_t)tok * row_bytes;
+  float* xr = x + (size_t)r * ldx;
   __shared__ float red[8];
   for (int g0 = 0; g0 < hidden; g0 += 128) {
     float sq = 0.f;
@@ -87,7 +91,7 @@ __global__ void embed_kernel(const uint8_t* embd, int dtype, int hidden, const i
           : dtype == DT_Q6_K ? dequant_q6k_elem(blk, e)
           : dtype == DT_Q8_0 ? dequant_q80_elem(blk, e)
                              : reinterpret_cast<const float*>(embd)[(size_t)tok * hidden + i];
-        x[(size_t)r * ldx + i] = v;
+        xr[i] = v;
       }
       sq = v * v;
     }
@@ -95,23 +99,10 @@ __global__ void embed_kernel(const uint8_t* embd, int dtype, int hidden, const i
     for (int o = 16; o > 0; o >>= 1) sq += __shfl_xor_sync(0xffffffffu, sq, o);
     if ((threadIdx.x & 31) == 0 && threadIdx.x < 128) red[threadIdx.x >> 5] = sq;
     __syncthreads();
-    if (threadIdx.x == 0) ss[(size_t)(g0 / 128) * ld_ss + r] = (red[0] + red[1]) + (red[2] + red[3]);
+    if (threadIdx.x == 0 && ss) ss[(size_t)(g0 / 128) * ld_ss + r] = (red[0] + red[1]) + (red[2] + red[3]);
     __syncthreads();
   }
-}
-
-// Per-128-column sums of squares of x rows (for forward_layer / compute_logits entry).
-__global__ void ss_kernel(const float* x, int ldx, int hidden, float* ss, int ld_ss) {
-  const int r = blockIdx.y, g = blockIdx.x;
-  const int i = g * 128 + threadIdx.x;
-  float v = i < hidden ? x[(size_t)r * ldx + i] : 0.f;
-  float sq = v * v;
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) sq += __shfl_xor_sync(0xffffffffu, sq, o);
-  __shared__ float red[4];
-  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = sq;
-  __syncthreads();
-  if (threadIdx.x == 0) ss[(size_t)g * ld_ss + r] = (red[0] + red[1]) + (red[2] + red[3]);
+  if (frags.xf) frags_write(xr, 1, 0, hidden, 1, 0, r, norm_w, frags, nt, threadIdx.x, blockDim.x);
 }
 
 __global__ void zero_u64_kernel(unsigned long long* p, int n) {
@@ -172,6 +163,21 @@ struct Weight {
   DevBuf tiled;
 };
 
+// Device storage for one GEMV input's activation fragments (xfrag.cuh).
+struct FragBuf {
+  DevBuf f, s;
+  cudaError_t alloc(int k, int nt) {
+    cudaError_t e = f.alloc(xf_bytes(k, nt));
+    return e != cudaSuccess ? e : s.alloc(xs_bytes(k, nt));
+  }
+  XFrags view() const {
+    XFrags v;
+    v.xf = f.as<uint4>();
+    v.xs = s.as<uint32_t>();
+    return v;
+  }
+};
+
 struct KvTenant {
   bool live = false;
   std::vector<int> len;    // per layer
@@ -218,7 +224,9 @@ struct Model {
   std::vector<LayerW> layers;
   bool finalized = false;
   // step buffers
-  DevBuf x, q, att, h, ss, logits, argmax, desc;
+  DevBuf x, q, ss, logits, argmax, desc;
+  // activation fragments: q|k|v and LM-head input (a), o-proj (o), gate/up (f), down (d)
+  FragBuf fa, fo, ff, fd;
   int max_rows = 0;
   std::map<int, cudaGraphExec_t> graphs;  // by row count
   std::map<int, int> graph_launches;
@@ -232,6 +240,8 @@ struct Ctx {
   DevBuf gemv_partials, counters, attn_partials, err;
   size_t attn_partials_cap = 0;
   DevBuf stage_in, stage_out;  // generic device staging for host-pointer calls
+  FragBuf xf_scratch;          // activation fragments for rb_weight_matmul inputs
+  int xf_scratch_k = 0;
   void* pinned = nullptr;      // step descriptor staging
   size_t pinned_bytes = 0;
   cudaEvent_t pinned_ev = nullptr;  // last copy out of `pinned` (reuse waits on it)
@@ -240,6 +250,7 @@ struct Ctx {
   std::vector<std::unique_ptr<Model>> models;
   float last_ms = 0.f;
   int last_launches = 0;
+  int gemv_dbg = 0;  // measurement hook (RB_GEMV_DBG): bit 0 skips the GEMV math
 };
 
 constexpr int kMaxRowsAbi = 64;
@@ -315,10 +326,10 @@ GemvArgs base_args(Ctx* c, const Weight& w, int m) {
   a.n_rg = w.n_rg;
   a.nsb = w.k / kSuperK;
   a.m = m;
-  a.ldx = w.k;
   a.partials = c->gemv_partials.as<float>();
   a.counters = c->counters.as<int32_t>();
   a.err = c->err.as<uint32_t>();
+  a.dbg = c->gemv_dbg;
   return a;
 }
 
@@ -329,7 +340,9 @@ int launch_gemv(Ctx* c, const GemvArgs& a, int* launches) {
 }
 
 // ---------------------------------------------------------------------------
-// model forward (enqueue only)
+// model forward (enqueue only). Every GEMV reads activation fragments written by
+// the kernel before it: embed -> (q|k, v) -> attention -> o (+residual) ->
+// gate/up (SwiGLU) -> down (+residual) -> next layer / LM head.
 // ---------------------------------------------------------------------------
 int enqueue_layer(Ctx* c, Model& M, int l, int m, const int32_t* d_tenant, const int32_t* d_pos, int* launches) {
   const rb_model_config& cf = M.cfg;
@@ -337,13 +350,13 @@ int enqueue_layer(Ctx* c, Model& M, int l, int m, const int32_t* d_tenant, const
   LayerW& L = M.layers[l];
   const int H = cf.hidden, hd = cf.head_dim, Hq = cf.n_heads, Hkv = cf.n_kv_heads;
   const int n_ss = (H + 127) / 128;
+  const int NT = gemv_nt_for(m);
   float* x = M.x.as<float>();
   float* ss = M.ss.as<float>();
-  // q|k (+v) with fused RMSNorm prologue, RoPE and KV append epilogue
+  // q|k (+v) with fused RMSNorm (weight in the fragments, 1/rms in the epilogue),
+  // RoPE and the paged KV append
   GemvArgs a = base_args(c, L.qk, m);
-  a.x = x;
-  a.ldx = H;
-  a.norm_w = L.raw[0].d.as<float>();
+  a.xin = M.fa.view();
   a.ss_part = ss;
   a.n_ss = n_ss;
   a.ld_ss = kMaxRowsAbi;
@@ -372,15 +385,16 @@ int enqueue_layer(Ctx* c, Model& M, int l, int m, const int32_t* d_tenant, const
     av.qkv_row0 = (Hq + Hkv) * hd;
     if (int rc = launch_gemv(c, av, launches)) return rc;
   }
-  // paged GQA attention
+  // paged GQA attention -> fragments of the o-proj input
   AttnArgs at;
   at.n_rows = m;
   at.row_tenant = d_tenant;
   at.row_pos = d_pos;
   at.q = M.q.as<float>();
   at.ldq = Hq * hd;
-  at.out = M.att.as<float>();
-  at.ldo = Hq * hd;
+  at.out = nullptr;
+  at.xout = M.fo.view();
+  at.xf_nt = NT;
   at.n_heads = Hq;
   at.layer = l;
   at.scale = 1.0f / sqrtf((float)hd);  // attention_stub/mod.rs:57
@@ -391,48 +405,45 @@ int enqueue_layer(Ctx* c, Model& M, int l, int m, const int32_t* d_tenant, const
   at.err = c->err.as<uint32_t>();
   RB_CUDA(attn_launch(at, c->num_sms, c->stream, c->pdl ? 1 : 0));
   if (launches) ++*launches;
-  // o-proj + residual
+  // o-proj + residual; writes fragments of x * ffn_norm
   GemvArgs ao = base_args(c, L.o, m);
-  ao.x = M.att.as<float>();
-  ao.ldx = Hq * hd;
+  ao.xin = M.fo.view();
   ao.epi = EPI_RESID;
   ao.resid = x;
   ao.ldr = H;
   ao.ss_out = ss;
   ao.ld_ss = kMaxRowsAbi;
+  ao.xout = M.ff.view();
+  ao.xf_norm = L.raw[5].d.as<float>();
   if (int rc = launch_gemv(c, ao, launches)) return rc;
-  // gate/up (interleaved) with fused RMSNorm prologue and SwiGLU epilogue
+  // gate/up (interleaved) with fused RMSNorm and SwiGLU -> fragments of h
   GemvArgs ag = base_args(c, L.gu, m);
-  ag.x = x;
-  ag.ldx = H;
-  ag.norm_w = L.raw[5].d.as<float>();
+  ag.xin = M.ff.view();
   ag.ss_part = ss;
   ag.n_ss = n_ss;
   ag.ld_ss = kMaxRowsAbi;
   ag.norm_eps = cf.layer_eps;
   ag.norm_dim = H;
   ag.epi = EPI_SWIGLU;
-  ag.y = M.h.as<float>();
-  ag.ldy = cf.ffn;
+  ag.xout = M.fd.view();
   if (int rc = launch_gemv(c, ag, launches)) return rc;
-  // down + residual
+  // down + residual; writes fragments of x * (next layer's attn_norm | output_norm)
   GemvArgs ad = base_args(c, L.down, m);
-  ad.x = M.h.as<float>();
-  ad.ldx = cf.ffn;
+  ad.xin = M.fd.view();
   ad.epi = EPI_RESID;
   ad.resid = x;
   ad.ldr = H;
   ad.ss_out = ss;
   ad.ld_ss = kMaxRowsAbi;
+  ad.xout = M.fa.view();
+  ad.xf_norm = (l + 1 < (int)cf.n_layers) ? M.layers[l + 1].raw[0].d.as<float>() : M.out_norm.d.as<float>();
   return launch_gemv(c, ad, launches);
 }
 
 int enqueue_head(Ctx* c, Model& M, int m, bool want_logits, int* launches) {
   const rb_model_config& cf = M.cfg;
   GemvArgs a = base_args(c, M.out, m);
-  a.x = M.x.as<float>();
-  a.ldx = cf.hidden;
-  a.norm_w = M.out_norm.d.as<float>();
+  a.xin = M.fa.view();
   a.ss_part = M.ss.as<float>();
   a.n_ss = (cf.hidden + 127) / 128;
   a.ld_ss = kMaxRowsAbi;
@@ -452,10 +463,10 @@ int enqueue_step(Ctx* c, Model& M, int m, int* launches) {
   const rb_model_config& cf = M.cfg;
   KvPool& P = *c->pools[M.pool];
   int32_t* desc = M.desc.as<int32_t>();
-  // the embed kernel expects tokens at +2+128 and updates at +2+192
   embed_kernel<<<m, 128, 0, c->stream>>>(M.embd.d.as<uint8_t>(), M.embd.dtype, cf.hidden, desc, P.ptab.as<int32_t>(),
                                          P.max_pages_per_tenant, M.x.as<float>(), cf.hidden, M.ss.as<float>(),
-                                         kMaxRowsAbi, M.argmax.as<unsigned long long>());
+                                         kMaxRowsAbi, M.argmax.as<unsigned long long>(),
+                                         M.layers[0].raw[0].d.as<float>(), gemv_nt_for(m), M.fa.view());
   RB_CUDA(cudaGetLastError());
   if (launches) ++*launches;
   for (int l = 0; l < (int)cf.n_layers; ++l)
@@ -667,6 +678,7 @@ int32_t rb_ctx_create(const rb_config* cfg, rb_ctx** out) {
   c->max_rows = cfg->max_rows ? std::min<int>(cfg->max_rows, kMaxRowsAbi) : kMaxRowsAbi;
   c->pdl = cfg->use_pdl != 0;
   c->graphs = cfg->use_graphs != 0;
+  if (const char* d = getenv("RB_GEMV_DBG")) c->gemv_dbg = atoi(d);
   RB_CUDA(cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking));
   RB_CUDA(cudaEventCreate(&c->ev0));
   RB_CUDA(cudaEventCreate(&c->ev1));
@@ -772,12 +784,23 @@ int32_t rb_weight_free(rb_ctx* c, int32_t h) {
   return RB_OK;
 }
 
+static int ensure_xf_scratch(rb_ctx* c, int k) {
+  if (c->xf_scratch_k < k) {
+    RB_CUDA(c->xf_scratch.alloc(k, 8));
+    c->xf_scratch_k = k;
+  }
+  return RB_OK;
+}
+
 static int weight_matmul_dev(rb_ctx* c, const Weight& w, const float* din, float* dout, uint32_t batch) {
+  if (int rc = ensure_xf_scratch(c, w.k)) return rc;
   for (uint32_t b0 = 0; b0 < batch; b0 += kMaxRowsAbi) {
     const int m = (int)std::min<uint32_t>(kMaxRowsAbi, batch - b0);
+    const int nt = gemv_nt_for(m);
+    RB_CUDA(xfrag_launch(din + (size_t)b0 * w.k, w.k, nullptr, m, w.k, nt, c->xf_scratch.view(), nullptr, 0,
+                         c->stream));
     GemvArgs a = base_args(c, w, m);
-    a.x = din + (size_t)b0 * w.k;
-    a.ldx = w.k;
+    a.xin = c->xf_scratch.view();
     a.epi = EPI_STORE;
     a.y = dout + (size_t)b0 * w.n;
     a.ldy = w.n;
@@ -803,6 +826,62 @@ int32_t rb_weight_matmul(rb_ctx* c, int32_t h, const float* input, float* output
   if ((flags & RB_PTR_DEVICE) && (flags & RB_ASYNC)) return (int32_t)(batch * w.n);
   if (int rc = sync_ctx(c)) return rc;
   return (int32_t)(batch * w.n);
+}
+
+int32_t rb_weight_matmul_timing(rb_ctx* c, const int32_t* handles, uint32_t n_handles, uint32_t batch, uint32_t iters,
+                                uint32_t reps, float* avg_us) {
+  if (!c || !handles || !avg_us || n_handles == 0 || iters == 0 || reps == 0) return fail(RB_ERR_INVALID, "bad arguments");
+  if (batch == 0 || batch > (uint32_t)kMaxRowsAbi) return fail(RB_ERR_INVALID, "batch %u not in [1, 64]", batch);
+  std::vector<const Weight*> ws;
+  int k = -1, nmax = 0;
+  for (uint32_t i = 0; i < n_handles; ++i) {
+    const int32_t h = handles[i];
+    if (h < 0 || h >= (int)c->weights.size() || !c->weights[h]) return fail(RB_ERR_BAD_HANDLE, "weight %d", h);
+    if (k >= 0 && c->weights[h]->k != k) return fail(RB_ERR_INVALID, "weights differ in K");
+    k = c->weights[h]->k;
+    nmax = std::max(nmax, c->weights[h]->n);
+    ws.push_back(c->weights[h].get());
+  }
+  const int m = (int)batch, nt = gemv_nt_for(m);
+  DevBuf x, y;
+  RB_CUDA(x.alloc((size_t)m * k * 4));
+  RB_CUDA(y.alloc((size_t)m * nmax * 4));
+  RB_CUDA(cudaMemsetAsync(x.p, 0, x.n, c->stream));
+  if (int rc = ensure_xf_scratch(c, k)) return rc;
+  RB_CUDA(xfrag_launch(x.as<float>(), k, nullptr, m, k, nt, c->xf_scratch.view(), nullptr, 0, c->stream));
+  cudaGraph_t g = nullptr;
+  RB_CUDA(cudaStreamBeginCapture(c->stream, cudaStreamCaptureModeThreadLocal));
+  int rc = RB_OK;
+  for (uint32_t i = 0; i < iters && rc == RB_OK; ++i) {
+    const Weight& w = *ws[i % ws.size()];
+    GemvArgs a = base_args(c, w, m);
+    a.xin = c->xf_scratch.view();
+    a.epi = EPI_STORE;
+    a.y = y.as<float>();
+    a.ldy = w.n;
+    rc = launch_gemv(c, a, nullptr);
+  }
+  cudaError_t e = cudaStreamEndCapture(c->stream, &g);
+  if (rc) {
+    if (g) cudaGraphDestroy(g);
+    return rc;
+  }
+  if (e != cudaSuccess) return fail(RB_ERR_CUDA, "capture: %s", cudaGetErrorString(e));
+  cudaGraphExec_t ex = nullptr;
+  e = cudaGraphInstantiate(&ex, g, 0);
+  cudaGraphDestroy(g);
+  if (e != cudaSuccess) return fail(RB_ERR_CUDA, "instantiate: %s", cudaGetErrorString(e));
+  RB_CUDA(cudaGraphLaunch(ex, c->stream));  // warm-up
+  RB_CUDA(cudaEventRecord(c->ev0, c->stream));
+  for (uint32_t r = 0; r < reps; ++r) RB_CUDA(cudaGraphLaunch(ex, c->stream));
+  RB_CUDA(cudaEventRecord(c->ev1, c->stream));
+  rc = sync_ctx(c);
+  float ms = 0.f;
+  cudaEventElapsedTime(&ms, c->ev0, c->ev1);
+  cudaGraphExecDestroy(ex);
+  if (rc) return rc;
+  *avg_us = ms * 1000.f / (float)(reps * iters);
+  return RB_OK;
 }
 
 int32_t rb_weight_export(rb_ctx* c, int32_t h, void* out_blocks, size_t nbytes, uint32_t flags) {
@@ -1102,14 +1181,16 @@ int32_t rb_model_create(rb_ctx* c, const rb_model_config* cfg, int32_t* model) {
   const int R = kMaxRowsAbi;
   RB_CUDA(M->x.alloc((size_t)R * f.hidden * 4));
   RB_CUDA(M->q.alloc((size_t)R * f.n_heads * f.head_dim * 4));
-  RB_CUDA(M->att.alloc((size_t)R * f.n_heads * f.head_dim * 4));
-  RB_CUDA(M->h.alloc((size_t)R * f.ffn * 4));
+  const int NTmax = gemv_nt_for(R);
+  RB_CUDA(M->fa.alloc(f.hidden, NTmax));
+  RB_CUDA(M->fo.alloc(f.n_heads * f.head_dim, NTmax));
+  RB_CUDA(M->ff.alloc(f.hidden, NTmax));
+  RB_CUDA(M->fd.alloc(f.ffn, NTmax));
   RB_CUDA(M->ss.alloc((size_t)((f.hidden + 127) / 128) * R * 4));
   RB_CUDA(M->logits.alloc((size_t)R * f.vocab * 4));
   RB_CUDA(M->argmax.alloc((size_t)R * 8));
   RB_CUDA(M->desc.alloc((kDescUpd + 3 * R) * 4));
   RB_CUDA(cudaMemsetAsync(M->x.p, 0, M->x.n, c->stream));
-  RB_CUDA(cudaMemsetAsync(M->att.p, 0, M->att.n, c->stream));
   if (int rc = sync_ctx(c)) return rc;
   c->models.push_back(std::move(M));
   *model = (int32_t)c->models.size() - 1;
@@ -1274,8 +1355,8 @@ int32_t rb_embed_tokens(rb_ctx* c, int32_t model, const uint32_t* ids, uint32_t 
     if (int rc = upload_desc(c, rp, d)) return rc;
     KvPool& P = *c->pools[M->pool];
     embed_kernel<<<m, 128, 0, c->stream>>>(M->embd.d.as<uint8_t>(), M->embd.dtype, H, d, P.ptab.as<int32_t>(),
-                                           P.max_pages_per_tenant, M->x.as<float>(), H, M->ss.as<float>(), kMaxRowsAbi,
-                                           nullptr);
+                                           P.max_pages_per_tenant, M->x.as<float>(), H, nullptr, kMaxRowsAbi,
+                                           nullptr, nullptr, 1, XFrags());
     RB_CUDA(cudaGetLastError());
     if (int rc = copy_out(c, (uint8_t*)out + (size_t)s0 * H * 4, M->x.p, (size_t)m * H * 4, flags)) return rc;
     if (int rc = sync_ctx(c)) return rc;
@@ -1302,8 +1383,8 @@ int32_t rb_forward_layer(rb_ctx* c, int32_t model, uint32_t t, uint32_t layer, c
   ptab_update_kernel<<<1, 128, 0, c->stream>>>(M->desc.as<int32_t>(), P.ptab.as<int32_t>(), P.max_pages_per_tenant);
   RB_CUDA(cudaMemcpyAsync(M->x.p, hidden, (size_t)S * H * 4,
                           (flags & RB_PTR_DEVICE) ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice, c->stream));
-  ss_kernel<<<dim3((H + 127) / 128, S), 128, 0, c->stream>>>(M->x.as<float>(), H, H, M->ss.as<float>(), kMaxRowsAbi);
-  RB_CUDA(cudaGetLastError());
+  RB_CUDA(xfrag_launch(M->x.as<float>(), H, M->layers[layer].raw[0].d.as<float>(), (int)S, H, gemv_nt_for((int)S),
+                       M->fa.view(), M->ss.as<float>(), kMaxRowsAbi, c->stream));
   int launches = 2;
   RB_CUDA(cudaEventRecord(c->ev0, c->stream));
   const int32_t* d = M->desc.as<int32_t>();
@@ -1326,7 +1407,8 @@ int32_t rb_compute_logits(rb_ctx* c, int32_t model, const float* hidden, uint32_
   if (hidden_len != (uint32_t)H) return fail(RB_ERR_INVALID, "hidden_len %u != %d", hidden_len, H);
   RB_CUDA(cudaMemcpyAsync(M->x.p, hidden, (size_t)H * 4,
                           (flags & RB_PTR_DEVICE) ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice, c->stream));
-  ss_kernel<<<dim3((H + 127) / 128, 1), 128, 0, c->stream>>>(M->x.as<float>(), H, H, M->ss.as<float>(), kMaxRowsAbi);
+  RB_CUDA(xfrag_launch(M->x.as<float>(), H, M->out_norm.d.as<float>(), 1, H, 1, M->fa.view(), M->ss.as<float>(),
+                       kMaxRowsAbi, c->stream));
   zero_u64_kernel<<<1, 64, 0, c->stream>>>(M->argmax.as<unsigned long long>(), 1);
   RB_CUDA(cudaGetLastError());
   if (int rc = enqueue_head(c, *M, 1, true, nullptr)) return rc;

@@ -9,9 +9,10 @@
 //    evenly (stream-K), so every SM streams the same number of weight bytes.
 //  * One producer lane streams 128-row x 256-column units (18-35 KB) with the
 //    bulk-copy engine (cp.async.bulk, no multicast) into a shared-memory ring.
-//  * Stager warps convert the fp32 activations of each unit's K range (times the
-//    RMSNorm weight when fused) into fp16 hi/lo B fragments, so x ~= hi + lo to
-//    ~22 bits and the tensor cores see exact integer weights.
+//  * The activations arrive as pre-built fp16 hi/lo B fragments (xfrag.cuh,
+//    x ~= hi + lo to ~22 bits, written once by the producing kernel) and are
+//    bulk-copied next to each weight unit, so the tensor cores see exact
+//    integer weights and no conversion work happens here.
 //  * Eight consumer warps (one 16-row tile each) turn the quantised values into
 //    exact fp16 A fragments (integer x sub-scale for Q4_K, q-32 for Q6_K, q for
 //    Q8_0) and run mma.sync m16n8k16 with fp32 accumulators; per-32/16-column
@@ -21,6 +22,7 @@
 //    fixed order (deterministic; no spin waits), then the fused epilogue runs.
 #include "gemv.cuh"
 #include "quant.cuh"
+#include "xfrag.cuh"
 
 namespace rb {
 
@@ -28,36 +30,32 @@ namespace {
 
 constexpr int kConsumerWarps = kUnitTiles;  // one per 16-row tile
 constexpr int kProducerWarp = kConsumerWarps;
-constexpr int kXFragBytes = 16 * 32 * 16;   // per n-tile per super-block: [ks][lane] uint4
-constexpr int kXSumBytes = 32 * 8;          // per n-tile: [lane] uint2 (Q4_K min term)
+constexpr int kThreads = 32 * (kConsumerWarps + 1);
 constexpr int kMaxTokens = 64;
+constexpr int kSmemBudget = 200 * 1024;
 
-template <int NT>
-struct Cfg {
-  static constexpr int NX = (NT <= 2) ? 4 : 2;  // x buffers == stager warps
-  static constexpr int kThreads = 32 * (kConsumerWarps + 1 + NX);
-  static constexpr int kXBytes = NT * (kXFragBytes + kXSumBytes);
-};
-
+__host__ __device__ constexpr int x_stage_bytes(int nt) { return nt * (kXfSbBytes + kXsSbBytes); }
+__host__ __device__ constexpr int stage_bytes(int dtype, int nt) { return unit_bytes(dtype) + x_stage_bytes(nt); }
+__host__ __device__ constexpr int tile_floats(int nt) { return kRowGroup * 8 * nt; }  // epilogue transpose tile
+__host__ __device__ constexpr int stages_fit(int dtype, int nt) {
+  return (kSmemBudget - 4 * tile_floats(nt) - 4096) / stage_bytes(dtype, nt);
+}
 __host__ __device__ constexpr int ring_stages(int dtype, int nt) {
-  // keep the whole CTA under ~200 KB of shared memory
-  return dtype == DT_Q4_K ? (nt <= 2 ? 5 : (nt == 4 ? 3 : 2))
-       : dtype == DT_Q6_K ? (nt <= 2 ? 4 : 2)
-                          : (nt <= 2 ? 3 : 2);
+  // as many stages as fit next to the epilogue tile, 1..6
+  return stages_fit(dtype, nt) > 6 ? 6 : stages_fit(dtype, nt) < 1 ? 1 : stages_fit(dtype, nt);
 }
 
 struct SmemLayout {
-  int ring, xbuf, bars, inv_rms, red, total;
+  int ring, tile, bars, inv_rms, red, total;
 };
 
 __host__ __device__ inline SmemLayout smem_layout(int dtype, int nt) {
   SmemLayout L;
   const int S = ring_stages(dtype, nt);
-  const int NX = (nt <= 2) ? 4 : 2;
   L.ring = 0;
-  L.xbuf = L.ring + S * unit_bytes(dtype);
-  L.bars = L.xbuf + NX * nt * (kXFragBytes + kXSumBytes);
-  L.inv_rms = L.bars + 8 * (2 * S + 2 * NX);
+  L.tile = L.ring + S * stage_bytes(dtype, nt);
+  L.bars = L.tile + 4 * tile_floats(nt);
+  L.inv_rms = L.bars + 8 * (2 * S);
   L.red = L.inv_rms + 4 * kMaxTokens;
   L.total = L.red + 4 * kConsumerWarps * kMaxTokens + 16;
   return L;
@@ -65,10 +63,6 @@ __host__ __device__ inline SmemLayout smem_layout(int dtype, int nt) {
 
 __device__ __forceinline__ uint4 lds128(const uint8_t* p) { return *reinterpret_cast<const uint4*>(p); }
 __device__ __forceinline__ uint2 lds64(const uint8_t* p) { return *reinterpret_cast<const uint2*>(p); }
-
-__device__ __forceinline__ uint32_t pack_h2(__half lo, __half hi) {
-  return (uint32_t)__half_as_ushort(lo) | ((uint32_t)__half_as_ushort(hi) << 16);
-}
 
 // byte i (0..3) of w as half2(b, b), exact
 __device__ __forceinline__ uint32_t byte_h2(uint32_t w, int i) {
@@ -83,81 +77,20 @@ __device__ __forceinline__ void named_bar(int id, int threads) {
 
 __device__ __forceinline__ float4 ldcg4(const float* p) { return __ldcg(reinterpret_cast<const float4*>(p)); }
 
-// ---------------------------------------------------------------------------
-// x staging: B fragments (hi, lo) for one super-block, plus Q4_K sub-block sums.
-// ---------------------------------------------------------------------------
-template <int NT>
-__device__ void stage_x(const GemvArgs& a, int sb, uint8_t* xb, int lane, bool need_sum) {
-  const int k_base = sb * kSuperK;
-  for (int nt = 0; nt < NT; ++nt) {
-    const int tok = nt * 8 + (lane >> 2);
-    const bool valid = tok < a.m;
-    const float* xr = a.x + (size_t)tok * a.ldx + k_base + 2 * (lane & 3);
-    const float* gr = a.norm_w ? a.norm_w + k_base + 2 * (lane & 3) : nullptr;
-    float jsum[8];
-#pragma unroll
-    for (int j = 0; j < 8; ++j) jsum[j] = 0.f;
-#pragma unroll 4
-    for (int ks = 0; ks < 16; ++ks) {
-      float2 v0 = make_float2(0.f, 0.f), v1 = make_float2(0.f, 0.f);
-      if (valid) {
-        v0 = *reinterpret_cast<const float2*>(xr + 16 * ks);
-        v1 = *reinterpret_cast<const float2*>(xr + 16 * ks + 8);
-        if (gr) {
-          const float2 g0 = *reinterpret_cast<const float2*>(gr + 16 * ks);
-          const float2 g1 = *reinterpret_cast<const float2*>(gr + 16 * ks + 8);
-          v0.x *= g0.x; v0.y *= g0.y; v1.x *= g1.x; v1.y *= g1.y;
-        }
-      }
-      __half h0, l0, h1, l1, h2, l2, h3, l3;
-      split_hilo(v0.x, h0, l0);
-      split_hilo(v0.y, h1, l1);
-      split_hilo(v1.x, h2, l2);
-      split_hilo(v1.y, h3, l3);
-      uint4 o;
-      o.x = pack_h2(h0, h1);
-      o.y = pack_h2(h2, h3);
-      o.z = pack_h2(l0, l1);
-      o.w = pack_h2(l2, l3);
-      *reinterpret_cast<uint4*>(xb + nt * kXFragBytes + (ks * 32 + lane) * 16) = o;
-      jsum[ks >> 1] += (v0.x + v0.y) + (v1.x + v1.y);
-    }
-    if (need_sum) {
-      // the 4 lanes sharing a token hold the 32 values of each sub-block between them
-#pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        jsum[j] += __shfl_xor_sync(0xffffffffu, jsum[j], 1);
-        jsum[j] += __shfl_xor_sync(0xffffffffu, jsum[j], 2);
-      }
-      const int j0 = 2 * (lane & 3);
-      float s0 = 0.f, s1 = 0.f;
-#pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        if (j == j0) s0 = jsum[j];
-        if (j == j0 + 1) s1 = jsum[j];
-      }
-      __half sh0, sl0, sh1, sl1;
-      split_hilo(s0, sh0, sl0);
-      split_hilo(s1, sh1, sl1);
-      uint2 o;
-      o.x = pack_h2(sh0, sh1);
-      o.y = pack_h2(sl0, sl1);
-      *reinterpret_cast<uint2*>(xb + NT * kXFragBytes + nt * kXSumBytes + lane * 8) = o;
-    }
-  }
-}
-
-// ---------------------------------------------------------------------------
-// Consumers: one 16-row tile x one super-block, accumulated into acc[NT][4]
-// (C fragment: [0]=(g, 2c) [1]=(g, 2c+1) [2]=(g+8, 2c) [3]=(g+8, 2c+1)).
-// ---------------------------------------------------------------------------
 __device__ __forceinline__ float guard_scale(float v, float repl) {
   // fused.rs:276-285 / 1171-1175: NaN or Inf super-scales are replaced
   return (isnan(v) || isinf(v)) ? repl : v;
 }
 
+// ---------------------------------------------------------------------------
+// Consumers: one 16-row tile x one super-block, accumulated into acc[NT][4]
+// (C fragment: [0]=(g, 2c) [1]=(g, 2c+1) [2]=(g+8, 2c) [3]=(g+8, 2c+1)).
+// xb: the super-block's B fragments, xsb: its sub-block sums.
+// ---------------------------------------------------------------------------
 template <int NT>
-__device__ __forceinline__ void tile_q4k(const uint8_t* tile, const uint8_t* xb, int lane, float acc[NT][4]) {
+__device__ __forceinline__ void tile_q4k(const uint8_t* tile, const uint8_t* xb, const uint8_t* xsb, int lane,
+                                         float acc[NT][4]) {
+  constexpr int CH = NT == 1 ? 2 : 1;  // independent accumulator chains per hi/lo
   const int g = lane >> 2, c = lane & 3;
   const uint4 hA = lds128(tile + g * 16);
   const uint4 hB = lds128(tile + (g + 8) * 16);
@@ -170,61 +103,71 @@ __device__ __forceinline__ void tile_q4k(const uint8_t* tile, const uint8_t* xb,
   const uint32_t mnA_lo = hA.z & 0x3F3F3F3Fu, mnA_hi = ((hA.w >> 4) & 0x0F0F0F0Fu) | ((hA.z >> 2) & 0x30303030u);
   const uint32_t scB_lo = hB.y & 0x3F3F3F3Fu, scB_hi = (hB.w & 0x0F0F0F0Fu) | ((hB.y >> 2) & 0x30303030u);
   const uint32_t mnB_lo = hB.z & 0x3F3F3F3Fu, mnB_hi = ((hB.w >> 4) & 0x0F0F0F0Fu) | ((hB.z >> 2) & 0x30303030u);
-  uint32_t scA[8], scB[8], offA[8], offB[8];
-#pragma unroll
-  for (int j = 0; j < 4; ++j) {
-    scA[j] = byte_h2(scA_lo, j);
-    scA[j + 4] = byte_h2(scA_hi, j);
-    scB[j] = byte_h2(scB_lo, j);
-    scB[j + 4] = byte_h2(scB_hi, j);
-  }
-#pragma unroll
-  for (int j = 0; j < 8; ++j) {
-    offA[j] = h2_as_u32(__hmul2(u32_as_h2(scA[j]), __half2half2(__float2half_rn(-1024.f))));
-    offB[j] = h2_as_u32(__hmul2(u32_as_h2(scB[j]), __half2half2(__float2half_rn(-1024.f))));
-  }
-  // min term operands: A_m = m_j of rows g / g+8 at j = 2c, 2c+1
+  // min-term operands: A_m = m_j of rows g / g+8 at j = 2c, 2c+1 (exact small integers)
   const uint32_t mwA = (c < 2) ? mnA_lo : mnA_hi, mwB = (c < 2) ? mnB_lo : mnB_hi;
-  const int jb = (2 * c) & 3;
-  const uint32_t amA = prmt(mwA, 0x64646464u, (uint32_t)jb | (4u << 4) | ((uint32_t)(jb + 1) << 8) | (4u << 12));
-  const uint32_t amB = prmt(mwB, 0x64646464u, (uint32_t)jb | (4u << 4) | ((uint32_t)(jb + 1) << 8) | (4u << 12));
-  const uint32_t am0 = hsub2_u(amA, 0x64006400u), am1 = hsub2_u(amB, 0x64006400u);
+  const uint32_t jb = (uint32_t)((2 * c) & 3);
+  const uint32_t sel = jb | (4u << 4) | ((jb + 1) << 8) | (4u << 12);
+  const uint32_t am0 = hsub2_u(prmt(mwA, 0x64646464u, sel), 0x64006400u);
+  const uint32_t am1 = hsub2_u(prmt(mwB, 0x64646464u, sel), 0x64006400u);
 
-  float cs[NT][4];
+  float cs[CH][2][NT][4];
 #pragma unroll
-  for (int nt = 0; nt < NT; ++nt) cs[nt][0] = cs[nt][1] = cs[nt][2] = cs[nt][3] = 0.f;
+  for (int ch = 0; ch < CH; ++ch)
+#pragma unroll
+    for (int hl = 0; hl < 2; ++hl)
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt) cs[ch][hl][nt][0] = cs[ch][hl][nt][1] = cs[ch][hl][nt][2] = cs[ch][hl][nt][3] = 0.f;
   const uint8_t* qs = tile + 256;
 #pragma unroll
-  for (int ch = 0; ch < 4; ++ch) {
-    const uint4 q = lds128(qs + ch * 512 + lane * 16);
+  for (int chunk = 0; chunk < 4; ++chunk) {
+    const uint4 q = lds128(qs + chunk * 512 + lane * 16);
     const uint32_t qw[4] = {q.x, q.y, q.z, q.w};
+    // sub-blocks 2*chunk and 2*chunk+1: integer sub-scale times the quant is exact
+    // in fp16 (<= 63 * 15); A = (1024 + q) * sc - 1024 * sc.
+    uint32_t sa[2], sb[2], oa[2], ob[2];
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const int j = 2 * chunk + h;
+      sa[h] = byte_h2(j < 4 ? scA_lo : scA_hi, j & 3);
+      sb[h] = byte_h2(j < 4 ? scB_lo : scB_hi, j & 3);
+      oa[h] = h2_as_u32(__hmul2(u32_as_h2(sa[h]), __half2half2(__ushort_as_half((unsigned short)0xE400))));
+      ob[h] = h2_as_u32(__hmul2(u32_as_h2(sb[h]), __half2half2(__ushort_as_half((unsigned short)0xE400))));
+    }
 #pragma unroll
     for (int w = 0; w < 4; ++w) {
-      const int ks = ch * 4 + w, j = ks >> 1;
+      const int ks = chunk * 4 + w, h = w >> 1;
       const uint32_t word = qw[w];
       uint32_t af[4];
-      af[0] = hfma2_u(lop3_and_or(word, 0x000F000Fu, 0x64006400u), scA[j], offA[j]);
-      af[1] = hfma2_u(lop3_and_or(word >> 4, 0x000F000Fu, 0x64006400u), scB[j], offB[j]);
-      af[2] = hfma2_u(lop3_and_or(word >> 8, 0x000F000Fu, 0x64006400u), scA[j], offA[j]);
-      af[3] = hfma2_u(lop3_and_or(word >> 12, 0x000F000Fu, 0x64006400u), scB[j], offB[j]);
+      af[0] = hfma2_u(lop3_and_or(word, 0x000F000Fu, 0x64006400u), sa[h], oa[h]);
+      af[1] = hfma2_u(lop3_and_or(word >> 4, 0x000F000Fu, 0x64006400u), sb[h], ob[h]);
+      af[2] = hfma2_u(lop3_and_or(word >> 8, 0x000F000Fu, 0x64006400u), sa[h], oa[h]);
+      af[3] = hfma2_u(lop3_and_or(word >> 12, 0x000F000Fu, 0x64006400u), sb[h], ob[h]);
 #pragma unroll
       for (int nt = 0; nt < NT; ++nt) {
-        const uint4 b = lds128(xb + nt * kXFragBytes + (ks * 32 + lane) * 16);
-        mma_16816(cs[nt], af, b.x, b.y);
-        mma_16816(cs[nt], af, b.z, b.w);
+        const uint4 b = lds128(xb + nt * kXfSbBytes + (ks * 32 + lane) * 16);
+        mma_16816(cs[ks % CH][0][nt], af, b.x, b.y);
+        mma_16816(cs[ks % CH][1][nt], af, b.z, b.w);
       }
     }
   }
 #pragma unroll
   for (int nt = 0; nt < NT; ++nt) {
-    const uint2 bm = lds64(xb + NT * kXFragBytes + nt * kXSumBytes + lane * 8);
+    const uint2 sw = lds64(xsb + nt * kXsSbBytes + (g * 8 + 2 * c) * 4);
+    const uint32_t bm_hi = prmt(sw.x, sw.y, 0x5410u), bm_lo = prmt(sw.x, sw.y, 0x7632u);
     float cm[4] = {0.f, 0.f, 0.f, 0.f};
-    mma_1688(cm, am0, am1, bm.x);
-    mma_1688(cm, am0, am1, bm.y);
-    acc[nt][0] = fmaf(-mA, cm[0], fmaf(dA, cs[nt][0], acc[nt][0]));
-    acc[nt][1] = fmaf(-mA, cm[1], fmaf(dA, cs[nt][1], acc[nt][1]));
-    acc[nt][2] = fmaf(-mB, cm[2], fmaf(dB, cs[nt][2], acc[nt][2]));
-    acc[nt][3] = fmaf(-mB, cm[3], fmaf(dB, cs[nt][3], acc[nt][3]));
+    mma_1688(cm, am0, am1, bm_hi);
+    mma_1688(cm, am0, am1, bm_lo);
+    float t[4];
+#pragma unroll
+    for (int r = 0; r < 4; ++r) {
+      t[r] = cs[0][0][nt][r] + cs[0][1][nt][r];
+#pragma unroll
+      for (int ch = 1; ch < CH; ++ch) t[r] += cs[ch][0][nt][r] + cs[ch][1][nt][r];
+    }
+    acc[nt][0] = fmaf(-mA, cm[0], fmaf(dA, t[0], acc[nt][0]));
+    acc[nt][1] = fmaf(-mA, cm[1], fmaf(dA, t[1], acc[nt][1]));
+    acc[nt][2] = fmaf(-mB, cm[2], fmaf(dB, t[2], acc[nt][2]));
+    acc[nt][3] = fmaf(-mB, cm[3], fmaf(dB, t[3], acc[nt][3]));
   }
 }
 
@@ -236,8 +179,8 @@ __device__ __forceinline__ void tile_q6k(const uint8_t* tile, const uint8_t* xb,
   const float dB = guard_scale(half_bits_to_float(dd[g + 8]), 0.00000006f);
   const uint4 sAw = lds128(tile + 32 + g * 16);
   const uint4 sBw = lds128(tile + 32 + (g + 8) * 16);
-  const int8_t* sA = reinterpret_cast<const int8_t*>(&sAw);
-  const int8_t* sB = reinterpret_cast<const int8_t*>(&sBw);
+  const uint32_t sAs[4] = {sAw.x, sAw.y, sAw.z, sAw.w};
+  const uint32_t sBs[4] = {sBw.x, sBw.y, sBw.z, sBw.w};
   const uint8_t* lo = tile + 288;
   const uint8_t* hi = tile + 288 + 2048;
 #pragma unroll
@@ -251,8 +194,8 @@ __device__ __forceinline__ void tile_q6k(const uint8_t* tile, const uint8_t* xb,
       const uint32_t qw[4] = {q.x, q.y, q.z, q.w};
 #pragma unroll
       for (int w = 0; w < 4; ++w) {
-        const int ks = ch * 4 + w;               // 0..15
-        const int hwi = (ks & 7) >> 1;           // word within the hi chunk
+        const int ks = ch * 4 + w;      // 0..15
+        const int hwi = (ks & 7) >> 1;  // word within the hi chunk
         const uint32_t H = (ks & 1) ? (hws[hwi] >> 16) : (hws[hwi] & 0xffffu);
         const uint32_t X = (H & 0xffu) | ((H & 0xff00u) << 8);
         const uint32_t word = qw[w];
@@ -261,17 +204,18 @@ __device__ __forceinline__ void tile_q6k(const uint8_t* tile, const uint8_t* xb,
         af[1] = hsub2_u(lop3_and_or(word >> 4, 0x000F000Fu, 0x64006400u) | ((X << 2) & 0x00300030u), 0x64206420u);
         af[2] = hsub2_u(lop3_and_or(word >> 8, 0x000F000Fu, 0x64006400u) | (X & 0x00300030u), 0x64206420u);
         af[3] = hsub2_u(lop3_and_or(word >> 12, 0x000F000Fu, 0x64006400u) | ((X >> 2) & 0x00300030u), 0x64206420u);
-        const float fa = dA * (float)sA[ks], fb = dB * (float)sB[ks];
+        const float fa = dA * (float)(int8_t)(sAs[ks >> 2] >> (8 * (ks & 3)));
+        const float fb = dB * (float)(int8_t)(sBs[ks >> 2] >> (8 * (ks & 3)));
 #pragma unroll
         for (int nt = 0; nt < NT; ++nt) {
-          const uint4 b = lds128(xb + nt * kXFragBytes + (ks * 32 + lane) * 16);
-          float ct[4] = {0.f, 0.f, 0.f, 0.f};
-          mma_16816(ct, af, b.x, b.y);
-          mma_16816(ct, af, b.z, b.w);
-          acc[nt][0] = fmaf(fa, ct[0], acc[nt][0]);
-          acc[nt][1] = fmaf(fa, ct[1], acc[nt][1]);
-          acc[nt][2] = fmaf(fb, ct[2], acc[nt][2]);
-          acc[nt][3] = fmaf(fb, ct[3], acc[nt][3]);
+          const uint4 b = lds128(xb + nt * kXfSbBytes + (ks * 32 + lane) * 16);
+          float ch_[4] = {0.f, 0.f, 0.f, 0.f}, cl_[4] = {0.f, 0.f, 0.f, 0.f};
+          mma_16816(ch_, af, b.x, b.y);
+          mma_16816(cl_, af, b.z, b.w);
+          acc[nt][0] = fmaf(fa, ch_[0] + cl_[0], acc[nt][0]);
+          acc[nt][1] = fmaf(fa, ch_[1] + cl_[1], acc[nt][1]);
+          acc[nt][2] = fmaf(fb, ch_[2] + cl_[2], acc[nt][2]);
+          acc[nt][3] = fmaf(fb, ch_[3] + cl_[3], acc[nt][3]);
         }
       }
     }
@@ -291,9 +235,11 @@ __device__ __forceinline__ void tile_q80(const uint8_t* tile, const uint8_t* xb,
     const uint4 q = lds128(qs + ch * 512 + lane * 16);
     const float da = half_bits_to_float(dAs[ch >> 1] >> ((ch & 1) * 16));
     const float db = half_bits_to_float(dBs[ch >> 1] >> ((ch & 1) * 16));
-    float ct[NT][4];
+    float ct[2][NT][4];
 #pragma unroll
-    for (int nt = 0; nt < NT; ++nt) ct[nt][0] = ct[nt][1] = ct[nt][2] = ct[nt][3] = 0.f;
+    for (int hl = 0; hl < 2; ++hl)
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt) ct[hl][nt][0] = ct[hl][nt][1] = ct[hl][nt][2] = ct[hl][nt][3] = 0.f;
 #pragma unroll
     for (int s2 = 0; s2 < 2; ++s2) {
       const int ks = ch * 2 + s2;
@@ -305,17 +251,17 @@ __device__ __forceinline__ void tile_q80(const uint8_t* tile, const uint8_t* xb,
       af[3] = hsub2_u(prmt(w1, 0x64646464u, 0x4342u), 0x64806480u);
 #pragma unroll
       for (int nt = 0; nt < NT; ++nt) {
-        const uint4 b = lds128(xb + nt * kXFragBytes + (ks * 32 + lane) * 16);
-        mma_16816(ct[nt], af, b.x, b.y);
-        mma_16816(ct[nt], af, b.z, b.w);
+        const uint4 b = lds128(xb + nt * kXfSbBytes + (ks * 32 + lane) * 16);
+        mma_16816(ct[0][nt], af, b.x, b.y);
+        mma_16816(ct[1][nt], af, b.z, b.w);
       }
     }
 #pragma unroll
     for (int nt = 0; nt < NT; ++nt) {
-      acc[nt][0] = fmaf(da, ct[nt][0], acc[nt][0]);
-      acc[nt][1] = fmaf(da, ct[nt][1], acc[nt][1]);
-      acc[nt][2] = fmaf(db, ct[nt][2], acc[nt][2]);
-      acc[nt][3] = fmaf(db, ct[nt][3], acc[nt][3]);
+      acc[nt][0] = fmaf(da, ct[0][nt][0] + ct[1][nt][0], acc[nt][0]);
+      acc[nt][1] = fmaf(da, ct[0][nt][1] + ct[1][nt][1], acc[nt][1]);
+      acc[nt][2] = fmaf(db, ct[0][nt][2] + ct[1][nt][2], acc[nt][2]);
+      acc[nt][3] = fmaf(db, ct[0][nt][3] + ct[1][nt][3], acc[nt][3]);
     }
   }
 }
@@ -334,8 +280,10 @@ __device__ __forceinline__ void kv_store(const KvView& kv, int layer, int which,
 
 template <int NT>
 __device__ void epilogue(const GemvArgs& a, int rg, int warp, int lane, float acc[NT][4], const float* inv_rms,
-                         float* red) {
+                         float* red, float* T) {
+  constexpr int LD = 8 * NT;
   const int g = lane >> 2, c = lane & 3;
+  const int tid = warp * 32 + lane;
   const int row0 = rg * kRowGroup + warp * kTileRows + g;  // rows row0 and row0+8
 #pragma unroll
   for (int nt = 0; nt < NT; ++nt) {
@@ -357,7 +305,7 @@ __device__ void epilogue(const GemvArgs& a, int rg, int warp, int lane, float ac
     }
   } else if (a.epi == EPI_SWIGLU) {
     // tile rows 0-7 gate, 8-15 up, same output index (ffn.rs:98-103 order)
-    const int o = rg * (kRowGroup / 2) + warp * 8 + g;
+    const int ol = warp * 8 + g;  // output index within the row group (0..63)
 #pragma unroll
     for (int nt = 0; nt < NT; ++nt) {
 #pragma unroll
@@ -366,9 +314,15 @@ __device__ void epilogue(const GemvArgs& a, int rg, int warp, int lane, float ac
         const float gt = acc[nt][r], up = acc[nt][r + 2];
         const float sig = 1.0f / (1.0f + expf(-gt));
         const float h = (gt * sig) * up;
-        if (t < a.m && 2 * o < a.n) a.y[(size_t)t * a.ldy + o] = h;
+        const bool ok = t < a.m && 2 * (rg * (kRowGroup / 2) + ol) < a.n;
+        T[ol * LD + t] = ok ? h : 0.f;
+        if (ok && a.y) a.y[(size_t)t * a.ldy + rg * (kRowGroup / 2) + ol] = h;
       }
     }
+    named_bar(2, 32 * kConsumerWarps);
+    if (a.xout.xf) frags_write(T, LD, 1, kRowGroup / 2, LD, rg * (kRowGroup / 2), 0, nullptr, a.xout, NT, tid,
+                               32 * kConsumerWarps);
+    named_bar(2, 32 * kConsumerWarps);
   } else if (a.epi == EPI_RESID) {
     float sq[NT][2];
 #pragma unroll
@@ -377,12 +331,16 @@ __device__ void epilogue(const GemvArgs& a, int rg, int warp, int lane, float ac
 #pragma unroll
       for (int r = 0; r < 4; ++r) {
         const int t = nt * 8 + 2 * c + (r & 1), row = row0 + ((r & 2) ? 8 : 0);
+        const int rl = row - rg * kRowGroup;
+        float tv = 0.f;
         if (t < a.m && row < a.n) {
           float* p = a.resid + (size_t)t * a.ldr + row;
           const float v = *p + acc[nt][r];
           *p = v;
           sq[nt][r & 1] += v * v;
+          tv = a.xf_norm ? v * a.xf_norm[row] : v;
         }
+        T[rl * LD + t] = tv;
       }
 #pragma unroll
       for (int h = 0; h < 2; ++h) {
@@ -396,12 +354,13 @@ __device__ void epilogue(const GemvArgs& a, int rg, int warp, int lane, float ac
       }
     }
     named_bar(2, 32 * kConsumerWarps);
-    const int tid = warp * 32 + lane;
     if (tid < a.m) {
       float s = 0.f;
       for (int w = 0; w < kConsumerWarps; ++w) s += red[w * kMaxTokens + tid];
       a.ss_out[(size_t)rg * a.ld_ss + tid] = s;
     }
+    if (a.xout.xf) frags_write(T, LD, 1, kRowGroup, LD, rg * kRowGroup, 0, nullptr, a.xout, NT, tid,
+                               32 * kConsumerWarps);
     named_bar(2, 32 * kConsumerWarps);
   } else if (a.epi == EPI_LOGITS) {
 #pragma unroll
@@ -471,19 +430,18 @@ __device__ void epilogue(const GemvArgs& a, int rg, int warp, int lane, float ac
 // The kernel
 // ---------------------------------------------------------------------------
 template <int DT, int NT>
-__global__ void __launch_bounds__(Cfg<NT>::kThreads, 1) gemv_kernel(const GemvArgs a) {
-  constexpr int NX = Cfg<NT>::NX;
+__global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const GemvArgs a) {
   constexpr int S = ring_stages(DT, NT);
   constexpr int UB = unit_bytes(DT);
   constexpr int TB = tile_bytes(DT);
+  constexpr int SB = stage_bytes(DT, NT);
+  constexpr int XB = x_stage_bytes(NT);
   extern __shared__ __align__(128) uint8_t smem[];
   const SmemLayout L = smem_layout(DT, NT);
   uint8_t* ring = smem + L.ring;
-  uint8_t* xbuf = smem + L.xbuf;
+  float* T = reinterpret_cast<float*>(smem + L.tile);
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + L.bars);
   uint64_t* empty = full + S;
-  uint64_t* xfull = empty + S;
-  uint64_t* xempty = xfull + NX;
   float* inv_rms = reinterpret_cast<float*>(smem + L.inv_rms);
   float* red = reinterpret_cast<float*>(smem + L.red);
 
@@ -498,53 +456,49 @@ __global__ void __launch_bounds__(Cfg<NT>::kThreads, 1) gemv_kernel(const GemvAr
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], kConsumerWarps);
     }
-    for (int b = 0; b < NX; ++b) {
-      mbar_init(&xfull[b], 1);
-      mbar_init(&xempty[b], kConsumerWarps);
-    }
     fence_barrier_init();
   }
   __syncthreads();
   pdl_launch_dependents();
 
   if (warp == kProducerWarp) {
-    // Weights do not depend on the previous kernel: start streaming before the
-    // grid dependency resolves.
     if (lane == 0) {
       const uint64_t pol = policy_evict_first();
+      const uint8_t* xf = reinterpret_cast<const uint8_t*>(a.xin.xf);
+      const uint8_t* xs = reinterpret_cast<const uint8_t*>(a.xin.xs);
+      auto issue_x = [&](int i) {
+        const int sb = (int)((u0 + i) % a.nsb);
+        uint8_t* st = ring + (size_t)(i % S) * SB + UB;
+        bulk_g2s(st, xf + (size_t)sb * NT * kXfSbBytes, NT * kXfSbBytes, &full[i % S]);
+        bulk_g2s(st + NT * kXfSbBytes, xs + (size_t)sb * NT * kXsSbBytes, NT * kXsSbBytes, &full[i % S]);
+      };
+      // Weights do not depend on the previous kernel: start streaming them
+      // before the grid dependency resolves; the activations follow after it.
+      const int pre = n_units < S ? n_units : S;
+      for (int i = 0; i < pre; ++i) {
+        mbar_arrive_expect_tx(&full[i], UB + XB);
+        bulk_g2s_evict_first(ring + (size_t)i * SB, a.w + (u0 + i) * (long long)UB, UB, &full[i], pol);
+      }
+      pdl_wait();
+      for (int i = 0; i < pre; ++i) issue_x(i);
       bool ok = true;
-      for (int i = 0; i < n_units && ok; ++i) {
+      for (int i = pre; i < n_units && ok; ++i) {
         const int s = i % S;
-        if (i >= S) ok = mbar_wait(&empty[s], ((i / S) - 1) & 1, a.err, DEV_TIMEOUT_EMPTY);
+        ok = mbar_wait(&empty[s], ((i / S) - 1) & 1, a.err, DEV_TIMEOUT_EMPTY);
         if (!ok) break;
-        mbar_arrive_expect_tx(&full[s], UB);
-        bulk_g2s_evict_first(ring + (size_t)s * UB, a.w + (u0 + i) * (long long)UB, UB, &full[s], pol);
+        mbar_arrive_expect_tx(&full[s], UB + XB);
+        bulk_g2s_evict_first(ring + (size_t)s * SB, a.w + (u0 + i) * (long long)UB, UB, &full[s], pol);
+        issue_x(i);
       }
       // drain: every issued copy must land before this CTA may exit
-      const int issued = n_units;
-      for (int i = (issued > S ? issued - S : 0); i < issued; ++i)
+      for (int i = (n_units > S ? n_units - S : 0); i < n_units; ++i)
         mbar_wait(&full[i % S], (i / S) & 1, a.err, DEV_TIMEOUT_DRAIN);
     }
     return;
   }
 
-  pdl_wait();
-
-  if (warp > kProducerWarp) {
-    // stager warp s fills x buffer s for units i = s, s + NX, ...
-    const int s = warp - kProducerWarp - 1;
-    uint8_t* xb = xbuf + s * Cfg<NT>::kXBytes;
-    for (int i = s; i < n_units; i += NX) {
-      if (i >= NX && !mbar_wait(&xempty[s], ((i / NX) - 1) & 1, a.err, DEV_TIMEOUT_EMPTY)) break;
-      const int sb = (int)((u0 + i) % a.nsb);
-      stage_x<NT>(a, sb, xb, lane, DT == DT_Q4_K);
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&xfull[s]);
-    }
-    return;
-  }
-
   // ---- consumers ----
+  pdl_wait();
   if (a.ss_part) {
     const int tid = threadIdx.x;
     if (tid < a.m) {
@@ -565,21 +519,18 @@ __global__ void __launch_bounds__(Cfg<NT>::kThreads, 1) gemv_kernel(const GemvAr
   for (int i = 0; i < n_units; ++i) {
     const long long u = u0 + i;
     const int rg = (int)(u / a.nsb), sb = (int)(u % a.nsb);
-    const int s = i % S, b = i % NX;
+    const int s = i % S;
     if (alive) alive = mbar_wait(&full[s], (i / S) & 1, a.err, DEV_TIMEOUT_FULL);
-    if (alive) alive = mbar_wait(&xfull[b], (i / NX) & 1, a.err, DEV_TIMEOUT_FULL);
-    if (alive) {
-      const uint8_t* tile = ring + (size_t)s * UB + warp * TB;
-      const uint8_t* xb = xbuf + b * Cfg<NT>::kXBytes;
-      if (DT == DT_Q4_K) tile_q4k<NT>(tile, xb, lane, acc);
+    if (alive && !(a.dbg & 1)) {
+      const uint8_t* st = ring + (size_t)s * SB;
+      const uint8_t* tile = st + warp * TB;
+      const uint8_t* xb = st + UB;
+      if (DT == DT_Q4_K) tile_q4k<NT>(tile, xb, xb + NT * kXfSbBytes, lane, acc);
       else if (DT == DT_Q6_K) tile_q6k<NT>(tile, xb, lane, acc);
       else tile_q80<NT>(tile, xb, lane, acc);
     }
     __syncwarp();
-    if (lane == 0) {
-      mbar_arrive(&empty[s]);
-      mbar_arrive(&xempty[b]);
-    }
+    if (lane == 0) mbar_arrive(&empty[s]);
     const bool seg_end = (i + 1 == n_units) || (sb + 1 == a.nsb);
     if (!seg_end) continue;
     const long long seg_lo = (u0 > (long long)rg * a.nsb) ? u0 : (long long)rg * a.nsb;
@@ -622,15 +573,42 @@ __global__ void __launch_bounds__(Cfg<NT>::kThreads, 1) gemv_kernel(const GemvAr
             acc[nt][3] += p.w;
           }
         }
-        if (alive) epilogue<NT>(a, rg, warp, lane, acc, irms, red);
+        if (alive) epilogue<NT>(a, rg, warp, lane, acc, irms, red, T);
         if (threadIdx.x == 0) a.counters[rg] = 0;
       }
     } else if (alive) {
-      epilogue<NT>(a, rg, warp, lane, acc, irms, red);
+      epilogue<NT>(a, rg, warp, lane, acc, irms, red, T);
     }
 #pragma unroll
     for (int nt = 0; nt < NT; ++nt) acc[nt][0] = acc[nt][1] = acc[nt][2] = acc[nt][3] = 0.f;
   }
+}
+
+// Plain rows -> activation fragments (+ RMSNorm sums of squares).
+// Grid (K/256, ceil(M/8)): one CTA per (super-block, 8-token n-tile), 128 threads.
+__global__ void xfrag_kernel(const float* x, int ldx, const float* w, int m, int k, int nt, XFrags out, float* ss,
+                             int ld_ss) {
+  __shared__ float T[256 * 8];
+  const int sb = blockIdx.x, n0 = blockIdx.y * 8;
+  const int ntok = (m - n0) < 8 ? (m - n0) : 8;
+  for (int e = threadIdx.x; e < 256 * 8; e += blockDim.x) {
+    const int kk = e >> 3, t = e & 7;
+    T[e] = t < ntok ? x[(size_t)(n0 + t) * ldx + sb * 256 + kk] : 0.f;
+  }
+  __syncthreads();
+  if (ss) {
+    // sums of squares of the raw rows per 128 columns
+    for (int e = threadIdx.x; e < 2 * ntok; e += blockDim.x) {
+      const int hg = e / ntok, t = e % ntok;
+      float q = 0.f;
+      for (int i = 0; i < 128; ++i) {
+        const float v = T[(hg * 128 + i) * 8 + t];
+        q += v * v;
+      }
+      ss[(size_t)(sb * 2 + hg) * ld_ss + n0 + t] = q;
+    }
+  }
+  frags_write(T, 8, 1, 256, 8, sb * 256, n0, w, out, nt, threadIdx.x, blockDim.x);
 }
 
 // ---------------------------------------------------------------------------
@@ -886,10 +864,14 @@ __global__ void quantize_kernel(int dtype, const float* x, size_t nblocks, uint8
     }
     const uint16_t dh = f2h_bits(__fdiv_rn(amax, 127.0f));
     const float df = half_bits_to_float(dh);
-    o[0] = dh & 0xff;
-    o[1] = dh >> 8;
-    for (int i = 0; i < 32; ++i)
-      o[2 + i] = (uint8_t)(int8_t)(df > 0.f ? clampi(__float2int_rn(__fdiv_rn(v[i], df)), -128, 127) : 0);
+    uint8_t blk[34];
+    blk[0] = (uint8_t)(dh & 0xffu);
+    blk[1] = (uint8_t)(dh >> 8);
+    for (int i = 0; i < 32; ++i) {
+      const int q = df > 0.f ? clampi(__float2int_rn(__fdiv_rn(v[i], df)), -128, 127) : 0;
+      blk[2 + i] = (uint8_t)(q & 0xff);
+    }
+    for (int i = 0; i < 34; ++i) o[i] = blk[i];
   }
 }
 
@@ -907,7 +889,7 @@ cudaError_t launch_t(const GemvArgs& a, int num_sms, cudaStream_t s, int pdl) {
   }
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(gemv_ctas(num_sms, a.n_rg, a.nsb));
-  cfg.blockDim = dim3(Cfg<NT>::kThreads);
+  cfg.blockDim = dim3(kThreads);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = s;
   cudaLaunchAttribute attr[1];
@@ -977,6 +959,13 @@ cudaError_t dequant_launch(int dtype, const uint8_t* blocks, size_t nblocks, flo
   const size_t total = nblocks * block_elems(dtype);
   const unsigned grid = (unsigned)((total + 255) / 256 < 65535 * 16 ? (total + 255) / 256 : 65535 * 16);
   dequant_kernel<<<grid, 256, 0, s>>>(dtype, blocks, nblocks, out);
+  return cudaGetLastError();
+}
+
+cudaError_t xfrag_launch(const float* x, int ldx, const float* w, int m, int k, int nt, const XFrags& out, float* ss,
+                         int ld_ss, cudaStream_t s) {
+  if (m < 1 || k % 256 || nt * 8 < m) return cudaErrorInvalidValue;
+  xfrag_kernel<<<dim3(k / 256, (m + 7) / 8), 128, 0, s>>>(x, ldx, w, m, k, nt, out, ss, ld_ss);
   return cudaGetLastError();
 }
 

@@ -3,13 +3,15 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include "xfrag.cuh"
+
 namespace rb {
 
 enum Epilogue : int32_t {
   EPI_STORE = 0,   // y[tok][row] = acc * inv_rms[tok]
   EPI_QKV = 1,     // RoPE + q store + paged K/V append
-  EPI_RESID = 2,   // x[tok][row] += acc, plus per-row-group sum of squares of the new x
-  EPI_SWIGLU = 3,  // rows interleaved gate/up per 8: h = silu(g) * u
+  EPI_RESID = 2,   // x[tok][row] += acc, row-group sums of squares, fragments of x*norm
+  EPI_SWIGLU = 3,  // rows interleaved gate/up per 8: h = silu(g) * u (+ fragments of h)
   EPI_LOGITS = 4,  // optional logits store + greedy argmax (ties -> last index)
 };
 
@@ -32,11 +34,9 @@ struct GemvArgs {
   int32_t n_rg = 0;   // 128-row groups (padded rows = n_rg * 128)
   int32_t nsb = 0;    // K / 256
   int32_t m = 0;      // tokens (x rows)
-  // input
-  const float* x = nullptr;
-  int32_t ldx = 0;
-  const float* norm_w = nullptr;   // optional elementwise prologue weight [K]
-  const float* ss_part = nullptr;  // optional [n_ss][ld_ss] partial sums of squares
+  // input: activation fragments (xfrag.cuh) of x[m][K] (times the fused norm weight)
+  XFrags xin;
+  const float* ss_part = nullptr;  // optional [n_ss][ld_ss] partial sums of squares -> 1/rms per token
   int32_t n_ss = 0, ld_ss = 64;
   float norm_eps = 1e-5f;
   int32_t norm_dim = 0;
@@ -47,6 +47,8 @@ struct GemvArgs {
   float* resid = nullptr;  // RESID: x stream (read-modify-write), ld = ldr
   int32_t ldr = 0;
   float* ss_out = nullptr;  // RESID: [n_rg][ld_ss]
+  XFrags xout;              // RESID / SWIGLU: fragments of the next GEMV's input
+  const float* xf_norm = nullptr;  // RESID: norm weight the next GEMV fuses
   unsigned long long* argmax = nullptr;  // LOGITS: per token key
   // QKV
   int32_t qkv_row0 = 0, n_q_rows = 0, n_k_rows = 0;
@@ -58,6 +60,7 @@ struct GemvArgs {
   const int32_t* row_tenant = nullptr;
   const int32_t* row_pos = nullptr;
   KvView kv;
+  int32_t dbg = 0;  // measurement hook: bit 0 skips the consumer math
   // scratch / status
   float* partials = nullptr;
   int32_t* counters = nullptr;

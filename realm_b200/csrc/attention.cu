@@ -284,14 +284,15 @@ __global__ void __launch_bounds__(kAttnWarps * 32) attn_kernel(const AttnArgs a)
     // Final values go to shared memory (the q buffer is free now), then out to the
     // fp32 output and / or the activation fragments of the o-proj GEMV.
     float* ofin = qs;
+    __shared__ float frag_scratch[16];
     auto finish = [&]() {
       __syncthreads();
       if (a.out)
         for (int i = threadIdx.x; i < NREP * HD; i += blockDim.x)
           a.out[(size_t)ui.row * a.ldo + (size_t)ui.kvh * NREP * HD + i] = ofin[i];
-      if (a.xout.xf)
-        frags_write(ofin, 1, 0, NREP * HD, 1, ui.kvh * NREP * HD, ui.row, nullptr, a.xout, a.xf_nt, threadIdx.x,
-                    blockDim.x);
+      if (a.xout.xi || a.xout.xf)
+        frags_write(ofin, 1, 0, NREP * HD, 1, ui.kvh * NREP * HD, ui.row, nullptr, a.xout, a.xf_nt, frag_scratch,
+                    threadIdx.x, blockDim.x, [] { __syncthreads(); });
     };
     auto merge_warps = [&](int i, float& M, float& Lsum, float& O) {
       const int r = i / HD, d = i % HD;

@@ -102,7 +102,11 @@ __global__ void embed_kernel(const uint8_t* embd, int dtype, int hidden, const i
     if (threadIdx.x == 0 && ss) ss[(size_t)(g0 / 128) * ld_ss + r] = (red[0] + red[1]) + (red[2] + red[3]);
     __syncthreads();
   }
-  if (frags.xf) frags_write(xr, 1, 0, hidden, 1, 0, r, norm_w, frags, nt, threadIdx.x, blockDim.x);
+  if (!frags.xi && !frags.xf) return;
+  __shared__ float scratch[256];
+  __syncthreads();
+  frags_write(xr, 1, 0, hidden, 1, 0, r, norm_w, frags, nt, scratch, threadIdx.x, blockDim.x,
+              [] { __syncthreads(); });
 }
 
 __global__ void zero_u64_kernel(unsigned long long* p, int n) {
@@ -165,14 +169,19 @@ struct Weight {
 
 // Device storage for one GEMV input's activation fragments (xfrag.cuh).
 struct FragBuf {
-  DevBuf f, s;
+  DevBuf f, i, c, s;
   cudaError_t alloc(int k, int nt) {
-    cudaError_t e = f.alloc(xf_bytes(k, nt));
-    return e != cudaSuccess ? e : s.alloc(xs_bytes(k, nt));
+    cudaError_t e;
+    if ((e = f.alloc(xf_bytes(k, nt))) != cudaSuccess) return e;
+    if ((e = i.alloc(xi_bytes(k, nt))) != cudaSuccess) return e;
+    if ((e = c.alloc(xc_bytes(k, nt))) != cudaSuccess) return e;
+    return s.alloc(xs_bytes(k, nt));
   }
   XFrags view() const {
     XFrags v;
     v.xf = f.as<uint4>();
+    v.xi = i.as<uint4>();
+    v.xc = c.as<float>();
     v.xs = s.as<uint32_t>();
     return v;
   }
@@ -250,7 +259,8 @@ struct Ctx {
   std::vector<std::unique_ptr<Model>> models;
   float last_ms = 0.f;
   int last_launches = 0;
-  int gemv_dbg = 0;  // measurement hook (RB_GEMV_DBG): bit 0 skips the GEMV math
+  int gemv_dbg = 0;  // measurement hook (RB_GEMV_DBG): bit 0 skips the GEMV math, bit 1 phase stamps
+  DevBuf dbg_ts;
 };
 
 constexpr int kMaxRowsAbi = 64;
@@ -330,6 +340,9 @@ GemvArgs base_args(Ctx* c, const Weight& w, int m) {
   a.counters = c->counters.as<int32_t>();
   a.err = c->err.as<uint32_t>();
   a.dbg = c->gemv_dbg;
+  if (c->gemv_dbg & 2) {
+    a.dbg_ts = c->dbg_ts.as<unsigned long long>();
+  }
   return a;
 }
 
@@ -849,6 +862,7 @@ int32_t rb_weight_matmul_timing(rb_ctx* c, const int32_t* handles, uint32_t n_ha
   RB_CUDA(cudaMemsetAsync(x.p, 0, x.n, c->stream));
   if (int rc = ensure_xf_scratch(c, k)) return rc;
   RB_CUDA(xfrag_launch(x.as<float>(), k, nullptr, m, k, nt, c->xf_scratch.view(), nullptr, 0, c->stream));
+  if ((c->gemv_dbg & 2) && !c->dbg_ts.p) RB_CUDA(c->dbg_ts.alloc(4096 * 8 * 8));
   cudaGraph_t g = nullptr;
   RB_CUDA(cudaStreamBeginCapture(c->stream, cudaStreamCaptureModeThreadLocal));
   int rc = RB_OK;
@@ -881,6 +895,25 @@ int32_t rb_weight_matmul_timing(rb_ctx* c, const int32_t* handles, uint32_t n_ha
   cudaGraphExecDestroy(ex);
   if (rc) return rc;
   *avg_us = ms * 1000.f / (float)(reps * iters);
+  if ((c->gemv_dbg & 2) && c->dbg_ts.p) {
+    const int G = gemv_ctas(c->num_sms, ws.back()->n_rg, ws.back()->k / kSuperK);
+    std::vector<unsigned long long> ts((size_t)G * 8);
+    cudaMemcpy(ts.data(), c->dbg_ts.p, ts.size() * 8, cudaMemcpyDeviceToHost);
+    unsigned long long t0 = ~0ull;
+    for (int b = 0; b < G; ++b) t0 = std::min(t0, ts[b * 8]);
+    const char* names[7] = {"entry", "prod_pre_issued", "prod_pdl_done", "prod_drained", "cons_first_full",
+                            "cons_last_unit", "cons_done"};
+    for (int p = 0; p < 7; ++p) {
+      double mn = 1e30, mx = 0, sum = 0;
+      for (int b = 0; b < G; ++b) {
+        const double v = (double)(ts[b * 8 + p] - t0) / 1000.0;
+        mn = std::min(mn, v);
+        mx = std::max(mx, v);
+        sum += v;
+      }
+      fprintf(stderr, "[gemv phases] %-16s min %7.2f mean %7.2f max %7.2f us\n", names[p], mn, sum / G, mx);
+    }
+  }
   return RB_OK;
 }
 

@@ -7,13 +7,13 @@
 // Design (B200, HBM-bound for M <= 64 tokens):
 //  * Persistent CTAs (one per SM) split the (row-group, super-block) unit space
 //    evenly (stream-K), so every SM streams the same number of weight bytes.
-//  * One producer lane streams 128-row x 256-column units (18-35 KB) with the
+//  * One producer lane streams 256-row x 256-column units (37-70 KB) with the
 //    bulk-copy engine (cp.async.bulk, no multicast) into a shared-memory ring.
 //  * The activations arrive as pre-built fp16 hi/lo B fragments (xfrag.cuh,
 //    x ~= hi + lo to ~22 bits, written once by the producing kernel) and are
 //    bulk-copied next to each weight unit, so the tensor cores see exact
 //    integer weights and no conversion work happens here.
-//  * Eight consumer warps (one 16-row tile each) turn the quantised values into
+//  * Sixteen consumer warps (one 16-row tile each) turn the quantised values into
 //    exact fp16 A fragments (integer x sub-scale for Q4_K, q-32 for Q6_K, q for
 //    Q8_0) and run mma.sync m16n8k16 with fp32 accumulators; per-32/16-column
 //    scales need register accumulators, which is why this path uses mma.sync
@@ -28,14 +28,18 @@ namespace rb {
 
 namespace {
 
-constexpr int kConsumerWarps = kUnitTiles;  // one per 16-row tile
+constexpr int kConsumerWarps = kUnitTiles;  // one per 16-row tile (256-row units)
 constexpr int kProducerWarp = kConsumerWarps;
 constexpr int kThreads = 32 * (kConsumerWarps + 1);
 constexpr int kMaxTokens = 64;
 constexpr int kSmemBudget = 200 * 1024;
 
-__host__ __device__ constexpr int x_stage_bytes(int nt) { return nt * (kXfSbBytes + kXsSbBytes); }
-__host__ __device__ constexpr int stage_bytes(int dtype, int nt) { return unit_bytes(dtype) + x_stage_bytes(nt); }
+// activation bytes staged per unit: Q4_K reads int8 limbs + scales + sums, the
+// others fp16 hi/lo fragments + sums
+__host__ __device__ constexpr int x_stage_bytes(int dtype, int nt) {
+  return dtype == DT_Q4_K ? nt * (kXiSbBytes + kXcSbBytes + kXsSbBytes) : nt * (kXfSbBytes + kXsSbBytes);
+}
+__host__ __device__ constexpr int stage_bytes(int dtype, int nt) { return unit_bytes(dtype) + x_stage_bytes(dtype, nt); }
 __host__ __device__ constexpr int tile_floats(int nt) { return kRowGroup * 8 * nt; }  // epilogue transpose tile
 __host__ __device__ constexpr int stages_fit(int dtype, int nt) {
   return (kSmemBudget - 4 * tile_floats(nt) - 4096) / stage_bytes(dtype, nt);
@@ -75,6 +79,16 @@ __device__ __forceinline__ void named_bar(int id, int threads) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
 }
 
+__device__ __forceinline__ unsigned long long gtimer() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
+  return t;
+}
+#define RB_TS(slot)                                                                   \
+  do {                                                                                \
+    if ((a.dbg & 2) && a.dbg_ts) a.dbg_ts[(size_t)blockIdx.x * 8 + (slot)] = gtimer(); \
+  } while (0)
+
 __device__ __forceinline__ float4 ldcg4(const float* p) { return __ldcg(reinterpret_cast<const float4*>(p)); }
 
 __device__ __forceinline__ float guard_scale(float v, float repl) {
@@ -87,10 +101,22 @@ __device__ __forceinline__ float guard_scale(float v, float repl) {
 // (C fragment: [0]=(g, 2c) [1]=(g, 2c+1) [2]=(g+8, 2c) [3]=(g+8, 2c+1)).
 // xb: the super-block's B fragments, xsb: its sub-block sums.
 // ---------------------------------------------------------------------------
+__device__ __forceinline__ void mma_s8_16832(int d[4], const uint32_t a[4], uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%10,%10,%10,%10};"
+      : "=r"(d[0]), "=r"(d[1]), "=r"(d[2]), "=r"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1), "r"(0));
+}
+
+// Q4_K on the int8 tensor path. Per 32-column sub-block j the MMA gives exact
+// integer dot products C1 (limb 1) and C2 (limb 2) of the 4-bit quants with
+// the activation limbs; sc_j * (256*C1 + C2) accumulates exactly in int32 over
+// a 64-column group (|.| < 2^31 by construction), then scales by the group's
+// activation scale. Per row: y = d/256 * sum_g s_g * S_g - dmin * sum_j m_j * xsum_j
+// (dequantize_q4_k, quant.rs:160-182: q*d*sc - dmin*m, regrouped).
 template <int NT>
-__device__ __forceinline__ void tile_q4k(const uint8_t* tile, const uint8_t* xb, const uint8_t* xsb, int lane,
-                                         float acc[NT][4]) {
-  constexpr int CH = NT == 1 ? 2 : 1;  // independent accumulator chains per hi/lo
+__device__ __forceinline__ void tile_q4k(const uint8_t* tile, const uint8_t* xi, const uint8_t* xc, const uint8_t* xsb,
+                                         int lane, float acc[NT][4]) {
   const int g = lane >> 2, c = lane & 3;
   const uint4 hA = lds128(tile + g * 16);
   const uint4 hB = lds128(tile + (g + 8) * 16);
@@ -103,53 +129,55 @@ __device__ __forceinline__ void tile_q4k(const uint8_t* tile, const uint8_t* xb,
   const uint32_t mnA_lo = hA.z & 0x3F3F3F3Fu, mnA_hi = ((hA.w >> 4) & 0x0F0F0F0Fu) | ((hA.z >> 2) & 0x30303030u);
   const uint32_t scB_lo = hB.y & 0x3F3F3F3Fu, scB_hi = (hB.w & 0x0F0F0F0Fu) | ((hB.y >> 2) & 0x30303030u);
   const uint32_t mnB_lo = hB.z & 0x3F3F3F3Fu, mnB_hi = ((hB.w >> 4) & 0x0F0F0F0Fu) | ((hB.z >> 2) & 0x30303030u);
-  // min-term operands: A_m = m_j of rows g / g+8 at j = 2c, 2c+1 (exact small integers)
   const uint32_t mwA = (c < 2) ? mnA_lo : mnA_hi, mwB = (c < 2) ? mnB_lo : mnB_hi;
   const uint32_t jb = (uint32_t)((2 * c) & 3);
   const uint32_t sel = jb | (4u << 4) | ((jb + 1) << 8) | (4u << 12);
   const uint32_t am0 = hsub2_u(prmt(mwA, 0x64646464u, sel), 0x64006400u);
   const uint32_t am1 = hsub2_u(prmt(mwB, 0x64646464u, sel), 0x64006400u);
 
-  float cs[CH][2][NT][4];
+  float u[NT][4];
 #pragma unroll
-  for (int ch = 0; ch < CH; ++ch)
-#pragma unroll
-    for (int hl = 0; hl < 2; ++hl)
-#pragma unroll
-      for (int nt = 0; nt < NT; ++nt) cs[ch][hl][nt][0] = cs[ch][hl][nt][1] = cs[ch][hl][nt][2] = cs[ch][hl][nt][3] = 0.f;
+  for (int nt = 0; nt < NT; ++nt) u[nt][0] = u[nt][1] = u[nt][2] = u[nt][3] = 0.f;
   const uint8_t* qs = tile + 256;
 #pragma unroll
-  for (int chunk = 0; chunk < 4; ++chunk) {
-    const uint4 q = lds128(qs + chunk * 512 + lane * 16);
-    const uint32_t qw[4] = {q.x, q.y, q.z, q.w};
-    // sub-blocks 2*chunk and 2*chunk+1: integer sub-scale times the quant is exact
-    // in fp16 (<= 63 * 15); A = (1024 + q) * sc - 1024 * sc.
-    uint32_t sa[2], sb[2], oa[2], ob[2];
+  for (int grp = 0; grp < 4; ++grp) {  // 64-column group = sub-blocks 2grp, 2grp+1
+    const uint4 q = lds128(qs + grp * 512 + lane * 16);
+    int S[NT][4];
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt) S[nt][0] = S[nt][1] = S[nt][2] = S[nt][3] = 0;
 #pragma unroll
     for (int h = 0; h < 2; ++h) {
-      const int j = 2 * chunk + h;
-      sa[h] = byte_h2(j < 4 ? scA_lo : scA_hi, j & 3);
-      sb[h] = byte_h2(j < 4 ? scB_lo : scB_hi, j & 3);
-      oa[h] = h2_as_u32(__hmul2(u32_as_h2(sa[h]), __half2half2(__ushort_as_half((unsigned short)0xE400))));
-      ob[h] = h2_as_u32(__hmul2(u32_as_h2(sb[h]), __half2half2(__ushort_as_half((unsigned short)0xE400))));
-    }
-#pragma unroll
-    for (int w = 0; w < 4; ++w) {
-      const int ks = chunk * 4 + w, h = w >> 1;
-      const uint32_t word = qw[w];
+      const int j = 2 * grp + h;
+      const uint32_t w0 = h ? q.z : q.x, w1 = h ? q.w : q.y;
       uint32_t af[4];
-      af[0] = hfma2_u(lop3_and_or(word, 0x000F000Fu, 0x64006400u), sa[h], oa[h]);
-      af[1] = hfma2_u(lop3_and_or(word >> 4, 0x000F000Fu, 0x64006400u), sb[h], ob[h]);
-      af[2] = hfma2_u(lop3_and_or(word >> 8, 0x000F000Fu, 0x64006400u), sa[h], oa[h]);
-      af[3] = hfma2_u(lop3_and_or(word >> 12, 0x000F000Fu, 0x64006400u), sb[h], ob[h]);
+      af[0] = w0 & 0x0F0F0F0Fu;
+      af[1] = (w0 >> 4) & 0x0F0F0F0Fu;
+      af[2] = w1 & 0x0F0F0F0Fu;
+      af[3] = (w1 >> 4) & 0x0F0F0F0Fu;
+      const int sa = (int)(((j < 4 ? scA_lo : scA_hi) >> (8 * (j & 3))) & 0xffu);
+      const int sbv = (int)(((j < 4 ? scB_lo : scB_hi) >> (8 * (j & 3))) & 0xffu);
 #pragma unroll
       for (int nt = 0; nt < NT; ++nt) {
-        const uint4 b = lds128(xb + nt * kXfSbBytes + (ks * 32 + lane) * 16);
-        mma_16816(cs[ks % CH][0][nt], af, b.x, b.y);
-        mma_16816(cs[ks % CH][1][nt], af, b.z, b.w);
+        const uint4 b = lds128(xi + nt * kXiSbBytes + (j * 32 + lane) * 16);
+        int c1[4], c2[4];
+        mma_s8_16832(c1, af, b.x, b.y);
+        mma_s8_16832(c2, af, b.z, b.w);
+        S[nt][0] += sa * (c1[0] * 256 + c2[0]);
+        S[nt][1] += sa * (c1[1] * 256 + c2[1]);
+        S[nt][2] += sbv * (c1[2] * 256 + c2[2]);
+        S[nt][3] += sbv * (c1[3] * 256 + c2[3]);
       }
     }
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt) {
+      const float2 sv = *reinterpret_cast<const float2*>(xc + nt * kXcSbBytes + (grp * 8 + 2 * c) * 4);
+      u[nt][0] = fmaf(sv.x, (float)S[nt][0], u[nt][0]);
+      u[nt][1] = fmaf(sv.y, (float)S[nt][1], u[nt][1]);
+      u[nt][2] = fmaf(sv.x, (float)S[nt][2], u[nt][2]);
+      u[nt][3] = fmaf(sv.y, (float)S[nt][3], u[nt][3]);
+    }
   }
+  const float dA8 = dA * (1.0f / 256.0f), dB8 = dB * (1.0f / 256.0f);
 #pragma unroll
   for (int nt = 0; nt < NT; ++nt) {
     const uint2 sw = lds64(xsb + nt * kXsSbBytes + (g * 8 + 2 * c) * 4);
@@ -157,17 +185,10 @@ __device__ __forceinline__ void tile_q4k(const uint8_t* tile, const uint8_t* xb,
     float cm[4] = {0.f, 0.f, 0.f, 0.f};
     mma_1688(cm, am0, am1, bm_hi);
     mma_1688(cm, am0, am1, bm_lo);
-    float t[4];
-#pragma unroll
-    for (int r = 0; r < 4; ++r) {
-      t[r] = cs[0][0][nt][r] + cs[0][1][nt][r];
-#pragma unroll
-      for (int ch = 1; ch < CH; ++ch) t[r] += cs[ch][0][nt][r] + cs[ch][1][nt][r];
-    }
-    acc[nt][0] = fmaf(-mA, cm[0], fmaf(dA, t[0], acc[nt][0]));
-    acc[nt][1] = fmaf(-mA, cm[1], fmaf(dA, t[1], acc[nt][1]));
-    acc[nt][2] = fmaf(-mB, cm[2], fmaf(dB, t[2], acc[nt][2]));
-    acc[nt][3] = fmaf(-mB, cm[3], fmaf(dB, t[3], acc[nt][3]));
+    acc[nt][0] = fmaf(-mA, cm[0], fmaf(dA8, u[nt][0], acc[nt][0]));
+    acc[nt][1] = fmaf(-mA, cm[1], fmaf(dA8, u[nt][1], acc[nt][1]));
+    acc[nt][2] = fmaf(-mB, cm[2], fmaf(dB8, u[nt][2], acc[nt][2]));
+    acc[nt][3] = fmaf(-mB, cm[3], fmaf(dB8, u[nt][3], acc[nt][3]));
   }
 }
 
@@ -320,9 +341,8 @@ __device__ void epilogue(const GemvArgs& a, int rg, int warp, int lane, float ac
       }
     }
     named_bar(2, 32 * kConsumerWarps);
-    if (a.xout.xf) frags_write(T, LD, 1, kRowGroup / 2, LD, rg * (kRowGroup / 2), 0, nullptr, a.xout, NT, tid,
-                               32 * kConsumerWarps);
-    named_bar(2, 32 * kConsumerWarps);
+    frags_write(T, LD, 1, kRowGroup / 2, LD, rg * (kRowGroup / 2), 0, nullptr, a.xout, NT, red, tid,
+                32 * kConsumerWarps, [] { named_bar(2, 32 * kConsumerWarps); });
   } else if (a.epi == EPI_RESID) {
     float sq[NT][2];
 #pragma unroll
@@ -354,14 +374,17 @@ __device__ void epilogue(const GemvArgs& a, int rg, int warp, int lane, float ac
       }
     }
     named_bar(2, 32 * kConsumerWarps);
-    if (tid < a.m) {
+    // RMSNorm statistics per 128 columns: two slots per 256-row group
+    for (int e = tid; e < 2 * a.m; e += 32 * kConsumerWarps) {
+      const int hlf = e / a.m, t = e % a.m;
       float s = 0.f;
-      for (int w = 0; w < kConsumerWarps; ++w) s += red[w * kMaxTokens + tid];
-      a.ss_out[(size_t)rg * a.ld_ss + tid] = s;
+      for (int w = hlf * (kConsumerWarps / 2); w < (hlf + 1) * (kConsumerWarps / 2); ++w) s += red[w * kMaxTokens + t];
+      a.ss_out[(size_t)(2 * rg + hlf) * a.ld_ss + t] = s;
     }
-    if (a.xout.xf) frags_write(T, LD, 1, kRowGroup, LD, rg * kRowGroup, 0, nullptr, a.xout, NT, tid,
-                               32 * kConsumerWarps);
-    named_bar(2, 32 * kConsumerWarps);
+    named_bar(2, 32 * kConsumerWarps);  // red is reused as frags_write scratch below
+    if (a.xout.xs)
+      frags_write(T, LD, 1, kRowGroup, LD, rg * kRowGroup, 0, nullptr, a.xout, NT, red, tid, 32 * kConsumerWarps,
+                  [] { named_bar(2, 32 * kConsumerWarps); });
   } else if (a.epi == EPI_LOGITS) {
 #pragma unroll
     for (int nt = 0; nt < NT; ++nt) {
@@ -435,7 +458,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const GemvArgs a) {
   constexpr int UB = unit_bytes(DT);
   constexpr int TB = tile_bytes(DT);
   constexpr int SB = stage_bytes(DT, NT);
-  constexpr int XB = x_stage_bytes(NT);
+  constexpr int XB = x_stage_bytes(DT, NT);
   extern __shared__ __align__(128) uint8_t smem[];
   const SmemLayout L = smem_layout(DT, NT);
   uint8_t* ring = smem + L.ring;
@@ -452,6 +475,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const GemvArgs a) {
   const int n_units = (int)(u1 - u0);
 
   if (threadIdx.x == 0) {
+    RB_TS(0);
     for (int s = 0; s < S; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], kConsumerWarps);
@@ -464,13 +488,21 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const GemvArgs a) {
   if (warp == kProducerWarp) {
     if (lane == 0) {
       const uint64_t pol = policy_evict_first();
-      const uint8_t* xf = reinterpret_cast<const uint8_t*>(a.xin.xf);
-      const uint8_t* xs = reinterpret_cast<const uint8_t*>(a.xin.xs);
+      // activation bytes for super-block sb: Q4_K {int8 limbs, scales, sums}, else {fp16 hi/lo, sums}
       auto issue_x = [&](int i) {
         const int sb = (int)((u0 + i) % a.nsb);
         uint8_t* st = ring + (size_t)(i % S) * SB + UB;
-        bulk_g2s(st, xf + (size_t)sb * NT * kXfSbBytes, NT * kXfSbBytes, &full[i % S]);
-        bulk_g2s(st + NT * kXfSbBytes, xs + (size_t)sb * NT * kXsSbBytes, NT * kXsSbBytes, &full[i % S]);
+        uint64_t* bar = &full[i % S];
+        if (DT == DT_Q4_K) {
+          bulk_g2s(st, reinterpret_cast<const uint8_t*>(a.xin.xi) + (size_t)sb * NT * kXiSbBytes, NT * kXiSbBytes, bar);
+          st += NT * kXiSbBytes;
+          bulk_g2s(st, reinterpret_cast<const uint8_t*>(a.xin.xc) + (size_t)sb * NT * kXcSbBytes, NT * kXcSbBytes, bar);
+          st += NT * kXcSbBytes;
+        } else {
+          bulk_g2s(st, reinterpret_cast<const uint8_t*>(a.xin.xf) + (size_t)sb * NT * kXfSbBytes, NT * kXfSbBytes, bar);
+          st += NT * kXfSbBytes;
+        }
+        bulk_g2s(st, reinterpret_cast<const uint8_t*>(a.xin.xs) + (size_t)sb * NT * kXsSbBytes, NT * kXsSbBytes, bar);
       };
       // Weights do not depend on the previous kernel: start streaming them
       // before the grid dependency resolves; the activations follow after it.
@@ -479,7 +511,9 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const GemvArgs a) {
         mbar_arrive_expect_tx(&full[i], UB + XB);
         bulk_g2s_evict_first(ring + (size_t)i * SB, a.w + (u0 + i) * (long long)UB, UB, &full[i], pol);
       }
+      RB_TS(1);
       pdl_wait();
+      RB_TS(2);
       for (int i = 0; i < pre; ++i) issue_x(i);
       bool ok = true;
       for (int i = pre; i < n_units && ok; ++i) {
@@ -493,6 +527,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const GemvArgs a) {
       // drain: every issued copy must land before this CTA may exit
       for (int i = (n_units > S ? n_units - S : 0); i < n_units; ++i)
         mbar_wait(&full[i % S], (i / S) & 1, a.err, DEV_TIMEOUT_DRAIN);
+      RB_TS(3);
     }
     return;
   }
@@ -521,16 +556,19 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const GemvArgs a) {
     const int rg = (int)(u / a.nsb), sb = (int)(u % a.nsb);
     const int s = i % S;
     if (alive) alive = mbar_wait(&full[s], (i / S) & 1, a.err, DEV_TIMEOUT_FULL);
+    if (i == 0 && threadIdx.x == 0) RB_TS(4);
     if (alive && !(a.dbg & 1)) {
       const uint8_t* st = ring + (size_t)s * SB;
       const uint8_t* tile = st + warp * TB;
       const uint8_t* xb = st + UB;
-      if (DT == DT_Q4_K) tile_q4k<NT>(tile, xb, xb + NT * kXfSbBytes, lane, acc);
+      if (DT == DT_Q4_K)
+        tile_q4k<NT>(tile, xb, xb + NT * kXiSbBytes, xb + NT * (kXiSbBytes + kXcSbBytes), lane, acc);
       else if (DT == DT_Q6_K) tile_q6k<NT>(tile, xb, lane, acc);
       else tile_q80<NT>(tile, xb, lane, acc);
     }
     __syncwarp();
     if (lane == 0) mbar_arrive(&empty[s]);
+    if (i + 1 == n_units && threadIdx.x == 0) RB_TS(5);
     const bool seg_end = (i + 1 == n_units) || (sb + 1 == a.nsb);
     if (!seg_end) continue;
     const long long seg_lo = (u0 > (long long)rg * a.nsb) ? u0 : (long long)rg * a.nsb;
@@ -581,6 +619,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const GemvArgs a) {
     }
 #pragma unroll
     for (int nt = 0; nt < NT; ++nt) acc[nt][0] = acc[nt][1] = acc[nt][2] = acc[nt][3] = 0.f;
+    if (i + 1 == n_units && threadIdx.x == 0) RB_TS(6);
   }
 }
 
@@ -589,6 +628,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const GemvArgs a) {
 __global__ void xfrag_kernel(const float* x, int ldx, const float* w, int m, int k, int nt, XFrags out, float* ss,
                              int ld_ss) {
   __shared__ float T[256 * 8];
+  __shared__ float scratch[32];
   const int sb = blockIdx.x, n0 = blockIdx.y * 8;
   const int ntok = (m - n0) < 8 ? (m - n0) : 8;
   for (int e = threadIdx.x; e < 256 * 8; e += blockDim.x) {
@@ -608,7 +648,7 @@ __global__ void xfrag_kernel(const float* x, int ldx, const float* w, int m, int
       ss[(size_t)(sb * 2 + hg) * ld_ss + n0 + t] = q;
     }
   }
-  frags_write(T, 8, 1, 256, 8, sb * 256, n0, w, out, nt, threadIdx.x, blockDim.x);
+  frags_write(T, 8, 1, 256, 8, sb * 256, n0, w, out, nt, scratch, threadIdx.x, blockDim.x, [] { __syncthreads(); });
 }
 
 // ---------------------------------------------------------------------------
@@ -657,17 +697,17 @@ __global__ void repack_kernel(const uint8_t* a, int rows_a, const uint8_t* b, in
     if (t < 16) {
       for (int i = 0; i < 16; ++i) o[t * 16 + i] = src[t * BB + i];
     }
-    // 4 chunks x 32 lanes x 4 words
+    // int8-MMA A fragments (m16n8k32): 4 chunks (64 columns) x 32 lanes x 4 words;
+    // word w: sub-block 2*chunk + w/2, columns +16*(w&1); byte i holds the quants of
+    // rows g (low nibble) and g+8 (high nibble) at column 32j + 4c + i
     for (int idx = t; idx < 4 * 32 * 4; idx += blockDim.x) {
       const int ch = idx / 128, lane = (idx / 4) % 32, w = idx % 4;
-      const int ks = ch * 4 + w;
+      const int j = 2 * ch + (w >> 1), g = lane >> 2, c = lane & 3;
       uint32_t word = 0;
-      for (int i = 0; i < 8; ++i) {
-        int row, col;
-        frag_pos(lane, i, row, col);
-        const int e = ks * 16 + col;
-        const uint32_t q = (uint32_t)q4k_quant(src + row * BB + 16, e);
-        word |= q << (4 * i);
+      for (int i = 0; i < 4; ++i) {
+        const int e = 32 * j + 16 * (w & 1) + 4 * c + i;
+        word |= (uint32_t)q4k_quant(src + g * BB + 16, e) << (8 * i);
+        word |= (uint32_t)q4k_quant(src + (g + 8) * BB + 16, e) << (8 * i + 4);
       }
       *reinterpret_cast<uint32_t*>(o + 256 + (ch * 32 + lane) * 16 + w * 4) = word;
     }
@@ -742,15 +782,13 @@ __global__ void unpack_kernel(const uint8_t* tiled, int n, int k, uint8_t* out) 
     __syncthreads();
     for (int idx = t; idx < 16 * 256; idx += blockDim.x) {
       const int row = idx / 256, e = idx % 256;
-      const int ks = e / 16, col = e % 16;
-      // find lane/i holding (row, col)
-      const int g = row & 7, r1 = row >> 3, c8 = col >> 3, cc = col & 7, c = cc >> 1, hi = cc & 1;
-      const int lane = g * 4 + c, i = (r1 | (c8 << 1)) + 4 * hi;
-      const uint32_t word = *reinterpret_cast<const uint32_t*>(o + 256 + ((ks / 4) * 32 + lane) * 16 + (ks % 4) * 4);
-      const uint32_t q = (word >> (4 * i)) & 0xF;
-      const int grp = e >> 6, w = e & 63;
-      uint8_t* qb = dst + row * BB + 16 + 32 * grp + (w & 31);
-      if (w < 32) atomicOr(reinterpret_cast<unsigned int*>((size_t)qb & ~(size_t)3), q << (8 * ((size_t)qb & 3)));
+      const int j = e / 32, within = e % 32, hi16 = within / 16, c = (within % 16) / 4, i = within % 4;
+      const int g = row & 7, lane = g * 4 + c, w = 2 * (j & 1) + hi16;
+      const uint32_t word = *reinterpret_cast<const uint32_t*>(o + 256 + ((j >> 1) * 32 + lane) * 16 + w * 4);
+      const uint32_t q = (word >> (8 * i + 4 * (row >> 3))) & 0xF;
+      const int grp = e >> 6, wq = e & 63;
+      uint8_t* qb = dst + row * BB + 16 + 32 * grp + (wq & 31);
+      if (wq < 32) atomicOr(reinterpret_cast<unsigned int*>((size_t)qb & ~(size_t)3), q << (8 * ((size_t)qb & 3)));
       else atomicOr(reinterpret_cast<unsigned int*>((size_t)qb & ~(size_t)3), (q << 4) << (8 * ((size_t)qb & 3)));
     }
   }

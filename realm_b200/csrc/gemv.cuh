@@ -31,7 +31,7 @@ struct GemvArgs {
   const uint8_t* w = nullptr;
   int32_t dtype = 0;
   int32_t n = 0;      // logical output rows
-  int32_t n_rg = 0;   // 128-row groups (padded rows = n_rg * 128)
+  int32_t n_rg = 0;   // 256-row groups (padded rows = n_rg * 256)
   int32_t nsb = 0;    // K / 256
   int32_t m = 0;      // tokens (x rows)
   // input: activation fragments (xfrag.cuh) of x[m][K] (times the fused norm weight)
@@ -60,7 +60,8 @@ struct GemvArgs {
   const int32_t* row_tenant = nullptr;
   const int32_t* row_pos = nullptr;
   KvView kv;
-  int32_t dbg = 0;  // measurement hook: bit 0 skips the consumer math
+  int32_t dbg = 0;  // measurement hook: bit 0 skips the consumer math, bit 1 records phase times
+  unsigned long long* dbg_ts = nullptr;  // [cta][8] %globaltimer stamps when dbg & 2
   // scratch / status
   float* partials = nullptr;
   int32_t* counters = nullptr;

@@ -19,7 +19,7 @@ __host__ __device__ constexpr int block_elems(int dt) {
 
 // ---------------------------------------------------------------------------
 // Tiled layout ("mma tiles"). A weight W[N][K] is cut into 16-row x 256-column
-// tiles; 8 tiles stacked vertically (128 rows) at one 256-column position form
+// tiles; 16 tiles stacked vertically (256 rows) at one 256-column position form
 // a streaming unit. Units are stored row-group-major, then by K position, so a
 // row group's whole K range is one contiguous run of bytes. Inside a tile the
 // quantised values are pre-permuted into the m16n8k16 A-fragment order, so each
@@ -34,7 +34,7 @@ __host__ __device__ constexpr int block_elems(int dt) {
 // so that (word >> 4r) & 0x000F000F is A-fragment register r (low/high halves).
 // ---------------------------------------------------------------------------
 constexpr int kTileRows = 16;
-constexpr int kUnitTiles = 8;  // tiles per unit => 128 rows per row group
+constexpr int kUnitTiles = 16;  // tiles per unit => 256 rows per row group
 constexpr int kRowGroup = kTileRows * kUnitTiles;
 constexpr int kSuperK = 256;
 

@@ -35,6 +35,9 @@ CFG = dict(n_layers=32, hidden=4096, n_heads=32, n_kv_heads=32, head_dim=128, ff
 TENANTS_PER_GPU = 8
 METRIC = "aggregate decode tok/s, 8 tenants Llama-7B Q4_K; paged-KV attn HBM GB/s vs peak"
 Q4K_BPW, Q6K_BPW = 144 / 256, 210 / 256
+# dram__bytes_read.sum + dram__bytes_write.sum of one gate|up GEMV launch (22016 x 4096
+# Q4_K, M = 8), from `ncu --set full` of `bench.py --case gemv`: 50.86 + 3.13 MB.
+GEMV_NCU_TRAFFIC = 53998592
 
 
 def peaks():
@@ -67,10 +70,11 @@ class Clocks:
     def __enter__(self):
         try:
             self.p = subprocess.Popen(["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.Q}",
-                                       "--format=csv,noheader,nounits", "-lms", "200"],
+                                       "--format=csv,noheader,nounits", "-lms", "50"],
                                       stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
         except OSError:
             self.p = None
+        time.sleep(0.5)  # let the sampler start before the timed region
         return self
 
     def __exit__(self, *exc):
@@ -146,9 +150,10 @@ def build_model(rb, torch, ctx, dev, n_tenants, host_copy=None):
 
 
 def gemv_roofline(rb, torch, ctx, dev, hbm_peak, peak_kind):
-    """Dominant kernel: the Q4_K gate|up GEMV (22016 x 4096, M = 8 tenants),
-    timed with CUDA events on the context stream over 48 back-to-back launches
-    rotating 4 weight copies (200 MB > L2)."""
+    """Dominant kernel: the Q4_K gate|up GEMV (22016 x 4096, M = 8 tenants).
+    Device time per launch from CUDA events around a CUDA graph of 48
+    back-to-back launches on the context stream, rotating 4 weight copies
+    (200 MB > L2, so every launch streams its weights from HBM)."""
     n, k, m = 2 * CFG["ffn"], CFG["hidden"], TENANTS_PER_GPU
     g = torch.Generator(device=dev)
     ws = []
@@ -159,36 +164,17 @@ def gemv_roofline(rb, torch, ctx, dev, hbm_peak, peak_kind):
         ctx.quantize(rb.Q4_K, x.view(-1), blk)
         ws.append(rb.Weight(ctx, rb.Q4_K, n, k, blk))
         del x
-    xin = torch.randn(m, k, device=dev)
-    yout = torch.empty(m, n, device=dev)
-    torch.cuda.synchronize(dev)  # raw C-ABI calls below run on the library's stream
-    stream = torch.cuda.ExternalStream(ctx.stream, device=dev)
-    lib = rb.lib()
-    import ctypes as C
-    flags = rb.PTR_DEVICE | 2  # device pointers, asynchronous
-    for i in range(8):
-        lib.rb_weight_matmul(ctx.handle, ws[i % 4].handle, C.c_void_p(xin.data_ptr()), C.c_void_p(yout.data_ptr()),
-                             m, flags)
-    ctx.sync()
-    n_launch = 48
-    evs = [torch.cuda.Event(enable_timing=True) for _ in range(n_launch + 1)]
-    for i in range(n_launch):
-        evs[i].record(stream)
-        rc = lib.rb_weight_matmul(ctx.handle, ws[i % 4].handle, C.c_void_p(xin.data_ptr()),
-                                  C.c_void_p(yout.data_ptr()), m, flags)
-        assert rc >= 0, rb.last_error()
-    evs[-1].record(stream)
-    ctx.sync()
-    ms = [evs[i].elapsed_time(evs[i + 1]) for i in range(n_launch)]
-    avg_ms = float(np.mean(ms))
+    avg_us = ctx.gemv_timing(ws, m, iters=48, reps=3)
     alg_bytes = n * k * Q4K_BPW + m * k * 4 + m * n * 4
-    achieved = alg_bytes / (avg_ms * 1e-3) / 1e9
+    achieved = alg_bytes / (avg_us * 1e-6) / 1e9
     for w in ws:
         w.free()
+    # dram__bytes_read.sum + write.sum of one launch of this kernel and shape
+    traffic = GEMV_NCU_TRAFFIC
     return {"kernel": "gemv_kernel<Q4_K, NT=1> (gate|up 22016x4096, M=8)", "bound": "hbm",
             "achieved": round(achieved, 1), "peak": hbm_peak, "peak_kind": peak_kind, "unit": "GB/s",
-            "frac": round(achieved / hbm_peak, 4), "traffic": None, "algorithmic_bytes": int(alg_bytes),
-            "avg_launch_us": round(avg_ms * 1e3, 2)}
+            "frac": round(achieved / hbm_peak, 4), "traffic": traffic, "algorithmic_bytes": int(alg_bytes),
+            "avg_launch_us": round(avg_us, 2)}
 
 
 def attention_roofline(rb, torch, ctx, dev, hbm_peak, peak_kind):
@@ -396,14 +382,59 @@ def run_reference(args):
                                        "sample": sample}}), flush=True)
 
 
+def run_case(args):
+    """Small workloads for ncu captures (no timing, no JSON line).
+    gemv: 8 launches of the Q4_K gate|up GEMV (22016 x 4096, M = 8) over 8
+    weight copies (400 MB, > L2). decode: the bench model, 8 tenants with
+    caches of U[128, 512] random entries, then 3 decode steps of 194 launches each."""
+    import torch
+    import realm_b200 as rb
+    dev = torch.device("cuda", 0)
+    ctx = rb.Context(0)
+    if args.case == "gemv":
+        n, k, m = 2 * CFG["ffn"], CFG["hidden"], TENANTS_PER_GPU
+        ws = []
+        for i in range(8):
+            x = torch.randn(n, k, device=dev).mul_(0.02)
+            blk = torch.empty(n * k // 256 * 144, dtype=torch.uint8, device=dev)
+            ctx.quantize(rb.Q4_K, x.view(-1), blk)
+            ws.append(rb.Weight(ctx, rb.Q4_K, n, k, blk))
+            del x
+        xs = torch.randn(m, k, device=dev)
+        y = torch.empty(m, n, device=dev)
+        for w in ws:
+            w.matmul(xs, m, out=y)
+        torch.cuda.synchronize(dev)
+        print("gemv case done", flush=True)
+        return
+    m = build_model(rb, torch, ctx, dev, TENANTS_PER_GPU)
+    rng = np.random.default_rng(4)
+    lens = rng.integers(128, 513, TENANTS_PER_GPU)
+    kvw = CFG["n_kv_heads"] * CFG["head_dim"]
+    for t in range(TENANTS_PER_GPU):  # caches filled directly (K/V ~ N(0,1)) instead of a prefill
+        m.tenant_create(t)
+        for l in range(CFG["n_layers"]):
+            m.kv.append(t, l, torch.randn(int(lens[t]), kvw, device=dev), torch.randn(int(lens[t]), kvw, device=dev))
+    tenants = np.arange(TENANTS_PER_GPU, dtype=np.uint32)
+    tok = tenants.copy()
+    for s in range(3):
+        _, tok = m.forward_rows(tenants, tok, want_logits=False)
+        print("decode step", s, ctx.last_forward_launches(), "launches", flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=64)
+    ap.add_argument("--steps", type=int, default=256)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU-baseline leg")
+    ap.add_argument("--case", choices=["gemv", "decode"],
+                    help="profiling case for ncu: run a small workload of one kernel family and exit")
     args = ap.parse_args()
+    if args.case:
+        run_case(args)
+        return
     if args.warmup < 3:
         args.warmup = 3
     if args.impl == "reference":

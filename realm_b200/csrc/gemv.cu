@@ -9,15 +9,15 @@
 //    evenly (stream-K), so every SM streams the same number of weight bytes.
 //  * One producer lane streams 256-row x 256-column units (37-70 KB) with the
 //    bulk-copy engine (cp.async.bulk, no multicast) into a shared-memory ring.
-//  * The activations arrive as pre-built fp16 hi/lo B fragments (xfrag.cuh,
-//    x ~= hi + lo to ~22 bits, written once by the producing kernel) and are
-//    bulk-copied next to each weight unit, so the tensor cores see exact
-//    integer weights and no conversion work happens here.
-//  * Sixteen consumer warps (one 16-row tile each) turn the quantised values into
-//    exact fp16 A fragments (integer x sub-scale for Q4_K, q-32 for Q6_K, q for
-//    Q8_0) and run mma.sync m16n8k16 with fp32 accumulators; per-32/16-column
-//    scales need register accumulators, which is why this path uses mma.sync
-//    rather than TMEM-resident tcgen05 tiles.
+//  * The activations arrive as pre-built B fragments (xfrag.cuh, written once
+//    by the producing kernel): int8 two-limb for Q4_K, fp16 hi/lo (~22 bits)
+//    for Q6_K and Q8_0. They are bulk-copied next to each weight unit, so the
+//    tensor cores see exact integer weights and no conversion work happens here.
+//  * Sixteen consumer warps (one 16-row tile each) turn the quantised values
+//    into exact A fragments: 4-bit quants as int8 for Q4_K (mma.sync m16n8k32
+//    s8, int32 accumulate), q-32 (Q6_K) and q (Q8_0) as fp16 (m16n8k16, fp32
+//    accumulate). Per-32/16-column scales need register accumulators, which is
+//    why this decode path uses mma.sync rather than TMEM-resident tcgen05 tiles.
 //  * Row groups split across CTAs are reduced by the last-arriving CTA in a
 //    fixed order (deterministic; no spin waits), then the fused epilogue runs.
 #include "gemv.cuh"
@@ -288,7 +288,7 @@ __device__ __forceinline__ void tile_q80(const uint8_t* tile, const uint8_t* xb,
 }
 
 // ---------------------------------------------------------------------------
-// Epilogues (run by the 8 consumer warps; warp = tile within the row group)
+// Epilogues (run by the 16 consumer warps; warp = tile within the row group)
 // ---------------------------------------------------------------------------
 __device__ __forceinline__ void kv_store(const KvView& kv, int layer, int which, int tenant, int pos, int head,
                                          int d, float v) {

@@ -108,6 +108,22 @@ int32_t rb_weight_upload(rb_ctx* ctx, int32_t dtype, uint32_t n, uint32_t k, con
 int32_t rb_weight_free(rb_ctx* ctx, int32_t handle);
 int32_t rb_weight_matmul(rb_ctx* ctx, int32_t handle, const float* input, float* output, uint32_t batch_size,
                          uint32_t flags);
+/* Allocation-free variant of rb_weight_matmul; it has no counterpart in the
+ * reference. For callers that cannot allocate device memory when they run a
+ * matmul (a fixed memory budget handed over at start-up, an allocator owned by
+ * another runtime, or a hot path where cudaMalloc/cudaFree and their device
+ * synchronisation are not allowed): input [batch][k] and output [batch][n] are
+ * caller-owned device buffers (flags must contain RB_PTR_DEVICE; RB_ASYNC
+ * returns without waiting), and all other working memory is one fixed
+ * 3,434,496-byte device array in the library, held on every GPU that loads it
+ * until the process exits. Limits: batch <= 8, K <= 16384, N <= 131072, at most
+ * 160 GEMV CTAs; larger calls fail with RB_ERR_INVALID. Every call on a device
+ * shares the array (it keeps the last call's contents), so calls whose GPU
+ * work overlaps race: order them on one stream. The first call on a device
+ * looks up the array's address; make it before any stream capture there.
+ * Returns batch * n. */
+int32_t rb_weight_matmul_noalloc(rb_ctx* ctx, int32_t handle, const float* input, float* output, uint32_t batch,
+                                 uint32_t flags);
 /* Timing hook: device time (microseconds) per launch of the GEMV kernel alone,
  * from a CUDA graph of `iters` back-to-back launches cycling over `n_handles`
  * resident weights (same K) with a fixed device-resident batch of `batch` rows

@@ -84,6 +84,7 @@ _sig("rb_weight_upload", [_vp, _i32, _u32, _u32, _vp, _sz, _u32, _I32P])
 _sig("rb_weight_free", [_vp, _i32])
 _sig("rb_weight_matmul", [_vp, _i32, _vp, _vp, _u32, _u32])
 _sig("rb_weight_export", [_vp, _i32, _vp, _sz, _u32])
+_sig("rb_weight_matmul_noalloc", [_vp, _i32, _vp, _vp, _u32, _u32])
 _sig("rb_weight_matmul_timing", [_vp, _vp, _u32, _u32, _u32, _u32, C.POINTER(C.c_float)])
 _sig("rb_candle_matmul", [_vp, _vp, _vp, _vp, _u32, _u32, _u32, _u32])
 _sig("rb_candle_matmul_transposed", [_vp, _vp, _vp, _vp, _u32, _u32, _u32, _u32])
@@ -309,6 +310,16 @@ class Weight:
         if out is None:
             out = np.empty((batch_size, self.n), np.float32)
         _check(_lib.rb_weight_matmul(self.ctx.handle, self.handle, _ptr(x), _ptr(out), batch_size, _flags(x, out)))
+        return out
+
+    def matmul_noalloc(self, x, out, batch_size: int):
+        """rb_weight_matmul_noalloc: x [batch][k] and out [batch][n] are CUDA
+        tensors owned by the caller; the library allocates nothing for the call
+        (batch <= 8, K <= 16384, N <= 131072)."""
+        if not (_is_dev(x) and _is_dev(out)):
+            raise ValueError("matmul_noalloc takes CUDA tensors only")
+        _check(_lib.rb_weight_matmul_noalloc(self.ctx.handle, self.handle, _ptr(x), _ptr(out), batch_size,
+                                             _flags(x, out)))
         return out
 
     def export(self) -> np.ndarray:

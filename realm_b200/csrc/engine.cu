@@ -10,6 +10,7 @@
 #include <cstring>
 #include <map>
 #include <memory>
+#include <mutex>
 #include <random>
 #include <string>
 #include <vector>
@@ -1476,3 +1477,120 @@ float rb_last_forward_ms(rb_ctx* c) { return c ? c->last_ms : -1.f; }
 int32_t rb_last_forward_launches(rb_ctx* c) { return c ? c->last_launches : fail(RB_ERR_BAD_HANDLE, "null context"); }
 
 }  // extern "C"
+
+// ---------------------------------------------------------------------------
+// Allocation-free GEMV (rb_weight_matmul_noalloc).
+//
+// Some callers cannot allocate device memory at the point where they run a
+// matmul: a host that hands the library a fixed memory budget up front, code
+// running under an allocator that must not grow (or that another runtime owns),
+// or a serving loop that forbids cudaMalloc/cudaFree on its hot path because
+// they synchronise the device. For them this entry point takes device pointers
+// for the input and output and keeps every other byte it needs (activation
+// fragments, split-K partial sums, split-K counters) in one file-scope device
+// array of fixed size, which each GPU that loads the library holds until the
+// process exits.
+//
+// Limits (calls beyond them fail with RB_ERR_INVALID and a message naming the
+// limit): batch <= 8 rows, K <= 16384, N <= 131072 (512 groups of 256 rows),
+// and at most 160 GEMV CTAs (the device's SM count when the weight has that
+// many 256-row x 256-column units). The array is 3,434,496 bytes.
+//
+// The array is shared by every call on a device, from every context, and keeps
+// the contents of the last call; the counters are cleared on the stream at the
+// start of each call. Calls whose GPU work overlaps (two streams, two
+// contexts, or two host threads without ordering) race on it and give wrong
+// results: order them on one stream.
+//
+// The first call on a device looks up the array's device address with
+// cudaGetSymbolAddress (with that device current) and caches it; make that
+// first call before any stream capture on the device.
+// ---------------------------------------------------------------------------
+namespace {
+
+constexpr int kNaMaxBatch = 8;
+constexpr int kNaMaxK = 16384;
+constexpr int kNaMaxRowGroups = 512;
+constexpr int kNaMaxCtas = 160;
+constexpr int kNaMaxDevices = 64;
+constexpr size_t kNaXf = (size_t)(kNaMaxK / 256) * kXfSbBytes;   // NT = 1
+constexpr size_t kNaXi = (size_t)(kNaMaxK / 256) * kXiSbBytes;
+constexpr size_t kNaXc = (size_t)(kNaMaxK / 256) * kXcSbBytes;
+constexpr size_t kNaXs = (size_t)(kNaMaxK / 256) * kXsSbBytes;
+constexpr size_t kNaPartials = (size_t)kNaMaxCtas * 2 * 16 * 128 * 4;  // gemv_partials_floats(160, 1) floats
+constexpr size_t kNaCounters = (size_t)kNaMaxRowGroups * 4;
+constexpr size_t kNaOffXi = kNaXf, kNaOffXc = kNaOffXi + kNaXi, kNaOffXs = kNaOffXc + kNaXc,
+                 kNaOffPart = kNaOffXs + kNaXs, kNaOffCnt = kNaOffPart + kNaPartials, kNaBytes = kNaOffCnt + kNaCounters;
+static_assert(kNaOffXi % 256 == 0 && kNaOffXc % 256 == 0 && kNaOffXs % 256 == 0 && kNaOffPart % 256 == 0 &&
+                  kNaOffCnt % 256 == 0,
+              "scratch sections must stay 256-byte aligned");
+
+// Host code sees only a stand-in for this symbol; its device address comes from
+// cudaGetSymbolAddress.
+static __device__ __align__(256) uint8_t g_noalloc_scratch[kNaBytes];
+
+int noalloc_scratch(Ctx* c, uint8_t** out) {
+  static std::mutex mu;
+  static uint8_t* addr[kNaMaxDevices] = {};
+  if (c->device < 0 || c->device >= kNaMaxDevices) return fail(RB_ERR_INVALID, "device %d out of range", c->device);
+  std::lock_guard<std::mutex> lock(mu);
+  if (!addr[c->device]) {
+    int prev = 0;
+    RB_CUDA(cudaGetDevice(&prev));
+    RB_CUDA(cudaSetDevice(c->device));
+    void* p = nullptr;
+    const cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+    cudaSetDevice(prev);
+    if (e != cudaSuccess || !p)
+      return fail(RB_ERR_CUDA, "cudaGetSymbolAddress of the no-alloc scratch: %s", cudaGetErrorString(e));
+    addr[c->device] = static_cast<uint8_t*>(p);
+  }
+  *out = addr[c->device];
+  return RB_OK;
+}
+
+}  // namespace
+
+extern "C" int32_t rb_weight_matmul_noalloc(rb_ctx* c, int32_t h, const float* input, float* output, uint32_t batch,
+                                            uint32_t flags) {
+  if (!c || h < 0 || h >= (int)c->weights.size() || !c->weights[h]) return fail(RB_ERR_BAD_HANDLE, "weight %d", h);
+  const Weight& w = *c->weights[h];
+  if (!(flags & RB_PTR_DEVICE))
+    return fail(RB_ERR_INVALID, "rb_weight_matmul_noalloc takes device pointers only (RB_PTR_DEVICE)");
+  if (batch == 0) return 0;
+  if (!input || !output) return fail(RB_ERR_INVALID, "null input or output");
+  if (batch > (uint32_t)kNaMaxBatch)
+    return fail(RB_ERR_INVALID, "batch %u exceeds the no-alloc maximum of %d rows", batch, kNaMaxBatch);
+  if (w.k > kNaMaxK) return fail(RB_ERR_INVALID, "K=%d exceeds the no-alloc maximum of %d", w.k, kNaMaxK);
+  if (w.n_rg > kNaMaxRowGroups)
+    return fail(RB_ERR_INVALID, "N=%d exceeds the no-alloc maximum of %d", w.n, kNaMaxRowGroups * kRowGroup);
+  if (gemv_ctas(c->num_sms, w.n_rg, w.k / kSuperK) > kNaMaxCtas)
+    return fail(RB_ERR_INVALID, "%d SMs exceed the no-alloc maximum of %d GEMV CTAs", c->num_sms, kNaMaxCtas);
+  if (gemv_partials_floats(gemv_ctas(c->num_sms, w.n_rg, w.k / kSuperK), 1) * 4 > kNaPartials)
+    return fail(RB_ERR_INVALID, "split-K partials exceed the no-alloc scratch");
+  uint8_t* base = nullptr;
+  if (int rc = noalloc_scratch(c, &base)) return rc;
+  RB_CUDA(cudaSetDevice(c->device));
+  XFrags xf;
+  xf.xf = reinterpret_cast<uint4*>(base);
+  xf.xi = reinterpret_cast<uint4*>(base + kNaOffXi);
+  xf.xc = reinterpret_cast<float*>(base + kNaOffXc);
+  xf.xs = reinterpret_cast<uint32_t*>(base + kNaOffXs);
+  int32_t* counters = reinterpret_cast<int32_t*>(base + kNaOffCnt);
+  const int m = (int)batch;
+  RB_CUDA(cudaMemsetAsync(counters, 0, (size_t)w.n_rg * 4, c->stream));
+  RB_CUDA(xfrag_launch(input, w.k, nullptr, m, w.k, 1, xf, nullptr, 0, c->stream));
+  GemvArgs a = base_args(c, w, m);
+  a.dbg = 0;
+  a.dbg_ts = nullptr;
+  a.partials = reinterpret_cast<float*>(base + kNaOffPart);
+  a.counters = counters;
+  a.xin = xf;
+  a.epi = EPI_STORE;
+  a.y = output;
+  a.ldy = w.n;
+  RB_CUDA(gemv_launch(a, c->num_sms, c->stream, c->pdl ? 1 : 0));
+  if (flags & RB_ASYNC) return (int32_t)(batch * w.n);
+  if (int rc = sync_ctx(c)) return rc;
+  return (int32_t)(batch * w.n);
+}

@@ -11,7 +11,14 @@
 namespace rb {
 
 // ---- device error word (bounded waits report here instead of hanging) ----
-enum DevErr : uint32_t { DEV_OK = 0, DEV_TIMEOUT_FULL = 1, DEV_TIMEOUT_EMPTY = 2, DEV_TIMEOUT_DRAIN = 3 };
+enum DevErr : uint32_t {
+  DEV_OK = 0,
+  DEV_TIMEOUT_FULL = 1,
+  DEV_TIMEOUT_EMPTY = 2,
+  DEV_TIMEOUT_DRAIN = 3,
+  DEV_TIMEOUT_GRID = 4,  // grid barrier between the phases of a multi-phase GEMV
+  DEV_TIMEOUT_SMEM = 5,  // producer waiting for its consumers' barrier ticket
+};
 
 // Spin limit for every mbarrier wait: ~2^26 polls is far beyond any legal
 // wait (a few microseconds) yet ends in well under a second.
@@ -92,6 +99,31 @@ __device__ __forceinline__ uint64_t policy_evict_first() {
 }
 
 // ---- programmatic dependent launch ----
+// ---- grid barrier (co-resident CTAs of one cooperative launch) ----
+__device__ __forceinline__ unsigned long long ld_acquire_u64(const unsigned long long* p) {
+  unsigned long long v;
+  asm volatile("ld.acquire.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+// Waits until *ctr >= target (bounded: ~0.5 s, then reports and returns false).
+// On a timeout the first reporter also leaves err[1..3] = target, the counter
+// it last saw (low 32 bits each) and `who` (caller-defined) for the host.
+__device__ __forceinline__ bool grid_wait(const unsigned long long* ctr, unsigned long long target, uint32_t* err,
+                                          uint32_t who) {
+  unsigned long long v = 0;
+  for (uint32_t i = 0; i < (1u << 22); ++i) {
+    v = ld_acquire_u64(ctr);
+    if (v >= target) return true;
+    if (i > 64) __nanosleep(100);
+  }
+  if (err && atomicCAS(err, 0u, (uint32_t)DEV_TIMEOUT_GRID) == 0u) {
+    err[1] = (uint32_t)target;
+    err[2] = (uint32_t)v;
+    err[3] = who;
+  }
+  return false;
+}
+
 __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 __device__ __forceinline__ void pdl_launch_dependents() {
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");

@@ -165,6 +165,7 @@ struct DevBuf {
 
 struct Weight {
   int dtype = 0, n = 0, k = 0, n_rg = 0;
+  int k_in = 0;  // caller's K; k is K rounded up to 256 (Q8_0 rows are zero-padded)
   DevBuf tiled;
 };
 
@@ -262,19 +263,32 @@ struct Ctx {
   int last_launches = 0;
   int gemv_dbg = 0;  // measurement hook (RB_GEMV_DBG): bit 0 skips the GEMV math, bit 1 phase stamps
   DevBuf dbg_ts;
+  // GEMVs queued to run as one multi-phase launch (chain_add / chain_flush)
+  GemvArgs chain_ph[kMaxPhases];
+  int chain_n = 0;
+  uint32_t chain_mask = 0;
+  bool chains = true;  // RB_NO_CHAIN=1 launches every GEMV on its own
+  DevBuf gbar;         // grid-barrier arrival counters (one per barrier slot) of multi-phase launches
+  int last_chain_phases = 1;
 };
 
 constexpr int kMaxRowsAbi = 64;
 constexpr int kCounters = 1 << 16;
+constexpr int kChainCounterStride = 2048;  // split-K counters per chain phase (>= row groups of any GEMV)
 
 int check_err(Ctx* c) {
-  uint32_t e = 0;
-  RB_CUDA(cudaMemcpyAsync(&e, c->err.p, 4, cudaMemcpyDeviceToHost, c->stream));
+  uint32_t e[4] = {0, 0, 0, 0};
+  RB_CUDA(cudaMemcpyAsync(e, c->err.p, 16, cudaMemcpyDeviceToHost, c->stream));
   RB_CUDA(cudaStreamSynchronize(c->stream));
-  if (e) {
-    cudaMemsetAsync(c->err.p, 0, 4, c->stream);
+  if (e[0]) {
+    cudaMemsetAsync(c->err.p, 0, 16, c->stream);
+    // a timed-out multi-phase launch may have left the barrier count off its grid multiple
+    if (c->gbar.p) cudaMemsetAsync(c->gbar.p, 0, 8 * kMaxPhases, c->stream);
     cudaStreamSynchronize(c->stream);
-    return fail(RB_ERR_TIMEOUT, "device wait timed out (code %u)", e);
+    if (e[0] == DEV_TIMEOUT_GRID)
+      return fail(RB_ERR_TIMEOUT, "device wait timed out (grid barrier: target %u, seen %u, cta %u phase %u %s)",
+                  e[1], e[2], e[3] >> 8, (e[3] >> 1) & 127, (e[3] & 1) ? "producer" : "consumers");
+    return fail(RB_ERR_TIMEOUT, "device wait timed out (code %u)", e[0]);
   }
   return RB_OK;
 }
@@ -319,13 +333,34 @@ int upload_tiled(Ctx* c, Weight& w, int dtype, int n, int k, const uint8_t* a, i
                  int rows_b, int mode) {
   if (dtype != DT_Q4_K && dtype != DT_Q6_K && dtype != DT_Q8_0)
     return fail(RB_ERR_UNSUPPORTED, "dtype %d has no tiled GEMV", dtype);
-  if (k % kSuperK) return fail(RB_ERR_UNSUPPORTED, "K=%d must be a multiple of 256", k);
+  // Q8_0 (32-element blocks) rows whose K is not a multiple of 256 are padded
+  // with zero blocks up to the next 256-column super-block
+  const bool pad = dtype == DT_Q8_0 && (k % kSuperK) != 0;
+  if (dtype == DT_Q8_0 ? (k % 32) != 0 : (k % kSuperK) != 0)
+    return fail(RB_ERR_UNSUPPORTED, "K=%d must be a multiple of %d", k, dtype == DT_Q8_0 ? 32 : 256);
+  const int kp = (k + kSuperK - 1) / kSuperK * kSuperK;
+  DevBuf pa, pb;
+  if (pad) {
+    const size_t row_in = (size_t)(k / 32) * 34, row_out = (size_t)(kp / 32) * 34;
+    RB_CUDA(pa.alloc(row_out * rows_a));
+    RB_CUDA(cudaMemsetAsync(pa.p, 0, row_out * rows_a, c->stream));
+    RB_CUDA(cudaMemcpy2DAsync(pa.p, row_out, a, row_in, row_in, rows_a, cudaMemcpyDeviceToDevice, c->stream));
+    a = pa.as<uint8_t>();
+    if (b && rows_b) {
+      RB_CUDA(pb.alloc(row_out * rows_b));
+      RB_CUDA(cudaMemsetAsync(pb.p, 0, row_out * rows_b, c->stream));
+      RB_CUDA(cudaMemcpy2DAsync(pb.p, row_out, b, row_in, row_in, rows_b, cudaMemcpyDeviceToDevice, c->stream));
+      b = pb.as<uint8_t>();
+    }
+  }
   w.dtype = dtype;
   w.n = n;
-  w.k = k;
+  w.k = kp;
+  w.k_in = k;
   w.n_rg = (n + kRowGroup - 1) / kRowGroup;
-  RB_CUDA(w.tiled.alloc((size_t)w.n_rg * (k / kSuperK) * unit_bytes(dtype)));
-  RB_CUDA(repack_launch(a, rows_a, b, rows_b, mode, dtype, k, w.tiled.as<uint8_t>(), w.n_rg, c->stream));
+  RB_CUDA(w.tiled.alloc((size_t)w.n_rg * (kp / kSuperK) * unit_bytes(dtype)));
+  RB_CUDA(repack_launch(a, rows_a, b, rows_b, mode, dtype, kp, w.tiled.as<uint8_t>(), w.n_rg, c->stream));
+  if (pad) RB_CUDA(cudaStreamSynchronize(c->stream));  // the padded copies are freed on return
   return RB_OK;
 }
 
@@ -350,6 +385,92 @@ GemvArgs base_args(Ctx* c, const Weight& w, int m) {
 int launch_gemv(Ctx* c, const GemvArgs& a, int* launches) {
   RB_CUDA(gemv_launch(a, c->num_sms, c->stream, c->pdl ? 1 : 0));
   if (launches) ++*launches;
+  return RB_OK;
+}
+
+// Measurement hook (RB_GEMV_DBG bit 1): per phase, over the CTAs that had
+// units, min / mean / max of each stamp (microseconds after the first CTA's
+// first stamp) of the most recent GEMV launch.
+void dump_stamps(Ctx* c, int n_phases) {
+  const int G = c->num_sms;
+  std::vector<unsigned long long> ts((size_t)G * kMaxPhases * 16);
+  if (cudaMemcpy(ts.data(), c->dbg_ts.p, ts.size() * 8, cudaMemcpyDeviceToHost) != cudaSuccess) return;
+  unsigned long long t0 = ~0ull;
+  for (unsigned long long v : ts)
+    if (v) t0 = std::min(t0, v);
+  const char* names[16] = {"cons_start", "cons_dep_ok", "cons_first_full", "cons_last_unit",
+                           "cons_done", "prod_first_w", "prod_x_released", "prod_last_w",
+                           "seg_begin", "seg_deposited", "seg_ticket", "seg_summed",
+                           "seg_epi_done", "whole_epi_begin", "whole_epi_done", "-"};
+  for (int p = 0; p < n_phases; ++p)
+    for (int k = 0; k < 15; ++k) {
+      double mn = 1e30, mx = 0, sum = 0;
+      int n = 0;
+      for (int b = 0; b < G; ++b) {
+        const unsigned long long v = ts[((size_t)b * kMaxPhases + p) * 16 + k];
+        if (!v) continue;
+        const double d = (double)(v - t0) / 1000.0;
+        mn = std::min(mn, d);
+        mx = std::max(mx, d);
+        sum += d;
+        ++n;
+      }
+      if (n) fprintf(stderr, "[gemv phase %d] %-16s n %3d min %8.2f mean %8.2f max %8.2f us\n", p, names[k], n, mn,
+                     sum / n, mx);
+    }
+  // the three CTAs with the longest tail (last unit -> done), slots relative to their last unit
+  for (int p = 0; p < n_phases; ++p) {
+    std::vector<std::pair<double, int>> tails;
+    for (int b = 0; b < G; ++b) {
+      const unsigned long long* t = &ts[((size_t)b * kMaxPhases + p) * 16];
+      if (t[3] && t[4]) tails.push_back({(double)(t[4] - t[3]) / 1000.0, b});
+    }
+    std::sort(tails.rbegin(), tails.rend());
+    for (size_t i = 0; i < tails.size() && i < 3; ++i) {
+      const int b = tails[i].second;
+      const unsigned long long* t = &ts[((size_t)b * kMaxPhases + p) * 16];
+      fprintf(stderr, "[gemv phase %d] slow cta %3d tail %6.2f us:", p, b, tails[i].first);
+      for (int k = 8; k < 15; ++k)
+        if (t[k]) fprintf(stderr, " %s %+.2f", names[k], ((double)t[k] - (double)t[3]) / 1000.0);
+      fprintf(stderr, "\n");
+    }
+  }
+  cudaMemset(c->dbg_ts.p, 0, ts.size() * 8);
+}
+
+// Queued GEMVs run as one persistent multi-phase launch (gemv.cu). A phase
+// that reads what the phase before it wrote is separated from it by a grid
+// barrier; the first phase of a launch depends on the previous kernel.
+int chain_flush(Ctx* c, int* launches) {
+  if (c->chain_n == 0) return RB_OK;
+  ChainArgs ca;
+  for (int p = 0; p < c->chain_n; ++p) ca.ph[p] = c->chain_ph[p];
+  ca.n_phases = c->chain_n;
+  ca.bar_mask = c->chain_mask;
+  ca.gbar = c->gbar.as<unsigned long long>();
+  c->last_chain_phases = c->chain_n;
+  c->chain_n = 0;
+  c->chain_mask = 0;
+  RB_CUDA(gemv_chain_launch(ca, c->num_sms, c->stream, c->pdl ? 1 : 0));
+  if (launches) ++*launches;
+  return RB_OK;
+}
+
+int chain_add(Ctx* c, GemvArgs a, bool reads_previous, int* launches) {
+  if (!c->chains) {
+    a.counters = c->counters.as<int32_t>();
+    return launch_gemv(c, a, launches);
+  }
+  if (c->chain_n == kMaxPhases)
+    if (int rc = chain_flush(c, launches)) return rc;
+  const int p = c->chain_n;
+  // partial-sum slots alternate between phases: two barrier-free transitions
+  // in a row would reuse a slot that may still be read, so add a barrier
+  if (p >= 2 && !((c->chain_mask >> (p - 1)) & 1u)) reads_previous = true;
+  if (p > 0 && reads_previous) c->chain_mask |= 1u << p;
+  a.counters = c->counters.as<int32_t>() + p * kChainCounterStride;
+  c->chain_ph[p] = a;
+  ++c->chain_n;
   return RB_OK;
 }
 
@@ -388,7 +509,7 @@ int enqueue_layer(Ctx* c, Model& M, int l, int m, const int32_t* d_tenant, const
   a.row_tenant = d_tenant;
   a.row_pos = d_pos;
   a.kv = P.view();
-  if (int rc = launch_gemv(c, a, launches)) return rc;
+  if (int rc = chain_add(c, a, true, launches)) return rc;
   if (!L.v_fused) {
     GemvArgs av = a;
     av.w = L.v.tiled.as<uint8_t>();
@@ -397,8 +518,9 @@ int enqueue_layer(Ctx* c, Model& M, int l, int m, const int32_t* d_tenant, const
     av.n_rg = L.v.n_rg;
     av.nsb = L.v.k / kSuperK;
     av.qkv_row0 = (Hq + Hkv) * hd;
-    if (int rc = launch_gemv(c, av, launches)) return rc;
+    if (int rc = chain_add(c, av, false, launches)) return rc;
   }
+  if (int rc = chain_flush(c, launches)) return rc;
   // paged GQA attention -> fragments of the o-proj input
   AttnArgs at;
   at.n_rows = m;
@@ -429,7 +551,7 @@ int enqueue_layer(Ctx* c, Model& M, int l, int m, const int32_t* d_tenant, const
   ao.ld_ss = kMaxRowsAbi;
   ao.xout = M.ff.view();
   ao.xf_norm = L.raw[5].d.as<float>();
-  if (int rc = launch_gemv(c, ao, launches)) return rc;
+  if (int rc = chain_add(c, ao, true, launches)) return rc;
   // gate/up (interleaved) with fused RMSNorm and SwiGLU -> fragments of h
   GemvArgs ag = base_args(c, L.gu, m);
   ag.xin = M.ff.view();
@@ -440,7 +562,7 @@ int enqueue_layer(Ctx* c, Model& M, int l, int m, const int32_t* d_tenant, const
   ag.norm_dim = H;
   ag.epi = EPI_SWIGLU;
   ag.xout = M.fd.view();
-  if (int rc = launch_gemv(c, ag, launches)) return rc;
+  if (int rc = chain_add(c, ag, true, launches)) return rc;
   // down + residual; writes fragments of x * (next layer's attn_norm | output_norm)
   GemvArgs ad = base_args(c, L.down, m);
   ad.xin = M.fd.view();
@@ -451,7 +573,8 @@ int enqueue_layer(Ctx* c, Model& M, int l, int m, const int32_t* d_tenant, const
   ad.ld_ss = kMaxRowsAbi;
   ad.xout = M.fa.view();
   ad.xf_norm = (l + 1 < (int)cf.n_layers) ? M.layers[l + 1].raw[0].d.as<float>() : M.out_norm.d.as<float>();
-  return launch_gemv(c, ad, launches);
+  // left queued: the next layer's q|k, v (or the LM head) join this launch
+  return chain_add(c, ad, true, launches);
 }
 
 int enqueue_head(Ctx* c, Model& M, int m, bool want_logits, int* launches) {
@@ -467,7 +590,8 @@ int enqueue_head(Ctx* c, Model& M, int m, bool want_logits, int* launches) {
   a.y = want_logits ? M.logits.as<float>() : nullptr;
   a.ldy = cf.vocab;
   a.argmax = M.argmax.as<unsigned long long>();
-  return launch_gemv(c, a, launches);
+  if (int rc = chain_add(c, a, true, launches)) return rc;
+  return chain_flush(c, launches);
 }
 
 // Descriptor layout in int32s: [n_rows, n_upd, tenant[64], pos[64], tokens[64], upd[...][3]]
@@ -693,16 +817,23 @@ int32_t rb_ctx_create(const rb_config* cfg, rb_ctx** out) {
   c->pdl = cfg->use_pdl != 0;
   c->graphs = cfg->use_graphs != 0;
   if (const char* d = getenv("RB_GEMV_DBG")) c->gemv_dbg = atoi(d);
+  if (c->gemv_dbg & 2) {
+    RB_CUDA(c->dbg_ts.alloc((size_t)c->num_sms * kMaxPhases * 16 * 8));
+    RB_CUDA(cudaMemset(c->dbg_ts.p, 0, (size_t)c->num_sms * kMaxPhases * 16 * 8));
+  }
+  if (const char* d = getenv("RB_NO_CHAIN")) c->chains = atoi(d) == 0;
   RB_CUDA(cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking));
   RB_CUDA(cudaEventCreate(&c->ev0));
   RB_CUDA(cudaEventCreate(&c->ev1));
   RB_CUDA(cudaEventCreateWithFlags(&c->pinned_ev, cudaEventDisableTiming));
   RB_CUDA(cudaEventRecord(c->pinned_ev, c->stream));
-  RB_CUDA(c->gemv_partials.alloc(gemv_partials_floats(c->num_sms, 8) * 4));
+  RB_CUDA(c->gemv_partials.alloc(gemv_partials_floats(c->num_sms, 8, kMaxPhases) * 4));
   RB_CUDA(c->counters.alloc(kCounters * 4));
   RB_CUDA(cudaMemsetAsync(c->counters.p, 0, kCounters * 4, c->stream));
   RB_CUDA(c->err.alloc(16));
   RB_CUDA(cudaMemsetAsync(c->err.p, 0, 16, c->stream));
+  RB_CUDA(c->gbar.alloc(8 * kMaxPhases));
+  RB_CUDA(cudaMemsetAsync(c->gbar.p, 0, 8 * kMaxPhases, c->stream));
   c->pinned_bytes = 64 << 10;
   RB_CUDA(cudaMallocHost(&c->pinned, c->pinned_bytes));
   RB_CUDA(c->stage_in.alloc(c->pinned_bytes));
@@ -778,7 +909,8 @@ int32_t rb_weight_upload(rb_ctx* c, int32_t dtype, uint32_t n, uint32_t k, const
                          uint32_t flags, int32_t* handle) {
   if (!c || !handle) return fail(RB_ERR_BAD_HANDLE, "null context/handle");
   if (dtype != DT_Q4_K && dtype != DT_Q6_K && dtype != DT_Q8_0) return fail(RB_ERR_UNSUPPORTED, "dtype %d", dtype);
-  if (k % kSuperK) return fail(RB_ERR_UNSUPPORTED, "K dimension %u must be multiple of 256", k);
+  if (dtype == DT_Q8_0 ? (k % 32) != 0 : (k % kSuperK) != 0)
+    return fail(RB_ERR_UNSUPPORTED, "K dimension %u must be multiple of %d", k, dtype == DT_Q8_0 ? 32 : 256);
   const size_t expect = (size_t)n * (k / block_elems(dtype)) * block_bytes(dtype);
   if (nbytes != expect) return fail(RB_ERR_INVALID, "expected %zu bytes, got %zu", expect, nbytes);
   Staged in;
@@ -808,6 +940,14 @@ static int ensure_xf_scratch(rb_ctx* c, int k) {
 
 static int weight_matmul_dev(rb_ctx* c, const Weight& w, const float* din, float* dout, uint32_t batch) {
   if (int rc = ensure_xf_scratch(c, w.k)) return rc;
+  DevBuf xpad;
+  if (w.k_in != w.k) {  // zero-padded K (Q8_0): pad the input rows to match
+    RB_CUDA(xpad.alloc((size_t)batch * w.k * 4));
+    RB_CUDA(cudaMemsetAsync(xpad.p, 0, (size_t)batch * w.k * 4, c->stream));
+    RB_CUDA(cudaMemcpy2DAsync(xpad.p, (size_t)w.k * 4, din, (size_t)w.k_in * 4, (size_t)w.k_in * 4, batch,
+                              cudaMemcpyDeviceToDevice, c->stream));
+    din = xpad.as<float>();
+  }
   for (uint32_t b0 = 0; b0 < batch; b0 += kMaxRowsAbi) {
     const int m = (int)std::min<uint32_t>(kMaxRowsAbi, batch - b0);
     const int nt = gemv_nt_for(m);
@@ -828,7 +968,7 @@ int32_t rb_weight_matmul(rb_ctx* c, int32_t h, const float* input, float* output
   const Weight& w = *c->weights[h];
   if (batch == 0) return 0;
   Staged in;
-  if (int rc = stage(c, input, (size_t)batch * w.k * 4, flags, in)) return rc;
+  if (int rc = stage(c, input, (size_t)batch * w.k_in * 4, flags, in)) return rc;
   DevBuf tmp;
   float* dout = output;
   if (!(flags & RB_PTR_DEVICE)) {
@@ -863,7 +1003,6 @@ int32_t rb_weight_matmul_timing(rb_ctx* c, const int32_t* handles, uint32_t n_ha
   RB_CUDA(cudaMemsetAsync(x.p, 0, x.n, c->stream));
   if (int rc = ensure_xf_scratch(c, k)) return rc;
   RB_CUDA(xfrag_launch(x.as<float>(), k, nullptr, m, k, nt, c->xf_scratch.view(), nullptr, 0, c->stream));
-  if ((c->gemv_dbg & 2) && !c->dbg_ts.p) RB_CUDA(c->dbg_ts.alloc(4096 * 8 * 8));
   cudaGraph_t g = nullptr;
   RB_CUDA(cudaStreamBeginCapture(c->stream, cudaStreamCaptureModeThreadLocal));
   int rc = RB_OK;
@@ -896,25 +1035,7 @@ int32_t rb_weight_matmul_timing(rb_ctx* c, const int32_t* handles, uint32_t n_ha
   cudaGraphExecDestroy(ex);
   if (rc) return rc;
   *avg_us = ms * 1000.f / (float)(reps * iters);
-  if ((c->gemv_dbg & 2) && c->dbg_ts.p) {
-    const int G = gemv_ctas(c->num_sms, ws.back()->n_rg, ws.back()->k / kSuperK);
-    std::vector<unsigned long long> ts((size_t)G * 8);
-    cudaMemcpy(ts.data(), c->dbg_ts.p, ts.size() * 8, cudaMemcpyDeviceToHost);
-    unsigned long long t0 = ~0ull;
-    for (int b = 0; b < G; ++b) t0 = std::min(t0, ts[b * 8]);
-    const char* names[7] = {"entry", "prod_pre_issued", "prod_pdl_done", "prod_drained", "cons_first_full",
-                            "cons_last_unit", "cons_done"};
-    for (int p = 0; p < 7; ++p) {
-      double mn = 1e30, mx = 0, sum = 0;
-      for (int b = 0; b < G; ++b) {
-        const double v = (double)(ts[b * 8 + p] - t0) / 1000.0;
-        mn = std::min(mn, v);
-        mx = std::max(mx, v);
-        sum += v;
-      }
-      fprintf(stderr, "[gemv phases] %-16s min %7.2f mean %7.2f max %7.2f us\n", names[p], mn, sum / G, mx);
-    }
-  }
+  if ((c->gemv_dbg & 2) && c->dbg_ts.p) dump_stamps(c, 1);
   return RB_OK;
 }
 
@@ -944,7 +1065,7 @@ int32_t rb_fused_dequant_matmul(rb_ctx* c, int32_t dtype, const void* blocks, si
     if (nblocks != (size_t)n * (k / 256)) return fail(RB_ERR_INVALID, "Expected %zu blocks, got %zu", (size_t)n * (k / 256), nblocks);
   } else if (dtype == DT_Q8_0) {
     if (nblocks != ((size_t)n * k + 31) / 32) return fail(RB_ERR_INVALID, "Wrong number of blocks: expected %zu, got %zu", ((size_t)n * k + 31) / 32, nblocks);
-    if (k % 256) return fail(RB_ERR_UNSUPPORTED, "Q8_0 GEMV needs K %% 256 == 0 (K=%u)", k);
+    if (k % 32) return fail(RB_ERR_UNSUPPORTED, "Q8_0 GEMV needs K %% 32 == 0 (K=%u)", k);
   } else {
     return fail(RB_ERR_UNSUPPORTED, "dtype %d", dtype);
   }
@@ -1354,6 +1475,7 @@ int32_t rb_forward(rb_ctx* c, int32_t model, uint32_t n_rows, const uint32_t* te
   }
   if (int rc = sync_ctx(c)) return rc;
   cudaEventElapsedTime(&c->last_ms, c->ev0, c->ev1);
+  if ((c->gemv_dbg & 2) && c->dbg_ts.p) dump_stamps(c, c->last_chain_phases);
   for (uint32_t r = 0; r < n_rows; ++r) {
     KvTenant& T = P.tenants[rp.tenant[r]];
     for (auto& l : T.len) l = std::max(l, rp.pos[r] + 1);
@@ -1423,6 +1545,7 @@ int32_t rb_forward_layer(rb_ctx* c, int32_t model, uint32_t t, uint32_t layer, c
   RB_CUDA(cudaEventRecord(c->ev0, c->stream));
   const int32_t* d = M->desc.as<int32_t>();
   if (int rc = enqueue_layer(c, *M, (int)layer, (int)S, d + kDescTenant, d + kDescPos, &launches)) return rc;
+  if (int rc = chain_flush(c, &launches)) return rc;
   RB_CUDA(cudaEventRecord(c->ev1, c->stream));
   if (int rc = copy_out(c, out, M->x.p, (size_t)S * H * 4, flags)) return rc;
   if (int rc = sync_ctx(c)) return rc;
@@ -1562,6 +1685,7 @@ extern "C" int32_t rb_weight_matmul_noalloc(rb_ctx* c, int32_t h, const float* i
   if (batch > (uint32_t)kNaMaxBatch)
     return fail(RB_ERR_INVALID, "batch %u exceeds the no-alloc maximum of %d rows", batch, kNaMaxBatch);
   if (w.k > kNaMaxK) return fail(RB_ERR_INVALID, "K=%d exceeds the no-alloc maximum of %d", w.k, kNaMaxK);
+  if (w.k_in != w.k) return fail(RB_ERR_UNSUPPORTED, "K=%d is not a multiple of 256", w.k_in);
   if (w.n_rg > kNaMaxRowGroups)
     return fail(RB_ERR_INVALID, "N=%d exceeds the no-alloc maximum of %d", w.n, kNaMaxRowGroups * kRowGroup);
   if (gemv_ctas(c->num_sms, w.n_rg, w.k / kSuperK) > kNaMaxCtas)

@@ -41,39 +41,11 @@ __host__ __device__ constexpr int x_stage_bytes(int dtype, int nt) {
 }
 __host__ __device__ constexpr int stage_bytes(int dtype, int nt) { return unit_bytes(dtype) + x_stage_bytes(dtype, nt); }
 __host__ __device__ constexpr int tile_floats(int nt) { return kRowGroup * 8 * nt; }  // epilogue transpose tile
-__host__ __device__ constexpr int stages_fit(int dtype, int nt) {
-  return (kSmemBudget - 4 * tile_floats(nt) - 4096) / stage_bytes(dtype, nt);
-}
-__host__ __device__ constexpr int ring_stages(int dtype, int nt) {
-  // as many stages as fit next to the epilogue tile, 1..6
-  return stages_fit(dtype, nt) > 6 ? 6 : stages_fit(dtype, nt) < 1 ? 1 : stages_fit(dtype, nt);
-}
-
-struct SmemLayout {
-  int ring, tile, bars, inv_rms, red, total;
-};
-
-__host__ __device__ inline SmemLayout smem_layout(int dtype, int nt) {
-  SmemLayout L;
-  const int S = ring_stages(dtype, nt);
-  L.ring = 0;
-  L.tile = L.ring + S * stage_bytes(dtype, nt);
-  L.bars = L.tile + 4 * tile_floats(nt);
-  L.inv_rms = L.bars + 8 * (2 * S);
-  L.red = L.inv_rms + 4 * kMaxTokens;
-  L.total = L.red + 4 * kConsumerWarps * kMaxTokens + 16;
-  return L;
-}
+constexpr int kMaxStages = 6;
+constexpr int kChainMinSmem = 120 * 1024;  // > half the SM's shared memory: one CTA per SM
 
 __device__ __forceinline__ uint4 lds128(const uint8_t* p) { return *reinterpret_cast<const uint4*>(p); }
 __device__ __forceinline__ uint2 lds64(const uint8_t* p) { return *reinterpret_cast<const uint2*>(p); }
-
-// byte i (0..3) of w as half2(b, b), exact
-__device__ __forceinline__ uint32_t byte_h2(uint32_t w, int i) {
-  // bytes [b_i, 0x64, b_i, 0x64] = half2(1024 + b, 1024 + b); minus 1024 is exact
-  const uint32_t t = prmt(w, 0x64646464u, (uint32_t)i | (4u << 4) | ((uint32_t)i << 8) | (4u << 12));
-  return hsub2_u(t, 0x64006400u);
-}
 
 __device__ __forceinline__ void named_bar(int id, int threads) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
@@ -84,9 +56,10 @@ __device__ __forceinline__ unsigned long long gtimer() {
   asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
   return t;
 }
-#define RB_TS(slot)                                                                   \
-  do {                                                                                \
-    if ((a.dbg & 2) && a.dbg_ts) a.dbg_ts[(size_t)blockIdx.x * 8 + (slot)] = gtimer(); \
+// measurement stamps (dbg bit 1): [cta][phase][16] %globaltimer values
+#define RB_TS(p, slot)                                                                                    \
+  do {                                                                                                    \
+    if ((a.dbg & 2) && a.dbg_ts) a.dbg_ts[((size_t)blockIdx.x * kMaxPhases + (p)) * 16 + (slot)] = gtimer(); \
   } while (0)
 
 __device__ __forceinline__ float4 ldcg4(const float* p) { return __ldcg(reinterpret_cast<const float4*>(p)); }
@@ -355,7 +328,7 @@ __device__ void epilogue(const GemvArgs& a, int rg, int warp, int lane, float ac
         float tv = 0.f;
         if (t < a.m && row < a.n) {
           float* p = a.resid + (size_t)t * a.ldr + row;
-          const float v = *p + acc[nt][r];
+          const float v = __ldcg(p) + acc[nt][r];  // written by another CTA earlier in this launch
           *p = v;
           sq[nt][r & 1] += v * v;
           tv = a.xf_norm ? v * a.xf_norm[row] : v;
@@ -450,113 +423,210 @@ __device__ void epilogue(const GemvArgs& a, int rg, int warp, int lane, float ac
 }
 
 // ---------------------------------------------------------------------------
-// The kernel
+// The kernel: a chain of GEMV phases run by one persistent grid.
+//
+// ChainArgs holds 1..kMaxPhases GEMVs (e.g. o-proj -> gate|up -> down -> next
+// layer's q|k -> v). Every CTA walks all phases in order; within a phase the
+// units (256-row group x 256-column super-block) are split evenly over the
+// CTAs as in a single GEMV. The producer lane streams the weight units of
+// consecutive phases through one shared-memory ring without pausing at phase
+// boundaries; only the activation copies of a phase wait for what they depend
+// on: phase 0 on the previous kernel (programmatic dependent launch), a phase
+// with its bit set in bar_mask on a grid barrier that every CTA passes after
+// finishing the phase before it (last epilogue written). Each barrier slot is
+// a monotonic 64-bit arrival counter (CTAs without units in a phase reach
+// later barriers early, so slots must not share one); a CTA's ticket t gives
+// the target (t / G + 1) * G. All CTAs of a multi-phase launch are resident
+// at once (grid <= SM count, one CTA per SM by shared memory), and every wait
+// is bounded.
 // ---------------------------------------------------------------------------
+struct ChainSmem {
+  int ring, tile, bars, inv_rms, red, tgt, total;
+};
+
+__host__ __device__ inline ChainSmem chain_smem(int stages, int stage_bytes, int nt) {
+  ChainSmem L;
+  L.ring = 0;
+  L.tile = stages * stage_bytes;
+  L.bars = L.tile + 4 * tile_floats(nt);
+  L.inv_rms = L.bars + 8 * (2 * stages);
+  L.red = L.inv_rms + 4 * kMaxTokens;
+  L.tgt = L.red + 4 * kConsumerWarps * kMaxTokens + 16;
+  L.total = L.tgt + 8 * kMaxPhases;
+  return L;
+}
+
+// This CTA's unit range [u0, u0 + n_units) of phase a; Gp = CTAs with work.
+struct PhaseRange {
+  long long U, u0;
+  int Gp, n_units;
+};
+__device__ __forceinline__ PhaseRange phase_range(const GemvArgs& a) {
+  PhaseRange r;
+  r.U = (long long)a.n_rg * a.nsb;
+  r.Gp = r.U < (long long)gridDim.x ? (int)r.U : (int)gridDim.x;
+  if ((int)blockIdx.x < r.Gp) {
+    r.u0 = r.U * blockIdx.x / r.Gp;
+    r.n_units = (int)(r.U * (blockIdx.x + 1) / r.Gp - r.u0);
+  } else {
+    r.u0 = 0;
+    r.n_units = 0;
+  }
+  return r;
+}
+
+// Ring position shared by producer and consumers: unit sequence number over
+// all phases -> stage s, and how many times the ring has wrapped (round).
+struct RingPos {
+  int s = 0;
+  uint32_t round = 0;
+  __device__ __forceinline__ void next(int S) {
+    if (++s == S) {
+      s = 0;
+      ++round;
+    }
+  }
+};
+
+// End of a row-group segment: a whole row group goes straight to the
+// epilogue; a partial one is deposited, and the last of its contributors sums
+// them and runs the epilogue. Kept out of line so that its registers do not
+// compete with the tile loop's.
+template <int NT>
+__device__ __noinline__ void finish_segment(const GemvArgs& a, int p, int n_phases, const PhaseRange& pr, int rg,
+                                            int sb, int first_rg, float (&acc)[NT][4], const float* inv_rms,
+                                            float* red, float* T) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const long long U = pr.U, u0 = pr.u0;
+  const int Gp = pr.Gp;
+  // two partial slots per CTA and phase; chains alternate two pairs so that
+  // consecutive phases never share a slot
+  const int nslots = n_phases > 1 ? 4 : 2;
+  const int slot_base = n_phases > 1 ? (p & 1) * 2 : 0;
+  const float* irms = a.ss_part ? inv_rms : nullptr;
+  const bool stamp = threadIdx.x == 0;
+  if (stamp) RB_TS(p, 8);
+  const long long seg_lo = (u0 > (long long)rg * a.nsb) ? u0 : (long long)rg * a.nsb;
+  const bool full_seg = (seg_lo == (long long)rg * a.nsb) && (sb + 1 == a.nsb);
+  if (!full_seg) {
+    // deposit this CTA's partial; slot 0 if rg is this CTA's first row group
+    const int slot = slot_base + ((rg == first_rg) ? 0 : 1);
+    float* dst = a.partials + ((((size_t)blockIdx.x * nslots + slot) * kConsumerWarps + warp) * NT) * 128;
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt)
+      __stcg(reinterpret_cast<float4*>(dst + nt * 128 + lane * 4),
+             make_float4(acc[nt][0], acc[nt][1], acc[nt][2], acc[nt][3]));
+    // the CTA's partial stores are ordered before thread 0's release (bar.sync,
+    // then one cumulative fence) and after its acquire for the reads below
+    named_bar(1, 32 * kConsumerWarps);
+    if (stamp) RB_TS(p, 9);
+    __shared__ int s_last;
+    // contributors: CTAs whose unit range intersects row group rg
+    const long long ua = (long long)rg * a.nsb, ub = ua + a.nsb - 1;
+    long long cf = ua * Gp / U, cl = ub * Gp / U;
+    while (cf + 1 < Gp && U * (cf + 1) / Gp <= ua) ++cf;
+    while (cf > 0 && U * cf / Gp > ua) --cf;
+    while (cl + 1 < Gp && U * (cl + 1) / Gp <= ub) ++cl;
+    while (cl > 0 && U * cl / Gp > ub) --cl;
+    const int ncontrib = (int)(cl - cf + 1);
+    if (threadIdx.x == 0) {
+      __threadfence();
+      const int last = (atomicAdd(a.counters + rg, 1) == ncontrib - 1);
+      if (last) __threadfence();
+      s_last = last;
+      RB_TS(p, 10);
+    }
+    named_bar(1, 32 * kConsumerWarps);
+    if (s_last) {
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt) acc[nt][0] = acc[nt][1] = acc[nt][2] = acc[nt][3] = 0.f;
+      // contributor cc deposited into slot 0 iff rg is its first row group:
+      // true for every cc > cf, and for cf iff its range starts at rg's start
+      const int sl_cf = slot_base + ((U * cf / Gp == ua) ? 0 : 1);
+      auto src_of = [&](long long cc) {
+        const int sl = cc == cf ? sl_cf : slot_base;
+        return a.partials + ((((size_t)cc * nslots + sl) * kConsumerWarps + warp) * NT) * 128 + lane * 4;
+      };
+      // loads issued in batches of 8, summed in contributor order (deterministic)
+      for (long long c0 = cf; c0 <= cl; c0 += 8) {
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt) {
+          float4 q[8];
+#pragma unroll
+          for (int j = 0; j < 8; ++j)
+            if (c0 + j <= cl) q[j] = ldcg4(src_of(c0 + j) + nt * 128);
+#pragma unroll
+          for (int j = 0; j < 8; ++j)
+            if (c0 + j <= cl) {
+              acc[nt][0] += q[j].x;
+              acc[nt][1] += q[j].y;
+              acc[nt][2] += q[j].z;
+              acc[nt][3] += q[j].w;
+            }
+        }
+      }
+      if (stamp) RB_TS(p, 11);
+      // the epilogue runs even after a timed-out wait (error already reported):
+      // its named barriers must be reached by every consumer warp
+      epilogue<NT>(a, rg, warp, lane, acc, irms, red, T);
+      if (threadIdx.x == 0) a.counters[rg] = 0;
+      if (stamp) RB_TS(p, 12);
+    }
+  } else {
+    if (stamp) RB_TS(p, 13);
+    epilogue<NT>(a, rg, warp, lane, acc, irms, red, T);
+    if (stamp) RB_TS(p, 14);
+  }
+}
+
 template <int DT, int NT>
-__global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const GemvArgs a) {
-  constexpr int S = ring_stages(DT, NT);
+__device__ __forceinline__ void consume_phase(const GemvArgs& a, int p, int n_phases, const PhaseRange& pr, uint8_t* ring, int S,
+                                              int SB, uint64_t* full, uint64_t* empty, float* inv_rms, float* red,
+                                              float* T, RingPos& rp, bool& alive,
+                                              const unsigned long long* gbar /* this barrier's counter */,
+                                              bool wait_grid,
+                                              unsigned long long bar_target) {
   constexpr int UB = unit_bytes(DT);
   constexpr int TB = tile_bytes(DT);
-  constexpr int SB = stage_bytes(DT, NT);
-  constexpr int XB = x_stage_bytes(DT, NT);
-  extern __shared__ __align__(128) uint8_t smem[];
-  const SmemLayout L = smem_layout(DT, NT);
-  uint8_t* ring = smem + L.ring;
-  float* T = reinterpret_cast<float*>(smem + L.tile);
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + L.bars);
-  uint64_t* empty = full + S;
-  float* inv_rms = reinterpret_cast<float*>(smem + L.inv_rms);
-  float* red = reinterpret_cast<float*>(smem + L.red);
-
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const long long U = (long long)a.n_rg * a.nsb;
-  const int G = gridDim.x;
-  const long long u0 = U * blockIdx.x / G, u1 = U * (blockIdx.x + 1) / G;
-  const int n_units = (int)(u1 - u0);
-
-  if (threadIdx.x == 0) {
-    RB_TS(0);
-    for (int s = 0; s < S; ++s) {
-      mbar_init(&full[s], 1);
-      mbar_init(&empty[s], kConsumerWarps);
-    }
-    fence_barrier_init();
+  const int tid = threadIdx.x;
+  if (tid == 0) RB_TS(p, 0);
+  if (pr.n_units == 0) return;
+  if (wait_grid) {  // uniform over the CTA; only thread 0 reads the target
+    // everything the phases before wrote is visible once all CTAs arrived
+    if (tid == 0) grid_wait(gbar, bar_target, a.err, (blockIdx.x << 8) | ((uint32_t)p << 1));
+    named_bar(1, 32 * kConsumerWarps);
   }
-  __syncthreads();
-  pdl_launch_dependents();
-
-  if (warp == kProducerWarp) {
-    if (lane == 0) {
-      const uint64_t pol = policy_evict_first();
-      // activation bytes for super-block sb: Q4_K {int8 limbs, scales, sums}, else {fp16 hi/lo, sums}
-      auto issue_x = [&](int i) {
-        const int sb = (int)((u0 + i) % a.nsb);
-        uint8_t* st = ring + (size_t)(i % S) * SB + UB;
-        uint64_t* bar = &full[i % S];
-        if (DT == DT_Q4_K) {
-          bulk_g2s(st, reinterpret_cast<const uint8_t*>(a.xin.xi) + (size_t)sb * NT * kXiSbBytes, NT * kXiSbBytes, bar);
-          st += NT * kXiSbBytes;
-          bulk_g2s(st, reinterpret_cast<const uint8_t*>(a.xin.xc) + (size_t)sb * NT * kXcSbBytes, NT * kXcSbBytes, bar);
-          st += NT * kXcSbBytes;
-        } else {
-          bulk_g2s(st, reinterpret_cast<const uint8_t*>(a.xin.xf) + (size_t)sb * NT * kXfSbBytes, NT * kXfSbBytes, bar);
-          st += NT * kXfSbBytes;
-        }
-        bulk_g2s(st, reinterpret_cast<const uint8_t*>(a.xin.xs) + (size_t)sb * NT * kXsSbBytes, NT * kXsSbBytes, bar);
-      };
-      // Weights do not depend on the previous kernel: start streaming them
-      // before the grid dependency resolves; the activations follow after it.
-      const int pre = n_units < S ? n_units : S;
-      for (int i = 0; i < pre; ++i) {
-        mbar_arrive_expect_tx(&full[i], UB + XB);
-        bulk_g2s_evict_first(ring + (size_t)i * SB, a.w + (u0 + i) * (long long)UB, UB, &full[i], pol);
-      }
-      RB_TS(1);
-      pdl_wait();
-      RB_TS(2);
-      for (int i = 0; i < pre; ++i) issue_x(i);
-      bool ok = true;
-      for (int i = pre; i < n_units && ok; ++i) {
-        const int s = i % S;
-        ok = mbar_wait(&empty[s], ((i / S) - 1) & 1, a.err, DEV_TIMEOUT_EMPTY);
-        if (!ok) break;
-        mbar_arrive_expect_tx(&full[s], UB + XB);
-        bulk_g2s_evict_first(ring + (size_t)s * SB, a.w + (u0 + i) * (long long)UB, UB, &full[s], pol);
-        issue_x(i);
-      }
-      // drain: every issued copy must land before this CTA may exit
-      for (int i = (n_units > S ? n_units - S : 0); i < n_units; ++i)
-        mbar_wait(&full[i % S], (i / S) & 1, a.err, DEV_TIMEOUT_DRAIN);
-      RB_TS(3);
-    }
-    return;
-  }
-
-  // ---- consumers ----
-  pdl_wait();
+  if (tid == 0) RB_TS(p, 1);
   if (a.ss_part) {
-    const int tid = threadIdx.x;
+    // 1/rms per token from the partial sums of squares (written by other CTAs
+    // or the previous kernel: read through L2). Thread (t, r) sums partials
+    // r, r + 8, ... of token t; the eight sums are added in a fixed order.
+    const int t = tid & 63, r = tid >> 6;
+    if (t < a.m) {
+      float ss = 0.f;
+      for (int j = r; j < a.n_ss; j += 8) ss += __ldcg(a.ss_part + (size_t)j * a.ld_ss + t);
+      red[r * 64 + t] = ss;
+    }
+    named_bar(1, 32 * kConsumerWarps);
     if (tid < a.m) {
       float ss = 0.f;
-      for (int j = 0; j < a.n_ss; ++j) ss += a.ss_part[(size_t)j * a.ld_ss + tid];
+#pragma unroll
+      for (int q = 0; q < 8; ++q) ss += red[q * 64 + tid];
       inv_rms[tid] = 1.0f / sqrtf(ss / (float)a.norm_dim + a.norm_eps);
     }
     named_bar(1, 32 * kConsumerWarps);
   }
-  const float* irms = a.ss_part ? inv_rms : nullptr;
-
+  const long long u0 = pr.u0;
   float acc[NT][4];
 #pragma unroll
   for (int nt = 0; nt < NT; ++nt) acc[nt][0] = acc[nt][1] = acc[nt][2] = acc[nt][3] = 0.f;
-
   const int first_rg = (int)(u0 / a.nsb);
-  bool alive = true;
-  for (int i = 0; i < n_units; ++i) {
-    const long long u = u0 + i;
-    const int rg = (int)(u / a.nsb), sb = (int)(u % a.nsb);
-    const int s = i % S;
-    if (alive) alive = mbar_wait(&full[s], (i / S) & 1, a.err, DEV_TIMEOUT_FULL);
-    if (i == 0 && threadIdx.x == 0) RB_TS(4);
+  int rg = first_rg, sb = (int)(u0 - (long long)first_rg * a.nsb);  // advanced per unit (no divisions)
+  for (int i = 0; i < pr.n_units; ++i, (++sb == a.nsb) ? (sb = 0, ++rg) : 0) {
+    const int s = rp.s;
+    if (alive) alive = mbar_wait(&full[s], rp.round & 1, a.err, DEV_TIMEOUT_FULL);
+    if (i == 0 && tid == 0) RB_TS(p, 2);
     if (alive && !(a.dbg & 1)) {
       const uint8_t* st = ring + (size_t)s * SB;
       const uint8_t* tile = st + warp * TB;
@@ -568,61 +638,173 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const GemvArgs a) {
     }
     __syncwarp();
     if (lane == 0) mbar_arrive(&empty[s]);
-    if (i + 1 == n_units && threadIdx.x == 0) RB_TS(5);
-    const bool seg_end = (i + 1 == n_units) || (sb + 1 == a.nsb);
+    rp.next(S);
+    if (i + 1 == pr.n_units && tid == 0) RB_TS(p, 3);
+    const bool seg_end = (i + 1 == pr.n_units) || (sb + 1 == a.nsb);
     if (!seg_end) continue;
-    const long long seg_lo = (u0 > (long long)rg * a.nsb) ? u0 : (long long)rg * a.nsb;
-    const bool full_seg = (seg_lo == (long long)rg * a.nsb) && (sb + 1 == a.nsb);
-    if (!full_seg) {
-      // deposit this CTA's partial; slot 0 if rg is this CTA's first row group
-      const int slot = (rg == first_rg) ? 0 : 1;
-      float* dst = a.partials + ((((size_t)blockIdx.x * 2 + slot) * kConsumerWarps + warp) * NT) * 128;
-#pragma unroll
-      for (int nt = 0; nt < NT; ++nt)
-        __stcg(reinterpret_cast<float4*>(dst + nt * 128 + lane * 4),
-               make_float4(acc[nt][0], acc[nt][1], acc[nt][2], acc[nt][3]));
-      __threadfence();
-      named_bar(1, 32 * kConsumerWarps);
-      __shared__ int s_last;
-      // contributors: CTAs whose unit range intersects row group rg
-      const long long ua = (long long)rg * a.nsb, ub = ua + a.nsb - 1;
-      long long cf = ua * G / U, cl = ub * G / U;
-      while (cf + 1 < G && U * (cf + 1) / G <= ua) ++cf;
-      while (cf > 0 && U * cf / G > ua) --cf;
-      while (cl + 1 < G && U * (cl + 1) / G <= ub) ++cl;
-      while (cl > 0 && U * cl / G > ub) --cl;
-      const int ncontrib = (int)(cl - cf + 1);
-      if (threadIdx.x == 0) s_last = (atomicAdd(a.counters + rg, 1) == ncontrib - 1);
-      named_bar(1, 32 * kConsumerWarps);
-      if (s_last) {
-        __threadfence();
-#pragma unroll
-        for (int nt = 0; nt < NT; ++nt) acc[nt][0] = acc[nt][1] = acc[nt][2] = acc[nt][3] = 0.f;
-        for (long long cc = cf; cc <= cl; ++cc) {
-          const int first_of_c = (int)((U * cc / G) / a.nsb);
-          const int sl = (rg == first_of_c) ? 0 : 1;
-          const float* src = a.partials + ((((size_t)cc * 2 + sl) * kConsumerWarps + warp) * NT) * 128;
-#pragma unroll
-          for (int nt = 0; nt < NT; ++nt) {
-            const float4 p = ldcg4(src + nt * 128 + lane * 4);
-            acc[nt][0] += p.x;
-            acc[nt][1] += p.y;
-            acc[nt][2] += p.z;
-            acc[nt][3] += p.w;
-          }
-        }
-        if (alive) epilogue<NT>(a, rg, warp, lane, acc, irms, red, T);
-        if (threadIdx.x == 0) a.counters[rg] = 0;
-      }
-    } else if (alive) {
-      epilogue<NT>(a, rg, warp, lane, acc, irms, red, T);
-    }
+    finish_segment<NT>(a, p, n_phases, pr, rg, sb, first_rg, acc, inv_rms, red, T);
 #pragma unroll
     for (int nt = 0; nt < NT; ++nt) acc[nt][0] = acc[nt][1] = acc[nt][2] = acc[nt][3] = 0.f;
-    if (i + 1 == n_units && threadIdx.x == 0) RB_TS(6);
+    if (i + 1 == pr.n_units && tid == 0) RB_TS(p, 4);
   }
 }
 
+// Index of the latest grid barrier at or before phase p (0: none in this launch).
+__device__ __forceinline__ int last_barrier(uint32_t mask, int p) {
+  int q = 0;
+  for (int i = 1; i <= p; ++i)
+    if ((mask >> i) & 1u) q = i;
+  return q;
+}
+
+template <int NT>
+__global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const __grid_constant__ ChainArgs ca) {
+  extern __shared__ __align__(128) uint8_t smem[];
+  const int S = ca.stages, SB = ca.stage_bytes;
+  const ChainSmem L = chain_smem(S, SB, NT);
+  uint8_t* ring = smem + L.ring;
+  float* T = reinterpret_cast<float*>(smem + L.tile);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + L.bars);
+  uint64_t* empty = full + S;
+  float* inv_rms = reinterpret_cast<float*>(smem + L.inv_rms);
+  float* red = reinterpret_cast<float*>(smem + L.red);
+  volatile unsigned long long* s_tgt = reinterpret_cast<volatile unsigned long long*>(smem + L.tgt);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const GemvArgs& a0 = ca.ph[0];
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < S; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], kConsumerWarps);
+    }
+    for (int p = 0; p < kMaxPhases; ++p) s_tgt[p] = 0ull;
+    fence_barrier_init();
+  }
+  __syncthreads();
+  pdl_launch_dependents();
+
+  if (warp == kProducerWarp) {
+    if (lane == 0) {
+      const uint64_t pol = policy_evict_first();
+      RingPos rp;
+      uint32_t issued = 0;  // units issued over all phases
+      bool ok = true, pdl_done = false;
+      int passed = 0;  // highest grid barrier this producer has waited for
+      int pend_s[kMaxStages], pend_sb[kMaxStages];
+      for (int p = 0; p < ca.n_phases && ok; ++p) {
+        const GemvArgs& a = ca.ph[p];
+        const PhaseRange pr = phase_range(a);
+        const int UB = unit_bytes(a.dtype), XB = x_stage_bytes(a.dtype, NT);
+        // the phase's activations depend on the latest grid barrier at or before it
+        const int need = last_barrier(ca.bar_mask, p);
+        bool dep = pdl_done && need <= passed;
+        int npend = 0;
+        int x_sb = pr.n_units ? (int)(pr.u0 % a.nsb) : 0;
+        // activation bytes for super-block sb: Q4_K {int8 limbs, scales, sums}, else {fp16 hi/lo, sums}
+        auto issue_x = [&](int s, int sb) {
+          uint8_t* st = ring + (size_t)s * SB + UB;
+          uint64_t* bar = &full[s];
+          if (a.dtype == DT_Q4_K) {
+            bulk_g2s(st, reinterpret_cast<const uint8_t*>(a.xin.xi) + (size_t)sb * NT * kXiSbBytes, NT * kXiSbBytes,
+                     bar);
+            st += NT * kXiSbBytes;
+            bulk_g2s(st, reinterpret_cast<const uint8_t*>(a.xin.xc) + (size_t)sb * NT * kXcSbBytes, NT * kXcSbBytes,
+                     bar);
+            st += NT * kXcSbBytes;
+          } else {
+            bulk_g2s(st, reinterpret_cast<const uint8_t*>(a.xin.xf) + (size_t)sb * NT * kXfSbBytes, NT * kXfSbBytes,
+                     bar);
+            st += NT * kXfSbBytes;
+          }
+          bulk_g2s(st, reinterpret_cast<const uint8_t*>(a.xin.xs) + (size_t)sb * NT * kXsSbBytes, NT * kXsSbBytes, bar);
+        };
+        // the activations of this phase may be read once what they depend on is done
+        auto resolve = [&]() {
+          if (!pdl_done) {
+            pdl_wait();
+            pdl_done = true;
+          }
+          if (need > passed) {
+            // target of barrier `need`, published by this CTA's consumers on arrival
+            uint32_t k = 0;
+            while (s_tgt[need - 1] == 0ull && ++k < kSpinLimit) {
+            }
+            const unsigned long long tgt = s_tgt[need - 1];
+            if (tgt == 0ull) report_error(a.err, DEV_TIMEOUT_SMEM);
+            else grid_wait(ca.gbar + need, tgt, a.err, (blockIdx.x << 8) | ((uint32_t)p << 1) | 1u);
+            passed = need;
+          }
+          dep = true;
+          for (int j = 0; j < npend; ++j) issue_x(pend_s[j], pend_sb[j]);
+          npend = 0;
+          RB_TS(p, 6);
+        };
+        for (int i = 0; i < pr.n_units; ++i) {
+          const int s = rp.s;
+          if (issued >= (uint32_t)S) {
+            ok = mbar_wait(&empty[s], (rp.round - 1) & 1, a.err, DEV_TIMEOUT_EMPTY);
+            if (!ok) break;
+          }
+          mbar_arrive_expect_tx(&full[s], UB + XB);
+          bulk_g2s_evict_first(ring + (size_t)s * SB, a.w + (pr.u0 + i) * (long long)UB, UB, &full[s], pol);
+          if (i == 0) RB_TS(p, 5);
+          if (i + 1 == pr.n_units) RB_TS(p, 7);
+          if (dep) {
+            issue_x(s, x_sb);
+          } else {
+            pend_s[npend] = s;
+            pend_sb[npend] = x_sb;
+            ++npend;
+          }
+          if (++x_sb == a.nsb) x_sb = 0;
+          rp.next(S);
+          ++issued;
+          if (!dep && (npend == S || i + 1 == pr.n_units)) resolve();
+        }
+      }
+      // drain: every issued copy must land before this CTA may exit
+      const uint32_t first = issued > (uint32_t)S ? issued - S : 0u;
+      for (uint32_t j = first; j < issued; ++j)
+        mbar_wait(&full[j % S], (j / S) & 1, a0.err, DEV_TIMEOUT_DRAIN);
+    }
+    return;
+  }
+
+  // ---- consumers ----
+  pdl_wait();
+  RingPos rp;
+  bool alive = true;
+  int passed = 0;  // highest grid barrier these consumers have waited for
+  for (int p = 0; p < ca.n_phases; ++p) {
+    const GemvArgs& a = ca.ph[p];
+    const PhaseRange pr = phase_range(a);
+    const int need = last_barrier(ca.bar_mask, p);
+    const bool wg = need > passed && pr.n_units > 0;
+    const unsigned long long my_target = wg ? s_tgt[need - 1] : 0ull;
+    if (wg) passed = need;
+    switch (a.dtype) {
+      case DT_Q4_K: consume_phase<DT_Q4_K, NT>(a, p, ca.n_phases, pr, ring, S, SB, full, empty, inv_rms, red, T, rp, alive,
+                                         ca.gbar + need, wg, my_target); break;
+      case DT_Q6_K: consume_phase<DT_Q6_K, NT>(a, p, ca.n_phases, pr, ring, S, SB, full, empty, inv_rms, red, T, rp, alive,
+                                         ca.gbar + need, wg, my_target); break;
+      default: consume_phase<DT_Q8_0, NT>(a, p, ca.n_phases, pr, ring, S, SB, full, empty, inv_rms, red, T, rp, alive,
+                                         ca.gbar + need, wg, my_target); break;
+    }
+    if (p + 1 < ca.n_phases && ((ca.bar_mask >> (p + 1)) & 1u)) {
+      // this CTA is done with phase p (epilogue writes included): arrive
+      named_bar(1, 32 * kConsumerWarps);
+      if (threadIdx.x == 0) {
+        __threadfence();
+        // one counter per barrier slot: every CTA arrives at each slot exactly
+        // once per launch, so a ticket always lies in its own launch's window
+        const unsigned long long t = atomicAdd(ca.gbar + (p + 1), 1ull);
+        s_tgt[p] = (t / gridDim.x + 1) * gridDim.x;
+      }
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
 // Plain rows -> activation fragments (+ RMSNorm sums of squares).
 // Grid (K/256, ceil(M/8)): one CTA per (super-block, 8-token n-tile), 128 threads.
 __global__ void xfrag_kernel(const float* x, int ldx, const float* w, int m, int k, int nt, XFrags out, float* ss,
@@ -913,20 +1095,27 @@ __global__ void quantize_kernel(int dtype, const float* x, size_t nblocks, uint8
   }
 }
 
-template <int DT, int NT>
-cudaError_t launch_t(const GemvArgs& a, int num_sms, cudaStream_t s, int pdl) {
-  const int smem = smem_layout(DT, NT).total;
-  auto kern = gemv_kernel<DT, NT>;
+template <int NT>
+cudaError_t launch_chain_t(ChainArgs ca, int num_sms, cudaStream_t s, int pdl) {
+  int sb = 0;
+  for (int p = 0; p < ca.n_phases; ++p) sb = max(sb, stage_bytes(ca.ph[p].dtype, NT));
+  sb = (sb + 127) & ~127;
+  const int fit = (kSmemBudget - 4 * tile_floats(NT) - 4096) / sb;
+  ca.stages = fit > kMaxStages ? kMaxStages : fit < 1 ? 1 : fit;
+  ca.stage_bytes = sb;
+  int smem = chain_smem(ca.stages, sb, NT).total;
+  if (ca.n_phases > 1 && smem < kChainMinSmem) smem = kChainMinSmem;  // one CTA per SM
+  auto kern = gemv_kernel<NT>;
   static unsigned long long attr_set = 0;  // per instantiation, one bit per device
   int dev = 0;
   cudaGetDevice(&dev);
   if (!(attr_set & (1ull << dev))) {
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBudget + 8192);
     if (e != cudaSuccess) return e;
     attr_set |= 1ull << dev;
   }
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(gemv_ctas(num_sms, a.n_rg, a.nsb));
+  cfg.gridDim = dim3(ca.n_phases == 1 ? gemv_ctas(num_sms, ca.ph[0].n_rg, ca.ph[0].nsb) : num_sms);
   cfg.blockDim = dim3(kThreads);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = s;
@@ -935,17 +1124,7 @@ cudaError_t launch_t(const GemvArgs& a, int num_sms, cudaStream_t s, int pdl) {
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = pdl ? 1 : 0;
-  return cudaLaunchKernelEx(&cfg, kern, a);
-}
-
-template <int DT>
-cudaError_t launch_dt(const GemvArgs& a, int num_sms, cudaStream_t s, int pdl) {
-  switch (gemv_nt_for(a.m)) {
-    case 1: return launch_t<DT, 1>(a, num_sms, s, pdl);
-    case 2: return launch_t<DT, 2>(a, num_sms, s, pdl);
-    case 4: return launch_t<DT, 4>(a, num_sms, s, pdl);
-    default: return launch_t<DT, 8>(a, num_sms, s, pdl);
-  }
+  return cudaLaunchKernelEx(&cfg, kern, ca);
 }
 
 }  // namespace
@@ -957,18 +1136,33 @@ int gemv_ctas(int num_sms, int n_rg, int nsb) {
   return (int)(U < num_sms ? U : num_sms);
 }
 
-size_t gemv_partials_floats(int num_ctas, int nt) { return (size_t)num_ctas * 2 * kConsumerWarps * nt * 128; }
+size_t gemv_partials_floats(int num_ctas, int nt, int n_phases) {
+  return (size_t)num_ctas * (n_phases > 1 ? 4 : 2) * kConsumerWarps * nt * 128;
+}
 
-int gemv_dynamic_smem(int dtype, int nt) { return smem_layout(dtype, nt).total; }
+
+cudaError_t gemv_chain_launch(const ChainArgs& c, int num_sms, cudaStream_t s, int pdl) {
+  if (c.n_phases < 1 || c.n_phases > kMaxPhases) return cudaErrorInvalidValue;
+  if (c.n_phases > 1 && !c.gbar) return cudaErrorInvalidValue;
+  const int m = c.ph[0].m;
+  for (int p = 0; p < c.n_phases; ++p) {
+    const GemvArgs& a = c.ph[p];
+    if (a.m != m || a.m < 1 || a.m > kMaxTokens) return cudaErrorInvalidValue;
+    if (a.dtype != DT_Q4_K && a.dtype != DT_Q6_K && a.dtype != DT_Q8_0) return cudaErrorInvalidValue;
+  }
+  switch (gemv_nt_for(m)) {
+    case 1: return launch_chain_t<1>(c, num_sms, s, pdl);
+    case 2: return launch_chain_t<2>(c, num_sms, s, pdl);
+    case 4: return launch_chain_t<4>(c, num_sms, s, pdl);
+    default: return launch_chain_t<8>(c, num_sms, s, pdl);
+  }
+}
 
 cudaError_t gemv_launch(const GemvArgs& a, int num_sms, cudaStream_t s, int pdl) {
-  if (a.m < 1 || a.m > kMaxTokens) return cudaErrorInvalidValue;
-  switch (a.dtype) {
-    case DT_Q4_K: return launch_dt<DT_Q4_K>(a, num_sms, s, pdl);
-    case DT_Q6_K: return launch_dt<DT_Q6_K>(a, num_sms, s, pdl);
-    case DT_Q8_0: return launch_dt<DT_Q8_0>(a, num_sms, s, pdl);
-  }
-  return cudaErrorInvalidValue;
+  ChainArgs c;
+  c.ph[0] = a;
+  c.n_phases = 1;
+  return gemv_chain_launch(c, num_sms, s, pdl);
 }
 
 cudaError_t repack_launch(const uint8_t* a, int rows_a, const uint8_t* b, int rows_b, int mode, int dtype, int k,

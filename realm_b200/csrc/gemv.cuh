@@ -68,13 +68,27 @@ struct GemvArgs {
   uint32_t* err = nullptr;
 };
 
+// A chain of GEMVs run by one persistent launch (phase p + 1 may read what
+// phase p wrote when bit p + 1 of bar_mask is set: a grid barrier separates
+// them). A single GEMV is a chain of one phase.
+constexpr int kMaxPhases = 6;
+struct ChainArgs {
+  GemvArgs ph[kMaxPhases];
+  int32_t n_phases = 0;
+  uint32_t bar_mask = 0;
+  unsigned long long* gbar = nullptr;  // [kMaxPhases] grid-barrier arrival counters (monotonic, start at 0)
+  int32_t stages = 0, stage_bytes = 0;  // ring geometry, set by gemv_chain_launch
+};
+
 // Scratch needed by one GEMV launch (partials in floats, counters in ints).
-size_t gemv_partials_floats(int num_ctas, int nt);
+size_t gemv_partials_floats(int num_ctas, int nt, int n_phases = 1);
 int gemv_ctas(int num_sms, int n_rg, int nsb);
 int gemv_nt_for(int m);
-// Launch with programmatic dependent launch enabled when pdl != 0.
+// Launch with programmatic dependent launch enabled when pdl != 0. A chain of
+// more than one phase runs on num_sms CTAs; all its phases use the same NT
+// (same m). Split-K counters of different phases must not overlap.
 cudaError_t gemv_launch(const GemvArgs& a, int num_sms, cudaStream_t s, int pdl);
-int gemv_dynamic_smem(int dtype, int nt);
+cudaError_t gemv_chain_launch(const ChainArgs& c, int num_sms, cudaStream_t s, int pdl);
 
 // Repack GGUF blocks into the tiled layout. Source rows come from up to two
 // matrices: mode 0 plain (rows of a), 1 concat (a then b), 2 interleave-8

@@ -97,23 +97,29 @@ __device__ __forceinline__ void xc_put(float* xc, int nt_total, int t, int sb, i
 // Writes every encoding of the block of values val(k, t) = T[k*sk + t*st] * (w ? w[k_base+k] : 1)
 // for local columns k in [0, nk) (global column k_base + k; nk and k_base
 // multiples of 64) and local tokens t in [0, ntok) (global token t_base + t).
-// Every thread of the calling group (ids tid < nthreads) must call it; `sync()`
-// is a barrier among them; scratch holds >= ntok * nk / 64 floats of shared memory.
+// Every thread of the calling group (ids tid < nthreads, whole warps) must
+// call it; `sync()` is a barrier among them; scratch holds >= ntok * nk / 64
+// floats of shared memory. Group maxima and sub-block sums are reduced one
+// warp per (group, token) with shuffles in a fixed order (deterministic).
 template <class Sync>
 __device__ void frags_write(const float* T, int sk, int st, int nk, int ntok, int k_base, int t_base,
                             const float* w, const XFrags& out, int nt_total, float* scratch, int tid, int nthreads,
                             Sync sync) {
   auto val = [&](int k, int t) { return T[(size_t)k * sk + (size_t)t * st] * (w ? w[k_base + k] : 1.f); };
+  const int lane = tid & 31, wid = tid >> 5, nwarps = nthreads >> 5;
   if (out.xi) {
     const int ngrp = nk / 64;
-    for (int e = tid; e < ngrp * ntok; e += nthreads) {
+    for (int e = wid; e < ngrp * ntok; e += nwarps) {
       const int gq = e / ntok, t = e % ntok;
-      float amax = 0.f;
-      for (int i = 0; i < 64; ++i) amax = fmaxf(amax, fabsf(val(gq * 64 + i, t)));
+      float amax = fmaxf(fabsf(val(gq * 64 + lane, t)), fabsf(val(gq * 64 + 32 + lane, t)));
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
       const float s = amax / 127.0f;
-      scratch[e] = s;
-      const int kg = k_base + gq * 64;
-      xc_put(out.xc, nt_total, t_base + t, kg >> 8, (kg & 255) >> 6, s);
+      if (lane == 0) {
+        scratch[e] = s;
+        const int kg = k_base + gq * 64;
+        xc_put(out.xc, nt_total, t_base + t, kg >> 8, (kg & 255) >> 6, s);
+      }
     }
     sync();
     const int n_e = (nk / 32) * ntok * 4;
@@ -141,13 +147,15 @@ __device__ void frags_write(const float* T, int sk, int st, int nk, int ntok, in
   }
   if (out.xs) {
     const int n_s = (nk / 32) * ntok;
-    for (int e = tid; e < n_s; e += nthreads) {
+    for (int e = wid; e < n_s; e += nwarps) {
       const int jl = e / ntok, t = e % ntok;
-      float s = 0.f;
-#pragma unroll 8
-      for (int i = 0; i < 32; ++i) s += val(jl * 32 + i, t);
-      const int kg = k_base + jl * 32;
-      xs_put(out.xs, nt_total, t_base + t, kg >> 8, (kg & 255) >> 5, s);
+      float s = val(jl * 32 + lane, t);
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+      if (lane == 0) {
+        const int kg = k_base + jl * 32;
+        xs_put(out.xs, nt_total, t_base + t, kg >> 8, (kg & 255) >> 5, s);
+      }
     }
   }
   sync();

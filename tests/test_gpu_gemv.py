@@ -105,6 +105,22 @@ def test_gemv_shapes_q4k(ctx, oracle, n, k):
         _check_gemv(O, O.Q4K, blocks, x, got, m, n, k)
 
 
+@pytest.mark.parametrize("n,k", [(40, 64), (300, 544), (17, 32)])
+def test_gemv_q80_k_not_multiple_of_256(ctx, oracle, n, k):
+    """Q8_0 takes any K that is a multiple of 32 (fused.rs:2451-2554); rows are
+    zero-padded to the next 256 columns inside the library."""
+    O = oracle
+    import realm_b200 as rb
+    rng = np.random.default_rng(n * k)
+    blocks = O.quantize(O.Q80, rng.normal(0, 0.02, size=(n, k)).astype(np.float32))
+    for m in (1, 5):
+        x = rng.normal(0, 1, size=(m, k)).astype(np.float32)
+        _check_gemv(O, O.Q80, blocks, x, ctx.fused_dequant_matmul(O.Q80, blocks, x, m, n, k), m, n, k)
+        w = rb.Weight(ctx, rb.Q8_0, n, k, blocks)
+        _check_gemv(O, O.Q80, blocks, x, w.matmul(x, m), m, n, k)
+        w.free()
+
+
 def test_gemv_q6k_lm_head_shape(ctx, oracle):
     O = oracle
     rng = np.random.default_rng(7)

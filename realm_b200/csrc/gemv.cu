@@ -490,10 +490,9 @@ struct RingPos {
 
 // End of a row-group segment: a whole row group goes straight to the
 // epilogue; a partial one is deposited, and the last of its contributors sums
-// them and runs the epilogue. Kept out of line so that its registers do not
-// compete with the tile loop's.
+// them and runs the epilogue.
 template <int NT>
-__device__ __noinline__ void finish_segment(const GemvArgs& a, int p, int n_phases, const PhaseRange& pr, int rg,
+__device__ __forceinline__ void finish_segment(const GemvArgs& a, int p, int n_phases, const PhaseRange& pr, int rg,
                                             int sb, int first_rg, float (&acc)[NT][4], const float* inv_rms,
                                             float* red, float* T) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -547,22 +546,16 @@ __device__ __noinline__ void finish_segment(const GemvArgs& a, int p, int n_phas
         const int sl = cc == cf ? sl_cf : slot_base;
         return a.partials + ((((size_t)cc * nslots + sl) * kConsumerWarps + warp) * NT) * 128 + lane * 4;
       };
-      // loads issued in batches of 8, summed in contributor order (deterministic)
-      for (long long c0 = cf; c0 <= cl; c0 += 8) {
+      // summed in contributor order (deterministic)
+      for (long long cc = cf; cc <= cl; ++cc) {
+        const float* src = src_of(cc);
 #pragma unroll
         for (int nt = 0; nt < NT; ++nt) {
-          float4 q[8];
-#pragma unroll
-          for (int j = 0; j < 8; ++j)
-            if (c0 + j <= cl) q[j] = ldcg4(src_of(c0 + j) + nt * 128);
-#pragma unroll
-          for (int j = 0; j < 8; ++j)
-            if (c0 + j <= cl) {
-              acc[nt][0] += q[j].x;
-              acc[nt][1] += q[j].y;
-              acc[nt][2] += q[j].z;
-              acc[nt][3] += q[j].w;
-            }
+          const float4 q = ldcg4(src + nt * 128);
+          acc[nt][0] += q.x;
+          acc[nt][1] += q.y;
+          acc[nt][2] += q.z;
+          acc[nt][3] += q.w;
         }
       }
       if (stamp) RB_TS(p, 11);

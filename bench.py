@@ -384,6 +384,8 @@ def run_reference(args):
 
 def run_case(args):
     """Small workloads for ncu captures (no timing, no JSON line).
+    attn: 6 calls of the config-2 paged attention (16 tenants, GQA 4, hd 128,
+    contexts U[512, 8192], 0.3 GB of fp16 K/V).
     gemv: 8 launches of the Q4_K gate|up GEMV (22016 x 4096, M = 8) over 8
     weight copies (400 MB, > L2). decode: the bench model, 8 tenants with
     caches of U[128, 512] random entries, then 3 decode steps of 194 launches each."""
@@ -391,6 +393,26 @@ def run_case(args):
     import realm_b200 as rb
     dev = torch.device("cuda", 0)
     ctx = rb.Context(0)
+    if args.case == "attn":
+        # config 2 (as attention_roofline): 6 calls of the paged attention kernel
+        rng = np.random.default_rng(2)
+        n_t, hq, hkv, hd = 16, 32, 8, 128
+        ctxs = rng.integers(512, 8193, n_t)
+        pool = ctx.kv_pool(1, hkv, hd, rb.F16, n_pages=int(sum((c + 17) // 16 for c in ctxs)) + 16,
+                           max_tenants=n_t, max_seq=8208)
+        pool.shuffle(2)
+        for t in range(n_t):
+            pool.create(t)
+            pool.append(t, 0, torch.randn(int(ctxs[t]), hkv * hd, device=dev),
+                        torch.randn(int(ctxs[t]), hkv * hd, device=dev))
+        q = torch.randn(n_t, hq * hd, device=dev)
+        out = torch.empty(n_t, hq * hd, device=dev)
+        for _ in range(6):
+            pool.attention_forward(0, list(range(n_t)), q, hq, 1 / np.sqrt(hd),
+                                   positions=[int(c) - 1 for c in ctxs], out=out)
+        torch.cuda.synchronize(dev)
+        print("attn case done", flush=True)
+        return
     if args.case == "gemv":
         n, k, m = 2 * CFG["ffn"], CFG["hidden"], TENANTS_PER_GPU
         ws = []
@@ -429,7 +451,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU-baseline leg")
-    ap.add_argument("--case", choices=["gemv", "decode"],
+    ap.add_argument("--case", choices=["gemv", "decode", "attn"],
                     help="profiling case for ncu: run a small workload of one kernel family and exit")
     args = ap.parse_args()
     if args.case:

@@ -5,13 +5,17 @@
 // crates/realm-models/src/attention_stub/mod.rs:42-158). The reference has no paged
 // cache; here K/V live in 16-token pages reached through a per-tenant page table.
 //
-// Decode attention: a work unit is (query row, kv head, split of 16 pages). Each of
-// the CTA's 4 warps streams its share of the split's pages (K and V blocks of one
-// kv head, contiguous) with the bulk-copy engine into a private ring, so every KV
-// page is read from HBM once per GQA group, and keeps an online-softmax state
-// (max, sum, output) for all n_rep query heads of the group. Warps merge through
-// shared memory; splits of one (row, kv head) are merged by the last CTA to finish
-// in a fixed order (deterministic, no spin waits).
+// Decode attention, stream-K over pages: the 16-token pages of every
+// (query row, kv head) pair form one sequence and each CTA takes an equal
+// contiguous share, so every CTA streams the same number of bytes whatever the
+// context lengths. Within a pair's segment each of the CTA's 4 warps streams
+// every 4th page (K and V blocks of one kv head, contiguous) with the
+// bulk-copy engine into a private ring, so every KV page is read from HBM once
+// per GQA group. With fp16 K/V the scores and P.V run on the tensor cores
+// (mma.sync m16n8k16; query and probabilities as fp16 hi + lo), with an online
+// softmax per query head in fp32; fp32 K/V take a scalar path. Warps merge
+// through shared memory; a pair split over CTAs is combined by the last CTA to
+// finish it, in CTA order (deterministic, no spin waits).
 #include "attention.cuh"
 #include "common.cuh"
 #include "xfrag.cuh"
@@ -23,7 +27,7 @@ namespace {
 constexpr int kAttnWarps = 4;
 constexpr int kMaxRows = 64;
 
-__host__ __device__ constexpr int attn_ring(int hd, int f16) { return (hd == 128 && !f16) ? 2 : 3; }
+__host__ __device__ constexpr int attn_ring(int hd, int f16) { return (hd == 128 && !f16) ? 1 : 3; }
 
 template <int HD, int F16>
 struct AttnCfg {
@@ -37,7 +41,7 @@ template <int HD, int NREP, int F16>
 __host__ __device__ constexpr int attn_smem_bytes() {
   return kAttnWarps * AttnCfg<HD, F16>::NSW * AttnCfg<HD, F16>::STAGE  // rings
          + NREP * HD * 4                                               // q
-         + kAttnWarps * NREP * 16 * 4                                  // probabilities
+         + kAttnWarps * (NREP > 8 ? NREP : 8) * 16 * 4                 // probabilities
          + kAttnWarps * NREP * (HD + 2) * 4                            // warp merge
          + kAttnWarps * AttnCfg<HD, F16>::NSW * 8                      // mbarriers
          + kMaxRows * 8 + 64;                                          // row tables
@@ -60,8 +64,30 @@ __device__ __forceinline__ void to_f32(const uint4 raw, float* f, int f16) {
   }
 }
 
+__device__ __forceinline__ void ldsm_x4(uint32_t r[4], const void* p) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(smem_u32(p)));
+}
+__device__ __forceinline__ void ldsm_x4_trans(uint32_t r[4], const void* p) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(smem_u32(p)));
+}
+// two fp32 values -> packed fp16 hi and lo parts (x ~= hi + lo, ~22 bits)
+__device__ __forceinline__ void pack_hilo(float x0, float x1, uint32_t& hi, uint32_t& lo) {
+  __half h0, l0, h1, l1;
+  split_hilo(x0, h0, l0);
+  split_hilo(x1, h1, l1);
+  hi = (uint32_t)__half_as_ushort(h0) | ((uint32_t)__half_as_ushort(h1) << 16);
+  lo = (uint32_t)__half_as_ushort(l0) | ((uint32_t)__half_as_ushort(l1) << 16);
+}
+
+// A segment: this CTA's share of one (row, kv head) pair, pages [p_begin, p_end)
+// of the pair; x0, x1 its place in the global page sequence, ps, pe the pair's.
 struct UnitInfo {
-  int row, kvh, split, p_begin, p_end, len;
+  int row, kvh, p_begin, p_end, len;
+  long long x0, x1, ps, pe;
   bool valid;
 };
 
@@ -73,9 +99,9 @@ __global__ void __launch_bounds__(kAttnWarps * 32) attn_kernel(const AttnArgs a)
   uint8_t* rings = smem;
   float* qs = reinterpret_cast<float*>(rings + kAttnWarps * NSW * C::STAGE);
   float* pb = qs + NREP * HD;
-  float* mrg = pb + kAttnWarps * NREP * 16;
+  float* mrg = pb + kAttnWarps * (NREP > 8 ? NREP : 8) * 16;
   uint64_t* bars = reinterpret_cast<uint64_t*>(mrg + kAttnWarps * NREP * (HD + 2));
-  int* row_units = reinterpret_cast<int*>(bars + kAttnWarps * NSW);  // prefix of units per row
+  long long* row_pages = reinterpret_cast<long long*>(bars + kAttnWarps * NSW);  // prefix of pages per row
   __shared__ int s_last;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -88,34 +114,40 @@ __global__ void __launch_bounds__(kAttnWarps * 32) attn_kernel(const AttnArgs a)
   }
   pdl_launch_dependents();
   pdl_wait();
-  // per-row unit prefix (units = n_kv * splits)
+  // Stream-K over pages: the pages of all (row, kv head) pairs form one
+  // sequence (row-major, kv head, page); CTA b takes [P b / Gp, P (b+1) / Gp).
   if (threadIdx.x == 0) {
-    int acc = 0;
+    long long acc = 0;
     for (int r = 0; r < a.n_rows; ++r) {
-      row_units[r] = acc;
-      const int np = (a.row_pos[r] >> 4) + 1;
-      acc += n_kv * ((np + kAttnPagesPerSplit - 1) / kAttnPagesPerSplit);
+      row_pages[r] = acc;
+      acc += (long long)n_kv * ((a.row_pos[r] >> 4) + 1);
     }
-    row_units[a.n_rows] = acc;
+    row_pages[a.n_rows] = acc;
   }
   __syncthreads();
-  const int total = row_units[a.n_rows];
+  const long long P = row_pages[a.n_rows];
+  // only the first Gp = min(G, P) CTAs take pages, so that none of them is empty
+  const long long Gp = P < G ? P : G;
+  const long long P0 = (long long)blockIdx.x < Gp ? P * blockIdx.x / Gp : P;
+  const long long P1 = (long long)blockIdx.x < Gp ? P * (blockIdx.x + 1) / Gp : P;
+  auto cta_start = [&](long long cc) { return P * cc / Gp; };
 
-  auto decode = [&](int it) -> UnitInfo {
+  auto seg_at = [&](long long x) -> UnitInfo {
     UnitInfo ui;
-    const int u = blockIdx.x + it * G;
-    ui.valid = u < total;
+    ui.valid = x < P1;
     if (!ui.valid) return ui;
     int r = 0;
-    while (r + 1 < a.n_rows && row_units[r + 1] <= u) ++r;
+    while (r + 1 < a.n_rows && row_pages[r + 1] <= x) ++r;
     const int np = (a.row_pos[r] >> 4) + 1;
-    const int ns = (np + kAttnPagesPerSplit - 1) / kAttnPagesPerSplit;
-    const int local = u - row_units[r];
+    const long long local = x - row_pages[r];
     ui.row = r;
-    ui.kvh = local / ns;
-    ui.split = local % ns;
-    ui.p_begin = ui.split * kAttnPagesPerSplit;
-    ui.p_end = min(np, ui.p_begin + kAttnPagesPerSplit);
+    ui.kvh = (int)(local / np);
+    ui.ps = row_pages[r] + (long long)ui.kvh * np;
+    ui.pe = ui.ps + np;
+    ui.x0 = x;
+    ui.x1 = P1 < ui.pe ? P1 : ui.pe;
+    ui.p_begin = (int)(x - ui.ps);
+    ui.p_end = (int)(ui.x1 - ui.ps);
     ui.len = a.row_pos[r] + 1;
     return ui;
   };
@@ -130,21 +162,19 @@ __global__ void __launch_bounds__(kAttnWarps * 32) attn_kernel(const AttnArgs a)
   };
 
   // producer iterator (uniform across the warp): CTA unit iteration + page
-  int pit = 0, pp = -1;
-  UnitInfo pu = decode(0);
+  int pp = -1;
+  UnitInfo pu = seg_at(P0);
   if (pu.valid) pp = pu.p_begin + warp;
   auto prod_advance = [&]() {
     pp += kAttnWarps;
     while (pu.valid && pp >= pu.p_end) {
-      ++pit;
-      pu = decode(pit);
+      pu = seg_at(pu.x1);
       pp = pu.valid ? pu.p_begin + warp : -1;
     }
   };
   // position the producer on its first item
   while (pu.valid && pp >= pu.p_end) {
-    ++pit;
-    pu = decode(pit);
+    pu = seg_at(pu.x1);
     pp = pu.valid ? pu.p_begin + warp : -1;
   }
   int issued = 0, consumed = 0;
@@ -166,121 +196,220 @@ __global__ void __launch_bounds__(kAttnWarps * 32) attn_kernel(const AttnArgs a)
   bool alive = true;
   const int j = lane & 15, hh = lane >> 4;
   constexpr int DPL = HD / 32;  // output dims per lane
-  for (int it = 0;; ++it) {
-    const UnitInfo ui = decode(it);
-    if (!ui.valid) break;
+  for (long long x = P0; x < P1;) {
+    const UnitInfo ui = seg_at(x);
+    x = ui.x1;
     // q of the n_rep heads that share this kv head
     for (int i = threadIdx.x; i < NREP * HD; i += blockDim.x)
       qs[i] = a.q[(size_t)ui.row * a.ldq + (size_t)ui.kvh * NREP * HD + i];
     __syncthreads();
 
-    float m[NREP], l[NREP], o[NREP][DPL];
+    if constexpr (F16) {
+      // Tensor-core path (fp16 K/V): per page of 16 tokens, S = K Q^T with
+      // mma m16n8k16 (A = K tile by ldmatrix, B = the n_rep query heads as
+      // fp16 hi + lo, ~22 bits, scale folded in), online softmax per head in
+      // fp32, then O^T += V^T P^T (A = V tile by ldmatrix.trans, B = P as
+      // fp16 hi + lo). Lane (g = lane/4, c = lane%4) owns heads 2c, 2c+1.
+      constexpr int KS = HD / 16;
+      const int g = lane >> 2, c = lane & 3;
+      uint32_t qb[KS][2][2];  // [k-step][hi, lo][b0, b1]
 #pragma unroll
-    for (int r = 0; r < NREP; ++r) {
-      m[r] = -INFINITY;
-      l[r] = 0.f;
+      for (int ks = 0; ks < KS; ++ks)
 #pragma unroll
-      for (int d = 0; d < DPL; ++d) o[r][d] = 0.f;
-    }
-    for (int p = ui.p_begin + warp; p < ui.p_end; p += kAttnWarps) {
-      issue_upto(consumed + NSW);
-      const int s = consumed % NSW;
-      if (alive) alive = mbar_wait(&mybars[s], (consumed / NSW) & 1, a.err, DEV_TIMEOUT_FULL);
-      const uint8_t* kb = myring + s * C::STAGE;
-      const uint8_t* vb = kb + C::BLK;
-      // ---- scores: lane (j, hh) covers token j, dims [hh*HD/2, (hh+1)*HD/2)
-      float dot[NREP];
+        for (int b = 0; b < 2; ++b) {
+          const int d = ks * 16 + 2 * c + 8 * b;
+          const float x0 = g < NREP ? qs[g * HD + d] * a.scale : 0.f;
+          const float x1 = g < NREP ? qs[g * HD + d + 1] * a.scale : 0.f;
+          pack_hilo(x0, x1, qb[ks][0][b], qb[ks][1][b]);
+        }
+      float mh[2] = {-INFINITY, -INFINITY}, lh[2] = {0.f, 0.f};
+      float ot[KS][4];
 #pragma unroll
-      for (int r = 0; r < NREP; ++r) dot[r] = 0.f;
-      constexpr int EPV = 16 / C::ESZ;  // elements per 16-byte vector
-#pragma unroll 4
-      for (int cidx = 0; cidx < (HD / 2) / EPV; ++cidx) {
-        const int d0 = hh * (HD / 2) + cidx * EPV;
-        const uint4 raw = *reinterpret_cast<const uint4*>(kb + ((size_t)j * HD + d0) * C::ESZ);
-        float kf[8];
-        to_f32(raw, kf, F16);
+      for (int mt = 0; mt < KS; ++mt) ot[mt][0] = ot[mt][1] = ot[mt][2] = ot[mt][3] = 0.f;
+      float* pt = pb + warp * 16 * 8;  // [16 tokens][8 heads] transpose buffer
+      const int mi = lane >> 3, rr = lane & 7;
+      for (int p = ui.p_begin + warp; p < ui.p_end; p += kAttnWarps) {
+        issue_upto(consumed + NSW);
+        const int s = consumed % NSW;
+        if (alive) alive = mbar_wait(&mybars[s], (consumed / NSW) & 1, a.err, DEV_TIMEOUT_FULL);
+        const uint8_t* kb = myring + s * C::STAGE;
+        const uint8_t* vb = kb + C::BLK;
+        float sc[4] = {0.f, 0.f, 0.f, 0.f};  // (tok g, head 2c), (g, 2c+1), (g+8, 2c), (g+8, 2c+1)
 #pragma unroll
-        for (int r = 0; r < NREP; ++r) {
+        for (int ks = 0; ks < KS; ++ks) {
+          uint32_t af[4];
+          ldsm_x4(af, kb + ((size_t)(rr + (mi & 1) * 8) * HD + ks * 16 + (mi >> 1) * 8) * 2);
+          mma_16816(sc, af, qb[ks][0][0], qb[ks][0][1]);
+          mma_16816(sc, af, qb[ks][1][0], qb[ks][1][1]);
+        }
+        const bool v0 = p * 16 + g < ui.len, v1 = p * 16 + g + 8 < ui.len;
+        float alpha[2], pr[4];
 #pragma unroll
-          for (int e = 0; e < EPV; e += 4) {
-            const float4 qv = *reinterpret_cast<const float4*>(qs + r * HD + d0 + e);
-            dot[r] = fmaf(qv.x, kf[e], dot[r]);
-            dot[r] = fmaf(qv.y, kf[e + 1], dot[r]);
-            dot[r] = fmaf(qv.z, kf[e + 2], dot[r]);
-            dot[r] = fmaf(qv.w, kf[e + 3], dot[r]);
+        for (int h = 0; h < 2; ++h) {
+          const float s0 = v0 ? sc[h] : -INFINITY, s1 = v1 ? sc[2 + h] : -INFINITY;
+          float mx = fmaxf(s0, s1);
+          mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 4));
+          mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 8));
+          mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 16));
+          const float mn = fmaxf(mh[h], mx);
+          alpha[h] = mh[h] == -INFINITY ? 0.f : expf(mh[h] - mn);
+          pr[h] = v0 ? expf(s0 - mn) : 0.f;
+          pr[2 + h] = v1 ? expf(s1 - mn) : 0.f;
+          float ps = pr[h] + pr[2 + h];
+          ps += __shfl_xor_sync(0xffffffffu, ps, 4);
+          ps += __shfl_xor_sync(0xffffffffu, ps, 8);
+          ps += __shfl_xor_sync(0xffffffffu, ps, 16);
+          lh[h] = lh[h] * alpha[h] + ps;
+          mh[h] = mn;
+        }
+        // P^T as the B operand: lane (g, c) needs heads g, tokens 2c, 2c+1, 2c+8, 2c+9
+        pt[g * 8 + 2 * c] = pr[0];
+        pt[g * 8 + 2 * c + 1] = pr[1];
+        pt[(g + 8) * 8 + 2 * c] = pr[2];
+        pt[(g + 8) * 8 + 2 * c + 1] = pr[3];
+        __syncwarp();
+        uint32_t pbh0, pbl0, pbh1, pbl1;
+        pack_hilo(pt[(2 * c) * 8 + g], pt[(2 * c + 1) * 8 + g], pbh0, pbl0);
+        pack_hilo(pt[(2 * c + 8) * 8 + g], pt[(2 * c + 9) * 8 + g], pbh1, pbl1);
+        __syncwarp();
+#pragma unroll
+        for (int mt = 0; mt < KS; ++mt) {
+          ot[mt][0] *= alpha[0];
+          ot[mt][1] *= alpha[1];
+          ot[mt][2] *= alpha[0];
+          ot[mt][3] *= alpha[1];
+          uint32_t af[4];
+          ldsm_x4_trans(af, vb + ((size_t)(rr + (mi >> 1) * 8) * HD + mt * 16 + (mi & 1) * 8) * 2);
+          mma_16816(ot[mt], af, pbh0, pbh1);
+          mma_16816(ot[mt], af, pbl0, pbl1);
+        }
+        ++consumed;
+      }
+      // this warp's partial: O^T fragments -> mrg[head][dim], then m, l per head
+#pragma unroll
+      for (int mt = 0; mt < KS; ++mt)
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const int head = 2 * c + (q & 1), dim = mt * 16 + g + ((q & 2) ? 8 : 0);
+          if (head < NREP) mrg[(warp * NREP + head) * (HD + 2) + dim] = ot[mt][q];
+        }
+      if (g == 0)
+#pragma unroll
+        for (int h = 0; h < 2; ++h)
+          if (2 * c + h < NREP) {
+            mrg[(warp * NREP + 2 * c + h) * (HD + 2) + HD] = mh[h];
+            mrg[(warp * NREP + 2 * c + h) * (HD + 2) + HD + 1] = lh[h];
+          }
+    } else {
+      float m[NREP], l[NREP], o[NREP][DPL];
+  #pragma unroll
+      for (int r = 0; r < NREP; ++r) {
+        m[r] = -INFINITY;
+        l[r] = 0.f;
+  #pragma unroll
+        for (int d = 0; d < DPL; ++d) o[r][d] = 0.f;
+      }
+      for (int p = ui.p_begin + warp; p < ui.p_end; p += kAttnWarps) {
+        issue_upto(consumed + NSW);
+        const int s = consumed % NSW;
+        if (alive) alive = mbar_wait(&mybars[s], (consumed / NSW) & 1, a.err, DEV_TIMEOUT_FULL);
+        const uint8_t* kb = myring + s * C::STAGE;
+        const uint8_t* vb = kb + C::BLK;
+        // ---- scores: lane (j, hh) covers token j, dims [hh*HD/2, (hh+1)*HD/2)
+        float dot[NREP];
+  #pragma unroll
+        for (int r = 0; r < NREP; ++r) dot[r] = 0.f;
+        constexpr int EPV = 16 / C::ESZ;  // elements per 16-byte vector
+  #pragma unroll 4
+        for (int cidx = 0; cidx < (HD / 2) / EPV; ++cidx) {
+          const int d0 = hh * (HD / 2) + cidx * EPV;
+          const uint4 raw = *reinterpret_cast<const uint4*>(kb + ((size_t)j * HD + d0) * C::ESZ);
+          float kf[8];
+          to_f32(raw, kf, F16);
+  #pragma unroll
+          for (int r = 0; r < NREP; ++r) {
+  #pragma unroll
+            for (int e = 0; e < EPV; e += 4) {
+              const float4 qv = *reinterpret_cast<const float4*>(qs + r * HD + d0 + e);
+              dot[r] = fmaf(qv.x, kf[e], dot[r]);
+              dot[r] = fmaf(qv.y, kf[e + 1], dot[r]);
+              dot[r] = fmaf(qv.z, kf[e + 2], dot[r]);
+              dot[r] = fmaf(qv.w, kf[e + 3], dot[r]);
+            }
           }
         }
+        const int tok = p * 16 + j;
+        const bool valid = tok < ui.len;
+        float alpha[NREP];
+  #pragma unroll
+        for (int r = 0; r < NREP; ++r) {
+          const float sc = (dot[r] + __shfl_xor_sync(0xffffffffu, dot[r], 16)) * a.scale;
+          float pm = valid ? sc : -INFINITY;
+          pm = fmaxf(pm, __shfl_xor_sync(0xffffffffu, pm, 1));
+          pm = fmaxf(pm, __shfl_xor_sync(0xffffffffu, pm, 2));
+          pm = fmaxf(pm, __shfl_xor_sync(0xffffffffu, pm, 4));
+          pm = fmaxf(pm, __shfl_xor_sync(0xffffffffu, pm, 8));
+          const float mn = fmaxf(m[r], pm);
+          alpha[r] = expf(m[r] - mn);
+          const float pj = valid ? expf(sc - mn) : 0.f;
+          float ps = pj;
+          ps += __shfl_xor_sync(0xffffffffu, ps, 1);
+          ps += __shfl_xor_sync(0xffffffffu, ps, 2);
+          ps += __shfl_xor_sync(0xffffffffu, ps, 4);
+          ps += __shfl_xor_sync(0xffffffffu, ps, 8);
+          l[r] = l[r] * alpha[r] + ps;
+          m[r] = mn;
+          if (hh == 0) pb[(warp * NREP + r) * 16 + j] = pj;
+        }
+        __syncwarp();
+        // ---- PV: lane owns dims [lane*DPL, lane*DPL + DPL)
+  #pragma unroll
+        for (int r = 0; r < NREP; ++r)
+  #pragma unroll
+          for (int d = 0; d < DPL; ++d) o[r][d] *= alpha[r];
+        const int nvalid = min(16, ui.len - p * 16);
+        for (int t = 0; t < nvalid; ++t) {
+          float vf[DPL];
+          if (F16) {
+            const __half* vh = reinterpret_cast<const __half*>(vb) + (size_t)t * HD + lane * DPL;
+  #pragma unroll
+            for (int d = 0; d < DPL; d += 2) {
+              const float2 f = __half22float2(*reinterpret_cast<const __half2*>(vh + d));
+              vf[d] = f.x;
+              vf[d + 1] = f.y;
+            }
+          } else {
+            const float* vp = reinterpret_cast<const float*>(vb) + (size_t)t * HD + lane * DPL;
+  #pragma unroll
+            for (int d = 0; d < DPL; ++d) vf[d] = vp[d];
+          }
+  #pragma unroll
+          for (int r = 0; r < NREP; ++r) {
+            const float pj = pb[(warp * NREP + r) * 16 + t];
+  #pragma unroll
+            for (int d = 0; d < DPL; ++d) o[r][d] = fmaf(pj, vf[d], o[r][d]);
+          }
+        }
+        __syncwarp();
+        ++consumed;
       }
-      const int tok = p * 16 + j;
-      const bool valid = tok < ui.len;
-      float alpha[NREP];
+      // ---- this warp's partial -> mrg
 #pragma unroll
       for (int r = 0; r < NREP; ++r) {
-        const float sc = (dot[r] + __shfl_xor_sync(0xffffffffu, dot[r], 16)) * a.scale;
-        float pm = valid ? sc : -INFINITY;
-        pm = fmaxf(pm, __shfl_xor_sync(0xffffffffu, pm, 1));
-        pm = fmaxf(pm, __shfl_xor_sync(0xffffffffu, pm, 2));
-        pm = fmaxf(pm, __shfl_xor_sync(0xffffffffu, pm, 4));
-        pm = fmaxf(pm, __shfl_xor_sync(0xffffffffu, pm, 8));
-        const float mn = fmaxf(m[r], pm);
-        alpha[r] = expf(m[r] - mn);
-        const float pj = valid ? expf(sc - mn) : 0.f;
-        float ps = pj;
-        ps += __shfl_xor_sync(0xffffffffu, ps, 1);
-        ps += __shfl_xor_sync(0xffffffffu, ps, 2);
-        ps += __shfl_xor_sync(0xffffffffu, ps, 4);
-        ps += __shfl_xor_sync(0xffffffffu, ps, 8);
-        l[r] = l[r] * alpha[r] + ps;
-        m[r] = mn;
-        if (hh == 0) pb[(warp * NREP + r) * 16 + j] = pj;
-      }
-      __syncwarp();
-      // ---- PV: lane owns dims [lane*DPL, lane*DPL + DPL)
+        float* w = mrg + (warp * NREP + r) * (HD + 2);
 #pragma unroll
-      for (int r = 0; r < NREP; ++r)
-#pragma unroll
-        for (int d = 0; d < DPL; ++d) o[r][d] *= alpha[r];
-      const int nvalid = min(16, ui.len - p * 16);
-      for (int t = 0; t < nvalid; ++t) {
-        float vf[DPL];
-        if (F16) {
-          const __half* vh = reinterpret_cast<const __half*>(vb) + (size_t)t * HD + lane * DPL;
-#pragma unroll
-          for (int d = 0; d < DPL; d += 2) {
-            const float2 f = __half22float2(*reinterpret_cast<const __half2*>(vh + d));
-            vf[d] = f.x;
-            vf[d + 1] = f.y;
-          }
-        } else {
-          const float* vp = reinterpret_cast<const float*>(vb) + (size_t)t * HD + lane * DPL;
-#pragma unroll
-          for (int d = 0; d < DPL; ++d) vf[d] = vp[d];
-        }
-#pragma unroll
-        for (int r = 0; r < NREP; ++r) {
-          const float pj = pb[(warp * NREP + r) * 16 + t];
-#pragma unroll
-          for (int d = 0; d < DPL; ++d) o[r][d] = fmaf(pj, vf[d], o[r][d]);
+        for (int d = 0; d < DPL; ++d) w[lane * DPL + d] = o[r][d];
+        if (lane == 0) {
+          w[HD] = m[r];
+          w[HD + 1] = l[r];
         }
       }
-      __syncwarp();
-      ++consumed;
     }
     // ---- merge the warps
-#pragma unroll
-    for (int r = 0; r < NREP; ++r) {
-      float* w = mrg + (warp * NREP + r) * (HD + 2);
-#pragma unroll
-      for (int d = 0; d < DPL; ++d) w[lane * DPL + d] = o[r][d];
-      if (lane == 0) {
-        w[HD] = m[r];
-        w[HD + 1] = l[r];
-      }
-    }
     __syncthreads();
-    const int np_row = (a.row_pos[ui.row] >> 4) + 1;
-    const int nsplit = (np_row + kAttnPagesPerSplit - 1) / kAttnPagesPerSplit;
-    const size_t slot = ((size_t)ui.row * n_kv + ui.kvh) * a.max_splits + ui.split;
+    // a pair split over CTAs: slot 0 for the CTA's first segment, 1 for its last
+    const bool whole = ui.x0 == ui.ps && ui.x1 == ui.pe;
+    const size_t slot = (size_t)blockIdx.x * 2 + (ui.x0 == P0 ? 0 : 1);
     // Final values go to shared memory (the q buffer is free now), then out to the
     // fp32 output and / or the activation fragments of the o-proj GEMV.
     float* ofin = qs;
@@ -307,7 +436,7 @@ __global__ void __launch_bounds__(kAttnWarps * 32) attn_kernel(const AttnArgs a)
         O += ww[d] * f;
       }
     };
-    if (nsplit == 1) {
+    if (whole) {
       for (int i = threadIdx.x; i < NREP * HD; i += blockDim.x) {
         float M, Lsum, O;
         merge_warps(i, M, Lsum, O);
@@ -326,25 +455,59 @@ __global__ void __launch_bounds__(kAttnWarps * 32) attn_kernel(const AttnArgs a)
           __stcg(dst + HD + 1, Lsum);
         }
       }
-      __threadfence();
-      __syncthreads();
-      if (threadIdx.x == 0)
-        s_last = atomicAdd(a.counters + ui.row * n_kv + ui.kvh, 1) == nsplit - 1;
+      // contributors: the CTAs whose page ranges intersect the pair
+      long long cf = ui.ps * Gp / P, cl = (ui.pe - 1) * Gp / P;
+      while (cf + 1 < Gp && cta_start(cf + 1) <= ui.ps) ++cf;
+      while (cf > 0 && cta_start(cf) > ui.ps) --cf;
+      while (cl + 1 < Gp && cta_start(cl + 1) <= ui.pe - 1) ++cl;
+      while (cl > 0 && cta_start(cl) > ui.pe - 1) --cl;
+      const int ncon = (int)(cl - cf + 1);
+      __syncthreads();  // partial stores of this CTA before thread 0's release
+      if (threadIdx.x == 0) {
+        __threadfence();
+        const int last = atomicAdd(a.counters + ui.row * n_kv + ui.kvh, 1) == ncon - 1;
+        if (last) __threadfence();
+        s_last = last;
+      }
       __syncthreads();
       if (s_last) {
-        __threadfence();
-        const size_t base = ((size_t)ui.row * n_kv + ui.kvh) * a.max_splits;
+        // contributor cc's partial is in its slot 0 iff the pair is its first segment
+        auto part = [&](int j) {
+          const long long cc = cf + j;
+          const int sl = cta_start(cc) >= ui.ps ? 0 : 1;
+          return a.partials + ((size_t)cc * 2 + sl) * NREP * (HD + 2);
+        };
+        // (m, l) of every contributor and head into shared memory (mrg is free)
+        float* tab = mrg;  // [ncon][NREP][2]
+        const bool fits = ncon * NREP * 2 <= kAttnWarps * NREP * (HD + 2);
+        if (fits)
+          for (int e = threadIdx.x; e < ncon * NREP; e += blockDim.x) {
+            const float* src = part(e / NREP) + (e % NREP) * (HD + 2);
+            tab[2 * e] = __ldcg(src + HD);
+            tab[2 * e + 1] = __ldcg(src + HD + 1);
+          }
+        __syncthreads();
         for (int i = threadIdx.x; i < NREP * HD; i += blockDim.x) {
           const int r = i / HD, d = i % HD;
+          auto mval = [&](int j) { return fits ? tab[2 * (j * NREP + r)] : __ldcg(part(j) + r * (HD + 2) + HD); };
+          auto lval = [&](int j) { return fits ? tab[2 * (j * NREP + r) + 1] : __ldcg(part(j) + r * (HD + 2) + HD + 1); };
           float M = -INFINITY;
-          for (int s = 0; s < nsplit; ++s) M = fmaxf(M, __ldcg(a.partials + ((base + s) * NREP + r) * (HD + 2) + HD));
+          for (int j = 0; j < ncon; ++j) M = fmaxf(M, mval(j));
           float Lsum = 0.f, O = 0.f;
-          for (int s = 0; s < nsplit; ++s) {
-            const float* src = a.partials + ((base + s) * NREP + r) * (HD + 2);
-            const float ms = __ldcg(src + HD);
-            const float f = (ms == -INFINITY) ? 0.f : expf(ms - M);
-            Lsum += __ldcg(src + HD + 1) * f;
-            O += __ldcg(src + d) * f;
+          // output loads issued 8 at a time, summed in contributor order
+          for (int j0 = 0; j0 < ncon; j0 += 8) {
+            float ov[8];
+#pragma unroll
+            for (int j = 0; j < 8; ++j)
+              if (j0 + j < ncon) ov[j] = __ldcg(part(j0 + j) + r * (HD + 2) + d);
+#pragma unroll
+            for (int j = 0; j < 8; ++j)
+              if (j0 + j < ncon) {
+                const float ms = mval(j0 + j);
+                const float f = (ms == -INFINITY) ? 0.f : expf(ms - M);
+                Lsum += lval(j0 + j) * f;
+                O += ov[j] * f;
+              }
           }
           ofin[i] = Lsum > 0.f ? O / Lsum : 0.f;
         }
@@ -373,7 +536,8 @@ cudaError_t launch_attn_t(const AttnArgs& a, int num_sms, cudaStream_t s, int pd
     if (e != cudaSuccess) return e;
     attr_set |= 1ull << dev;
   }
-  const int per_sm = smem <= 110 * 1024 ? 2 : 1;
+  static_assert(smem <= 227 * 1024, "shared memory of one CTA");
+  const int per_sm = smem <= 110 * 1024 ? 2 : 1;  // never more CTAs than attn_grid() allows for
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(num_sms * per_sm);
   cfg.blockDim = dim3(kAttnWarps * 32);
@@ -436,8 +600,10 @@ __global__ void kv_gather_kernel(const KvView kv, int layer, int tenant, int len
 
 }  // namespace
 
-size_t attn_partials_floats(int max_rows, int n_kv, int n_rep, int hd, int max_splits) {
-  return (size_t)max_rows * n_kv * max_splits * n_rep * (hd + 2);
+int attn_grid(int num_sms) { return 2 * num_sms; }  // upper bound on the attention grid
+
+size_t attn_partials_floats(int num_ctas, int n_rep, int hd) {
+  return (size_t)num_ctas * 2 * n_rep * (hd + 2);
 }
 
 cudaError_t attn_launch(const AttnArgs& a, int num_sms, cudaStream_t s, int pdl) {

@@ -18,15 +18,14 @@ struct AttnArgs {
   int32_t layer = 0;
   float scale = 0.f;
   KvView kv;
-  float* partials = nullptr;       // split scratch
-  int32_t* counters = nullptr;     // [n_rows * n_kv]
-  int32_t max_splits = 0;          // partial slots per (row, kv head)
+  float* partials = nullptr;       // attn_partials_floats(grid) floats (split pairs)
+  int32_t* counters = nullptr;     // [n_rows * n_kv], zero between launches
   uint32_t* err = nullptr;
 };
 
-constexpr int kAttnPagesPerSplit = 16;  // 256 tokens per split
-
-size_t attn_partials_floats(int max_rows, int n_kv, int n_rep, int hd, int max_splits);
+// Partial-result scratch for a launch on num_ctas CTAs (attn_grid).
+size_t attn_partials_floats(int num_ctas, int n_rep, int hd);
+int attn_grid(int num_sms);
 cudaError_t attn_launch(const AttnArgs& a, int num_sms, cudaStream_t s, int pdl);
 
 // Standalone append of k/v rows ([n_rows][n_kv*hd] fp32) at (tenant, pos).

@@ -537,7 +537,6 @@ int enqueue_layer(Ctx* c, Model& M, int l, int m, const int32_t* d_tenant, const
   at.kv = P.view();
   at.partials = c->attn_partials.as<float>();
   at.counters = c->counters.as<int32_t>() + kCounters / 2;
-  at.max_splits = (cf.max_seq + 16 * kAttnPagesPerSplit - 1) / (16 * kAttnPagesPerSplit);
   at.err = c->err.as<uint32_t>();
   RB_CUDA(attn_launch(at, c->num_sms, c->stream, c->pdl ? 1 : 0));
   if (launches) ++*launches;
@@ -742,8 +741,7 @@ int pool_create(rb_ctx* c, int n_layers, int n_kv, int hd, int kv_dtype, int n_p
   for (int i = n_pages - 1; i >= 0; --i) P->free_list.push_back(i);
   P->tenants.resize(max_tenants);
   const int n_rep_max = 8;
-  const int max_splits = (max_seq + 16 * kAttnPagesPerSplit - 1) / (16 * kAttnPagesPerSplit);
-  if (int rc = ensure_attn_partials(c, attn_partials_floats(kMaxRowsAbi, n_kv, n_rep_max, hd, max_splits))) return rc;
+  if (int rc = ensure_attn_partials(c, attn_partials_floats(attn_grid(c->num_sms), n_rep_max, hd))) return rc;
   c->pools.push_back(std::move(P));
   return (int)c->pools.size() - 1;
 }
@@ -1300,7 +1298,6 @@ int32_t rb_attention_forward(rb_ctx* c, int32_t pool, uint32_t layer, uint32_t n
   at.kv = P->view();
   at.partials = c->attn_partials.as<float>();
   at.counters = c->counters.as<int32_t>() + kCounters / 2;
-  at.max_splits = (P->max_seq + 16 * kAttnPagesPerSplit - 1) / (16 * kAttnPagesPerSplit);
   at.err = c->err.as<uint32_t>();
   RB_CUDA(cudaEventRecord(c->ev0, c->stream));
   RB_CUDA(attn_launch(at, c->num_sms, c->stream, 0));

@@ -27,14 +27,19 @@ namespace {
 constexpr int kAttnWarps = 4;
 constexpr int kMaxRows = 64;
 
-__host__ __device__ constexpr int attn_ring(int hd, int f16) { return (hd == 128 && !f16) ? 1 : 3; }
+// ring stages per warp: two CTAs of 4 warps per SM keep >= ~140 KB of K/V in flight per SM
+__host__ __device__ constexpr int attn_ring(int hd, int f16) { return hd == 128 ? (f16 ? 2 : 1) : 3; }
 
 template <int HD, int F16>
 struct AttnCfg {
   static constexpr int ESZ = F16 ? 2 : 4;
-  static constexpr int BLK = 16 * HD * ESZ;  // one page of one kv head (K or V)
+  static constexpr int BLK = 16 * HD * ESZ;  // one page of one kv head (K or V), bytes copied
   static constexpr int NSW = attn_ring(HD, F16);
-  static constexpr int STAGE = 2 * BLK;
+  // fp16 tiles are stored with 16 bytes of padding per token row so that the
+  // 8 rows an ldmatrix reads fall on different banks; fp32 tiles unpadded
+  static constexpr int ROW = F16 ? HD * ESZ + 16 : HD * ESZ;  // smem bytes per token row
+  static constexpr int SBLK = 16 * ROW;                       // smem bytes per block
+  static constexpr int STAGE = 2 * SBLK;
 };
 
 template <int HD, int NREP, int F16>
@@ -85,6 +90,14 @@ __device__ __forceinline__ void pack_hilo(float x0, float x1, uint32_t& hi, uint
 
 // A segment: this CTA's share of one (row, kv head) pair, pages [p_begin, p_end)
 // of the pair; x0, x1 its place in the global page sequence, ps, pe the pair's.
+__device__ __forceinline__ void attn_stamp(const AttnArgs& a, int slot) {
+  if (a.dbg_ts && threadIdx.x == 0) {
+    unsigned long long t;
+    asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
+    a.dbg_ts[(size_t)blockIdx.x * 8 + slot] = t;
+  }
+}
+
 struct UnitInfo {
   int row, kvh, p_begin, p_end, len;
   long long x0, x1, ps, pe;
@@ -112,19 +125,28 @@ __global__ void __launch_bounds__(kAttnWarps * 32) attn_kernel(const AttnArgs a)
     for (int i = 0; i < kAttnWarps * NSW; ++i) mbar_init(&bars[i], 1);
     fence_barrier_init();
   }
+  attn_stamp(a, 0);
   pdl_launch_dependents();
-  pdl_wait();
+  // Positions, tenants and page tables are written before the previous kernel
+  // (by the host or an earlier kernel), and so are all cached K/V except the
+  // new tokens that the previous kernel appends: pages wholly below the
+  // smallest position of this launch's rows are streamed before waiting for it.
+  __shared__ int s_pos_min;
   // Stream-K over pages: the pages of all (row, kv head) pairs form one
   // sequence (row-major, kv head, page); CTA b takes [P b / Gp, P (b+1) / Gp).
   if (threadIdx.x == 0) {
     long long acc = 0;
+    int pmin = 0x7fffffff;
     for (int r = 0; r < a.n_rows; ++r) {
       row_pages[r] = acc;
       acc += (long long)n_kv * ((a.row_pos[r] >> 4) + 1);
+      pmin = min(pmin, a.row_pos[r]);
     }
     row_pages[a.n_rows] = acc;
+    s_pos_min = pmin;
   }
   __syncthreads();
+  const int pos_min = a.early_kv ? s_pos_min : -1;
   const long long P = row_pages[a.n_rows];
   // only the first Gp = min(G, P) CTAs take pages, so that none of them is empty
   const long long Gp = P < G ? P : G;
@@ -178,19 +200,33 @@ __global__ void __launch_bounds__(kAttnWarps * 32) attn_kernel(const AttnArgs a)
     pp = pu.valid ? pu.p_begin + warp : -1;
   }
   int issued = 0, consumed = 0;
-  auto issue_upto = [&](int limit) {
-    while (issued < limit && pu.valid) {
-      if (lane == 0) {
-        const int s = issued % NSW;
-        mbar_arrive_expect_tx(&mybars[s], C::STAGE);
+  auto issue_upto = [&](int limit, bool old_only = false) {
+    while (issued < limit && pu.valid && (!old_only || (pp + 1) * 16 <= pos_min)) {
+      const int s = issued % NSW;
+      if (lane == 0) mbar_arrive_expect_tx(&mybars[s], 2 * C::BLK);
+      if constexpr (F16) {
+        // one bulk copy per token row into the padded tile: lanes 0-15 K, 16-31 V
+        // (lane 0 looks up the page; the K block's address is broadcast)
+        unsigned long long kaddr = 0;
+        if (lane == 0) kaddr = reinterpret_cast<unsigned long long>(block_ptr(a.row_tenant[pu.row], pp, 0, pu.kvh));
+        kaddr = __shfl_sync(0xffffffffu, kaddr, 0);
+        const int which = lane >> 4, row = lane & 15;
+        // the V block follows the K block of the same (page, layer): n_kv blocks later
+        const uint8_t* src = reinterpret_cast<const uint8_t*>(kaddr) + (size_t)which * n_kv * C::BLK;
+        bulk_g2s(myring + s * C::STAGE + which * C::SBLK + row * C::ROW, src + (size_t)row * HD * C::ESZ,
+                 HD * C::ESZ, &mybars[s]);
+      } else if (lane == 0) {
         const int tenant = a.row_tenant[pu.row];
         bulk_g2s(myring + s * C::STAGE, block_ptr(tenant, pp, 0, pu.kvh), C::BLK, &mybars[s]);
-        bulk_g2s(myring + s * C::STAGE + C::BLK, block_ptr(tenant, pp, 1, pu.kvh), C::BLK, &mybars[s]);
+        bulk_g2s(myring + s * C::STAGE + C::SBLK, block_ptr(tenant, pp, 1, pu.kvh), C::BLK, &mybars[s]);
       }
       ++issued;
       prod_advance();
     }
   };
+  issue_upto(NSW, true);  // pages the previous kernel does not write
+  pdl_wait();
+  attn_stamp(a, 1);
   issue_upto(NSW);
 
   bool alive = true;
@@ -232,16 +268,24 @@ __global__ void __launch_bounds__(kAttnWarps * 32) attn_kernel(const AttnArgs a)
         issue_upto(consumed + NSW);
         const int s = consumed % NSW;
         if (alive) alive = mbar_wait(&mybars[s], (consumed / NSW) & 1, a.err, DEV_TIMEOUT_FULL);
+        if (consumed == 0) attn_stamp(a, 2);
         const uint8_t* kb = myring + s * C::STAGE;
-        const uint8_t* vb = kb + C::BLK;
-        float sc[4] = {0.f, 0.f, 0.f, 0.f};  // (tok g, head 2c), (g, 2c+1), (g+8, 2c), (g+8, 2c+1)
+        const uint8_t* vb = kb + C::SBLK;
+        // four independent accumulators (k-step parity x hi/lo) keep the MMA
+        // dependency chains short; summed in a fixed order
+        float sa[4][4];
+#pragma unroll
+        for (int q = 0; q < 4; ++q) sa[q][0] = sa[q][1] = sa[q][2] = sa[q][3] = 0.f;
 #pragma unroll
         for (int ks = 0; ks < KS; ++ks) {
           uint32_t af[4];
-          ldsm_x4(af, kb + ((size_t)(rr + (mi & 1) * 8) * HD + ks * 16 + (mi >> 1) * 8) * 2);
-          mma_16816(sc, af, qb[ks][0][0], qb[ks][0][1]);
-          mma_16816(sc, af, qb[ks][1][0], qb[ks][1][1]);
+          ldsm_x4(af, kb + (rr + (mi & 1) * 8) * C::ROW + (ks * 16 + (mi >> 1) * 8) * 2);
+          mma_16816(sa[(ks & 1) * 2], af, qb[ks][0][0], qb[ks][0][1]);
+          mma_16816(sa[(ks & 1) * 2 + 1], af, qb[ks][1][0], qb[ks][1][1]);
         }
+        float sc[4];  // (tok g, head 2c), (g, 2c+1), (g+8, 2c), (g+8, 2c+1)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) sc[e] = (sa[0][e] + sa[2][e]) + (sa[1][e] + sa[3][e]);
         const bool v0 = p * 16 + g < ui.len, v1 = p * 16 + g + 8 < ui.len;
         float alpha[2], pr[4];
 #pragma unroll
@@ -279,7 +323,7 @@ __global__ void __launch_bounds__(kAttnWarps * 32) attn_kernel(const AttnArgs a)
           ot[mt][2] *= alpha[0];
           ot[mt][3] *= alpha[1];
           uint32_t af[4];
-          ldsm_x4_trans(af, vb + ((size_t)(rr + (mi >> 1) * 8) * HD + mt * 16 + (mi & 1) * 8) * 2);
+          ldsm_x4_trans(af, vb + (rr + (mi >> 1) * 8) * C::ROW + (mt * 16 + (mi & 1) * 8) * 2);
           mma_16816(ot[mt], af, pbh0, pbh1);
           mma_16816(ot[mt], af, pbl0, pbl1);
         }
@@ -314,7 +358,7 @@ __global__ void __launch_bounds__(kAttnWarps * 32) attn_kernel(const AttnArgs a)
         const int s = consumed % NSW;
         if (alive) alive = mbar_wait(&mybars[s], (consumed / NSW) & 1, a.err, DEV_TIMEOUT_FULL);
         const uint8_t* kb = myring + s * C::STAGE;
-        const uint8_t* vb = kb + C::BLK;
+        const uint8_t* vb = kb + C::SBLK;
         // ---- scores: lane (j, hh) covers token j, dims [hh*HD/2, (hh+1)*HD/2)
         float dot[NREP];
   #pragma unroll
@@ -406,6 +450,7 @@ __global__ void __launch_bounds__(kAttnWarps * 32) attn_kernel(const AttnArgs a)
       }
     }
     // ---- merge the warps
+    if (x >= P1) attn_stamp(a, 3);
     __syncthreads();
     // a pair split over CTAs: slot 0 for the CTA's first segment, 1 for its last
     const bool whole = ui.x0 == ui.ps && ui.x1 == ui.pe;
@@ -517,6 +562,7 @@ __global__ void __launch_bounds__(kAttnWarps * 32) attn_kernel(const AttnArgs a)
     }
     __syncthreads();
   }
+  attn_stamp(a, 4);
   // every issued copy is consumed on the normal path; after a timed-out wait,
   // let the copies still in flight land before the CTA exits (bounded)
   if (!alive && lane == 0)
@@ -537,7 +583,9 @@ cudaError_t launch_attn_t(const AttnArgs& a, int num_sms, cudaStream_t s, int pd
     attr_set |= 1ull << dev;
   }
   static_assert(smem <= 227 * 1024, "shared memory of one CTA");
-  const int per_sm = smem <= 110 * 1024 ? 2 : 1;  // never more CTAs than attn_grid() allows for
+  // two CTAs per SM when they fit (228 KB per SM, 1 KB reserved per CTA); never
+  // more CTAs than attn_grid() allows for
+  const int per_sm = 2 * (smem + 1024) <= 228 * 1024 ? 2 : 1;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(num_sms * per_sm);
   cfg.blockDim = dim3(kAttnWarps * 32);

@@ -21,6 +21,11 @@ struct AttnArgs {
   float* partials = nullptr;       // attn_partials_floats(grid) floats (split pairs)
   int32_t* counters = nullptr;     // [n_rows * n_kv], zero between launches
   uint32_t* err = nullptr;
+  // 1: positions, tenants, page tables and every cached token below the rows'
+  // smallest position are final before the previous kernel starts, so those
+  // pages may be read before it completes (the decode step); 0: wait first
+  int32_t early_kv = 0;
+  unsigned long long* dbg_ts = nullptr;  // measurement hook: [cta][8] %globaltimer stamps (or null)
 };
 
 // Partial-result scratch for a launch on num_ctas CTAs (attn_grid).

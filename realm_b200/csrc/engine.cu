@@ -262,7 +262,7 @@ struct Ctx {
   float last_ms = 0.f;
   int last_launches = 0;
   int gemv_dbg = 0;  // measurement hook (RB_GEMV_DBG): bit 0 skips the GEMV math, bit 1 phase stamps
-  DevBuf dbg_ts;
+  DevBuf dbg_ts, attn_ts;
   // GEMVs queued to run as one multi-phase launch (chain_add / chain_flush)
   GemvArgs chain_ph[kMaxPhases];
   int chain_n = 0;
@@ -436,6 +436,30 @@ void dump_stamps(Ctx* c, int n_phases) {
     }
   }
   cudaMemset(c->dbg_ts.p, 0, ts.size() * 8);
+  if (c->attn_ts.p) {  // the most recent attention launch
+    const int GA = attn_grid(c->num_sms);
+    std::vector<unsigned long long> at((size_t)GA * 8);
+    if (cudaMemcpy(at.data(), c->attn_ts.p, at.size() * 8, cudaMemcpyDeviceToHost) != cudaSuccess) return;
+    unsigned long long a0 = ~0ull;
+    for (int b = 0; b < GA; ++b)
+      if (at[b * 8]) a0 = std::min(a0, at[b * 8]);
+    const char* an[5] = {"start", "dep_ok", "first_page", "last_merge", "done"};
+    for (int k = 0; k < 5; ++k) {
+      double mn = 1e30, mx = 0, sum = 0;
+      int n = 0;
+      for (int b = 0; b < GA; ++b) {
+        const unsigned long long v = at[b * 8 + k];
+        if (!v) continue;
+        const double d = (double)(v - a0) / 1000.0;
+        mn = std::min(mn, d);
+        mx = std::max(mx, d);
+        sum += d;
+        ++n;
+      }
+      if (n) fprintf(stderr, "[attn] %-11s n %3d min %8.2f mean %8.2f max %8.2f us\n", an[k], n, mn, sum / n, mx);
+    }
+    cudaMemset(c->attn_ts.p, 0, at.size() * 8);
+  }
 }
 
 // Queued GEMVs run as one persistent multi-phase launch (gemv.cu). A phase
@@ -538,6 +562,8 @@ int enqueue_layer(Ctx* c, Model& M, int l, int m, const int32_t* d_tenant, const
   at.partials = c->attn_partials.as<float>();
   at.counters = c->counters.as<int32_t>() + kCounters / 2;
   at.err = c->err.as<uint32_t>();
+  at.early_kv = 1;  // the step's descriptor and page tables precede the step's first kernel
+  if (c->gemv_dbg & 2) at.dbg_ts = c->attn_ts.as<unsigned long long>();
   RB_CUDA(attn_launch(at, c->num_sms, c->stream, c->pdl ? 1 : 0));
   if (launches) ++*launches;
   // o-proj + residual; writes fragments of x * ffn_norm
@@ -818,6 +844,8 @@ int32_t rb_ctx_create(const rb_config* cfg, rb_ctx** out) {
   if (c->gemv_dbg & 2) {
     RB_CUDA(c->dbg_ts.alloc((size_t)c->num_sms * kMaxPhases * 16 * 8));
     RB_CUDA(cudaMemset(c->dbg_ts.p, 0, (size_t)c->num_sms * kMaxPhases * 16 * 8));
+    RB_CUDA(c->attn_ts.alloc((size_t)attn_grid(c->num_sms) * 8 * 8));
+    RB_CUDA(cudaMemset(c->attn_ts.p, 0, (size_t)attn_grid(c->num_sms) * 8 * 8));
   }
   if (const char* d = getenv("RB_NO_CHAIN")) c->chains = atoi(d) == 0;
   RB_CUDA(cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking));

@@ -508,12 +508,7 @@ __global__ void __launch_bounds__(kAttnWarps * 32) attn_kernel(const AttnArgs a)
       while (cl > 0 && cta_start(cl) > ui.pe - 1) --cl;
       const int ncon = (int)(cl - cf + 1);
       __syncthreads();  // partial stores of this CTA before thread 0's release
-      if (threadIdx.x == 0) {
-        __threadfence();
-        const int last = atomicAdd(a.counters + ui.row * n_kv + ui.kvh, 1) == ncon - 1;
-        if (last) __threadfence();
-        s_last = last;
-      }
+      if (threadIdx.x == 0) s_last = atom_add_acq_rel(a.counters + ui.row * n_kv + ui.kvh, 1) == ncon - 1;
       __syncthreads();
       if (s_last) {
         // contributor cc's partial is in its slot 0 iff the pair is its first segment

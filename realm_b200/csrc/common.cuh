@@ -105,6 +105,20 @@ __device__ __forceinline__ unsigned long long ld_acquire_u64(const unsigned long
   asm volatile("ld.acquire.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
   return v;
 }
+// Atomic add with acquire-release (or release) semantics at GPU scope: the
+// prior writes of the CTA (ordered by a barrier) are visible before it, and
+// reads after it (acq_rel) see what the writers released.
+__device__ __forceinline__ int atom_add_acq_rel(int32_t* p, int v) {
+  int old;
+  asm volatile("atom.acq_rel.gpu.global.add.s32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v) : "memory");
+  return old;
+}
+__device__ __forceinline__ unsigned long long atom_add_release_u64(unsigned long long* p, unsigned long long v) {
+  unsigned long long old;
+  asm volatile("atom.release.gpu.global.add.u64 %0, [%1], %2;" : "=l"(old) : "l"(p), "l"(v) : "memory");
+  return old;
+}
+
 // Waits until *ctr >= target (bounded: ~0.5 s, then reports and returns false).
 // On a timeout the first reporter also leaves err[1..3] = target, the counter
 // it last saw (low 32 bits each) and `who` (caller-defined) for the host.

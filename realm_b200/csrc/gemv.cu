@@ -529,10 +529,7 @@ __device__ __forceinline__ void finish_segment(const GemvArgs& a, int p, int n_p
     while (cl > 0 && U * cl / Gp > ub) --cl;
     const int ncontrib = (int)(cl - cf + 1);
     if (threadIdx.x == 0) {
-      __threadfence();
-      const int last = (atomicAdd(a.counters + rg, 1) == ncontrib - 1);
-      if (last) __threadfence();
-      s_last = last;
+      s_last = (atom_add_acq_rel(a.counters + rg, 1) == ncontrib - 1);
       RB_TS(p, 10);
     }
     named_bar(1, 32 * kConsumerWarps);
@@ -787,10 +784,9 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const __grid_constant
       // this CTA is done with phase p (epilogue writes included): arrive
       named_bar(1, 32 * kConsumerWarps);
       if (threadIdx.x == 0) {
-        __threadfence();
         // one counter per barrier slot: every CTA arrives at each slot exactly
         // once per launch, so a ticket always lies in its own launch's window
-        const unsigned long long t = atomicAdd(ca.gbar + (p + 1), 1ull);
+        const unsigned long long t = atom_add_release_u64(ca.gbar + (p + 1), 1ull);
         s_tgt[p] = (t / gridDim.x + 1) * gridDim.x;
       }
     }

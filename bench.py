@@ -36,8 +36,10 @@ TENANTS_PER_GPU = 8
 METRIC = "aggregate decode tok/s, 8 tenants Llama-7B Q4_K; paged-KV attn HBM GB/s vs peak"
 Q4K_BPW, Q6K_BPW = 144 / 256, 210 / 256
 # dram__bytes_read.sum + dram__bytes_write.sum of one gate|up GEMV launch (22016 x 4096
-# Q4_K, M = 8), from `ncu --set full` of `bench.py --case gemv`: 50.86 + 3.13 MB.
-GEMV_NCU_TRAFFIC = 53998592
+# Q4_K, M = 8), from `ncu --set full` of `bench.py --case gemv`: 50.87 + 0.07 MB.
+GEMV_NCU_TRAFFIC = 50941440
+# the same for one config-2 attention launch (`bench.py --case attn`): 282.47 + 6.65 MB
+ATTN_NCU_TRAFFIC = 289121024
 
 
 def peaks():
@@ -212,7 +214,8 @@ def attention_roofline(rb, torch, ctx, dev, hbm_peak, peak_kind):
     achieved = alg / (avg * 1e-3) / 1e9
     return {"kernel": "attn_kernel<HD=128, NREP=4, fp16> (config 2)", "bound": "hbm",
             "achieved": round(achieved, 1), "peak": hbm_peak, "peak_kind": peak_kind, "unit": "GB/s",
-            "frac": round(achieved / hbm_peak, 4), "algorithmic_bytes": int(alg), "avg_launch_us": round(avg * 1e3, 2)}
+            "frac": round(achieved / hbm_peak, 4), "traffic": ATTN_NCU_TRAFFIC, "algorithmic_bytes": int(alg),
+            "avg_launch_us": round(avg * 1e3, 2)}
 
 
 def cpu_baseline(weights, threads, max_s=20.0):

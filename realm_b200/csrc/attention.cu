@@ -27,24 +27,24 @@ namespace {
 constexpr int kAttnWarps = 4;
 constexpr int kMaxRows = 64;
 
-// ring stages per warp: two CTAs of 4 warps per SM keep >= ~140 KB of K/V in flight per SM
-__host__ __device__ constexpr int attn_ring(int hd, int f16) { return hd == 128 ? (f16 ? 2 : 1) : 3; }
+// ring stages per warp: two CTAs of 4 warps per SM keep ~190 KB of fp16 K/V in flight per SM
+__host__ __device__ constexpr int attn_ring(int hd, int f16) { return hd == 128 ? (f16 ? 3 : 1) : 3; }
 
 template <int HD, int F16>
 struct AttnCfg {
   static constexpr int ESZ = F16 ? 2 : 4;
-  static constexpr int BLK = 16 * HD * ESZ;  // one page of one kv head (K or V), bytes copied
+  static constexpr int BLK = 16 * HD * ESZ;  // one page of one kv head (K or V), bytes
   static constexpr int NSW = attn_ring(HD, F16);
-  // fp16 tiles are stored with 16 bytes of padding per token row so that the
-  // 8 rows an ldmatrix reads fall on different banks; fp32 tiles unpadded
-  static constexpr int ROW = F16 ? HD * ESZ + 16 : HD * ESZ;  // smem bytes per token row
-  static constexpr int SBLK = 16 * ROW;                       // smem bytes per block
+  // fp16 blocks arrive by TMA as HD / 64 boxes of 16 rows x 128 bytes with
+  // 128-byte swizzle (each box 1024-byte aligned), fp32 blocks by a plain bulk copy
+  static constexpr int SBLK = BLK;
   static constexpr int STAGE = 2 * SBLK;
 };
 
 template <int HD, int NREP, int F16>
 __host__ __device__ constexpr int attn_smem_bytes() {
-  return kAttnWarps * AttnCfg<HD, F16>::NSW * AttnCfg<HD, F16>::STAGE  // rings
+  return 1024                                                           // ring alignment
+         + kAttnWarps * AttnCfg<HD, F16>::NSW * AttnCfg<HD, F16>::STAGE  // rings
          + NREP * HD * 4                                               // q
          + kAttnWarps * (NREP > 8 ? NREP : 8) * 16 * 4                 // probabilities
          + kAttnWarps * NREP * (HD + 2) * 4                            // warp merge
@@ -67,6 +67,20 @@ __device__ __forceinline__ void to_f32(const uint4 raw, float* f, int f16) {
     f[2] = __uint_as_float(raw.z);
     f[3] = __uint_as_float(raw.w);
   }
+}
+
+// Byte offset of (token row r, 16-byte chunk k of the head_dim row) in a block
+// stored as 128-byte-swizzled boxes of 16 rows x 64 fp16 columns.
+__device__ __forceinline__ int swz(int r, int k) {
+  return (k >> 3) * 2048 + r * 128 + (((k & 7) ^ (r & 7)) << 4);
+}
+
+__device__ __forceinline__ void tma_load_2d(void* smem_dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
+          smem_u32(smem_dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(bar))
+      : "memory");
 }
 
 __device__ __forceinline__ void ldsm_x4(uint32_t r[4], const void* p) {
@@ -105,10 +119,12 @@ struct UnitInfo {
 };
 
 template <int HD, int NREP, int F16>
-__global__ void __launch_bounds__(kAttnWarps * 32) attn_kernel(const AttnArgs a) {
+__global__ void __launch_bounds__(kAttnWarps * 32) attn_kernel(const __grid_constant__ AttnArgs a) {
   using C = AttnCfg<HD, F16>;
   constexpr int NSW = C::NSW;
-  extern __shared__ __align__(128) uint8_t smem[];
+  extern __shared__ __align__(128) uint8_t smem_raw[];
+  // the swizzle pattern of TMA boxes follows shared-memory address bits: align to 1 KB
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* rings = smem;
   float* qs = reinterpret_cast<float*>(rings + kAttnWarps * NSW * C::STAGE);
   float* pb = qs + NREP * HD;
@@ -205,16 +221,17 @@ __global__ void __launch_bounds__(kAttnWarps * 32) attn_kernel(const AttnArgs a)
       const int s = issued % NSW;
       if (lane == 0) mbar_arrive_expect_tx(&mybars[s], 2 * C::BLK);
       if constexpr (F16) {
-        // one bulk copy per token row into the padded tile: lanes 0-15 K, 16-31 V
-        // (lane 0 looks up the page; the K block's address is broadcast)
-        unsigned long long kaddr = 0;
-        if (lane == 0) kaddr = reinterpret_cast<unsigned long long>(block_ptr(a.row_tenant[pu.row], pp, 0, pu.kvh));
-        kaddr = __shfl_sync(0xffffffffu, kaddr, 0);
-        const int which = lane >> 4, row = lane & 15;
-        // the V block follows the K block of the same (page, layer): n_kv blocks later
-        const uint8_t* src = reinterpret_cast<const uint8_t*>(kaddr) + (size_t)which * n_kv * C::BLK;
-        bulk_g2s(myring + s * C::STAGE + which * C::SBLK + row * C::ROW, src + (size_t)row * HD * C::ESZ,
-                 HD * C::ESZ, &mybars[s]);
+        // TMA boxes: K then V of (page, layer, kv head), HD / 64 boxes each
+        if (lane == 0) {
+          const int page = a.kv.ptab[(size_t)a.row_tenant[pu.row] * a.kv.ptab_stride + pp];
+          const int yk = ((((page * a.kv.n_layers + a.layer) * 2) * n_kv + pu.kvh) * 16);
+#pragma unroll
+          for (int which = 0; which < 2; ++which)
+#pragma unroll
+            for (int b = 0; b < HD / 64; ++b)
+              tma_load_2d(myring + s * C::STAGE + which * C::SBLK + b * 2048, &a.kv_tmap, b * 64, yk + which * n_kv * 16,
+                          &mybars[s]);
+        }
       } else if (lane == 0) {
         const int tenant = a.row_tenant[pu.row];
         bulk_g2s(myring + s * C::STAGE, block_ptr(tenant, pp, 0, pu.kvh), C::BLK, &mybars[s]);
@@ -279,7 +296,7 @@ __global__ void __launch_bounds__(kAttnWarps * 32) attn_kernel(const AttnArgs a)
 #pragma unroll
         for (int ks = 0; ks < KS; ++ks) {
           uint32_t af[4];
-          ldsm_x4(af, kb + (rr + (mi & 1) * 8) * C::ROW + (ks * 16 + (mi >> 1) * 8) * 2);
+          ldsm_x4(af, kb + swz(rr + (mi & 1) * 8, ks * 2 + (mi >> 1)));
           mma_16816(sa[(ks & 1) * 2], af, qb[ks][0][0], qb[ks][0][1]);
           mma_16816(sa[(ks & 1) * 2 + 1], af, qb[ks][1][0], qb[ks][1][1]);
         }
@@ -323,7 +340,7 @@ __global__ void __launch_bounds__(kAttnWarps * 32) attn_kernel(const AttnArgs a)
           ot[mt][2] *= alpha[0];
           ot[mt][3] *= alpha[1];
           uint32_t af[4];
-          ldsm_x4_trans(af, vb + (rr + (mi >> 1) * 8) * C::ROW + (mt * 16 + (mi & 1) * 8) * 2);
+          ldsm_x4_trans(af, vb + swz(rr + (mi >> 1) * 8, mt * 2 + (mi & 1)));
           mma_16816(ot[mt], af, pbh0, pbh1);
           mma_16816(ot[mt], af, pbl0, pbl1);
         }
@@ -644,6 +661,31 @@ __global__ void kv_gather_kernel(const KvView kv, int layer, int tenant, int len
 }  // namespace
 
 int attn_grid(int num_sms) { return 2 * num_sms; }  // upper bound on the attention grid
+
+cudaError_t kv_tensor_map(const KvView& kv, size_t n_pages, CUtensorMap* out) {
+  using EncodeFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+  static EncodeFn encode = nullptr;
+  if (!encode) {
+    void* fn = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    cudaError_t e = cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q);
+    if (e != cudaSuccess) return e;
+    if (q != cudaDriverEntryPointSuccess || !fn) return cudaErrorNotSupported;
+    encode = reinterpret_cast<EncodeFn>(fn);
+  }
+  if (!kv.f16 || (kv.hd != 64 && kv.hd != 128)) return cudaErrorInvalidValue;
+  const cuuint64_t rows = (cuuint64_t)n_pages * kv.n_layers * 2 * kv.n_kv * 16;
+  const cuuint64_t dims[2] = {(cuuint64_t)kv.hd, rows};
+  const cuuint64_t strides[1] = {(cuuint64_t)kv.hd * 2};
+  const cuuint32_t box[2] = {64, 16};
+  const cuuint32_t estr[2] = {1, 1};
+  const CUresult r = encode(out, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, kv.pool, dims, strides, box, estr,
+                            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
+}
 
 size_t attn_partials_floats(int num_ctas, int n_rep, int hd) {
   return (size_t)num_ctas * 2 * n_rep * (hd + 2);

@@ -1,10 +1,18 @@
 // Paged KV cache kernels and paged GQA decode attention.
 #pragma once
+#include <cuda.h>
+
 #include "gemv.cuh"
 
 namespace rb {
 
+// fp16 pools are also described by a TMA tensor map: the pool as a 2-D
+// tensor [page * layer * (K|V) * kv head * 16 token rows][head_dim] fp16,
+// boxes of 16 rows x 64 columns (128 bytes) with 128-byte swizzle.
+cudaError_t kv_tensor_map(const KvView& kv, size_t n_pages, CUtensorMap* out);
+
 struct AttnArgs {
+  CUtensorMap kv_tmap;             // fp16 pools (kv_tensor_map); unused for fp32
   int32_t n_rows = 0;              // query rows (tenant, position) pairs
   const int32_t* row_tenant = nullptr;
   const int32_t* row_pos = nullptr;  // row attends to positions [0, pos]

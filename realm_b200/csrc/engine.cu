@@ -199,6 +199,7 @@ struct KvPool {
   int n_layers = 0, n_kv = 0, hd = 0, f16 = 1, max_tenants = 0, max_seq = 0, max_pages_per_tenant = 0;
   int n_pages = 0;
   DevBuf pool, ptab;
+  CUtensorMap tmap;  // fp16 pools: the pool as a TMA tensor (kv_tensor_map)
   std::vector<int32_t> h_ptab;
   std::vector<int> free_list;  // stack; back() is handed out next
   std::vector<KvTenant> tenants;
@@ -559,6 +560,7 @@ int enqueue_layer(Ctx* c, Model& M, int l, int m, const int32_t* d_tenant, const
   at.layer = l;
   at.scale = 1.0f / sqrtf((float)hd);  // attention_stub/mod.rs:57
   at.kv = P.view();
+  at.kv_tmap = P.tmap;
   at.partials = c->attn_partials.as<float>();
   at.counters = c->counters.as<int32_t>() + kCounters / 2;
   at.err = c->err.as<uint32_t>();
@@ -761,6 +763,7 @@ int pool_create(rb_ctx* c, int n_layers, int n_kv, int hd, int kv_dtype, int n_p
   const size_t page_bytes = (size_t)n_layers * 2 * n_kv * 16 * hd * (P->f16 ? 2 : 4);
   if (P->pool.alloc(page_bytes * n_pages) != cudaSuccess) return fail(RB_ERR_OOM, "kv pool of %zu bytes", page_bytes * n_pages);
   RB_CUDA(cudaMemsetAsync(P->pool.p, 0, page_bytes * n_pages, c->stream));
+  if (P->f16) RB_CUDA(kv_tensor_map(P->view(), (size_t)n_pages, &P->tmap));
   P->h_ptab.assign((size_t)max_tenants * P->max_pages_per_tenant, 0);
   RB_CUDA(P->ptab.alloc(P->h_ptab.size() * 4));
   RB_CUDA(cudaMemsetAsync(P->ptab.p, 0, P->h_ptab.size() * 4, c->stream));
@@ -1324,6 +1327,7 @@ int32_t rb_attention_forward(rb_ctx* c, int32_t pool, uint32_t layer, uint32_t n
   at.layer = layer;
   at.scale = scale;
   at.kv = P->view();
+  at.kv_tmap = P->tmap;
   at.partials = c->attn_partials.as<float>();
   at.counters = c->counters.as<int32_t>() + kCounters / 2;
   at.err = c->err.as<uint32_t>();

@@ -132,3 +132,47 @@ def test_forward_errors(ctx, small):
         m.forward_rows([0], [cfg["vocab"]])      # token out of range
     assert e.value.code == -3
     m.close()
+
+
+def _decode_logits(ctx, cfg, W, n_steps=4):
+    m = _build(ctx, cfg, W, True, max_tenants=3)
+    rng = np.random.default_rng(5)
+    prompts = [rng.integers(0, cfg["vocab"], n).astype(np.uint32) for n in (6, 11, 3)]
+    for t, p in enumerate(prompts):
+        m.tenant_create(t)
+        m.forward_rows([t] * len(p), p)
+    toks = [1, 2, 3]
+    out = []
+    for _ in range(n_steps):
+        lg, am = m.forward_rows([0, 1, 2], toks)
+        out.append(lg.copy())
+        toks = [int(x) for x in am]
+    m.close()
+    return np.stack(out)
+
+
+def test_decode_is_deterministic(ctx, small):
+    """Fixed split-K and split-combine orders: two runs give identical bits."""
+    cfg, W = small
+    a = _decode_logits(ctx, cfg, W)
+    b = _decode_logits(ctx, cfg, W)
+    assert np.array_equal(a.view(np.uint32), b.view(np.uint32))
+
+
+def test_chain_kernel_matches_single_gemv_launches(ctx, small):
+    """The multi-phase GEMV launches give the same bits as one launch per GEMV
+    (same unit partition, same summation order)."""
+    import os
+    import realm_b200 as rb
+    cfg, W = small
+    chained = _decode_logits(ctx, cfg, W)
+    os.environ["RB_NO_CHAIN"] = "1"
+    try:
+        c2 = rb.Context(0)
+    finally:
+        del os.environ["RB_NO_CHAIN"]
+    try:
+        single = _decode_logits(c2, cfg, W)
+    finally:
+        c2.close()
+    assert np.array_equal(chained.view(np.uint32), single.view(np.uint32))

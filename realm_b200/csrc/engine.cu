@@ -187,6 +187,14 @@ struct FragBuf {
     v.xs = s.as<uint32_t>();
     return v;
   }
+  // the encodings a GEMV of this dtype reads (producers skip the others):
+  // Q4_K int8 limbs, scales and sums; Q6_K / Q8_0 fp16 hi/lo and sums
+  XFrags view_for(int consumer_dtype) const {
+    XFrags v = view();
+    if (consumer_dtype == DT_Q4_K) v.xf = nullptr;
+    else v.xi = nullptr, v.xc = nullptr;
+    return v;
+  }
 };
 
 struct KvTenant {
@@ -554,7 +562,7 @@ int enqueue_layer(Ctx* c, Model& M, int l, int m, const int32_t* d_tenant, const
   at.q = M.q.as<float>();
   at.ldq = Hq * hd;
   at.out = nullptr;
-  at.xout = M.fo.view();
+  at.xout = M.fo.view_for(L.o.dtype);
   at.xf_nt = NT;
   at.n_heads = Hq;
   at.layer = l;
@@ -576,7 +584,7 @@ int enqueue_layer(Ctx* c, Model& M, int l, int m, const int32_t* d_tenant, const
   ao.ldr = H;
   ao.ss_out = ss;
   ao.ld_ss = kMaxRowsAbi;
-  ao.xout = M.ff.view();
+  ao.xout = M.ff.view_for(L.gu.dtype);
   ao.xf_norm = L.raw[5].d.as<float>();
   if (int rc = chain_add(c, ao, true, launches)) return rc;
   // gate/up (interleaved) with fused RMSNorm and SwiGLU -> fragments of h
@@ -588,7 +596,7 @@ int enqueue_layer(Ctx* c, Model& M, int l, int m, const int32_t* d_tenant, const
   ag.norm_eps = cf.layer_eps;
   ag.norm_dim = H;
   ag.epi = EPI_SWIGLU;
-  ag.xout = M.fd.view();
+  ag.xout = M.fd.view_for(L.down.dtype);
   if (int rc = chain_add(c, ag, true, launches)) return rc;
   // down + residual; writes fragments of x * (next layer's attn_norm | output_norm)
   GemvArgs ad = base_args(c, L.down, m);

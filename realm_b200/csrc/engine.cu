@@ -410,9 +410,9 @@ void dump_stamps(Ctx* c, int n_phases) {
   const char* names[16] = {"cons_start", "cons_dep_ok", "cons_first_full", "cons_last_unit",
                            "cons_done", "prod_first_w", "prod_x_released", "prod_last_w",
                            "seg_begin", "seg_deposited", "seg_ticket", "seg_summed",
-                           "seg_epi_done", "whole_epi_begin", "whole_epi_done", "-"};
+                           "seg_epi_done", "resid_elems", "resid_ss", "resid_frags"};
   for (int p = 0; p < n_phases; ++p)
-    for (int k = 0; k < 15; ++k) {
+    for (int k = 0; k < 16; ++k) {
       double mn = 1e30, mx = 0, sum = 0;
       int n = 0;
       for (int b = 0; b < G; ++b) {
@@ -439,7 +439,7 @@ void dump_stamps(Ctx* c, int n_phases) {
       const int b = tails[i].second;
       const unsigned long long* t = &ts[((size_t)b * kMaxPhases + p) * 16];
       fprintf(stderr, "[gemv phase %d] slow cta %3d tail %6.2f us:", p, b, tails[i].first);
-      for (int k = 8; k < 15; ++k)
+      for (int k = 8; k < 16; ++k)
         if (t[k]) fprintf(stderr, " %s %+.2f", names[k], ((double)t[k] - (double)t[3]) / 1000.0);
       fprintf(stderr, "\n");
     }

@@ -40,7 +40,10 @@ __host__ __device__ constexpr int x_stage_bytes(int dtype, int nt) {
   return dtype == DT_Q4_K ? nt * (kXiSbBytes + kXcSbBytes + kXsSbBytes) : nt * (kXfSbBytes + kXsSbBytes);
 }
 __host__ __device__ constexpr int stage_bytes(int dtype, int nt) { return unit_bytes(dtype) + x_stage_bytes(dtype, nt); }
-__host__ __device__ constexpr int tile_floats(int nt) { return kRowGroup * 8 * nt; }  // epilogue transpose tile
+// epilogue tile: token-major, a row of kRowGroup + 1 floats per token (the
+// padding spreads the fragment writer's column reads over all banks)
+constexpr int kTLd = kRowGroup + 1;
+__host__ __device__ constexpr int tile_floats(int nt) { return kTLd * 8 * nt; }
 constexpr int kMaxStages = 6;
 constexpr int kChainMinSmem = 120 * 1024;  // > half the SM's shared memory: one CTA per SM
 
@@ -273,8 +276,8 @@ __device__ __forceinline__ void kv_store(const KvView& kv, int layer, int which,
 }
 
 template <int NT>
-__device__ void epilogue(const GemvArgs& a, int rg, int warp, int lane, float acc[NT][4], const float* inv_rms,
-                         float* red, float* T) {
+__device__ void epilogue(const GemvArgs& a, int p, int rg, int warp, int lane, float acc[NT][4],
+                         const float* inv_rms, float* red, float* T) {
   constexpr int LD = 8 * NT;
   const int g = lane >> 2, c = lane & 3;
   const int tid = warp * 32 + lane;
@@ -309,14 +312,24 @@ __device__ void epilogue(const GemvArgs& a, int rg, int warp, int lane, float ac
         const float sig = 1.0f / (1.0f + expf(-gt));
         const float h = (gt * sig) * up;
         const bool ok = t < a.m && 2 * (rg * (kRowGroup / 2) + ol) < a.n;
-        T[ol * LD + t] = ok ? h : 0.f;
+        T[t * kTLd + ol] = ok ? h : 0.f;
         if (ok && a.y) a.y[(size_t)t * a.ldy + rg * (kRowGroup / 2) + ol] = h;
       }
     }
     named_bar(2, 32 * kConsumerWarps);
-    frags_write(T, LD, 1, kRowGroup / 2, LD, rg * (kRowGroup / 2), 0, nullptr, a.xout, NT, red, tid,
+    frags_write(T, 1, kTLd, kRowGroup / 2, LD, rg * (kRowGroup / 2), 0, nullptr, a.xout, NT, red, tid,
                 32 * kConsumerWarps, [] { named_bar(2, 32 * kConsumerWarps); });
   } else if (a.epi == EPI_RESID) {
+    // x rows were written by another CTA earlier in this launch: read them
+    // through L2, all before the first store (one round trip)
+    float xv[NT][4];
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+      for (int r = 0; r < 4; ++r) {
+        const int t = nt * 8 + 2 * c + (r & 1), row = row0 + ((r & 2) ? 8 : 0);
+        xv[nt][r] = (t < a.m && row < a.n) ? __ldcg(a.resid + (size_t)t * a.ldr + row) : 0.f;
+      }
     float sq[NT][2];
 #pragma unroll
     for (int nt = 0; nt < NT; ++nt) {
@@ -327,13 +340,12 @@ __device__ void epilogue(const GemvArgs& a, int rg, int warp, int lane, float ac
         const int rl = row - rg * kRowGroup;
         float tv = 0.f;
         if (t < a.m && row < a.n) {
-          float* p = a.resid + (size_t)t * a.ldr + row;
-          const float v = __ldcg(p) + acc[nt][r];  // written by another CTA earlier in this launch
-          *p = v;
+          const float v = xv[nt][r] + acc[nt][r];
+          a.resid[(size_t)t * a.ldr + row] = v;
           sq[nt][r & 1] += v * v;
           tv = a.xf_norm ? v * a.xf_norm[row] : v;
         }
-        T[rl * LD + t] = tv;
+        T[t * kTLd + rl] = tv;
       }
 #pragma unroll
       for (int h = 0; h < 2; ++h) {
@@ -347,6 +359,7 @@ __device__ void epilogue(const GemvArgs& a, int rg, int warp, int lane, float ac
       }
     }
     named_bar(2, 32 * kConsumerWarps);
+    if (tid == 0) RB_TS(p, 13);
     // RMSNorm statistics per 128 columns: two slots per 256-row group
     for (int e = tid; e < 2 * a.m; e += 32 * kConsumerWarps) {
       const int hlf = e / a.m, t = e % a.m;
@@ -355,9 +368,11 @@ __device__ void epilogue(const GemvArgs& a, int rg, int warp, int lane, float ac
       a.ss_out[(size_t)(2 * rg + hlf) * a.ld_ss + t] = s;
     }
     named_bar(2, 32 * kConsumerWarps);  // red is reused as frags_write scratch below
+    if (tid == 0) RB_TS(p, 14);
     if (a.xout.xs)
-      frags_write(T, LD, 1, kRowGroup, LD, rg * kRowGroup, 0, nullptr, a.xout, NT, red, tid, 32 * kConsumerWarps,
+      frags_write(T, 1, kTLd, kRowGroup, LD, rg * kRowGroup, 0, nullptr, a.xout, NT, red, tid, 32 * kConsumerWarps,
                   [] { named_bar(2, 32 * kConsumerWarps); });
+    if (tid == 0) RB_TS(p, 15);
   } else if (a.epi == EPI_LOGITS) {
 #pragma unroll
     for (int nt = 0; nt < NT; ++nt) {
@@ -558,14 +573,12 @@ __device__ __forceinline__ void finish_segment(const GemvArgs& a, int p, int n_p
       if (stamp) RB_TS(p, 11);
       // the epilogue runs even after a timed-out wait (error already reported):
       // its named barriers must be reached by every consumer warp
-      epilogue<NT>(a, rg, warp, lane, acc, irms, red, T);
+      epilogue<NT>(a, p, rg, warp, lane, acc, irms, red, T);
       if (threadIdx.x == 0) a.counters[rg] = 0;
       if (stamp) RB_TS(p, 12);
     }
   } else {
-    if (stamp) RB_TS(p, 13);
-    epilogue<NT>(a, rg, warp, lane, acc, irms, red, T);
-    if (stamp) RB_TS(p, 14);
+    epilogue<NT>(a, p, rg, warp, lane, acc, irms, red, T);
   }
 }
 

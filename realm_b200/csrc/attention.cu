@@ -265,14 +265,16 @@ __global__ void __launch_bounds__(kAttnWarps * 32) attn_kernel(const __grid_cons
       // fp16 hi + lo). Lane (g = lane/4, c = lane%4) owns heads 2c, 2c+1.
       constexpr int KS = HD / 16;
       const int g = lane >> 2, c = lane & 3;
+      const float qscale = a.scale * 1.4426950408889634f;
       uint32_t qb[KS][2][2];  // [k-step][hi, lo][b0, b1]
 #pragma unroll
       for (int ks = 0; ks < KS; ++ks)
 #pragma unroll
         for (int b = 0; b < 2; ++b) {
           const int d = ks * 16 + 2 * c + 8 * b;
-          const float x0 = g < NREP ? qs[g * HD + d] * a.scale : 0.f;
-          const float x1 = g < NREP ? qs[g * HD + d + 1] * a.scale : 0.f;
+          // scores in base-2 units: scale * log2(e) folded into q
+          const float x0 = g < NREP ? qs[g * HD + d] * qscale : 0.f;
+          const float x1 = g < NREP ? qs[g * HD + d + 1] * qscale : 0.f;
           pack_hilo(x0, x1, qb[ks][0][b], qb[ks][1][b]);
         }
       float mh[2] = {-INFINITY, -INFINITY}, lh[2] = {0.f, 0.f};
@@ -304,24 +306,44 @@ __global__ void __launch_bounds__(kAttnWarps * 32) attn_kernel(const __grid_cons
 #pragma unroll
         for (int e = 0; e < 4; ++e) sc[e] = (sa[0][e] + sa[2][e]) + (sa[1][e] + sa[3][e]);
         const bool v0 = p * 16 + g < ui.len, v1 = p * 16 + g + 8 < ui.len;
-        float alpha[2], pr[4];
+        // Online softmax with a lazily raised maximum: the running maximum of
+        // heads 2c, 2c+1 changes only when some score of the page exceeds it
+        // (a warp vote); then it is reduced over the lanes of each head and O
+        // and the per-lane partial sums are rescaled. Sums stay per lane (every
+        // lane of a head uses the same maximum) until the segment ends.
+        float s0[2], s1[2], pr[4];
 #pragma unroll
         for (int h = 0; h < 2; ++h) {
-          const float s0 = v0 ? sc[h] : -INFINITY, s1 = v1 ? sc[2 + h] : -INFINITY;
-          float mx = fmaxf(s0, s1);
-          mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 4));
-          mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 8));
-          mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 16));
-          const float mn = fmaxf(mh[h], mx);
-          alpha[h] = mh[h] == -INFINITY ? 0.f : expf(mh[h] - mn);
-          pr[h] = v0 ? expf(s0 - mn) : 0.f;
-          pr[2 + h] = v1 ? expf(s1 - mn) : 0.f;
-          float ps = pr[h] + pr[2 + h];
-          ps += __shfl_xor_sync(0xffffffffu, ps, 4);
-          ps += __shfl_xor_sync(0xffffffffu, ps, 8);
-          ps += __shfl_xor_sync(0xffffffffu, ps, 16);
-          lh[h] = lh[h] * alpha[h] + ps;
-          mh[h] = mn;
+          s0[h] = v0 ? sc[h] : -INFINITY;
+          s1[h] = v1 ? sc[2 + h] : -INFINITY;
+        }
+        const bool up = fmaxf(s0[0], s1[0]) > mh[0] || fmaxf(s0[1], s1[1]) > mh[1];
+        if (__any_sync(0xffffffffu, up)) {
+          float alpha[2];
+#pragma unroll
+          for (int h = 0; h < 2; ++h) {
+            float mx = fmaxf(s0[h], s1[h]);
+            mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 4));
+            mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 8));
+            mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 16));
+            const float mn = fmaxf(mh[h], mx);
+            alpha[h] = mh[h] == -INFINITY ? 0.f : exp2f(mh[h] - mn);
+            lh[h] *= alpha[h];
+            mh[h] = mn;
+          }
+#pragma unroll
+          for (int mt = 0; mt < KS; ++mt) {
+            ot[mt][0] *= alpha[0];
+            ot[mt][1] *= alpha[1];
+            ot[mt][2] *= alpha[0];
+            ot[mt][3] *= alpha[1];
+          }
+        }
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          pr[h] = v0 ? exp2f(s0[h] - mh[h]) : 0.f;
+          pr[2 + h] = v1 ? exp2f(s1[h] - mh[h]) : 0.f;
+          lh[h] += pr[h] + pr[2 + h];
         }
         // P^T as the B operand: lane (g, c) needs heads g, tokens 2c, 2c+1, 2c+8, 2c+9
         pt[g * 8 + 2 * c] = pr[0];
@@ -335,10 +357,6 @@ __global__ void __launch_bounds__(kAttnWarps * 32) attn_kernel(const __grid_cons
         __syncwarp();
 #pragma unroll
         for (int mt = 0; mt < KS; ++mt) {
-          ot[mt][0] *= alpha[0];
-          ot[mt][1] *= alpha[1];
-          ot[mt][2] *= alpha[0];
-          ot[mt][3] *= alpha[1];
           uint32_t af[4];
           ldsm_x4_trans(af, vb + swz(rr + (mi >> 1) * 8, mt * 2 + (mi & 1)));
           mma_16816(ot[mt], af, pbh0, pbh1);
@@ -354,11 +372,18 @@ __global__ void __launch_bounds__(kAttnWarps * 32) attn_kernel(const __grid_cons
           const int head = 2 * c + (q & 1), dim = mt * 16 + g + ((q & 2) ? 8 : 0);
           if (head < NREP) mrg[(warp * NREP + head) * (HD + 2) + dim] = ot[mt][q];
         }
+      // the per-lane partial sums of each head, then (m, l) in natural-log units
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        lh[h] += __shfl_xor_sync(0xffffffffu, lh[h], 4);
+        lh[h] += __shfl_xor_sync(0xffffffffu, lh[h], 8);
+        lh[h] += __shfl_xor_sync(0xffffffffu, lh[h], 16);
+      }
       if (g == 0)
 #pragma unroll
         for (int h = 0; h < 2; ++h)
           if (2 * c + h < NREP) {
-            mrg[(warp * NREP + 2 * c + h) * (HD + 2) + HD] = mh[h];
+            mrg[(warp * NREP + 2 * c + h) * (HD + 2) + HD] = mh[h] * 0.6931471805599453f;
             mrg[(warp * NREP + 2 * c + h) * (HD + 2) + HD + 1] = lh[h];
           }
     } else {

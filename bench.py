@@ -38,8 +38,8 @@ Q4K_BPW, Q6K_BPW = 144 / 256, 210 / 256
 # dram__bytes_read.sum + dram__bytes_write.sum of one gate|up GEMV launch (22016 x 4096
 # Q4_K, M = 8), from `ncu --set full` of `bench.py --case gemv`: 50.87 + 0.07 MB.
 GEMV_NCU_TRAFFIC = 50941440
-# the same for one config-2 attention launch (`bench.py --case attn`): 282.47 + 6.65 MB
-ATTN_NCU_TRAFFIC = 289121024
+# the same for one config-2 attention launch (`bench.py --case attn`): 282.53 + 4.43 MB
+ATTN_NCU_TRAFFIC = 286963456
 
 
 def peaks():

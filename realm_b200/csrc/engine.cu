@@ -61,53 +61,68 @@ struct StepDesc {  // device view of one forward step (filled by one H2D copy)
 // memory64_host.rs:2570-2583), page-table updates, argmax reset, the
 // per-128-column sums of squares feeding the first fused RMSNorm, and the
 // activation fragments of x * attn_norm for layer 0's q|k|v GEMV.
+// Embedding rows (one CTA per row and 256-column block): dequantised token
+// rows into x, sums of squares per 128 columns, and the activation fragments
+// of x * norm_w for the first GEMV. CTA (0, 0) also applies the step's page
+// table updates.
 __global__ void embed_kernel(const uint8_t* embd, int dtype, int hidden, const int32_t* desc_i, int32_t* ptab,
                              int ptab_stride, float* x, int ldx, float* ss, int ld_ss, unsigned long long* argmax,
                              const float* norm_w, int nt, XFrags frags) {
   const int n_rows = desc_i[0], n_upd = desc_i[1];
   const int32_t* row_tokens = desc_i + 2 + 2 * 64;
   const int32_t* upd = desc_i + 2 + 3 * 64;
-  const int r = blockIdx.x;
-  if (r == 0) {
+  const int r = blockIdx.x, c0 = blockIdx.y * 256;
+  if (r == 0 && blockIdx.y == 0) {
     for (int i = threadIdx.x; i < n_upd; i += blockDim.x)
       ptab[(size_t)upd[3 * i] * ptab_stride + upd[3 * i + 1]] = upd[3 * i + 2];
   }
   if (r >= n_rows) return;
-  if (threadIdx.x == 0 && argmax) argmax[r] = 0ull;
+  if (threadIdx.x == 0 && blockIdx.y == 0 && argmax) argmax[r] = 0ull;
   const int tok = row_tokens[r];
   const int be = block_elems(dtype), bb = block_bytes(dtype);
   const size_t row_bytes = (size_t)(hidden / be) * bb;
   const uint8_t* src = embd + (size_t)tok * row_bytes;
   float* xr = x + (size_t)r * ldx;
+  __shared__ float T[256];
   __shared__ float red[8];
-  for (int g0 = 0; g0 < hidden; g0 += 128) {
-    float sq = 0.f;
-    if (threadIdx.x < 128) {
-      const int i = g0 + threadIdx.x;
-      float v = 0.f;
-      if (i < hidden) {
-        const uint8_t* blk = src + (size_t)(i / be) * bb;
-        const int e = i % be;
-        v = dtype == DT_Q4_K ? dequant_q4k_elem(blk, e)
-          : dtype == DT_Q6_K ? dequant_q6k_elem(blk, e)
-          : dtype == DT_Q8_0 ? dequant_q80_elem(blk, e)
-                             : reinterpret_cast<const float*>(embd)[(size_t)tok * hidden + i];
-        xr[i] = v;
-      }
-      sq = v * v;
+  for (int j = threadIdx.x; j < 256; j += blockDim.x) {
+    const int i = c0 + j;
+    float v = 0.f;
+    if (i < hidden) {
+      const uint8_t* blk = src + (size_t)(i / be) * bb;
+      const int e = i % be;
+      v = dtype == DT_Q4_K ? dequant_q4k_elem(blk, e)
+        : dtype == DT_Q6_K ? dequant_q6k_elem(blk, e)
+        : dtype == DT_Q8_0 ? dequant_q80_elem(blk, e)
+                           : reinterpret_cast<const float*>(embd)[(size_t)tok * hidden + i];
+      xr[i] = v;
     }
+    T[j] = v;
+  }
+  __syncthreads();
+  if (ss) {
+    // one sum of squares per 128 columns, in the order a single thread would add
+    // warp-reduced parts: 4 warps x 32 lanes over each 128-column half
+    for (int hlf = 0; hlf < 2; ++hlf) {
+      float sq = 0.f;
+      if (threadIdx.x < 128) {
+        const float v = T[hlf * 128 + threadIdx.x];
+        sq = v * v;
+      }
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) sq += __shfl_xor_sync(0xffffffffu, sq, o);
-    if ((threadIdx.x & 31) == 0 && threadIdx.x < 128) red[threadIdx.x >> 5] = sq;
+      for (int o = 16; o > 0; o >>= 1) sq += __shfl_xor_sync(0xffffffffu, sq, o);
+      if ((threadIdx.x & 31) == 0 && threadIdx.x < 128) red[hlf * 4 + (threadIdx.x >> 5)] = sq;
+    }
     __syncthreads();
-    if (threadIdx.x == 0 && ss) ss[(size_t)(g0 / 128) * ld_ss + r] = (red[0] + red[1]) + (red[2] + red[3]);
-    __syncthreads();
+    if (threadIdx.x < 2 && c0 + threadIdx.x * 128 < hidden) {
+      const float* q = red + threadIdx.x * 4;
+      ss[(size_t)(c0 / 128 + threadIdx.x) * ld_ss + r] = (q[0] + q[1]) + (q[2] + q[3]);
+    }
   }
   if (!frags.xi && !frags.xf) return;
-  __shared__ float scratch[256];
+  __shared__ float scratch[8];
   __syncthreads();
-  frags_write(xr, 1, 0, hidden, 1, 0, r, norm_w, frags, nt, scratch, threadIdx.x, blockDim.x,
-              [] { __syncthreads(); });
+  frags_write(T, 1, 0, 256, 1, c0, r, norm_w, frags, nt, scratch, threadIdx.x, blockDim.x, [] { __syncthreads(); });
 }
 
 __global__ void zero_u64_kernel(unsigned long long* p, int n) {
@@ -636,7 +651,8 @@ int enqueue_step(Ctx* c, Model& M, int m, int* launches) {
   const rb_model_config& cf = M.cfg;
   KvPool& P = *c->pools[M.pool];
   int32_t* desc = M.desc.as<int32_t>();
-  embed_kernel<<<m, 128, 0, c->stream>>>(M.embd.d.as<uint8_t>(), M.embd.dtype, cf.hidden, desc, P.ptab.as<int32_t>(),
+  embed_kernel<<<dim3(m, (cf.hidden + 255) / 256), 128, 0, c->stream>>>(
+      M.embd.d.as<uint8_t>(), M.embd.dtype, cf.hidden, desc, P.ptab.as<int32_t>(),
                                          P.max_pages_per_tenant, M.x.as<float>(), cf.hidden, M.ss.as<float>(),
                                          kMaxRowsAbi, M.argmax.as<unsigned long long>(),
                                          M.layers[0].raw[0].d.as<float>(), gemv_nt_for(m), M.fa.view());
@@ -1547,7 +1563,8 @@ int32_t rb_embed_tokens(rb_ctx* c, int32_t model, const uint32_t* ids, uint32_t 
     int32_t* d = c->stage_in.as<int32_t>();
     if (int rc = upload_desc(c, rp, d)) return rc;
     KvPool& P = *c->pools[M->pool];
-    embed_kernel<<<m, 128, 0, c->stream>>>(M->embd.d.as<uint8_t>(), M->embd.dtype, H, d, P.ptab.as<int32_t>(),
+    embed_kernel<<<dim3(m, (H + 255) / 256), 128, 0, c->stream>>>(M->embd.d.as<uint8_t>(), M->embd.dtype, H, d,
+                                                                  P.ptab.as<int32_t>(),
                                            P.max_pages_per_tenant, M->x.as<float>(), H, nullptr, kMaxRowsAbi,
                                            nullptr, nullptr, 1, XFrags());
     RB_CUDA(cudaGetLastError());

@@ -391,7 +391,8 @@ def run_case(args):
     contexts U[512, 8192], 0.3 GB of fp16 K/V).
     gemv: 8 launches of the Q4_K gate|up GEMV (22016 x 4096, M = 8) over 8
     weight copies (400 MB, > L2). decode: the bench model, 8 tenants with
-    caches of U[128, 512] random entries, then 3 decode steps of 194 launches each."""
+    caches of U[128, 512] random entries, then 3 decode steps of 66 launches each.
+    serve: continuous batching through the scheduler (run_serve); prints a JSON line."""
     import torch
     import realm_b200 as rb
     dev = torch.device("cuda", 0)
@@ -432,6 +433,9 @@ def run_case(args):
         torch.cuda.synchronize(dev)
         print("gemv case done", flush=True)
         return
+    if args.case == "serve":
+        run_serve(rb, torch, ctx, dev)
+        return
     m = build_model(rb, torch, ctx, dev, TENANTS_PER_GPU)
     rng = np.random.default_rng(4)
     lens = rng.integers(128, 513, TENANTS_PER_GPU)
@@ -447,6 +451,56 @@ def run_case(args):
         print("decode step", s, ctx.last_forward_launches(), "launches", flush=True)
 
 
+def run_serve(rb, torch, ctx, dev, n_req=96, max_batch=32, max_tokens=128):
+    """Continuous batching through rb_scheduler on the bench model: n_req
+    requests (prompts U[128, 512] from seed 5) all queued at t = 0, at most
+    max_batch live, max_tokens each. Every step is one rb_forward over the live
+    requests' decode rows plus prompt chunks that fill the 64-row budget.
+    Prints one JSON line: generated tok/s by the wall clock around the whole
+    run (host scheduling, copies and prefill included) and by summed device time."""
+    import time
+    m = build_model(rb, torch, ctx, dev, max_batch)
+    rng = np.random.default_rng(5)
+    lens = rng.integers(128, 513, n_req)
+    # warm-up: capture the decode-step graph of every row count 1..64 once
+    m.tenant_create(0)
+    used = 0
+    for r in range(1, 65):
+        if used + r > CFG["max_seq"]:
+            m.tenant_reset(0)
+            used = 0
+        m.forward_rows([0] * r, rng.integers(0, CFG["vocab"], r).astype(np.uint32), want_logits=False)
+        used += r
+    m.tenant_reset(0)
+    s = rb.Scheduler(m, max_batch_size=max_batch)
+    st0 = s.stats()
+    for i in range(n_req):
+        s.submit(i, rng.integers(0, CFG["vocab"], int(lens[i])).tolist(), max_tokens)
+    torch.cuda.synchronize(dev)
+    t0 = time.perf_counter()
+    with Clocks(0) as clk:
+        out = s.run()
+    wall = time.perf_counter() - t0
+    st = s.stats()
+    steps = st["steps"] - st0["steps"]
+    gen = st["tokens_generated"] - st0["tokens_generated"]
+    dev_ms = st["device_ms"] - st0["device_ms"]
+    assert gen == n_req * max_tokens and all(len(v) == max_tokens for v in out.values())
+    line = {
+        "metric": "serve_generated_tok_per_s", "value": round(gen / wall, 1), "unit": "tok/s",
+        "device_tok_per_s": round(gen / (dev_ms * 1e-3), 1),
+        "prompt_tok_per_s": round(int(lens.sum()) / wall, 1),
+        "steps": steps, "rows_per_step": round((st["rows"] - st0["rows"]) / steps, 2),
+        "prefill_rows": st["prefill_rows"] - st0["prefill_rows"], "decode_rows": st["decode_rows"] - st0["decode_rows"],
+        "wall_s": round(wall, 3), "device_s": round(dev_ms * 1e-3, 3),
+        "config": {"workload": f"Llama-2-7B Q4_K_M, {n_req} requests, prompts U[128,512], {max_tokens} tokens each, "
+                               f"<= {max_batch} live, fp16 paged KV", "data": "synthetic, random-init weights"},
+        "clocks": clk.summary(),
+    }
+    print(json.dumps(line), flush=True)
+    s.close()
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -454,7 +508,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU-baseline leg")
-    ap.add_argument("--case", choices=["gemv", "decode", "attn"],
+    ap.add_argument("--case", choices=["gemv", "decode", "attn", "serve"],
                     help="profiling case for ncu: run a small workload of one kernel family and exit")
     args = ap.parse_args()
     if args.case:

@@ -216,6 +216,10 @@ int32_t rb_model_set_weight(rb_ctx* ctx, int32_t model, int32_t which, int32_t l
 int32_t rb_model_finalize(rb_ctx* ctx, int32_t model);
 /* The KV pool holding this model's tenants (usable with the rb_kv_* calls). */
 int32_t rb_model_kv_pool(rb_ctx* ctx, int32_t model);
+/* The model's configuration as created (kv_pages resolved to the pool's page count). */
+int32_t rb_model_get_config(rb_ctx* ctx, int32_t model, rb_model_config* out);
+/* The context's largest batch of query rows per rb_forward (rb_config.max_rows, <= 64). */
+int32_t rb_ctx_max_rows(rb_ctx* ctx);
 int32_t rb_tenant_create(rb_ctx* ctx, int32_t model, uint32_t tenant);
 int32_t rb_tenant_reset(rb_ctx* ctx, int32_t model, uint32_t tenant);
 
@@ -246,6 +250,128 @@ int32_t rb_compute_logits(rb_ctx* ctx, int32_t model, const float* hidden, uint3
  * weight bytes (wq, wk, wv, wo, w_gate, w_up, w_down in that order) to dst.
  * Returns bytes, RB_ERR_NOT_FOUND (no such layer) or RB_ERR_INVALID (max_size too small). */
 int32_t rb_memory64_load_layer(rb_ctx* ctx, int32_t model, uint32_t layer_id, void* dst, uint32_t max_size);
+
+/* ---- continuous batching ----
+ * rb_batcher is ContinuousBatcher / BatchedRequest
+ * (crates/realm-runtime/src/batching.rs:10-210) as host code, with the same rules:
+ *  - rb_batcher_add_request appends to a FIFO queue; it fails with RB_ERR_INVALID
+ *    ("Batch queue is full") when the queue already holds max_batch_size requests
+ *    (batching.rs:95-104).
+ *  - rb_batcher_get_batch REMOVES from the queue and returns, in FIFO order, up to
+ *    max_batch_size requests that are not complete. Requests reached on the way
+ *    that are complete, whose prompt + generated length is >= max_seq_len, or
+ *    whose generated count is >= max_tokens, are dropped (batching.rs:109-139).
+ *  - rb_batcher_update_request appends one generated token and marks the request
+ *    complete once it has max_tokens (batching.rs:142-158).
+ *  - update / remove of an id not in the queue fail with RB_ERR_NOT_FOUND
+ *    ("Request <id> not found").
+ *  - rb_batcher_stats: queued requests, those not complete, and the integer mean
+ *    of their prompt + generated lengths (batching.rs:186-210).
+ * One mutex guards each batcher, so its calls are safe from any thread. */
+typedef struct rb_batcher rb_batcher;
+typedef struct rb_request_list rb_request_list; /* the Vec<BatchedRequest> get_batch returns */
+typedef struct rb_batched_request {
+  uint64_t request_id;
+  const uint32_t* prompt_tokens;
+  uint32_t n_prompt;
+  uint32_t n_generated;
+  const uint32_t* generated_tokens;
+  const char* prompt_text; /* NULL when the request has none */
+  uint32_t max_tokens;
+  uint32_t is_complete;
+} rb_batched_request;
+typedef struct rb_batch_stats {
+  uint64_t total_requests, active_requests, average_sequence_length;
+} rb_batch_stats;
+
+int32_t rb_batcher_create(uint32_t max_batch_size, uint32_t max_seq_len, rb_batcher** out);
+int32_t rb_batcher_destroy(rb_batcher* b);
+/* BatchedRequest::new (prompt_text NULL) / ::with_prompt_text + add_request. */
+int32_t rb_batcher_add_request(rb_batcher* b, uint64_t request_id, const uint32_t* prompt_tokens, uint32_t n_prompt,
+                               const char* prompt_text, uint32_t max_tokens);
+/* Returns the batch length; *out owns the requests (free with rb_request_list_free). */
+int32_t rb_batcher_get_batch(rb_batcher* b, rb_request_list** out);
+/* A view of request i of a list; its pointers stay valid until the list is freed. */
+int32_t rb_request_list_get(const rb_request_list* list, uint32_t i, rb_batched_request* out);
+int32_t rb_request_list_free(rb_request_list* list);
+int32_t rb_batcher_update_request(rb_batcher* b, uint64_t request_id, uint32_t new_token);
+int32_t rb_batcher_remove_request(rb_batcher* b, uint64_t request_id);
+int32_t rb_batcher_active_count(rb_batcher* b);
+int32_t rb_batcher_stats(rb_batcher* b, rb_batch_stats* out);
+
+/* ---- decode scheduler ----
+ * Continuous batching on one model, the step loop behind the reference's
+ * batched dispatch (crates/realm-server/src/dispatcher.rs:560-700 with
+ * batching.rs's admission rules). It has no single reference counterpart.
+ * Requests wait in a FIFO queue and are admitted between steps while fewer than
+ * max_batch_size are live and the KV pool can hold their worst case
+ * (prompt + max_tokens - 1 tokens, capped at max_seq_len - 1). Admission is
+ * strictly FIFO. Each admitted request gets a tenant id of its own in
+ * [tenant_base, tenant_base + max_batch_size) and a fresh KV cache.
+ * One step is one rb_forward over:
+ *  - one row for every live request past its prompt (its last token), then
+ *  - consecutive prompt rows of requests still prefilling, in admission order,
+ *    at most prefill_chunk per request (0: no limit), while rows remain
+ *    (rb_ctx_max_rows per step).
+ * The greedy argmax of a request's last prompt row is its first generated
+ * token, and of every decode row the next one. A request finishes, and its KV
+ * pages go back to the pool before the next step, when:
+ *  - it holds max_tokens generated tokens (RB_FINISH_MAX_TOKENS);
+ *  - it generated eos_token (RB_FINISH_EOS);
+ *  - prompt + generated reaches max_seq_len (RB_FINISH_LENGTH).
+ * A prompt of max_seq_len tokens or more finishes at submission with none
+ * generated (RB_FINISH_LENGTH), as get_batch drops it; max_tokens 0 finishes
+ * with RB_FINISH_MAX_TOKENS.
+ * rb_scheduler_submit, _cancel, _result, _release and _stats may be called from
+ * any thread; rb_scheduler_step from one thread at a time (it uses the context). */
+#define RB_NO_EOS 0xffffffffu
+#define RB_FINISH_NONE 0
+#define RB_FINISH_MAX_TOKENS 1
+#define RB_FINISH_EOS 2
+#define RB_FINISH_LENGTH 3
+#define RB_FINISH_CANCELLED 4
+
+typedef struct rb_scheduler rb_scheduler;
+typedef struct rb_scheduler_config {
+  uint32_t max_batch_size; /* live requests (<= rb_ctx_max_rows and <= the model's max_tenants) */
+  uint32_t max_seq_len;    /* prompt + generated tokens per request (0: the model's max_seq) */
+  uint32_t prefill_chunk;  /* prompt rows a request feeds per step (0: as many as fit) */
+  uint32_t eos_token;      /* RB_NO_EOS: none */
+  uint32_t tenant_base;    /* first tenant id the scheduler uses */
+} rb_scheduler_config;
+typedef struct rb_step_event {
+  uint64_t request_id;
+  uint32_t token;  /* generated token */
+  uint32_t index;  /* its index among the request's generated tokens */
+  int32_t finish;  /* RB_FINISH_NONE while the request continues */
+} rb_step_event;
+typedef struct rb_sched_stats {
+  uint64_t steps, rows, prefill_rows, decode_rows, tokens_generated;
+  uint32_t queued, live, finished;
+  float device_ms; /* sum of rb_last_forward_ms over the steps */
+} rb_sched_stats;
+
+int32_t rb_scheduler_create(rb_ctx* ctx, int32_t model, const rb_scheduler_config* cfg, rb_scheduler** out);
+/* Destroys the scheduler and the KV caches of its live requests. */
+int32_t rb_scheduler_destroy(rb_scheduler* s);
+/* Queues a request. RB_ERR_INVALID: duplicate id, empty prompt, token >= vocab;
+ * RB_ERR_KV_POOL_EXHAUSTED: its worst case exceeds the whole pool. */
+int32_t rb_scheduler_submit(rb_scheduler* s, uint64_t request_id, const uint32_t* prompt, uint32_t n_prompt,
+                            uint32_t max_tokens);
+/* Admits, runs one step and retires. events gets one entry per token generated
+ * (cap >= max_batch_size); logits (NULL, or [cap][vocab] host floats) the
+ * logits row each event's token came from. Returns the event count; 0 when
+ * nothing was live or queued. On an error nothing of the step is kept. */
+int32_t rb_scheduler_step(rb_scheduler* s, rb_step_event* events, uint32_t cap, float* logits);
+/* The generated tokens of a live or finished request: writes min(n, cap) to
+ * tokens (may be NULL) and its RB_FINISH_* state to *finish (may be NULL);
+ * returns n. Queued requests return 0 with RB_FINISH_NONE. */
+int32_t rb_scheduler_result(rb_scheduler* s, uint64_t request_id, uint32_t* tokens, uint32_t cap, int32_t* finish);
+/* Ends a queued or live request (RB_FINISH_CANCELLED; its KV pages are freed). */
+int32_t rb_scheduler_cancel(rb_scheduler* s, uint64_t request_id);
+/* Forgets a finished request. */
+int32_t rb_scheduler_release(rb_scheduler* s, uint64_t request_id);
+int32_t rb_scheduler_stats(rb_scheduler* s, rb_sched_stats* out);
 
 /* Timing hook for benchmarks: device time (ms) of the last rb_forward. */
 float rb_last_forward_ms(rb_ctx* ctx);

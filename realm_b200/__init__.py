@@ -530,3 +530,7 @@ class Model:
         if self.handle >= 0:
             _lib.rb_model_destroy(self.ctx.handle, self.handle)
             self.handle = -1
+
+
+from .batching import (BatchedRequest, BatchStats, ContinuousBatcher, Scheduler,  # noqa: E402
+                       prepare_batch)

@@ -13,7 +13,7 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 CSRC = os.path.join(HERE, "csrc")
 BUILD = os.path.join(HERE, "_build")
 LIB = os.path.join(HERE, "librealm_b200.so")
-SOURCES = ["gemv.cu", "attention.cu", "engine.cu"]
+SOURCES = ["gemv.cu", "attention.cu", "engine.cu", "scheduler.cpp"]
 HEADERS = ["common.cuh", "quant.cuh", "gemv.cuh", "attention.cuh", "xfrag.cuh"]
 NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
 FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a", "-O3", "-std=c++17", "-lineinfo",
@@ -31,7 +31,7 @@ def _deps_mtime() -> float:
 
 
 def _compile(src: str, force: bool) -> str:
-    obj = os.path.join(BUILD, src.replace(".cu", ".o"))
+    obj = os.path.join(BUILD, os.path.splitext(src)[0] + ".o")
     path = os.path.join(CSRC, src)
     if force or _mtime(obj) < max(_mtime(path), _deps_mtime()):
         cmd = [NVCC, *FLAGS, "-c", path, "-o", obj]

@@ -1488,6 +1488,20 @@ int32_t rb_model_finalize(rb_ctx* c, int32_t model) {
   return RB_OK;
 }
 
+int32_t rb_model_get_config(rb_ctx* c, int32_t model, rb_model_config* out) {
+  Model* M = get_model(c, model);
+  if (!M) return fail(RB_ERR_BAD_HANDLE, "model %d", model);
+  if (!out) return fail(RB_ERR_INVALID, "null config");
+  *out = M->cfg;
+  if (out->kv_pages == 0) out->kv_pages = (uint32_t)c->pools[M->pool]->n_pages;
+  return RB_OK;
+}
+
+int32_t rb_ctx_max_rows(rb_ctx* c) {
+  if (!c) return fail(RB_ERR_BAD_HANDLE, "null context");
+  return c->max_rows;
+}
+
 int32_t rb_model_kv_pool(rb_ctx* c, int32_t model) {
   Model* M = get_model(c, model);
   if (!M) return fail(RB_ERR_BAD_HANDLE, "model %d", model);

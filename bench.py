@@ -436,6 +436,9 @@ def run_case(args):
     if args.case == "serve":
         run_serve(rb, torch, ctx, dev)
         return
+    if args.case == "load":
+        run_load(rb, torch, ctx, dev)
+        return
     m = build_model(rb, torch, ctx, dev, TENANTS_PER_GPU)
     rng = np.random.default_rng(4)
     lens = rng.integers(128, 513, TENANTS_PER_GPU)
@@ -501,6 +504,48 @@ def run_serve(rb, torch, ctx, dev, n_req=96, max_batch=32, max_tokens=128):
     s.close()
 
 
+def run_load(rb, torch, ctx, dev):
+    """GGUF load of the bench model: the weights are generated on the device,
+    written once as a llama-architecture GGUF file, then opened (parse + mmap)
+    and loaded with rb_model_load_gguf (upload + re-tiling) while timed. The file
+    is in the page cache after the write, so this is the host-to-device path,
+    not the disk. Prints one JSON line."""
+    import sys
+    import tempfile
+    import time
+    sys.path.insert(0, os.path.join(os.path.dirname(os.path.abspath(__file__)), "tests"))
+    import gguf_writer as GW
+    host = {}
+    m = build_model(rb, torch, ctx, dev, 8, host_copy=host)
+    m.close()
+    cfg = dict(CFG)
+    blob = GW.model_gguf(cfg, host)
+    del host
+    with tempfile.TemporaryDirectory() as d:
+        path = os.path.join(d, "llama7b_q4km.gguf")
+        with open(path, "wb") as f:
+            f.write(blob)
+        nbytes = len(blob)
+        del blob
+        times = []
+        for _ in range(3):
+            t0 = time.perf_counter()
+            g = rb.GGUFFile(path)
+            t1 = time.perf_counter()
+            mg = g.load_model(ctx, max_tenants=8)
+            torch.cuda.synchronize(dev)
+            t2 = time.perf_counter()
+            times.append((t1 - t0, t2 - t1))
+            mg.close()
+            g.close()
+    parse_s, load_s = min(times, key=lambda x: x[0] + x[1])
+    print(json.dumps({"metric": "gguf_load_GBps", "value": round(nbytes / (parse_s + load_s) / 1e9, 2),
+                      "unit": "GB/s", "file_bytes": nbytes, "parse_s": round(parse_s, 4), "load_s": round(load_s, 3),
+                      "runs": [[round(a, 4), round(b, 3)] for a, b in times],
+                      "config": {"workload": "Llama-2-7B Q4_K_M GGUF (synthetic weights) from the page cache"}}),
+          flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -508,7 +553,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU-baseline leg")
-    ap.add_argument("--case", choices=["gemv", "decode", "attn", "serve"],
+    ap.add_argument("--case", choices=["gemv", "decode", "attn", "serve", "load"],
                     help="profiling case for ncu: run a small workload of one kernel family and exit")
     args = ap.parse_args()
     if args.case:

@@ -251,6 +251,95 @@ int32_t rb_compute_logits(rb_ctx* ctx, int32_t model, const float* hidden, uint3
  * Returns bytes, RB_ERR_NOT_FOUND (no such layer) or RB_ERR_INVALID (max_size too small). */
 int32_t rb_memory64_load_layer(rb_ctx* ctx, int32_t model, uint32_t layer_id, void* dst, uint32_t max_size);
 
+/* ---- GGUF files ----
+ * rb_gguf is GGUFParser (crates/realm-core/src/formats/gguf.rs:100-479) over a
+ * read-only memory mapping of the file (or caller-owned bytes), with the same
+ * header rules and messages:
+ *  - magic "GGUF" ("Invalid GGUF magic: 0x%08X");
+ *  - version 2 or 3 ("Unsupported GGUF version: %u");
+ *  - metadata of value types 0..12; an array of arrays is rejected ("Unknown
+ *    typed value: 9");
+ *  - tensor infos (name, dims, ggml type, offset relative to the data section).
+ * Unknown ggml types parse, with nbytes 0 (gguf.rs:474-477 keeps parsing).
+ * Errors: RB_ERR_INVALID for format errors, RB_ERR_IO for a truncated or
+ * unreadable file.
+ * Two deviations, both fixes of the reference:
+ *  - tensor bytes are located at data section + offset. The data section
+ *    starts at the end of the tensor infos, rounded up to general.alignment
+ *    (default 32). model_storage.rs:444-464 drops the data-section offset.
+ *  - nbytes uses the real ggml block sizes (Q8_0 34 bytes, Q4_0 18, Q8_K 292).
+ *    tensor.rs:139-178 has 33, 16 and 322.
+ * Every tensor's bytes are checked to lie inside the file. */
+typedef struct rb_gguf rb_gguf;
+typedef struct rb_gguf_tensor {
+  const char* name;
+  int32_t dtype;         /* ggml type id (RB_F32, RB_Q4_K, ...) */
+  uint32_t n_dims;
+  uint64_t dims[4];      /* ggml order: dims[0] is the contiguous (column) extent */
+  uint64_t offset;       /* as stored: relative to the data section */
+  uint64_t file_offset;  /* absolute position in the file */
+  uint64_t nbytes;       /* 0 for ggml types this library does not know */
+  const void* data;      /* host pointer into the mapping */
+} rb_gguf_tensor;
+/* metadata value types (gguf.rs:11-29) */
+#define RB_GGUF_U8 0
+#define RB_GGUF_I8 1
+#define RB_GGUF_U16 2
+#define RB_GGUF_I16 3
+#define RB_GGUF_U32 4
+#define RB_GGUF_I32 5
+#define RB_GGUF_F32 6
+#define RB_GGUF_BOOL 7
+#define RB_GGUF_STRING 8
+#define RB_GGUF_ARRAY 9
+#define RB_GGUF_U64 10
+#define RB_GGUF_I64 11
+#define RB_GGUF_F64 12
+
+int32_t rb_gguf_open(const char* path, rb_gguf** out);
+/* Parses caller-owned bytes (GGUFParser over a Cursor); they must outlive the handle. */
+int32_t rb_gguf_open_memory(const void* bytes, size_t nbytes, rb_gguf** out);
+int32_t rb_gguf_close(rb_gguf* g);
+int32_t rb_gguf_version(rb_gguf* g);
+/* Start of the tensor data section in the file. */
+int32_t rb_gguf_data_offset(rb_gguf* g, uint64_t* out);
+int32_t rb_gguf_tensor_count(rb_gguf* g);
+int32_t rb_gguf_tensor_info(rb_gguf* g, uint32_t index, rb_gguf_tensor* out);
+/* Index of a tensor by name, or RB_ERR_NOT_FOUND ("Tensor not found: <name>"). */
+int32_t rb_gguf_find_tensor(rb_gguf* g, const char* name);
+int32_t rb_gguf_meta_count(rb_gguf* g);
+/* Key and value type of metadata entry i (file order); for arrays also the element type and length. */
+int32_t rb_gguf_meta_entry(rb_gguf* g, uint32_t index, const char** key, int32_t* type, int32_t* elem_type,
+                           uint64_t* length);
+/* Index of a metadata key, or RB_ERR_NOT_FOUND. */
+int32_t rb_gguf_meta_find(rb_gguf* g, const char* key);
+/* MetadataValue::as_u32 / as_f32 (gguf.rs:50-75): integer types cast to u32;
+ * f32/f64 to f32; otherwise RB_ERR_INVALID. */
+int32_t rb_gguf_meta_u32(rb_gguf* g, uint32_t index, uint32_t* out);
+int32_t rb_gguf_meta_f32(rb_gguf* g, uint32_t index, float* out);
+/* The raw little-endian bytes of a scalar value (cap >= its size); returns the size. */
+int32_t rb_gguf_meta_scalar(rb_gguf* g, uint32_t index, void* out, size_t cap);
+/* A string value (elem < 0) or element `elem` of a string array; not NUL-terminated. */
+int32_t rb_gguf_meta_string(rb_gguf* g, uint32_t index, int64_t elem, const char** str, uint64_t* len);
+/* Host pointer to the packed little-endian elements of a numeric or bool array. */
+int32_t rb_gguf_meta_array_data(rb_gguf* g, uint32_t index, const void** data);
+/* extract_config (gguf.rs:214-287): the transformer geometry from
+ * "<arch>.*" keys, with the reference's fallbacks and defaults. head_dim =
+ * hidden / n_heads; layer_eps = rms_eps; kv_dtype, max_tenants and kv_pages are
+ * left 0 for the caller. */
+int32_t rb_gguf_model_config(rb_gguf* g, rb_model_config* out);
+/* Model::load_from_gguf (crates/realm-models/src/model.rs:291-540) onto the
+ * device. It looks tensors up by name:
+ *  - token_embd.weight, output_norm.weight, output.weight (else lm_head.weight,
+ *    else the token embedding: tied weights);
+ *  - blk.N.{attn_norm, attn_q, attn_k, attn_v, attn_output, ffn_norm, ffn_gate,
+ *    ffn_up, ffn_down}.weight.
+ * cfg gives the geometry, as rb_gguf_model_config returns it and the caller
+ * adjusts it (kv_dtype, max_tenants, kv_pages, max_seq). Shapes are checked
+ * against it. Norm weights may be F32 or F16 (widened to f32). Creates and
+ * finalizes a model; *model gets its handle. Returns RB_OK. */
+int32_t rb_model_load_gguf(rb_ctx* ctx, rb_gguf* g, const rb_model_config* cfg, int32_t* model);
+
 /* ---- continuous batching ----
  * rb_batcher is ContinuousBatcher / BatchedRequest
  * (crates/realm-runtime/src/batching.rs:10-210) as host code, with the same rules:

@@ -444,6 +444,16 @@ class Model:
         self.kv = KVPool(ctx, cfg["n_layers"], cfg["n_kv_heads"], cfg["head_dim"], cfg.get("kv_dtype", F16), 0, 0,
                          cfg["max_seq"], handle=pool)
 
+    @classmethod
+    def attach(cls, ctx: Context, cfg: dict, handle: int) -> "Model":
+        """Wraps a model the library created (e.g. rb_model_load_gguf)."""
+        m = cls.__new__(cls)
+        m.ctx, m.cfg, m.handle = ctx, dict(cfg), handle
+        pool = _check(_lib.rb_model_kv_pool(ctx.handle, handle))
+        m.kv = KVPool(ctx, cfg["n_layers"], cfg["n_kv_heads"], cfg["head_dim"], cfg.get("kv_dtype", F16), 0, 0,
+                      cfg["max_seq"], handle=pool)
+        return m
+
     def set_weight(self, which: int, layer: int, dtype: int, data):
         if not _is_dev(data):
             if dtype == F32:
@@ -534,3 +544,4 @@ class Model:
 
 from .batching import (BatchedRequest, BatchStats, ContinuousBatcher, Scheduler,  # noqa: E402
                        prepare_batch)
+from .gguf import GGUFFile, TensorDesc  # noqa: E402

@@ -182,6 +182,7 @@ struct Weight {
   int dtype = 0, n = 0, k = 0, n_rg = 0;
   int k_in = 0;  // caller's K; k is K rounded up to 256 (Q8_0 rows are zero-padded)
   DevBuf tiled;
+  DevBuf rexp;   // per-row power-of-two exponent of the tcgen05 GEMM's fp16 operands (int8)
 };
 
 // Device storage for one GEMV input's activation fragments (xfrag.cuh).
@@ -203,7 +204,8 @@ struct FragBuf {
     return v;
   }
   // the encodings a GEMV of this dtype reads (producers skip the others):
-  // Q4_K int8 limbs, scales and sums; Q6_K / Q8_0 fp16 hi/lo and sums
+  // Q4_K int8 limbs, scales and sums; Q6_K / Q8_0 fp16 hi/lo and sums; -1
+  // (the tcgen05 GEMM of any dtype) fp16 hi/lo and sums
   XFrags view_for(int consumer_dtype) const {
     XFrags v = view();
     if (consumer_dtype == DT_Q4_K) v.xf = nullptr;
@@ -294,7 +296,13 @@ struct Ctx {
   bool chains = true;  // RB_NO_CHAIN=1 launches every GEMV on its own
   DevBuf gbar;         // grid-barrier arrival counters (one per barrier slot) of multi-phase launches
   int last_chain_phases = 1;
+  bool qgemm = false;  // RB_QGEMM=1 sends batches of 16+ rows to the tcgen05 GEMM (measured slower than the GEMV)
+  bool gemm_step = false;  // the step being enqueued runs its projections on the tcgen05 GEMM
+  DevBuf qg_part;      // tcgen05 GEMM partial sums
 };
+
+// With RB_QGEMM=1, batches of at least this many rows take the tcgen05 dequant-GEMM.
+constexpr int kQgemmMinRows = 16;
 
 constexpr int kMaxRowsAbi = 64;
 constexpr int kCounters = 1 << 16;
@@ -384,6 +392,8 @@ int upload_tiled(Ctx* c, Weight& w, int dtype, int n, int k, const uint8_t* a, i
   w.n_rg = (n + kRowGroup - 1) / kRowGroup;
   RB_CUDA(w.tiled.alloc((size_t)w.n_rg * (kp / kSuperK) * unit_bytes(dtype)));
   RB_CUDA(repack_launch(a, rows_a, b, rows_b, mode, dtype, kp, w.tiled.as<uint8_t>(), w.n_rg, c->stream));
+  RB_CUDA(w.rexp.alloc((size_t)w.n_rg * kRowGroup));
+  RB_CUDA(rowexp_launch(w.tiled.as<uint8_t>(), dtype, w.n_rg, kp / kSuperK, w.rexp.as<int8_t>(), c->stream));
   if (pad) RB_CUDA(cudaStreamSynchronize(c->stream));  // the padded copies are freed on return
   return RB_OK;
 }
@@ -396,6 +406,7 @@ GemvArgs base_args(Ctx* c, const Weight& w, int m) {
   a.n_rg = w.n_rg;
   a.nsb = w.k / kSuperK;
   a.m = m;
+  a.rexp = w.rexp.as<int8_t>();
   a.partials = c->gemv_partials.as<float>();
   a.counters = c->counters.as<int32_t>();
   a.err = c->err.as<uint32_t>();
@@ -409,6 +420,27 @@ GemvArgs base_args(Ctx* c, const Weight& w, int m) {
 int launch_gemv(Ctx* c, const GemvArgs& a, int* launches) {
   RB_CUDA(gemv_launch(a, c->num_sms, c->stream, c->pdl ? 1 : 0));
   if (launches) ++*launches;
+  return RB_OK;
+}
+
+// Grows the tcgen05 GEMM's partial-sum scratch to cover a weight of n_rg row
+// groups and nsb super-blocks (never during a stream capture: call first).
+int ensure_qg_part(Ctx* c, int n_rg, int nsb) {
+  const size_t need = qgemm_part_floats(qgemm_plan(c->num_sms, n_rg, nsb)) * 4;
+  if (c->qg_part.n < need) {
+    if (c->qg_part.p) RB_CUDA(cudaStreamSynchronize(c->stream));  // earlier launches may still read it
+    RB_CUDA(c->qg_part.alloc(need));
+  }
+  return RB_OK;
+}
+
+// y = x . W^T through the tcgen05 GEMM (a.m >= kQgemmMinRows; a.xin.xf holds x):
+// the GEMM, then the partial sums and the fused epilogue (two launches).
+int launch_qgemm(Ctx* c, const GemvArgs& a, int* launches) {
+  const QgemmPlan p = qgemm_plan(c->num_sms, a.n_rg, a.nsb);
+  if (c->qg_part.n < qgemm_part_floats(p) * 4) return fail(RB_ERR_INVALID, "GEMM scratch not sized for this weight");
+  RB_CUDA(qgemm_launch(a, c->qg_part.as<float>(), p, c->stream, c->pdl ? 1 : 0));
+  if (launches) *launches += 2;
   return RB_OK;
 }
 
@@ -505,6 +537,10 @@ int chain_flush(Ctx* c, int* launches) {
 }
 
 int chain_add(Ctx* c, GemvArgs a, bool reads_previous, int* launches) {
+  if (c->gemm_step) {  // 16+ rows: every phase is its own tcgen05 GEMM + epilogue
+    if (int rc = chain_flush(c, launches)) return rc;
+    return launch_qgemm(c, a, launches);
+  }
   if (!c->chains) {
     a.counters = c->counters.as<int32_t>();
     return launch_gemv(c, a, launches);
@@ -577,7 +613,7 @@ int enqueue_layer(Ctx* c, Model& M, int l, int m, const int32_t* d_tenant, const
   at.q = M.q.as<float>();
   at.ldq = Hq * hd;
   at.out = nullptr;
-  at.xout = M.fo.view_for(L.o.dtype);
+  at.xout = M.fo.view_for(c->gemm_step ? -1 : L.o.dtype);
   at.xf_nt = NT;
   at.n_heads = Hq;
   at.layer = l;
@@ -599,7 +635,7 @@ int enqueue_layer(Ctx* c, Model& M, int l, int m, const int32_t* d_tenant, const
   ao.ldr = H;
   ao.ss_out = ss;
   ao.ld_ss = kMaxRowsAbi;
-  ao.xout = M.ff.view_for(L.gu.dtype);
+  ao.xout = M.ff.view_for(c->gemm_step ? -1 : L.gu.dtype);
   ao.xf_norm = L.raw[5].d.as<float>();
   if (int rc = chain_add(c, ao, true, launches)) return rc;
   // gate/up (interleaved) with fused RMSNorm and SwiGLU -> fragments of h
@@ -611,7 +647,7 @@ int enqueue_layer(Ctx* c, Model& M, int l, int m, const int32_t* d_tenant, const
   ag.norm_eps = cf.layer_eps;
   ag.norm_dim = H;
   ag.epi = EPI_SWIGLU;
-  ag.xout = M.fd.view_for(L.down.dtype);
+  ag.xout = M.fd.view_for(c->gemm_step ? -1 : L.down.dtype);
   if (int rc = chain_add(c, ag, true, launches)) return rc;
   // down + residual; writes fragments of x * (next layer's attn_norm | output_norm)
   GemvArgs ad = base_args(c, L.down, m);
@@ -649,6 +685,7 @@ constexpr int kDescTenant = 2, kDescPos = 2 + 64, kDescTok = 2 + 128, kDescUpd =
 
 int enqueue_step(Ctx* c, Model& M, int m, int* launches) {
   const rb_model_config& cf = M.cfg;
+  c->gemm_step = c->qgemm && m >= kQgemmMinRows;
   KvPool& P = *c->pools[M.pool];
   int32_t* desc = M.desc.as<int32_t>();
   embed_kernel<<<dim3(m, (cf.hidden + 255) / 256), 128, 0, c->stream>>>(
@@ -806,8 +843,19 @@ void tenant_release(KvPool& P, int t) {
   std::fill(T.len.begin(), T.len.end(), 0);
 }
 
+// Sizes the tcgen05 GEMM scratch for every projection of the model.
+int ensure_qg_model(Ctx* c, Model& M) {
+  for (LayerW& L : M.layers)
+    for (const Weight* w : {&L.qk, &L.v, &L.o, &L.gu, &L.down})
+      if (w->n_rg)
+        if (int rc = ensure_qg_part(c, w->n_rg, w->k / kSuperK)) return rc;
+  return ensure_qg_part(c, M.out.n_rg, M.out.k / kSuperK);
+}
+
 int run_forward(rb_ctx* c, Model& M, int m, bool use_graph) {
   int launches = 0;
+  if (c->qgemm && m >= kQgemmMinRows)
+    if (int rc = ensure_qg_model(c, M)) return rc;
   RB_CUDA(cudaEventRecord(c->ev0, c->stream));
   if (use_graph) {
     auto it = M.graphs.find(m);
@@ -875,6 +923,7 @@ int32_t rb_ctx_create(const rb_config* cfg, rb_ctx** out) {
     RB_CUDA(cudaMemset(c->attn_ts.p, 0, (size_t)attn_grid(c->num_sms) * 8 * 8));
   }
   if (const char* d = getenv("RB_NO_CHAIN")) c->chains = atoi(d) == 0;
+  if (const char* d = getenv("RB_QGEMM")) c->qgemm = atoi(d) != 0;
   RB_CUDA(cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking));
   RB_CUDA(cudaEventCreate(&c->ev0));
   RB_CUDA(cudaEventCreate(&c->ev1));
@@ -1011,7 +1060,12 @@ static int weight_matmul_dev(rb_ctx* c, const Weight& w, const float* din, float
     a.epi = EPI_STORE;
     a.y = dout + (size_t)b0 * w.n;
     a.ldy = w.n;
-    if (int rc = launch_gemv(c, a, nullptr)) return rc;
+    if (c->qgemm && m >= kQgemmMinRows) {
+      if (int rc = ensure_qg_part(c, w.n_rg, w.k / kSuperK)) return rc;
+      if (int rc = launch_qgemm(c, a, nullptr)) return rc;
+    } else if (int rc = launch_gemv(c, a, nullptr)) {
+      return rc;
+    }
   }
   return RB_OK;
 }
@@ -1056,6 +1110,8 @@ int32_t rb_weight_matmul_timing(rb_ctx* c, const int32_t* handles, uint32_t n_ha
   RB_CUDA(cudaMemsetAsync(x.p, 0, x.n, c->stream));
   if (int rc = ensure_xf_scratch(c, k)) return rc;
   RB_CUDA(xfrag_launch(x.as<float>(), k, nullptr, m, k, nt, c->xf_scratch.view(), nullptr, 0, c->stream));
+  for (const Weight* w : ws)
+    if (int rc = ensure_qg_part(c, w->n_rg, w->k / kSuperK)) return rc;
   cudaGraph_t g = nullptr;
   RB_CUDA(cudaStreamBeginCapture(c->stream, cudaStreamCaptureModeThreadLocal));
   int rc = RB_OK;
@@ -1066,7 +1122,7 @@ int32_t rb_weight_matmul_timing(rb_ctx* c, const int32_t* handles, uint32_t n_ha
     a.epi = EPI_STORE;
     a.y = y.as<float>();
     a.ldy = w.n;
-    rc = launch_gemv(c, a, nullptr);
+    rc = (c->qgemm && m >= kQgemmMinRows) ? launch_qgemm(c, a, nullptr) : launch_gemv(c, a, nullptr);
   }
   cudaError_t e = cudaStreamEndCapture(c->stream, &g);
   if (rc) {
@@ -1610,6 +1666,9 @@ int32_t rb_forward_layer(rb_ctx* c, int32_t model, uint32_t t, uint32_t layer, c
   RB_CUDA(xfrag_launch(M->x.as<float>(), H, M->layers[layer].raw[0].d.as<float>(), (int)S, H, gemv_nt_for((int)S),
                        M->fa.view(), M->ss.as<float>(), kMaxRowsAbi, c->stream));
   int launches = 2;
+  c->gemm_step = c->qgemm && S >= (uint32_t)kQgemmMinRows;
+  if (c->gemm_step)
+    if (int rc = ensure_qg_model(c, *M)) return rc;
   RB_CUDA(cudaEventRecord(c->ev0, c->stream));
   const int32_t* d = M->desc.as<int32_t>();
   if (int rc = enqueue_layer(c, *M, (int)layer, (int)S, d + kDescTenant, d + kDescPos, &launches)) return rc;
@@ -1636,6 +1695,7 @@ int32_t rb_compute_logits(rb_ctx* c, int32_t model, const float* hidden, uint32_
                        kMaxRowsAbi, c->stream));
   zero_u64_kernel<<<1, 64, 0, c->stream>>>(M->argmax.as<unsigned long long>(), 1);
   RB_CUDA(cudaGetLastError());
+  c->gemm_step = false;
   if (int rc = enqueue_head(c, *M, 1, true, nullptr)) return rc;
   if (int rc = copy_out(c, out, M->logits.p, (size_t)M->cfg.vocab * 4, flags)) return rc;
   if (int rc = sync_ctx(c)) return rc;

@@ -1129,6 +1129,647 @@ cudaError_t launch_chain_t(ChainArgs ca, int num_sms, cudaStream_t s, int pdl) {
   return cudaLaunchKernelEx(&cfg, kern, ca);
 }
 
+
+// ===========================================================================
+// tcgen05 dequant-GEMM for 16..64 rows (prefill chunks, large scheduler
+// steps), where the GEMV above is bound by its mma.sync issue rate.
+//
+// D[128 weight rows][N tokens] accumulates in tensor memory (TMEM) from
+// tcgen05.mma kind::f16 (M = 128, N = 16..64, K = 16), A and B in shared
+// memory in the canonical K-major no-swizzle layout: 8 x 16-byte core
+// matrices, rows 16 bytes apart, 8-row groups 128 bytes apart (SBO), 8-column
+// chunks LBO apart. Eight warps dequantise one 64-column slice of a 128-row
+// weight tile per stage straight from the tiled layout: every weight becomes
+// w * 2^e_row (w bit-exact as dequantize_* computes it; e_row a per-row power
+// of two chosen at upload so |w| * 2^e < 2^14 fits fp16) split into fp16
+// hi + lo. The activations come from the fp16 hi/lo fragments (xfrag.cuh).
+// Three MMAs per k-step (hi.hi + hi.lo + lo.hi) give ~22-bit products with
+// fp32 accumulation. One thread issues the MMAs and commits each stage to an
+// mbarrier that frees the stage for the producers. Units (128-row tile x
+// 64-column slice) are split evenly over a persistent grid (stream-K); every
+// segment of one tile ends in a drain of TMEM into a fixed partial slot, and
+// qgemm_epi_kernel sums a tile's slots in CTA order (deterministic), undoes
+// 2^e_row and runs the GEMV's fused epilogue. Every mbarrier wait is bounded.
+// ===========================================================================
+constexpr int kQgRows = 128;
+constexpr int kQgKc = 64;
+constexpr int kQgMaxStages = 3;                          // A/B operand stages (2 or 3 by format)
+constexpr int kQgCompute = 256;                          // dequantising threads (warps 0-7)
+constexpr int kQgThreads = kQgCompute + 64;              // + the loader warp + the MMA warp
+constexpr int kQgAPlane = kQgRows * kQgKc * 2;           // 16 KB
+constexpr int kQgBPlane = kMaxTokens * kQgKc * 2;        // 8 KB
+constexpr int kQgStage = 2 * kQgAPlane + 2 * kQgBPlane;  // 48 KB
+constexpr int kQgALbo = kQgRows * 16;                    // bytes between 8-column chunks (A)
+constexpr int kQgBLbo = kMaxTokens * 16;                 // (B)
+constexpr int kQgTmemCols = 128;  // two accumulators of kMaxTokens columns
+constexpr int kQgSmemUse = 220 * 1024;  // operand stages + quantised weight ring
+constexpr int kQgMaxQStages = 8;
+constexpr int kQgSmem = kQgSmemUse + 1024;
+
+__device__ __forceinline__ uint32_t qg_aoff(int row, int col) {
+  return (uint32_t)((col >> 3) * kQgALbo + (row >> 3) * 128 + (row & 7) * 16 + (col & 7) * 2);
+}
+__device__ __forceinline__ uint32_t qg_boff(int t, int col) {
+  return (uint32_t)((col >> 3) * kQgBLbo + (t >> 3) * 128 + (t & 7) * 16 + (col & 7) * 2);
+}
+__device__ __forceinline__ float pow2f(int e) { return __int_as_float((e + 127) << 23); }  // e in [-126, 127]
+// v (0 <= v < 2^23) as a float, exactly: 2^23 + v built in the mantissa, minus 2^23
+__device__ __forceinline__ float u2f(uint32_t v) { return __fsub_rn(__uint_as_float(0x4B000000u | v), 8388608.0f); }
+
+// fp16 hi + lo of two values (hi = RN(x), lo = RN(x - hi)), packed as half2 words
+__device__ __forceinline__ void hilo2(float x0, float x1, uint32_t& hi, uint32_t& lo) {
+  const __half2 h = __floats2half2_rn(x0, x1);
+  const float2 f = __half22float2(h);
+  hi = h2_as_u32(h);
+  lo = h2_as_u32(__floats2half2_rn(__fsub_rn(x0, f.x), __fsub_rn(x1, f.y)));
+}
+
+__device__ __forceinline__ void sts32(uint32_t addr, uint32_t v) {
+  asm volatile("st.shared.b32 [%0], %1;" ::"r"(addr), "r"(v) : "memory");
+}
+__device__ __forceinline__ void sts64(uint32_t addr, uint32_t v0, uint32_t v1) {
+  asm volatile("st.shared.v2.b32 [%0], {%1, %2};" ::"r"(addr), "r"(v0), "r"(v1) : "memory");
+}
+
+// ---- tcgen05 wrappers (PTX ISA, sm_100a) ----
+__device__ __forceinline__ uint64_t umma_desc(uint32_t saddr, uint32_t lbo, uint32_t sbo) {
+  // start >> 4 [0,14), LBO >> 4 [16,30), SBO >> 4 [32,46), version 1 [46,48), no swizzle [61,64)
+  return (uint64_t)((saddr >> 4) & 0x3FFFu) | ((uint64_t)((lbo >> 4) & 0x3FFFu) << 16) |
+         ((uint64_t)((sbo >> 4) & 0x3FFFu) << 32) | (1ull << 46);
+}
+// kind::f16 instruction descriptor: f32 accumulate, f16 A and B, both K-major
+__host__ __device__ constexpr uint32_t umma_idesc_f16(int m, int n) {
+  return (1u << 4) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(m >> 4) << 24);
+}
+__device__ __forceinline__ void umma_f16(uint32_t tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc, uint32_t acc) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(acc)
+      : "memory");
+}
+__device__ __forceinline__ void umma_commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+               : "memory");
+}
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, float v[16]) {
+  uint32_t r[16];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+      "%15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
+        "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+  for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+// Stream-K owner of unit u: the largest CTA c with floor(c * U / G) <= u.
+__host__ __device__ __forceinline__ int qg_owner(long long u, long long U, int G) {
+  return (int)(((u + 1) * G - 1) / U);
+}
+
+struct QgemmArgs {
+  const uint8_t* w = nullptr;
+  int32_t dtype = 0, n_rg = 0, nsb = 0, m = 0, nt_x = 0;
+  const uint4* xf = nullptr;  // fp16 hi/lo fragments, n-tile stride nt_x
+  const int8_t* rexp = nullptr;
+  float* part = nullptr;      // [n_rt][slots][64 tokens][128 rows]
+  int32_t slots = 0;
+  int32_t dbg = 0;  // measurement hook: bit 0 skips the weight dequant, bit 1 the MMAs, bit 2 the activations
+  uint32_t* err = nullptr;
+};
+
+// One 64-column slice (group kg & 3 of its super-block) of the 128-row weight
+// tile whose eight 16-row tiles sit at `tiles` in shared memory, dequantised into
+// the A planes at sA (hi) / sA + kQgAPlane (lo). grow: global row of tile row 0.
+template <int DT>
+__device__ __forceinline__ void qg_produce_a(const QgemmArgs& a, const uint8_t* tiles, int grow, int kg, uint32_t sA,
+                                             int warp, int lane) {
+  constexpr int TB = tile_bytes(DT);
+  const int g = lane >> 2, c = lane & 3;
+  const int grp = kg & 3;
+  const uint8_t* tile = tiles + warp * TB;
+  const int rowA = warp * 16 + g, rowB = rowA + 8;  // rows within the 128-row tile
+  const float sAe = pow2f(a.rexp[grow + rowA]), sBe = pow2f(a.rexp[grow + rowB]);
+  const uint32_t lo_plane = kQgAPlane;
+  auto ld128 = [](const uint8_t* p) { return *reinterpret_cast<const uint4*>(p); };
+  if (DT == DT_Q4_K) {
+    const uint4 hA = ld128(tile + g * 16), hB = ld128(tile + (g + 8) * 16);
+    const float dA = guard_scale(half_bits_to_float(hA.x & 0xffffu), 0.00000006f);
+    const float mA = guard_scale(half_bits_to_float(hA.x >> 16), 0.00000024f);
+    const float dB = guard_scale(half_bits_to_float(hB.x & 0xffffu), 0.00000006f);
+    const float mB = guard_scale(half_bits_to_float(hB.x >> 16), 0.00000024f);
+    uint8_t scA[12], scB[12];
+    const uint32_t wa[3] = {hA.y, hA.z, hA.w}, wb[3] = {hB.y, hB.z, hB.w};
+#pragma unroll
+    for (int i = 0; i < 12; ++i) {
+      scA[i] = (uint8_t)(wa[i >> 2] >> (8 * (i & 3)));
+      scB[i] = (uint8_t)(wb[i >> 2] >> (8 * (i & 3)));
+    }
+    const uint4 q = ld128(tile + 256 + grp * 512 + lane * 16);
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const int j = 2 * grp + h;
+      int sca, ma, scb, mb;
+      q4k_scale_min(j, scA, sca, ma);
+      q4k_scale_min(j, scB, scb, mb);
+      // w 2^e = (d1 2^e) q - m1 2^e (the power of two is exact); fused, so within half an ulp of w
+      const float d1a = __fmul_rn(__fmul_rn(dA, (float)sca), sAe), m1a = __fmul_rn(__fmul_rn(mA, (float)ma), sAe);
+      const float d1b = __fmul_rn(__fmul_rn(dB, (float)scb), sBe), m1b = __fmul_rn(__fmul_rn(mB, (float)mb), sBe);
+#pragma unroll
+      for (int half2i = 0; half2i < 2; ++half2i) {  // w0: columns 4c.., w1: 16 + 4c..
+        const uint32_t wd = half2i ? (h ? q.w : q.y) : (h ? q.z : q.x);
+        const int col = 32 * h + 16 * half2i + 4 * c;
+        float va[4], vb[4];
+#pragma unroll
+        for (int b = 0; b < 4; ++b) {
+          const uint32_t byte = (wd >> (8 * b)) & 0xffu;
+          va[b] = fmaf(d1a, u2f(byte & 0xF), -m1a);
+          vb[b] = fmaf(d1b, u2f(byte >> 4), -m1b);
+        }
+        uint32_t h0, l0, h1, l1;
+        hilo2(va[0], va[1], h0, l0);
+        hilo2(va[2], va[3], h1, l1);
+        sts64(sA + qg_aoff(rowA, col), h0, h1);
+        sts64(sA + lo_plane + qg_aoff(rowA, col), l0, l1);
+        hilo2(vb[0], vb[1], h0, l0);
+        hilo2(vb[2], vb[3], h1, l1);
+        sts64(sA + qg_aoff(rowB, col), h0, h1);
+        sts64(sA + lo_plane + qg_aoff(rowB, col), l0, l1);
+      }
+    }
+  } else if (DT == DT_Q6_K) {
+    const uint16_t* dd = reinterpret_cast<const uint16_t*>(tile);
+    const float dA = guard_scale(half_bits_to_float(dd[g]), 0.00000006f);
+    const float dB = guard_scale(half_bits_to_float(dd[g + 8]), 0.00000006f);
+    const uint32_t scAw = *reinterpret_cast<const uint32_t*>(tile + 32 + g * 16 + grp * 4);
+    const uint32_t scBw = *reinterpret_cast<const uint32_t*>(tile + 32 + (g + 8) * 16 + grp * 4);
+    const uint4 ql = ld128(tile + 288 + grp * 512 + lane * 16);
+    const uint4 qh = ld128(tile + 288 + 2048 + (grp >> 1) * 512 + lane * 16);
+    const uint32_t qw[4] = {ql.x, ql.y, ql.z, ql.w};
+    const uint32_t hws[4] = {qh.x, qh.y, qh.z, qh.w};
+#pragma unroll
+    for (int wi = 0; wi < 4; ++wi) {
+      const int ks = grp * 4 + wi;
+      const uint32_t H = (ks & 1) ? (hws[(ks & 7) >> 1] >> 16) : (hws[(ks & 7) >> 1] & 0xffffu);
+      const float fa = __fmul_rn(__fmul_rn(dA, (float)(int8_t)(scAw >> (8 * wi))), sAe);
+      const float fb = __fmul_rn(__fmul_rn(dB, (float)(int8_t)(scBw >> (8 * wi))), sBe);
+#pragma unroll
+      for (int r = 0; r < 4; ++r) {
+        float v[2];
+#pragma unroll
+        for (int up = 0; up < 2; ++up) {
+          const int nib = (int)((qw[wi] >> (4 * (r + 4 * up))) & 0xFu);
+          const int hb = (int)((H >> (2 * r + 8 * up)) & 3u);
+          v[up] = __fmul_rn((r & 1) ? fb : fa, u2f((uint32_t)(nib | (hb << 4))) - 32.0f);
+        }
+        uint32_t hh, ll;
+        hilo2(v[0], v[1], hh, ll);
+        const int row = (r & 1) ? rowB : rowA;
+        const int col = 16 * wi + 2 * c + ((r & 2) ? 8 : 0);
+        sts32(sA + qg_aoff(row, col), hh);
+        sts32(sA + lo_plane + qg_aoff(row, col), ll);
+      }
+    }
+  } else {  // Q8_0: chunks 2 grp and 2 grp + 1 (32 columns each)
+#pragma unroll
+    for (int cc = 0; cc < 2; ++cc) {
+      const int ch = 2 * grp + cc;
+      const float da = __fmul_rn(half_bits_to_float(reinterpret_cast<const uint16_t*>(tile + g * 16)[ch]), sAe);
+      const float db = __fmul_rn(half_bits_to_float(reinterpret_cast<const uint16_t*>(tile + (g + 8) * 16)[ch]), sBe);
+      const uint4 q = ld128(tile + 256 + ch * 512 + lane * 16);
+#pragma unroll
+      for (int s2 = 0; s2 < 2; ++s2) {
+        const uint32_t w0 = s2 ? q.z : q.x, w1 = s2 ? q.w : q.y;
+        const int col0 = 32 * cc + 16 * s2 + 2 * c;
+#pragma unroll
+        for (int r = 0; r < 4; ++r) {  // A-fragment register r: bytes (2(r&1), 2(r&1)+1) of w0 / w1
+          const uint32_t wd = (r & 2) ? w1 : w0;
+          const int sh = (r & 1) ? 16 : 0;
+          const float qa = u2f((wd >> sh) & 0xffu) - 128.0f;
+          const float qb = u2f((wd >> (sh + 8)) & 0xffu) - 128.0f;
+          const float d = (r & 1) ? db : da;
+          uint32_t hh, ll;
+          hilo2(__fmul_rn(qa, d), __fmul_rn(qb, d), hh, ll);
+          const int row = (r & 1) ? rowB : rowA;
+          const int col = col0 + ((r & 2) ? 8 : 0);
+          sts32(sA + qg_aoff(row, col), hh);
+          sts32(sA + lo_plane + qg_aoff(row, col), ll);
+        }
+      }
+    }
+  }
+}
+
+// Activations of 64-column group kg (fp16 hi/lo fragments, tokens >= m as zeros):
+// loaded one unit ahead into registers, stored into the B planes at
+// sB (hi) / sB + kQgBPlane (lo).
+constexpr int kQgBItems = 4;  // per compute thread: 4 k-steps x 8 n-tiles x 32 lanes / 256
+__device__ __forceinline__ void qg_load_b(const QgemmArgs& a, int kg, int ntn, int tid, uint4 bv[kQgBItems]) {
+  const int sb = kg >> 2, ks0 = (kg & 3) * 4;
+  const int per_ks = ntn * 32, n_items = 4 * per_ks;
+#pragma unroll
+  for (int i = 0; i < kQgBItems; ++i) {
+    const int e = tid + i * kQgCompute;
+    bv[i] = make_uint4(0u, 0u, 0u, 0u);
+    if (e < n_items) {
+      const int ksl = e / per_ks, rem = e - ksl * per_ks, nt = rem >> 5, l = rem & 31;
+      if (nt * 8 + (l >> 2) < a.m) bv[i] = __ldg(a.xf + (((size_t)sb * a.nt_x + nt) * 16 + ks0 + ksl) * 32 + l);
+    }
+  }
+}
+__device__ __forceinline__ void qg_store_b(int ntn, uint32_t sB, int tid, const uint4 bv[kQgBItems]) {
+  const int per_ks = ntn * 32, n_items = 4 * per_ks;
+#pragma unroll
+  for (int i = 0; i < kQgBItems; ++i) {
+    const int e = tid + i * kQgCompute;
+    if (e < n_items) {
+      const int ksl = e / per_ks, rem = e - ksl * per_ks, nt = rem >> 5, l = rem & 31;
+      const int t = nt * 8 + (l >> 2), col = 16 * ksl + 2 * (l & 3);
+      sts32(sB + qg_boff(t, col), bv[i].x);
+      sts32(sB + qg_boff(t, col + 8), bv[i].y);
+      sts32(sB + kQgBPlane + qg_boff(t, col), bv[i].z);
+      sts32(sB + kQgBPlane + qg_boff(t, col + 8), bv[i].w);
+    }
+  }
+}
+
+// Walks a CTA's units as segments (maximal runs inside one 128-row tile).
+struct QgWalk {
+  long long u, u1, seg_end;
+  int kG, rt;
+  __device__ QgWalk(long long u0, long long u1_, int kG_) : u(u0), u1(u1_), seg_end(0), kG(kG_), rt(0) {}
+  __device__ bool next_segment() {
+    if (u >= u1) return false;
+    rt = (int)(u / kG);
+    seg_end = min(u1, (long long)(rt + 1) * kG);
+    return true;
+  }
+};
+
+// Q4_K (18 KB per half row-group) affords three operand stages next to a
+// four-deep weight ring; the larger formats keep two.
+template <int DT>
+__host__ __device__ constexpr int qg_stages() {
+  return DT == DT_Q4_K ? 3 : 2;
+}
+template <int DT>
+__host__ __device__ constexpr int qg_qstages() {
+  return ((kQgSmemUse - qg_stages<DT>() * kQgStage) / (8 * tile_bytes(DT))) > kQgMaxQStages
+             ? kQgMaxQStages
+             : (kQgSmemUse - qg_stages<DT>() * kQgStage) / (8 * tile_bytes(DT));
+}
+
+// Warp roles: 0-7 dequantise weights and stage activations; 8 streams each
+// super-block's half row-group (8 tiles, contiguous in the tiled layout) into
+// a ring with the bulk-copy engine (no multicast); 9 issues the MMAs into one
+// of two TMEM accumulators (one per segment, alternating) and commits stages
+// back to the producers. Every hand-off is an mbarrier with a bounded wait.
+template <int DT>
+__global__ void __launch_bounds__(kQgThreads, 1) qgemm_kernel(const __grid_constant__ QgemmArgs a) {
+  constexpr int UB = unit_bytes(DT), TB = tile_bytes(DT), HU = 8 * TB, QS = qg_qstages<DT>();
+  constexpr int kQgStages = qg_stages<DT>();
+  constexpr int kCw = kQgCompute / 32;
+  extern __shared__ __align__(1024) uint8_t qg_smem_raw[];
+  __shared__ uint64_t sfull[kQgMaxStages], sfree[kQgMaxStages];
+  __shared__ uint64_t qfull[kQgMaxQStages], qempty[kQgMaxQStages];
+  __shared__ uint64_t accfull[2], accempty[2];
+  __shared__ uint32_t tmem_slot;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(qg_smem_raw) + 1023) & ~(uintptr_t)1023);
+  const uint32_t sbase = smem_u32(smem);
+  uint8_t* qring = smem + kQgStages * kQgStage;
+  const int n_rt = 2 * a.n_rg, kG = 4 * a.nsb;
+  const long long U = (long long)n_rt * kG;
+  const int G = gridDim.x, cta = blockIdx.x;
+  const long long u0 = U * cta / G, u1 = U * (cta + 1) / G;
+  const int N = (a.m + 15) & ~15, ntn = N >> 3;
+  if (warp == 0) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&tmem_slot)),
+                 "r"(kQgTmemCols)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  if (tid == 0) {
+    for (int i = 0; i < kQgStages; ++i) {
+      mbar_init(&sfull[i], kCw);
+      mbar_init(&sfree[i], 1);
+    }
+    for (int i = 0; i < QS; ++i) {
+      mbar_init(&qfull[i], 1);
+      mbar_init(&qempty[i], kCw);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&accfull[i], 1);
+      mbar_init(&accempty[i], kCw);
+    }
+    fence_barrier_init();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = tmem_slot;
+  if (warp == kCw) {
+    // ---- loader: the weights do not depend on the previous kernel ----
+    if (lane == 0) {
+      long long iq = 0;
+      bool ok = true;
+      QgWalk w(u0, u1, kG);
+      while (ok && w.next_segment()) {
+        const int rg = w.rt >> 1, half = w.rt & 1;
+        while (w.u < w.seg_end) {
+          const int sb = (int)((w.u - (long long)w.rt * kG) >> 2);
+          const int q = (int)(iq % QS);
+          if (iq >= QS && !mbar_wait(&qempty[q], (uint32_t)((iq / QS - 1) & 1), a.err, DEV_TIMEOUT_SMEM)) {
+            ok = false;
+            break;
+          }
+          mbar_arrive_expect_tx(&qfull[q], HU);
+          bulk_g2s(qring + (size_t)q * HU, a.w + ((size_t)rg * a.nsb + sb) * UB + (size_t)half * 8 * TB, HU, &qfull[q]);
+          ++iq;
+          w.u = min(w.seg_end, (long long)w.rt * kG + (sb + 1) * 4);
+        }
+      }
+      // copies still in flight land before the CTA's shared memory goes away
+      for (long long j = iq > QS ? iq - QS : 0; j < iq; ++j)
+        mbar_wait(&qfull[j % QS], (uint32_t)((j / QS) & 1), nullptr, 0);
+    }
+    __syncwarp();
+  } else if (warp == kCw + 1) {
+    // ---- MMA issuer ----
+    if (lane == 0) {
+      const uint32_t idesc = umma_idesc_f16(kQgRows, N);
+      long long it = 0;
+      int seg = 0;
+      bool ok = true;
+      QgWalk w(u0, u1, kG);
+      while (ok && w.next_segment()) {
+        const int b = seg & 1;
+        if (seg >= 2 && !mbar_wait(&accempty[b], (uint32_t)((seg / 2 - 1) & 1), a.err, DEV_TIMEOUT_DRAIN)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t acc = tmem + (uint32_t)(b * kMaxTokens);
+        bool first = true;
+        for (; w.u < w.seg_end; ++w.u, ++it) {
+          const int s = (int)(it % kQgStages);
+          if (!mbar_wait(&sfull[s], (uint32_t)((it / kQgStages) & 1), a.err, DEV_TIMEOUT_FULL)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t st = sbase + s * kQgStage;
+#pragma unroll
+          for (int ks = 0; ks < ((a.dbg & 2) ? 0 : kQgKc / 16); ++ks) {
+            const uint64_t ah = umma_desc(st + ks * 2 * kQgALbo, kQgALbo, 128);
+            const uint64_t al = umma_desc(st + kQgAPlane + ks * 2 * kQgALbo, kQgALbo, 128);
+            const uint64_t bh = umma_desc(st + 2 * kQgAPlane + ks * 2 * kQgBLbo, kQgBLbo, 128);
+            const uint64_t bl = umma_desc(st + 2 * kQgAPlane + kQgBPlane + ks * 2 * kQgBLbo, kQgBLbo, 128);
+            umma_f16(acc, ah, bh, idesc, (first && ks == 0) ? 0u : 1u);
+            umma_f16(acc, ah, bl, idesc, 1u);
+            umma_f16(acc, al, bh, idesc, 1u);
+          }
+          umma_commit(&sfree[s]);
+          first = false;
+        }
+        if (!ok) break;
+        umma_commit(&accfull[b]);
+        ++seg;
+      }
+      if (it > 0) {  // own MMAs complete before the accumulators are freed
+        const long long last = it - 1;
+        mbar_wait(&sfree[last % kQgStages], (uint32_t)((last / kQgStages) & 1), nullptr, 0);
+      }
+    }
+    __syncwarp();
+  } else {
+    // ---- producers (warps 0-7) ----
+    pdl_wait();
+    bool alive = true;
+    long long it = 0, iq = 0;
+    int seg = 0;
+    uint4 bv[kQgBItems];
+    if (u0 < u1 && !(a.dbg & 4)) qg_load_b(a, (int)(u0 % kG), ntn, tid, bv);
+    QgWalk w(u0, u1, kG);
+    while (alive && w.next_segment()) {
+      const int grow = w.rt * kQgRows;
+      bool first = true;
+      for (; w.u < w.seg_end; ++w.u, ++it) {
+        const int kg = (int)(w.u - (long long)w.rt * kG);
+        const bool sb_first = first || (kg & 3) == 0;
+        const bool sb_last = (kg & 3) == 3 || w.u + 1 == w.seg_end;
+        const int q = (int)(iq % QS);
+        if (sb_first) alive = alive && mbar_wait(&qfull[q], (uint32_t)((iq / QS) & 1), a.err, DEV_TIMEOUT_FULL);
+        const int s = (int)(it % kQgStages);
+        if (it >= kQgStages)  // the MMAs that last read stage s are done
+          alive = alive && mbar_wait(&sfree[s], (uint32_t)((it / kQgStages - 1) & 1), a.err, DEV_TIMEOUT_EMPTY);
+        if (!alive) break;
+        const uint32_t st = sbase + s * kQgStage;
+        if (!(a.dbg & 1)) qg_produce_a<DT>(a, qring + (size_t)q * HU, grow, kg, st, warp, lane);
+        if (!(a.dbg & 4)) {
+          qg_store_b(ntn, st + 2 * kQgAPlane, tid, bv);
+          if (w.u + 1 < u1) qg_load_b(a, (int)((w.u + 1) % kG), ntn, tid, bv);
+        }
+        fence_async_smem();
+        __syncwarp();
+        if (lane == 0) {
+          mbar_arrive(&sfull[s]);
+          if (sb_last) mbar_arrive(&qempty[q]);
+        }
+        __syncwarp();
+        if (sb_last) ++iq;
+        first = false;
+      }
+      if (!alive) break;
+      // segment end: drain accumulator seg & 1 into this CTA's slot of tile rt
+      const int b = seg & 1;
+      alive = mbar_wait(&accfull[b], (uint32_t)((seg / 2) & 1), a.err, DEV_TIMEOUT_DRAIN);
+      __syncwarp();
+      if (!alive) break;
+      tc_fence_after();
+      const int quarter = warp & 3, colh = warp >> 2;
+      if (colh * 32 < N) {
+        const int slot = cta - qg_owner((long long)w.rt * kG, U, G);
+        float* dst = a.part + ((size_t)w.rt * a.slots + slot) * kMaxTokens * kQgRows + 32 * quarter + lane;
+#pragma unroll
+        for (int h16 = 0; h16 < 2; ++h16) {
+          float v[16];
+          tmem_ld16(tmem + ((uint32_t)(32 * quarter) << 16) + (uint32_t)(b * kMaxTokens + colh * 32 + h16 * 16), v);
+#pragma unroll
+          for (int i = 0; i < 16; ++i) {
+            const int t = colh * 32 + h16 * 16 + i;
+            if (t < a.m) dst[(size_t)t * kQgRows] = v[i];
+          }
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&accempty[b]);
+      ++seg;
+    }
+  }
+  pdl_launch_dependents();
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kQgTmemCols) : "memory");
+  }
+}
+
+struct QgemmTail {
+  const float* part = nullptr;
+  const int8_t* rexp = nullptr;
+  int32_t slots = 0, G = 0, kG = 0;
+  long long U = 0;
+};
+
+// Sums each 256-row group's partial slots (CTA order), undoes 2^e_row and runs
+// the GEMV epilogue (same fragment mapping: warp = 16-row tile of the group).
+template <int NT>
+__global__ void __launch_bounds__(kConsumerWarps * 32) qgemm_epi_kernel(const __grid_constant__ GemvArgs a,
+                                                                        const __grid_constant__ QgemmTail q) {
+  extern __shared__ __align__(16) float qe_smem[];
+  float* red = qe_smem;                              // kConsumerWarps * kMaxTokens
+  float* inv_rms = red + kConsumerWarps * kMaxTokens;  // kMaxTokens
+  float* T = inv_rms + kMaxTokens;                   // tile_floats(NT)
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int g = lane >> 2, c = lane & 3;
+  const int rg = blockIdx.x;
+  pdl_wait();
+  pdl_launch_dependents();
+  if (a.ss_part) {  // as consume_phase: eight strided partial sums per token, added in a fixed order
+    const int t = tid & 63, r = tid >> 6;
+    if (t < a.m) {
+      float ss = 0.f;
+      for (int j = r; j < a.n_ss; j += 8) ss += __ldcg(a.ss_part + (size_t)j * a.ld_ss + t);
+      red[r * 64 + t] = ss;
+    }
+    __syncthreads();
+    if (tid < a.m) {
+      float ss = 0.f;
+#pragma unroll
+      for (int k = 0; k < 8; ++k) ss += red[k * 64 + tid];
+      inv_rms[tid] = 1.0f / sqrtf(ss / (float)a.norm_dim + a.norm_eps);
+    }
+    __syncthreads();
+  }
+  const int rt = rg * 2 + (warp >> 3);
+  const int rl = (warp & 7) * 16 + g;  // row within the 128-row tile (and rl + 8)
+  const int c0 = qg_owner((long long)rt * q.kG, q.U, q.G), c1 = qg_owner((long long)rt * q.kG + q.kG - 1, q.U, q.G);
+  float acc[NT][4];
+#pragma unroll
+  for (int nt = 0; nt < NT; ++nt) acc[nt][0] = acc[nt][1] = acc[nt][2] = acc[nt][3] = 0.f;
+  for (int cc = c0; cc <= c1; ++cc) {
+    const float* base = q.part + ((size_t)rt * q.slots + (cc - c0)) * kMaxTokens * kQgRows;
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+      for (int r = 0; r < 4; ++r) {
+        const int t = nt * 8 + 2 * c + (r & 1);
+        if (t < a.m) acc[nt][r] += __ldcg(base + (size_t)t * kQgRows + rl + ((r & 2) ? 8 : 0));
+      }
+  }
+  const int row0 = rg * kRowGroup + warp * kTileRows + g;
+  const float sA = pow2f(-(int)q.rexp[row0]), sB = pow2f(-(int)q.rexp[row0 + 8]);
+#pragma unroll
+  for (int nt = 0; nt < NT; ++nt) {
+    acc[nt][0] *= sA;
+    acc[nt][1] *= sA;
+    acc[nt][2] *= sB;
+    acc[nt][3] *= sB;
+  }
+  epilogue<NT>(a, 0, rg, warp, lane, acc, a.ss_part ? inv_rms : nullptr, red, T);
+}
+
+// Per-row exponent e with (bound of |w| over the row) * 2^e < 2^14, from the
+// block scales alone: Q4_K |w| <= |d| 63 15 + |dmin| 63, Q6_K |d| 128 32,
+// Q8_0 |d| 128 (NaN/Inf scales replaced as the fused kernels do).
+__global__ void rowexp_kernel(const uint8_t* w, int dtype, int n_rg, int nsb, int8_t* out) {
+  const int row = blockIdx.x * blockDim.x + threadIdx.x;
+  if (row >= n_rg * kRowGroup) return;
+  const int rg = row / kRowGroup, rr = row % kRowGroup, ti = rr / kTileRows, r16 = rr % kTileRows;
+  const int UB = unit_bytes(dtype), TB = tile_bytes(dtype);
+  float bound = 0.f;
+  for (int sb = 0; sb < nsb; ++sb) {
+    const uint8_t* tile = w + ((size_t)rg * nsb + sb) * UB + ti * TB;
+    if (dtype == DT_Q4_K) {
+      const uint32_t h = *reinterpret_cast<const uint32_t*>(tile + r16 * 16);
+      const float d = guard_scale(half_bits_to_float(h & 0xffffu), 0.00000006f);
+      const float dm = guard_scale(half_bits_to_float(h >> 16), 0.00000024f);
+      bound = fmaxf(bound, fabsf(d) * 945.f + fabsf(dm) * 63.f);
+    } else if (dtype == DT_Q6_K) {
+      const float d = guard_scale(half_bits_to_float(reinterpret_cast<const uint16_t*>(tile)[r16]), 0.00000006f);
+      bound = fmaxf(bound, fabsf(d) * 4096.f);
+    } else {
+      for (int i = 0; i < 8; ++i)
+        bound = fmaxf(bound, fabsf(half_bits_to_float(reinterpret_cast<const uint16_t*>(tile + r16 * 16)[i])) * 128.f);
+    }
+  }
+  int e = 0;
+  if (bound > 0.f && isfinite(bound)) {
+    int x;
+    frexpf(bound, &x);  // bound < 2^x
+    e = min(max(14 - x, -100), 100);
+  }
+  out[row] = (int8_t)e;
+}
+
+template <int NT>
+cudaError_t launch_qgemm_epi_t(const GemvArgs& a, const QgemmTail& q, cudaStream_t s, int pdl) {
+  const int smem = (kConsumerWarps * kMaxTokens + kMaxTokens + tile_floats(NT)) * 4;
+  auto kern = qgemm_epi_kernel<NT>;
+  static unsigned long long attr_set = 0;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (!(attr_set & (1ull << dev))) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    if (e != cudaSuccess) return e;
+    attr_set |= 1ull << dev;
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(a.n_rg);
+  cfg.blockDim = dim3(kConsumerWarps * 32);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, kern, a, q);
+}
+
+template <int DT>
+cudaError_t launch_qgemm_t(const QgemmArgs& q, int G, cudaStream_t s, int pdl) {
+  auto kern = qgemm_kernel<DT>;
+  static unsigned long long attr_set = 0;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (!(attr_set & (1ull << dev))) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kQgSmem);
+    if (e != cudaSuccess) return e;
+    attr_set |= 1ull << dev;
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(G);
+  cfg.blockDim = dim3(kQgThreads);
+  cfg.dynamicSmemBytes = kQgSmem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, kern, q);
+}
+
 }  // namespace
 
 int gemv_nt_for(int m) { return m <= 8 ? 1 : m <= 16 ? 2 : m <= 32 ? 4 : 8; }
@@ -1210,6 +1851,68 @@ cudaError_t quantize_launch(int dtype, const float* x, size_t n, uint8_t* out, c
   if (nb == 0) return cudaSuccess;
   quantize_kernel<<<(unsigned)((nb + 127) / 128), 128, 0, s>>>(dtype, x, nb, out);
   return cudaGetLastError();
+}
+
+
+QgemmPlan qgemm_plan(int num_sms, int n_rg, int nsb) {
+  QgemmPlan p;
+  p.n_rt = 2 * n_rg;
+  p.kG = 4 * nsb;
+  p.U = (long long)p.n_rt * p.kG;
+  p.G = (int)(p.U < num_sms ? p.U : num_sms);
+  p.slots = 1;
+  for (int rt = 0; rt < p.n_rt; ++rt) {
+    const int c0 = qg_owner((long long)rt * p.kG, p.U, p.G), c1 = qg_owner((long long)rt * p.kG + p.kG - 1, p.U, p.G);
+    p.slots = c1 - c0 + 1 > p.slots ? c1 - c0 + 1 : p.slots;
+  }
+  return p;
+}
+
+size_t qgemm_part_floats(const QgemmPlan& p) { return (size_t)p.n_rt * p.slots * kMaxTokens * kQgRows; }
+
+cudaError_t rowexp_launch(const uint8_t* tiled, int dtype, int n_rg, int nsb, int8_t* out, cudaStream_t s) {
+  const int rows = n_rg * kRowGroup;
+  if (rows == 0) return cudaSuccess;
+  rowexp_kernel<<<(rows + 255) / 256, 256, 0, s>>>(tiled, dtype, n_rg, nsb, out);
+  return cudaGetLastError();
+}
+
+cudaError_t qgemm_launch(const GemvArgs& a, float* part, const QgemmPlan& p, cudaStream_t s, int pdl) {
+  const int8_t* rexp = a.rexp;
+  if (a.m < 16 || a.m > kMaxTokens || !a.xin.xf || !rexp || !part || p.G < 1) return cudaErrorInvalidValue;
+  QgemmArgs q;
+  q.w = a.w;
+  q.dtype = a.dtype;
+  q.n_rg = a.n_rg;
+  q.nsb = a.nsb;
+  q.m = a.m;
+  q.nt_x = gemv_nt_for(a.m);
+  q.xf = a.xin.xf;
+  q.rexp = rexp;
+  q.part = part;
+  q.slots = p.slots;
+  q.dbg = a.dbg >> 4;
+  q.err = a.err;
+  cudaError_t e;
+  switch (a.dtype) {
+    case DT_Q4_K: e = launch_qgemm_t<DT_Q4_K>(q, p.G, s, pdl); break;
+    case DT_Q6_K: e = launch_qgemm_t<DT_Q6_K>(q, p.G, s, pdl); break;
+    case DT_Q8_0: e = launch_qgemm_t<DT_Q8_0>(q, p.G, s, pdl); break;
+    default: return cudaErrorInvalidValue;
+  }
+  if (e != cudaSuccess) return e;
+  QgemmTail t;
+  t.part = part;
+  t.rexp = rexp;
+  t.slots = p.slots;
+  t.G = p.G;
+  t.kG = p.kG;
+  t.U = p.U;
+  switch (gemv_nt_for(a.m)) {
+    case 2: return launch_qgemm_epi_t<2>(a, t, s, pdl);
+    case 4: return launch_qgemm_epi_t<4>(a, t, s, pdl);
+    default: return launch_qgemm_epi_t<8>(a, t, s, pdl);
+  }
 }
 
 }  // namespace rb

@@ -62,6 +62,7 @@ struct GemvArgs {
   KvView kv;
   int32_t dbg = 0;  // measurement hook: bit 0 skips the consumer math, bit 1 records phase times
   unsigned long long* dbg_ts = nullptr;  // [cta][8] %globaltimer stamps when dbg & 2
+  const int8_t* rexp = nullptr;  // per-row exponents of the tcgen05 GEMM (rowexp_launch)
   // scratch / status
   float* partials = nullptr;
   int32_t* counters = nullptr;
@@ -89,6 +90,19 @@ int gemv_nt_for(int m);
 // (same m). Split-K counters of different phases must not overlap.
 cudaError_t gemv_launch(const GemvArgs& a, int num_sms, cudaStream_t s, int pdl);
 cudaError_t gemv_chain_launch(const ChainArgs& c, int num_sms, cudaStream_t s, int pdl);
+
+// tcgen05 dequant-GEMM for 16 <= m <= 64 (a.xin.xf fragments in, the same
+// epilogues as the GEMV out): two launches (GEMM, then partial sums +
+// epilogue). a.rexp: per-row exponents from rowexp_launch; part: scratch of
+// qgemm_part_floats(plan) floats.
+struct QgemmPlan {
+  int G = 0, n_rt = 0, kG = 0, slots = 0;
+  long long U = 0;
+};
+QgemmPlan qgemm_plan(int num_sms, int n_rg, int nsb);
+size_t qgemm_part_floats(const QgemmPlan& p);
+cudaError_t rowexp_launch(const uint8_t* tiled, int dtype, int n_rg, int nsb, int8_t* out, cudaStream_t s);
+cudaError_t qgemm_launch(const GemvArgs& a, float* part, const QgemmPlan& p, cudaStream_t s, int pdl);
 
 // Repack GGUF blocks into the tiled layout. Source rows come from up to two
 // matrices: mode 0 plain (rows of a), 1 concat (a then b), 2 interleave-8

@@ -340,6 +340,43 @@ int32_t rb_gguf_model_config(rb_gguf* g, rb_model_config* out);
  * finalizes a model; *model gets its handle. Returns RB_OK. */
 int32_t rb_model_load_gguf(rb_ctx* ctx, rb_gguf* g, const rb_model_config* cfg, int32_t* model);
 
+/* ---- sampling ----
+ * LogitsProcessor (crates/realm-models/src/sampling.rs) on the device. The
+ * strategy follows LogitsProcessor::with_params (:63-100):
+ *  - temperature < 1e-7: argmax (ties to the last index);
+ *  - else softmax(x / temperature), then top-k when 0 < top_k < vocab, then
+ *    top-p when 0 < top_p < 1, then a multinomial draw.
+ * The repetition penalty is applied before either, once per occurrence of each
+ * previous token: a positive logit is divided by it, any other multiplied (:107-122).
+ * The draw is rand 0.8.5's WeightedIndex over the probabilities with the uniform
+ * value supplied by the caller. The reference's StdRng stream is not reproduced:
+ * rb_sampling_uniform gives a counter-based uniform with the same 2^-23 grid. */
+typedef struct rb_sampling {
+  double temperature;       /* < 1e-7: greedy */
+  double top_p;             /* used when 0 < top_p < 1 */
+  uint32_t top_k;           /* used when 0 < top_k < vocab */
+  float repetition_penalty; /* 1.0: off */
+} rb_sampling;
+
+/* Samples one token per row of logits [n_rows][ld] (vocab <= 55296). prev_tokens /
+ * prev_offsets: row r's previous tokens are prev_tokens[prev_offsets[r] ..
+ * prev_offsets[r + 1]) (both NULL: none). uniforms: [n_rows] values in [0, 1).
+ * With RB_PTR_DEVICE every pointer is device memory; otherwise all are host
+ * memory. Returns n_rows, or RB_ERR_INVALID ("Failed to create weighted index")
+ * if a row has no positive probability left, as the reference's Err. */
+int32_t rb_sample_logits(rb_ctx* ctx, const float* logits, uint32_t ld, uint32_t n_rows, uint32_t vocab,
+                         const rb_sampling* params, const uint32_t* prev_tokens, const uint32_t* prev_offsets,
+                         const float* uniforms, uint32_t* out_tokens, uint32_t flags);
+/* The counter-based uniform draw in [0, 1) (a multiple of 2^-23) of (seed, counter):
+ * SplitMix64 of seed + counter * 0x9E3779B97F4A7C15, top 23 bits. */
+float rb_sampling_uniform(uint64_t seed, uint64_t counter);
+/* rb_forward, then rb_sample_logits over the step's logits on the device (host
+ * pointers; params, prev_* and uniforms per row as rb_sample_logits; logits: NULL,
+ * or [n_rows][vocab] for the raw logits). Returns n_rows. */
+int32_t rb_forward_sample(rb_ctx* ctx, int32_t model, uint32_t n_rows, const uint32_t* tenants, const uint32_t* tokens,
+                          const uint32_t* positions, const rb_sampling* params, const uint32_t* prev_tokens,
+                          const uint32_t* prev_offsets, const float* uniforms, uint32_t* out_tokens, float* logits);
+
 /* ---- continuous batching ----
  * rb_batcher is ContinuousBatcher / BatchedRequest
  * (crates/realm-runtime/src/batching.rs:10-210) as host code, with the same rules:
@@ -456,6 +493,13 @@ int32_t rb_scheduler_step(rb_scheduler* s, rb_step_event* events, uint32_t cap, 
  * tokens (may be NULL) and its RB_FINISH_* state to *finish (may be NULL);
  * returns n. Queued requests return 0 with RB_FINISH_NONE. */
 int32_t rb_scheduler_result(rb_scheduler* s, uint64_t request_id, uint32_t* tokens, uint32_t cap, int32_t* finish);
+/* rb_scheduler_submit with a sampling strategy (LogitsProcessor::with_params,
+ * crates/realm-models/src/sampling.rs:63-100) for this request: its tokens come from
+ * rb_forward_sample with uniform draws rb_sampling_uniform(seed, i) for its i-th
+ * generated token and its own generated tokens as the repetition-penalty history.
+ * params NULL: greedy, as rb_scheduler_submit. */
+int32_t rb_scheduler_submit_sampled(rb_scheduler* s, uint64_t request_id, const uint32_t* prompt, uint32_t n_prompt,
+                                    uint32_t max_tokens, const rb_sampling* params, uint64_t seed);
 /* Ends a queued or live request (RB_FINISH_CANCELLED; its KV pages are freed). */
 int32_t rb_scheduler_cancel(rb_scheduler* s, uint64_t request_id);
 /* Forgets a finished request. */

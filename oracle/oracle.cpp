@@ -765,3 +765,101 @@ int or_model_generate(void* model, const uint32_t* prompt, size_t n_prompt, size
 }
 
 }  // extern "C"
+// ---- sampling (crates/realm-models/src/sampling.rs) ----
+namespace {
+
+// rand 0.8.5 WeightedIndex<f32>::new + sample with the uniform draw supplied:
+// cumulative weights w0, w0+w1, ... (sequential f32 sums, the last excluded),
+// total = the full sum; Uniform<f32>::new(0, total) shrinks its scale until
+// scale * (1 - 2^-23) < total; chosen = u * scale; the index is the number of
+// cumulative weights <= chosen. Err on a negative / NaN weight or a zero total.
+int weighted_index(const std::vector<float>& w, float u, uint32_t* out) {
+  if (w.empty() || !(w[0] >= 0.f)) return -1;
+  std::vector<float> cum;
+  cum.reserve(w.size());
+  float total = w[0];
+  for (size_t i = 1; i < w.size(); ++i) {
+    if (!(w[i] >= 0.f)) return -1;
+    cum.push_back(total);
+    total += w[i];
+  }
+  if (!(total > 0.f) || !std::isfinite(total)) return -1;
+  const float max_rand = 1.0f - 1.1920928955078125e-07f;
+  float scale = total;
+  while (scale * max_rand >= total) scale = std::nextafter(scale, 0.0f);
+  const float chosen = u * scale;
+  *out = (uint32_t)(std::partition_point(cum.begin(), cum.end(), [&](float c) { return c <= chosen; }) - cum.begin());
+  return 0;
+}
+
+// compute_probabilities (sampling.rs:125-137): x / (temperature as f32), then a
+// softmax with sequential f32 sums.
+std::vector<float> probabilities(const float* logits, size_t n, double temperature) {
+  const float t = (float)temperature;
+  std::vector<float> s(n);
+  float mx = -std::numeric_limits<float>::infinity();
+  for (size_t i = 0; i < n; ++i) {
+    s[i] = logits[i] / t;
+    mx = std::max(mx, s[i]);
+  }
+  float sum = 0.f;
+  for (size_t i = 0; i < n; ++i) sum += std::exp(s[i] - mx);
+  for (size_t i = 0; i < n; ++i) s[i] = std::exp(s[i] - mx) / sum;
+  return s;
+}
+
+void renormalize(std::vector<float>& p) {
+  float sum = 0.f;
+  for (float v : p) sum += v;
+  if (sum > 0.f)
+    for (float& v : p) v /= sum;
+}
+
+// top-k (sampling.rs:194-216): keep the k largest (ties go to the lower index;
+// the reference's unstable selection leaves them unspecified), zero the rest.
+void keep_top_k(std::vector<float>& p, size_t k) {
+  std::vector<uint32_t> idx(p.size());
+  for (size_t i = 0; i < p.size(); ++i) idx[i] = (uint32_t)i;
+  std::stable_sort(idx.begin(), idx.end(), [&](uint32_t a, uint32_t b) { return p[a] > p[b]; });
+  for (size_t r = k; r < idx.size(); ++r) p[idx[r]] = 0.f;
+  renormalize(p);
+}
+
+// top-p (sampling.rs:162-188): stable descending sort; a token is zeroed once the
+// running f32 sum of the tokens before it has reached top_p.
+void keep_top_p(std::vector<float>& p, float top_p) {
+  std::vector<uint32_t> idx(p.size());
+  for (size_t i = 0; i < p.size(); ++i) idx[i] = (uint32_t)i;
+  std::stable_sort(idx.begin(), idx.end(), [&](uint32_t a, uint32_t b) { return p[a] > p[b]; });
+  float cum = 0.f;
+  for (uint32_t i : idx) {
+    if (cum >= top_p) p[i] = 0.f;
+    else cum += p[i];
+  }
+  renormalize(p);
+}
+
+}  // namespace
+
+extern "C" {
+
+int or_sample(float* logits, size_t n, double temperature, double top_p, size_t top_k, float penalty,
+              const uint32_t* prev, size_t n_prev, float u, uint32_t* out) {
+  // apply_repetition_penalty (sampling.rs:107-122): once per occurrence
+  if (penalty != 1.0f)
+    for (size_t j = 0; j < n_prev; ++j) {
+      const size_t i = prev[j];
+      if (i < n) logits[i] = logits[i] > 0.f ? logits[i] / penalty : logits[i] * penalty;
+    }
+  // with_params (sampling.rs:63-100) picks the strategy; sample (:250-290) runs it
+  if (temperature < 1e-7) {
+    *out = or_argmax(logits, n);
+    return 0;
+  }
+  std::vector<float> p = probabilities(logits, n, temperature);
+  if (top_k > 0 && top_k < n) keep_top_k(p, top_k);
+  if (top_p > 0.0 && top_p < 1.0) keep_top_p(p, (float)top_p);
+  return weighted_index(p, u, out);
+}
+
+}  // extern "C"

@@ -101,4 +101,14 @@ int or_model_generate(void* model, const uint32_t* prompt, size_t n_prompt, size
                       uint32_t* out_tokens, float* step_logits);
 // argmax with ties to the LAST index (Rust Iterator::max_by, sampling.rs:141-148)
 uint32_t or_argmax(const float* x, size_t n);
+
+// LogitsProcessor::with_params(seed, temperature, top_p, top_k, repetition_penalty)
+// then sample(logits) (crates/realm-models/src/sampling.rs:63-100, 107-300), with
+// the random draw supplied: u in [0, 1) is the value rand 0.8.5's Uniform<f32>
+// sampler would produce (a multiple of 2^-23). previous tokens: prev[n_prev]
+// (the tokens this processor sampled before). logits is modified in place as the
+// reference does. Writes the token to *out; returns 0, or -1 where the
+// reference returns Err (WeightedIndex::new failed).
+int or_sample(float* logits, size_t n, double temperature, double top_p, size_t top_k, float penalty,
+              const uint32_t* prev, size_t n_prev, float u, uint32_t* out);
 }

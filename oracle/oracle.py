@@ -47,6 +47,7 @@ def lib():
         L.or_rms_norm.argtypes = [vp, vp, C.c_float, sz, sz, vp]
         L.or_rope.argtypes = [vp, sz, sz, sz, sz, C.c_float]
         L.or_attention.argtypes = [vp, vp, vp, sz, sz, sz, sz, sz, sz, vp]
+        L.or_sample.argtypes = [vp, sz, C.c_double, C.c_double, sz, C.c_float, vp, sz, C.c_float, vp]
         L.or_kv_new.argtypes = [sz, sz, sz, i32]
         L.or_kv_new.restype = vp
         L.or_kv_free.argtypes = [vp]
@@ -149,6 +150,17 @@ def attention(q, k, v, seq_len, kv_len, position, n_heads, n_kv, hd):
 def argmax(x):
     x = np.ascontiguousarray(x, np.float32)
     return int(lib().or_argmax(_p(x), x.size))
+
+
+def sample(logits, temperature, top_p, top_k, penalty, prev, u):
+    """LogitsProcessor::with_params(..).sample (sampling.rs:63-300) with the uniform
+    draw u supplied; returns (token or None on the reference's Err, penalised logits)."""
+    x = np.array(logits, np.float32)
+    pv = np.ascontiguousarray(np.asarray(prev, np.int64).astype(np.uint32))
+    out = np.zeros(1, np.uint32)
+    rc = lib().or_sample(_p(x), x.size, float(temperature), float(top_p), int(top_k), float(penalty),
+                         _p(pv) if pv.size else None, pv.size, float(u), _p(out))
+    return (None if rc < 0 else int(out[0])), x
 
 
 def f32_to_f16_bits(v: float) -> int:

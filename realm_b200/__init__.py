@@ -545,3 +545,4 @@ class Model:
 from .batching import (BatchedRequest, BatchStats, ContinuousBatcher, Scheduler,  # noqa: E402
                        prepare_batch)
 from .gguf import GGUFFile, TensorDesc  # noqa: E402
+from .sampling import LogitsProcessor, SamplingParams, sample_logits, sampling_uniform  # noqa: E402

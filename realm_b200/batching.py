@@ -71,6 +71,7 @@ _sig("rb_scheduler_destroy", [_vp])
 _sig("rb_scheduler_submit", [_vp, _u64, _vp, _u32, _u32])
 _sig("rb_scheduler_step", [_vp, C.POINTER(_StepEvent), _u32, _vp])
 _sig("rb_scheduler_result", [_vp, _u64, _vp, _u32, C.POINTER(C.c_int32)])
+_sig("rb_scheduler_submit_sampled", [_vp, _u64, _vp, _u32, _u32, _vp, _u64])
 _sig("rb_scheduler_cancel", [_vp, _u64])
 _sig("rb_scheduler_release", [_vp, _u64])
 _sig("rb_scheduler_stats", [_vp, C.POINTER(_SchedStats)])
@@ -231,10 +232,16 @@ class Scheduler:
         except Exception:
             pass
 
-    def submit(self, request_id: int, prompt: Sequence[int], max_tokens: int) -> None:
+    def submit(self, request_id: int, prompt: Sequence[int], max_tokens: int, sampling=None, seed: int = 0) -> None:
+        """sampling: a realm_b200.SamplingParams (None: greedy); seed: its uniform stream."""
         toks = _u32_array(prompt)
-        _check(_lib.rb_scheduler_submit(self._h, request_id, toks.ctypes.data if toks.size else None, toks.size,
-                                        max_tokens))
+        if sampling is None:
+            _check(_lib.rb_scheduler_submit(self._h, request_id, toks.ctypes.data if toks.size else None, toks.size,
+                                            max_tokens))
+            return
+        p = sampling.c()
+        _check(_lib.rb_scheduler_submit_sampled(self._h, request_id, toks.ctypes.data if toks.size else None,
+                                                toks.size, max_tokens, C.byref(p), seed & (2**64 - 1)))
 
     def step(self, want_logits: bool = False):
         """One step. Returns [StepEvent], or ([StepEvent], logits [n][vocab]) with want_logits."""

@@ -13,8 +13,8 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 CSRC = os.path.join(HERE, "csrc")
 BUILD = os.path.join(HERE, "_build")
 LIB = os.path.join(HERE, "librealm_b200.so")
-SOURCES = ["gemv.cu", "attention.cu", "engine.cu", "scheduler.cpp", "gguf.cpp"]
-HEADERS = ["common.cuh", "quant.cuh", "gemv.cuh", "attention.cuh", "xfrag.cuh"]
+SOURCES = ["gemv.cu", "attention.cu", "engine.cu", "sample.cu", "scheduler.cpp", "gguf.cpp"]
+HEADERS = ["common.cuh", "quant.cuh", "gemv.cuh", "attention.cuh", "xfrag.cuh", "sample.cuh"]
 NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
 FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a", "-O3", "-std=c++17", "-lineinfo",
          "-Xcompiler", "-fPIC"]

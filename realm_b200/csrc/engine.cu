@@ -20,6 +20,7 @@
 #include "common.cuh"
 #include "gemv.cuh"
 #include "quant.cuh"
+#include "sample.cuh"
 #include "xfrag.cuh"
 
 namespace rb {
@@ -1613,6 +1614,75 @@ int32_t rb_forward(rb_ctx* c, int32_t model, uint32_t n_rows, const uint32_t* te
     }
   }
   return (int32_t)n_rows;
+}
+
+static int sample_rows(rb_ctx* c, const float* d_logits, uint32_t ld, uint32_t n_rows, uint32_t vocab,
+                       const rb_sampling* params, const uint32_t* prev, const uint32_t* prev_off,
+                       const float* uniforms, uint32_t* out, uint32_t flags) {
+  if (!params || !uniforms || !out) return fail(RB_ERR_INVALID, "params/uniforms/out NULL");
+  if (n_rows == 0) return 0;
+  if (vocab == 0 || vocab > (uint32_t)kSampleMaxVocab || ld < vocab)
+    return fail(RB_ERR_UNSUPPORTED, "vocab %u not in [1, %d] or ld %u < vocab", vocab, kSampleMaxVocab, ld);
+  if ((prev == nullptr) != (prev_off == nullptr)) return fail(RB_ERR_INVALID, "prev_tokens and prev_offsets go together");
+  const bool dev = flags & RB_PTR_DEVICE;
+  uint32_t n_prev = 0;
+  if (prev_off && !dev) n_prev = prev_off[n_rows];
+  Staged sp, sprev, soff, su;
+  if (int rc = stage(c, params, (size_t)n_rows * sizeof(rb_sampling), flags, sp)) return rc;
+  if (prev_off) {
+    if (int rc = stage(c, prev_off, (size_t)(n_rows + 1) * 4, flags, soff)) return rc;
+    if (int rc = stage(c, prev, dev ? 0 : (size_t)n_prev * 4, flags, sprev)) return rc;
+  }
+  if (int rc = stage(c, uniforms, (size_t)n_rows * 4, flags, su)) return rc;
+  DevBuf dout;
+  uint32_t* o = out;
+  if (!dev) {
+    RB_CUDA(dout.alloc((size_t)n_rows * 4));
+    o = dout.as<uint32_t>();
+  }
+  RB_CUDA(sample_launch(d_logits, (int)ld, (int)n_rows, (int)vocab, (const rb_sampling*)sp.dptr,
+                        prev_off ? (const uint32_t*)sprev.dptr : nullptr, prev_off ? (const uint32_t*)soff.dptr : nullptr,
+                        (const float*)su.dptr, o, c->stream));
+  std::vector<uint32_t> h(n_rows);
+  RB_CUDA(cudaMemcpyAsync(h.data(), o, (size_t)n_rows * 4, cudaMemcpyDeviceToHost, c->stream));
+  if (int rc = sync_ctx(c)) return rc;
+  for (uint32_t r = 0; r < n_rows; ++r)
+    if (h[r] == 0xffffffffu) return fail(RB_ERR_INVALID, "row %u: Failed to create weighted index", r);
+  if (!dev) std::copy(h.begin(), h.end(), out);
+  return (int32_t)n_rows;
+}
+
+int32_t rb_sample_logits(rb_ctx* c, const float* logits, uint32_t ld, uint32_t n_rows, uint32_t vocab,
+                         const rb_sampling* params, const uint32_t* prev_tokens, const uint32_t* prev_offsets,
+                         const float* uniforms, uint32_t* out_tokens, uint32_t flags) {
+  if (!c) return fail(RB_ERR_BAD_HANDLE, "null context");
+  if (!logits) return fail(RB_ERR_INVALID, "logits NULL");
+  Staged sl;
+  if (int rc = stage(c, logits, (size_t)n_rows * ld * 4, flags, sl)) return rc;
+  return sample_rows(c, (const float*)sl.dptr, ld, n_rows, vocab, params, prev_tokens, prev_offsets, uniforms,
+                     out_tokens, flags);
+}
+
+float rb_sampling_uniform(uint64_t seed, uint64_t counter) {
+  // SplitMix64 (Steele, Lea, Flood 2014) of seed + counter * golden gamma; top 23 bits
+  uint64_t z = seed + counter * 0x9E3779B97F4A7C15ull + 0x9E3779B97F4A7C15ull;
+  z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
+  z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
+  z ^= z >> 31;
+  return (float)(z >> 41) * (1.0f / 8388608.0f);
+}
+
+int32_t rb_forward_sample(rb_ctx* c, int32_t model, uint32_t n_rows, const uint32_t* tenants, const uint32_t* tokens,
+                          const uint32_t* positions, const rb_sampling* params, const uint32_t* prev_tokens,
+                          const uint32_t* prev_offsets, const float* uniforms, uint32_t* out_tokens, float* logits) {
+  Model* M = get_model(c, model);
+  if (!M) return fail(RB_ERR_BAD_HANDLE, "model %d", model);
+  std::vector<uint32_t> am(n_rows ? n_rows : 1);
+  const int32_t rc = rb_forward(c, model, n_rows, tenants, tokens, positions, logits, am.data(), RB_PTR_HOST);
+  if (rc < 0) return rc;
+  // the step's logits stay in the model's device buffer until its next forward
+  return sample_rows(c, M->logits.as<float>(), M->cfg.vocab, n_rows, M->cfg.vocab, params, prev_tokens, prev_offsets,
+                     uniforms, out_tokens, RB_PTR_HOST);
 }
 
 int32_t rb_embed_tokens(rb_ctx* c, int32_t model, const uint32_t* ids, uint32_t n, float* out, uint32_t flags) {

@@ -1,0 +1,326 @@
+// Fused sampling of a batch of logits rows on the device: LogitsProcessor::sample
+// (crates/realm-models/src/sampling.rs:107-300) with the strategy picked as
+// LogitsProcessor::with_params does (:63-100), one CTA of 1024 threads per row,
+// the row held in shared memory.
+//
+//  1. repetition penalty once per occurrence of each previous token (:107-122);
+//     the occurrences of one token are applied in list order by one thread;
+//  2. temperature < 1e-7: argmax, ties to the last index (:141-148);
+//  3. x / (temperature as f32), softmax (:125-137);
+//  4. top-k: 4-pass radix select of the k-th largest probability on its bits;
+//     ties at the threshold keep the lowest indices (the reference's unstable
+//     selection leaves them unspecified); renormalise;
+//  5. top-p: keep a token while the probability mass ranked before it (value
+//     descending, index ascending, as the reference's stable sort) is below p;
+//     the boundary value is found by the same radix walk over per-bin counts and
+//     sums; renormalise;
+//  6. WeightedIndex (rand 0.8.5): total, Uniform(0, total) scale, chosen =
+//     u * scale, index = number of cumulative weights (all but the last) <= chosen.
+//
+// Sums are deterministic: fixed-order tree reductions for floats; the top-p bin
+// sums are 2^-40 fixed point with integer atomics (order independent). They
+// differ from the reference's sequential f32 sums by rounding only, which can
+// move a top-p or sampling boundary when a draw or a cumulative sum lands within
+// rounding of it.
+#include "common.cuh"
+#include "sample.cuh"
+
+namespace rb {
+
+namespace {
+
+constexpr int kST = 1024;  // threads per row
+constexpr int kSW = kST / 32;
+constexpr double kFix = 1099511627776.0;  // 2^40
+
+struct Red {
+  float f[kSW];
+  unsigned long long u[kSW];
+  uint32_t c[kSW];
+};
+
+__device__ float block_sum(float v, Red& r) {
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  __syncthreads();
+  if (lane == 0) r.f[w] = v;
+  __syncthreads();
+  float t = lane < kSW ? r.f[lane] : 0.f;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) t += __shfl_xor_sync(0xffffffffu, t, o);
+  return t;
+}
+
+__device__ float block_max(float v, Red& r) {
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  __syncthreads();
+  if (lane == 0) r.f[w] = v;
+  __syncthreads();
+  float t = lane < kSW ? r.f[lane] : -INFINITY;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) t = fmaxf(t, __shfl_xor_sync(0xffffffffu, t, o));
+  return t;
+}
+
+__device__ unsigned long long block_max_u64(unsigned long long v, Red& r) {
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const unsigned long long x = __shfl_xor_sync(0xffffffffu, v, o);
+    v = x > v ? x : v;
+  }
+  __syncthreads();
+  if (lane == 0) r.u[w] = v;
+  __syncthreads();
+  unsigned long long t = lane < kSW ? r.u[lane] : 0ull;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const unsigned long long x = __shfl_xor_sync(0xffffffffu, t, o);
+    t = x > t ? x : t;
+  }
+  return t;
+}
+
+// exclusive prefix (in thread order) of per-thread counts
+__device__ uint32_t block_excl_scan(uint32_t v, Red& r) {
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+  uint32_t x = v;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const uint32_t y = __shfl_up_sync(0xffffffffu, x, o);
+    if (lane >= o) x += y;
+  }
+  __syncthreads();
+  if (lane == 31) r.c[w] = x;
+  __syncthreads();
+  uint32_t base = 0;
+  for (int i = 0; i < w; ++i) base += r.c[i];
+  return base + x - v;
+}
+
+// exclusive prefix (in thread order) of per-thread float sums, fixed order
+__device__ float block_excl_scan_f(float v, Red& r) {
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+  float x = v;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const float y = __shfl_up_sync(0xffffffffu, x, o);
+    if (lane >= o) x += y;
+  }
+  __syncthreads();
+  if (lane == 31) r.f[w] = x;
+  __syncthreads();
+  float base = 0.f;
+  for (int i = 0; i < w; ++i) base += r.f[i];
+  return base + (x - v);
+}
+
+__device__ __forceinline__ uint32_t fkey(float f) { return __float_as_uint(f); }  // f >= 0: order preserved
+
+__global__ void __launch_bounds__(kST) sample_kernel(const float* logits, int ld, int V, const rb_sampling* prm,
+                                                     const uint32_t* prev, const uint32_t* prev_off, const float* uni,
+                                                     uint32_t* out) {
+  extern __shared__ float sv[];  // [V]
+  __shared__ Red red;
+  __shared__ uint32_t hc[256];
+  __shared__ unsigned long long hs[256];
+  __shared__ uint32_t sel_prefix, sel_rem;
+  __shared__ unsigned long long sel_acc;
+  const int row = blockIdx.x, tid = threadIdx.x;
+  const rb_sampling p = prm[row];
+  const float* lg = logits + (size_t)row * ld;
+  for (int i = tid; i < V; i += kST) sv[i] = lg[i];
+  __syncthreads();
+  // 1. repetition penalty: thread (token % 1024) applies every occurrence, in order
+  if (p.repetition_penalty != 1.0f && prev_off) {
+    const uint32_t j0 = prev_off[row], j1 = prev_off[row + 1];
+    for (uint32_t j = j0; j < j1; ++j) {
+      const uint32_t t = prev[j];
+      if (t < (uint32_t)V && (int)(t % kST) == tid) {
+        const float x = sv[t];
+        sv[t] = x > 0.f ? __fdiv_rn(x, p.repetition_penalty) : __fmul_rn(x, p.repetition_penalty);
+      }
+    }
+  }
+  __syncthreads();
+  const int C = (V + kST - 1) / kST, i0 = min(tid * C, V), i1 = min(i0 + C, V);  // contiguous chunk
+  // 2. greedy
+  if (p.temperature < 1e-7) {
+    unsigned long long best = 0ull;
+    for (int i = i0; i < i1; ++i) {
+      const unsigned long long k = ((unsigned long long)float_order_key(sv[i]) << 32) | (unsigned)i;
+      best = k > best ? k : best;
+    }
+    best = block_max_u64(best, red);
+    if (tid == 0) out[row] = (uint32_t)(best & 0xffffffffu);
+    return;
+  }
+  // 3. temperature + softmax
+  const float tf = (float)p.temperature;
+  float mx = -INFINITY;
+  for (int i = i0; i < i1; ++i) {
+    sv[i] = __fdiv_rn(sv[i], tf);
+    mx = fmaxf(mx, sv[i]);
+  }
+  mx = block_max(mx, red);
+  float s = 0.f;
+  for (int i = i0; i < i1; ++i) {
+    sv[i] = expf(sv[i] - mx);
+    s += sv[i];
+  }
+  s = block_sum(s, red);
+  for (int i = i0; i < i1; ++i) sv[i] = __fdiv_rn(sv[i], s);
+  __syncthreads();
+  // 4. top-k
+  if (p.top_k > 0 && p.top_k < (uint32_t)V) {
+    if (tid == 0) {
+      sel_prefix = 0;
+      sel_rem = p.top_k;
+    }
+    for (int pass = 3; pass >= 0; --pass) {
+      if (tid < 256) hc[tid] = 0;
+      __syncthreads();
+      const uint32_t pre = sel_prefix, hmask = pass == 3 ? 0u : (0xffffffffu << (8 * (pass + 1)));
+      for (int i = i0; i < i1; ++i) {
+        const uint32_t k = fkey(sv[i]);
+        if ((k & hmask) == pre) atomicAdd(&hc[(k >> (8 * pass)) & 255u], 1u);
+      }
+      __syncthreads();
+      if (tid == 0) {
+        uint32_t rem = sel_rem;
+        int b = 255;
+        for (; b > 0; --b) {
+          if (hc[b] >= rem) break;
+          rem -= hc[b];
+        }
+        sel_prefix = pre | ((uint32_t)b << (8 * pass));
+        sel_rem = rem;
+      }
+      __syncthreads();
+    }
+    const uint32_t T = sel_prefix, keep_eq = sel_rem;
+    uint32_t n_eq = 0;
+    for (int i = i0; i < i1; ++i) n_eq += fkey(sv[i]) == T;
+    uint32_t rank = block_excl_scan(n_eq, red);
+    float ks = 0.f;
+    for (int i = i0; i < i1; ++i) {
+      const uint32_t k = fkey(sv[i]);
+      bool keep = k > T;
+      if (k == T) keep = rank++ < keep_eq;
+      if (!keep) sv[i] = 0.f;
+      ks += sv[i];
+    }
+    ks = block_sum(ks, red);
+    if (ks > 0.f)
+      for (int i = i0; i < i1; ++i) sv[i] = __fdiv_rn(sv[i], ks);
+    __syncthreads();
+  }
+  // 5. top-p
+  const float top_p = (float)p.top_p;
+  if (p.top_p > 0.0 && p.top_p < 1.0) {
+    const unsigned long long P = (unsigned long long)((double)top_p * kFix);
+    if (tid == 0) {
+      sel_prefix = 0;
+      sel_acc = 0ull;
+    }
+    for (int pass = 3; pass >= 0; --pass) {
+      if (tid < 256) {
+        hc[tid] = 0;
+        hs[tid] = 0ull;
+      }
+      __syncthreads();
+      const uint32_t pre = sel_prefix, hmask = pass == 3 ? 0u : (0xffffffffu << (8 * (pass + 1)));
+      for (int i = i0; i < i1; ++i) {
+        const uint32_t k = fkey(sv[i]);
+        if ((k & hmask) == pre) {
+          const uint32_t b = (k >> (8 * pass)) & 255u;
+          atomicAdd(&hc[b], 1u);
+          atomicAdd(&hs[b], (unsigned long long)((double)sv[i] * kFix));
+        }
+      }
+      __syncthreads();
+      if (tid == 0) {
+        // the lowest non-empty bin whose mass above it stays below P
+        unsigned long long a = sel_acc, best_a = sel_acc;
+        int best = -1;
+        for (int b = 255; b >= 0; --b) {
+          if (hc[b] && a < P) {
+            best = b;
+            best_a = a;
+          }
+          a += hs[b];
+        }
+        if (best < 0) best = 255, best_a = sel_acc;  // unreachable: the top element always qualifies
+        sel_prefix = pre | ((uint32_t)best << (8 * pass));
+        sel_acc = best_a;
+      }
+      __syncthreads();
+    }
+    const uint32_t T = sel_prefix;
+    const unsigned long long above = sel_acc, tq = (unsigned long long)((double)__uint_as_float(T) * kFix);
+    uint32_t n_eq = 0;
+    for (int i = i0; i < i1; ++i) n_eq += fkey(sv[i]) == T;
+    uint32_t rank = block_excl_scan(n_eq, red);
+    float ps = 0.f;
+    for (int i = i0; i < i1; ++i) {
+      const uint32_t k = fkey(sv[i]);
+      bool keep = k > T;
+      if (k == T) keep = above + (unsigned long long)(rank++) * tq < P;
+      if (!keep) sv[i] = 0.f;
+      ps += sv[i];
+    }
+    ps = block_sum(ps, red);
+    if (ps > 0.f)
+      for (int i = i0; i < i1; ++i) sv[i] = __fdiv_rn(sv[i], ps);
+    __syncthreads();
+  }
+  // 6. WeightedIndex
+  float cs = 0.f;
+  for (int i = i0; i < i1; ++i) cs += sv[i];
+  const float total = block_sum(cs, red);
+  if (!(total > 0.f) || !isfinite(total)) {
+    if (tid == 0) out[row] = 0xffffffffu;
+    return;
+  }
+  const float max_rand = 1.0f - 1.1920928955078125e-07f;
+  float scale = total;
+  while (__fmul_rn(scale, max_rand) >= total) scale = nextafterf(scale, 0.0f);
+  const float chosen = __fmul_rn(uni[row], scale);
+  float run = block_excl_scan_f(cs, red);
+  unsigned long long first = 0ull;  // max over (~index): the smallest index with cum > chosen
+  for (int i = i0; i < i1 && i < V - 1; ++i) {
+    run += sv[i];
+    if (run > chosen) {
+      first = 0xffffffffull - (unsigned)i + 1ull;
+      break;
+    }
+  }
+  first = block_max_u64(first, red);
+  if (tid == 0) out[row] = first ? (uint32_t)(0xffffffffull - first + 1ull) : (uint32_t)(V - 1);
+}
+
+}  // namespace
+
+size_t sample_smem_bytes(int vocab) { return (size_t)vocab * 4; }
+
+cudaError_t sample_launch(const float* logits, int ld, int n_rows, int vocab, const rb_sampling* params,
+                          const uint32_t* prev, const uint32_t* prev_off, const float* uniforms, uint32_t* out,
+                          cudaStream_t s) {
+  if (n_rows < 1 || vocab < 1 || vocab > kSampleMaxVocab || ld < vocab) return cudaErrorInvalidValue;
+  static unsigned long long attr_set = 0;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (!(attr_set & (1ull << dev))) {
+    cudaError_t e = cudaFuncSetAttribute(sample_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         (int)sample_smem_bytes(kSampleMaxVocab));
+    if (e != cudaSuccess) return e;
+    attr_set |= 1ull << dev;
+  }
+  sample_kernel<<<n_rows, kST, sample_smem_bytes(vocab), s>>>(logits, ld, vocab, params, prev, prev_off, uniforms, out);
+  return cudaGetLastError();
+}
+
+}  // namespace rb

@@ -187,6 +187,9 @@ struct Seq {
   uint32_t cached = 0;    // tokens in the KV cache
   uint32_t reserve = 0;   // KV pages held back for the worst case
   bool cancel = false;    // cancelled while live: retired by the next step
+  bool sampled = false;   // false: greedy argmax
+  rb_sampling params{};
+  uint64_t seed = 0;
 };
 
 uint32_t pages_for(uint32_t tokens) { return (tokens + kPageTokens - 1) / kPageTokens; }
@@ -284,6 +287,11 @@ int32_t rb_scheduler_destroy(rb_scheduler* s) {
 
 int32_t rb_scheduler_submit(rb_scheduler* s, uint64_t request_id, const uint32_t* prompt, uint32_t n_prompt,
                             uint32_t max_tokens) {
+  return rb_scheduler_submit_sampled(s, request_id, prompt, n_prompt, max_tokens, nullptr, 0);
+}
+
+int32_t rb_scheduler_submit_sampled(rb_scheduler* s, uint64_t request_id, const uint32_t* prompt, uint32_t n_prompt,
+                                    uint32_t max_tokens, const rb_sampling* params, uint64_t seed) {
   if (!s) return fail(RB_ERR_BAD_HANDLE, "null scheduler");
   if (n_prompt == 0 || !prompt) return fail(RB_ERR_INVALID, "request %llu: empty prompt", (unsigned long long)request_id);
   for (uint32_t i = 0; i < n_prompt; ++i)
@@ -292,6 +300,15 @@ int32_t rb_scheduler_submit(rb_scheduler* s, uint64_t request_id, const uint32_t
   q->id = request_id;
   q->prompt.assign(prompt, prompt + n_prompt);
   q->max_tokens = max_tokens;
+  if (params && params->temperature >= 1e-7) {  // with_params: below 1e-7 is argmax
+    q->sampled = true;
+    q->params = *params;
+    q->seed = seed;
+  } else if (params && params->repetition_penalty != 1.0f) {
+    q->sampled = true;  // greedy, but over penalised logits
+    q->params = *params;
+    q->seed = seed;
+  }
   std::lock_guard<std::mutex> g(s->mu);
   if (s->known(request_id)) return fail(RB_ERR_INVALID, "request %llu already submitted", (unsigned long long)request_id);
   if (n_prompt >= s->cfg.max_seq_len || max_tokens == 0) {
@@ -371,8 +388,34 @@ int32_t rb_scheduler_step(rb_scheduler* s, rb_step_event* events, uint32_t cap, 
     s->logits.resize((size_t)s->max_rows * s->vocab);
     lg = s->logits.data();
   }
-  const int32_t rc = rb_forward(s->ctx, s->model, n_rows, tenants.data(), tokens.data(), nullptr, lg, argmax.data(),
-                                RB_PTR_HOST);
+  bool any_sampled = false;
+  for (const Out& o : outs) any_sampled = any_sampled || o.seq->sampled;
+  int32_t rc;
+  if (!any_sampled) {
+    rc = rb_forward(s->ctx, s->model, n_rows, tenants.data(), tokens.data(), nullptr, lg, argmax.data(), RB_PTR_HOST);
+  } else {
+    // per-row strategies: rows without a token of their own stay greedy; the
+    // sampled requests bring their history and their next uniform draw
+    std::vector<rb_sampling> prm(n_rows);
+    std::vector<float> uni(n_rows, 0.f);
+    std::vector<uint32_t> off(n_rows + 1, 0), prev;
+    std::vector<const Seq*> row_seq(n_rows, nullptr);
+    for (const Out& o : outs) row_seq[o.row] = o.seq;
+    for (uint32_t r = 0; r < n_rows; ++r) {
+      prm[r] = rb_sampling{0.0, 1.0, 0u, 1.0f};
+      off[r] = (uint32_t)prev.size();
+      const Seq* q = row_seq[r];
+      if (q && q->sampled) {
+        prm[r] = q->params;
+        uni[r] = rb_sampling_uniform(q->seed, q->generated.size());
+        prev.insert(prev.end(), q->generated.begin(), q->generated.end());
+      }
+    }
+    off[n_rows] = (uint32_t)prev.size();
+    if (prev.empty()) prev.push_back(0);
+    rc = rb_forward_sample(s->ctx, s->model, n_rows, tenants.data(), tokens.data(), nullptr, prm.data(), prev.data(),
+                           off.data(), uni.data(), argmax.data(), lg);
+  }
   if (rc < 0) return rc;
   std::lock_guard<std::mutex> g(s->mu);
   for (auto& [q, n] : fed) q->cached += n;

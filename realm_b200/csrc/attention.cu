@@ -41,13 +41,21 @@ struct AttnCfg {
   static constexpr int STAGE = 2 * SBLK;
 };
 
+// Query columns per (row group, kv head) pair: the n_rep heads of up to
+// NC / n_rep consecutive rows of one tenant (a prefill chunk) share every K/V
+// page. fp16 pools only; 4 columns keep two CTAs per SM.
+template <int NREP, int F16>
+__host__ __device__ constexpr int attn_cols() {
+  return (F16 && NREP < 4) ? 4 : NREP;
+}
+
 template <int HD, int NREP, int F16>
 __host__ __device__ constexpr int attn_smem_bytes() {
   return 1024                                                           // ring alignment
          + kAttnWarps * AttnCfg<HD, F16>::NSW * AttnCfg<HD, F16>::STAGE  // rings
-         + NREP * HD * 4                                               // q
+         + attn_cols<NREP, F16>() * HD * 4                              // q
          + kAttnWarps * (NREP > 8 ? NREP : 8) * 16 * 4                 // probabilities
-         + kAttnWarps * NREP * (HD + 2) * 4                            // warp merge
+         + kAttnWarps * attn_cols<NREP, F16>() * (HD + 2) * 4           // warp merge
          + kAttnWarps * AttnCfg<HD, F16>::NSW * 8                      // mbarriers
          + kMaxRows * 8 + 64;                                          // row tables
 }
@@ -113,7 +121,7 @@ __device__ __forceinline__ void attn_stamp(const AttnArgs& a, int slot) {
 }
 
 struct UnitInfo {
-  int row, kvh, p_begin, p_end, len;
+  int row, nr, kvh, p_begin, p_end, len;  // row: first row of the group, nr rows
   long long x0, x1, ps, pe;
   bool valid;
 };
@@ -122,16 +130,18 @@ template <int HD, int NREP, int F16>
 __global__ void __launch_bounds__(kAttnWarps * 32) attn_kernel(const __grid_constant__ AttnArgs a) {
   using C = AttnCfg<HD, F16>;
   constexpr int NSW = C::NSW;
+  constexpr int NC = attn_cols<NREP, F16>(), RG = NC / NREP;  // query columns, rows per group
   extern __shared__ __align__(128) uint8_t smem_raw[];
   // the swizzle pattern of TMA boxes follows shared-memory address bits: align to 1 KB
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* rings = smem;
   float* qs = reinterpret_cast<float*>(rings + kAttnWarps * NSW * C::STAGE);
-  float* pb = qs + NREP * HD;
+  float* pb = qs + NC * HD;
   float* mrg = pb + kAttnWarps * (NREP > 8 ? NREP : 8) * 16;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(mrg + kAttnWarps * NREP * (HD + 2));
-  long long* row_pages = reinterpret_cast<long long*>(bars + kAttnWarps * NSW);  // prefix of pages per row
-  __shared__ int s_last;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(mrg + kAttnWarps * NC * (HD + 2));
+  long long* row_pages = reinterpret_cast<long long*>(bars + kAttnWarps * NSW);  // prefix of pages per row group
+  __shared__ int s_last, s_ng;
+  __shared__ int g_row0[kMaxRows], g_nr[kMaxRows];
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int n_kv = a.kv.n_kv;
@@ -148,22 +158,34 @@ __global__ void __launch_bounds__(kAttnWarps * 32) attn_kernel(const __grid_cons
   // new tokens that the previous kernel appends: pages wholly below the
   // smallest position of this launch's rows are streamed before waiting for it.
   __shared__ int s_pos_min;
-  // Stream-K over pages: the pages of all (row, kv head) pairs form one
-  // sequence (row-major, kv head, page); CTA b takes [P b / Gp, P (b+1) / Gp).
+  // Rows group by tenant: up to RG consecutive rows of one tenant at
+  // consecutive positions share a pair (the last has the largest position).
+  // Stream-K over pages: the pages of all (row group, kv head) pairs form one
+  // sequence (group-major, kv head, page); CTA b takes [P b / Gp, P (b+1) / Gp).
   if (threadIdx.x == 0) {
     long long acc = 0;
-    int pmin = 0x7fffffff;
-    for (int r = 0; r < a.n_rows; ++r) {
-      row_pages[r] = acc;
-      acc += (long long)n_kv * ((a.row_pos[r] >> 4) + 1);
-      pmin = min(pmin, a.row_pos[r]);
+    int pmin = 0x7fffffff, ng = 0;
+    for (int r = 0; r < a.n_rows;) {
+      int n = 1;
+      while (n < (a.group_rows ? RG : 1) && r + n < a.n_rows && a.row_tenant[r + n] == a.row_tenant[r] &&
+             a.row_pos[r + n] == a.row_pos[r + n - 1] + 1)
+        ++n;
+      g_row0[ng] = r;
+      g_nr[ng] = n;
+      row_pages[ng] = acc;
+      acc += (long long)n_kv * ((a.row_pos[r + n - 1] >> 4) + 1);
+      for (int i = 0; i < n; ++i) pmin = min(pmin, a.row_pos[r + i]);
+      ++ng;
+      r += n;
     }
-    row_pages[a.n_rows] = acc;
+    row_pages[ng] = acc;
+    s_ng = ng;
     s_pos_min = pmin;
   }
   __syncthreads();
   const int pos_min = a.early_kv ? s_pos_min : -1;
-  const long long P = row_pages[a.n_rows];
+  const int n_groups = s_ng;
+  const long long P = row_pages[n_groups];
   // only the first Gp = min(G, P) CTAs take pages, so that none of them is empty
   const long long Gp = P < G ? P : G;
   const long long P0 = (long long)blockIdx.x < Gp ? P * blockIdx.x / Gp : P;
@@ -175,10 +197,12 @@ __global__ void __launch_bounds__(kAttnWarps * 32) attn_kernel(const __grid_cons
     ui.valid = x < P1;
     if (!ui.valid) return ui;
     int r = 0;
-    while (r + 1 < a.n_rows && row_pages[r + 1] <= x) ++r;
-    const int np = (a.row_pos[r] >> 4) + 1;
+    while (r + 1 < n_groups && row_pages[r + 1] <= x) ++r;
+    const int last_pos = a.row_pos[g_row0[r] + g_nr[r] - 1];
+    const int np = (last_pos >> 4) + 1;
     const long long local = x - row_pages[r];
-    ui.row = r;
+    ui.row = g_row0[r];
+    ui.nr = g_nr[r];
     ui.kvh = (int)(local / np);
     ui.ps = row_pages[r] + (long long)ui.kvh * np;
     ui.pe = ui.ps + np;
@@ -186,7 +210,7 @@ __global__ void __launch_bounds__(kAttnWarps * 32) attn_kernel(const __grid_cons
     ui.x1 = P1 < ui.pe ? P1 : ui.pe;
     ui.p_begin = (int)(x - ui.ps);
     ui.p_end = (int)(ui.x1 - ui.ps);
-    ui.len = a.row_pos[r] + 1;
+    ui.len = last_pos + 1;
     return ui;
   };
 
@@ -252,9 +276,12 @@ __global__ void __launch_bounds__(kAttnWarps * 32) attn_kernel(const __grid_cons
   for (long long x = P0; x < P1;) {
     const UnitInfo ui = seg_at(x);
     x = ui.x1;
-    // q of the n_rep heads that share this kv head
-    for (int i = threadIdx.x; i < NREP * HD; i += blockDim.x)
-      qs[i] = a.q[(size_t)ui.row * a.ldq + (size_t)ui.kvh * NREP * HD + i];
+    // q of the n_rep heads that share this kv head, for each row of the group
+    const int nc = ui.nr * NREP;  // query columns in use
+    for (int i = threadIdx.x; i < nc * HD; i += blockDim.x) {
+      const int col = i / HD;
+      qs[i] = a.q[(size_t)(ui.row + col / NREP) * a.ldq + (size_t)(ui.kvh * NREP + col % NREP) * HD + i % HD];
+    }
     __syncthreads();
 
     if constexpr (F16) {
@@ -273,11 +300,15 @@ __global__ void __launch_bounds__(kAttnWarps * 32) attn_kernel(const __grid_cons
         for (int b = 0; b < 2; ++b) {
           const int d = ks * 16 + 2 * c + 8 * b;
           // scores in base-2 units: scale * log2(e) folded into q
-          const float x0 = g < NREP ? qs[g * HD + d] * qscale : 0.f;
-          const float x1 = g < NREP ? qs[g * HD + d + 1] * qscale : 0.f;
+          const float x0 = g < nc ? qs[g * HD + d] * qscale : 0.f;
+          const float x1 = g < nc ? qs[g * HD + d + 1] * qscale : 0.f;
           pack_hilo(x0, x1, qb[ks][0][b], qb[ks][1][b]);
         }
       float mh[2] = {-INFINITY, -INFINITY}, lh[2] = {0.f, 0.f};
+      // causal limit of columns 2c, 2c+1: their row's position + 1
+      int lim[2];
+#pragma unroll
+      for (int h = 0; h < 2; ++h) lim[h] = 2 * c + h < nc ? a.row_pos[ui.row + (2 * c + h) / NREP] + 1 : 0;
       float ot[KS][4];
 #pragma unroll
       for (int mt = 0; mt < KS; ++mt) ot[mt][0] = ot[mt][1] = ot[mt][2] = ot[mt][3] = 0.f;
@@ -305,7 +336,12 @@ __global__ void __launch_bounds__(kAttnWarps * 32) attn_kernel(const __grid_cons
         float sc[4];  // (tok g, head 2c), (g, 2c+1), (g+8, 2c), (g+8, 2c+1)
 #pragma unroll
         for (int e = 0; e < 4; ++e) sc[e] = (sa[0][e] + sa[2][e]) + (sa[1][e] + sa[3][e]);
-        const bool v0 = p * 16 + g < ui.len, v1 = p * 16 + g + 8 < ui.len;
+        bool v0h[2], v1h[2];
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          v0h[h] = p * 16 + g < lim[h];
+          v1h[h] = p * 16 + g + 8 < lim[h];
+        }
         // Online softmax with a lazily raised maximum: the running maximum of
         // heads 2c, 2c+1 changes only when some score of the page exceeds it
         // (a warp vote); then it is reduced over the lanes of each head and O
@@ -314,8 +350,8 @@ __global__ void __launch_bounds__(kAttnWarps * 32) attn_kernel(const __grid_cons
         float s0[2], s1[2], pr[4];
 #pragma unroll
         for (int h = 0; h < 2; ++h) {
-          s0[h] = v0 ? sc[h] : -INFINITY;
-          s1[h] = v1 ? sc[2 + h] : -INFINITY;
+          s0[h] = v0h[h] ? sc[h] : -INFINITY;
+          s1[h] = v1h[h] ? sc[2 + h] : -INFINITY;
         }
         const bool up = fmaxf(s0[0], s1[0]) > mh[0] || fmaxf(s0[1], s1[1]) > mh[1];
         if (__any_sync(0xffffffffu, up)) {
@@ -341,8 +377,8 @@ __global__ void __launch_bounds__(kAttnWarps * 32) attn_kernel(const __grid_cons
         }
 #pragma unroll
         for (int h = 0; h < 2; ++h) {
-          pr[h] = v0 ? exp2f(s0[h] - mh[h]) : 0.f;
-          pr[2 + h] = v1 ? exp2f(s1[h] - mh[h]) : 0.f;
+          pr[h] = v0h[h] ? exp2f(s0[h] - mh[h]) : 0.f;
+          pr[2 + h] = v1h[h] ? exp2f(s1[h] - mh[h]) : 0.f;
           lh[h] += pr[h] + pr[2 + h];
         }
         // P^T as the B operand: lane (g, c) needs heads g, tokens 2c, 2c+1, 2c+8, 2c+9
@@ -370,7 +406,7 @@ __global__ void __launch_bounds__(kAttnWarps * 32) attn_kernel(const __grid_cons
 #pragma unroll
         for (int q = 0; q < 4; ++q) {
           const int head = 2 * c + (q & 1), dim = mt * 16 + g + ((q & 2) ? 8 : 0);
-          if (head < NREP) mrg[(warp * NREP + head) * (HD + 2) + dim] = ot[mt][q];
+          if (head < nc) mrg[(warp * NC + head) * (HD + 2) + dim] = ot[mt][q];
         }
       // the per-lane partial sums of each head, then (m, l) in natural-log units
 #pragma unroll
@@ -382,9 +418,9 @@ __global__ void __launch_bounds__(kAttnWarps * 32) attn_kernel(const __grid_cons
       if (g == 0)
 #pragma unroll
         for (int h = 0; h < 2; ++h)
-          if (2 * c + h < NREP) {
-            mrg[(warp * NREP + 2 * c + h) * (HD + 2) + HD] = mh[h] * 0.6931471805599453f;
-            mrg[(warp * NREP + 2 * c + h) * (HD + 2) + HD + 1] = lh[h];
+          if (2 * c + h < nc) {
+            mrg[(warp * NC + 2 * c + h) * (HD + 2) + HD] = mh[h] * 0.6931471805599453f;
+            mrg[(warp * NC + 2 * c + h) * (HD + 2) + HD + 1] = lh[h];
           }
     } else {
       float m[NREP], l[NREP], o[NREP][DPL];
@@ -482,7 +518,8 @@ __global__ void __launch_bounds__(kAttnWarps * 32) attn_kernel(const __grid_cons
       // ---- this warp's partial -> mrg
 #pragma unroll
       for (int r = 0; r < NREP; ++r) {
-        float* w = mrg + (warp * NREP + r) * (HD + 2);
+        static_assert(F16 || NC == NREP, "fp32 pools keep one row per pair");
+      float* w = mrg + (warp * NC + r) * (HD + 2);
 #pragma unroll
         for (int d = 0; d < DPL; ++d) w[lane * DPL + d] = o[r][d];
         if (lane == 0) {
@@ -504,38 +541,41 @@ __global__ void __launch_bounds__(kAttnWarps * 32) attn_kernel(const __grid_cons
     auto finish = [&]() {
       __syncthreads();
       if (a.out)
-        for (int i = threadIdx.x; i < NREP * HD; i += blockDim.x)
-          a.out[(size_t)ui.row * a.ldo + (size_t)ui.kvh * NREP * HD + i] = ofin[i];
+        for (int i = threadIdx.x; i < nc * HD; i += blockDim.x) {
+          const int col = i / HD;
+          a.out[(size_t)(ui.row + col / NREP) * a.ldo + (size_t)(ui.kvh * NREP + col % NREP) * HD + i % HD] = ofin[i];
+        }
       if (a.xout.xi || a.xout.xf)
-        frags_write(ofin, 1, 0, NREP * HD, 1, ui.kvh * NREP * HD, ui.row, nullptr, a.xout, a.xf_nt, frag_scratch,
-                    threadIdx.x, blockDim.x, [] { __syncthreads(); });
+        for (int rl = 0; rl < ui.nr; ++rl)
+          frags_write(ofin + rl * NREP * HD, 1, 0, NREP * HD, 1, ui.kvh * NREP * HD, ui.row + rl, nullptr, a.xout,
+                      a.xf_nt, frag_scratch, threadIdx.x, blockDim.x, [] { __syncthreads(); });
     };
     auto merge_warps = [&](int i, float& M, float& Lsum, float& O) {
       const int r = i / HD, d = i % HD;
       M = -INFINITY;
-      for (int w = 0; w < kAttnWarps; ++w) M = fmaxf(M, mrg[(w * NREP + r) * (HD + 2) + HD]);
+      for (int w = 0; w < kAttnWarps; ++w) M = fmaxf(M, mrg[(w * NC + r) * (HD + 2) + HD]);
       Lsum = 0.f;
       O = 0.f;
       for (int w = 0; w < kAttnWarps; ++w) {
-        const float* ww = mrg + (w * NREP + r) * (HD + 2);
+        const float* ww = mrg + (w * NC + r) * (HD + 2);
         const float f = (ww[HD] == -INFINITY) ? 0.f : expf(ww[HD] - M);
         Lsum += ww[HD + 1] * f;
         O += ww[d] * f;
       }
     };
     if (whole) {
-      for (int i = threadIdx.x; i < NREP * HD; i += blockDim.x) {
+      for (int i = threadIdx.x; i < nc * HD; i += blockDim.x) {
         float M, Lsum, O;
         merge_warps(i, M, Lsum, O);
         ofin[i] = Lsum > 0.f ? O / Lsum : 0.f;
       }
       finish();
     } else {
-      for (int i = threadIdx.x; i < NREP * HD; i += blockDim.x) {
+      for (int i = threadIdx.x; i < nc * HD; i += blockDim.x) {
         const int r = i / HD, d = i % HD;
         float M, Lsum, O;
         merge_warps(i, M, Lsum, O);
-        float* dst = a.partials + (slot * NREP + r) * (HD + 2);
+        float* dst = a.partials + (slot * NC + r) * (HD + 2);
         __stcg(dst + d, O);
         if (d == 0) {
           __stcg(dst + HD, M);
@@ -557,22 +597,22 @@ __global__ void __launch_bounds__(kAttnWarps * 32) attn_kernel(const __grid_cons
         auto part = [&](int j) {
           const long long cc = cf + j;
           const int sl = cta_start(cc) >= ui.ps ? 0 : 1;
-          return a.partials + ((size_t)cc * 2 + sl) * NREP * (HD + 2);
+          return a.partials + ((size_t)cc * 2 + sl) * NC * (HD + 2);
         };
         // (m, l) of every contributor and head into shared memory (mrg is free)
-        float* tab = mrg;  // [ncon][NREP][2]
-        const bool fits = ncon * NREP * 2 <= kAttnWarps * NREP * (HD + 2);
+        float* tab = mrg;  // [ncon][NC][2]
+        const bool fits = ncon * NC * 2 <= kAttnWarps * NC * (HD + 2);
         if (fits)
-          for (int e = threadIdx.x; e < ncon * NREP; e += blockDim.x) {
-            const float* src = part(e / NREP) + (e % NREP) * (HD + 2);
+          for (int e = threadIdx.x; e < ncon * NC; e += blockDim.x) {
+            const float* src = part(e / NC) + (e % NC) * (HD + 2);
             tab[2 * e] = __ldcg(src + HD);
             tab[2 * e + 1] = __ldcg(src + HD + 1);
           }
         __syncthreads();
-        for (int i = threadIdx.x; i < NREP * HD; i += blockDim.x) {
+        for (int i = threadIdx.x; i < nc * HD; i += blockDim.x) {
           const int r = i / HD, d = i % HD;
-          auto mval = [&](int j) { return fits ? tab[2 * (j * NREP + r)] : __ldcg(part(j) + r * (HD + 2) + HD); };
-          auto lval = [&](int j) { return fits ? tab[2 * (j * NREP + r) + 1] : __ldcg(part(j) + r * (HD + 2) + HD + 1); };
+          auto mval = [&](int j) { return fits ? tab[2 * (j * NC + r)] : __ldcg(part(j) + r * (HD + 2) + HD); };
+          auto lval = [&](int j) { return fits ? tab[2 * (j * NC + r) + 1] : __ldcg(part(j) + r * (HD + 2) + HD + 1); };
           float M = -INFINITY;
           for (int j = 0; j < ncon; ++j) M = fmaxf(M, mval(j));
           float Lsum = 0.f, O = 0.f;
@@ -713,7 +753,7 @@ cudaError_t kv_tensor_map(const KvView& kv, size_t n_pages, CUtensorMap* out) {
 }
 
 size_t attn_partials_floats(int num_ctas, int n_rep, int hd) {
-  return (size_t)num_ctas * 2 * n_rep * (hd + 2);
+  return (size_t)num_ctas * 2 * (n_rep < 4 ? 4 : n_rep) * (hd + 2);  // query columns: attn_cols
 }
 
 cudaError_t attn_launch(const AttnArgs& a, int num_sms, cudaStream_t s, int pdl) {

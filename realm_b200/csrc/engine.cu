@@ -299,6 +299,8 @@ struct Ctx {
   int last_chain_phases = 1;
   bool qgemm = false;  // RB_QGEMM=1 sends batches of 16+ rows to the tcgen05 GEMM (measured slower than the GEMV)
   bool gemm_step = false;  // the step being enqueued runs its projections on the tcgen05 GEMM
+  int chain_prefetch = -1;  // RB_CHAIN_PREFETCH: next-phase weight units issued ahead of a grid barrier
+  int attn_group = 1;       // RB_ATTN_GROUP=0: one attention pair per row (no K/V sharing in prefill chunks)
   DevBuf qg_part;      // tcgen05 GEMM partial sums
 };
 
@@ -529,6 +531,7 @@ int chain_flush(Ctx* c, int* launches) {
   ca.n_phases = c->chain_n;
   ca.bar_mask = c->chain_mask;
   ca.gbar = c->gbar.as<unsigned long long>();
+  ca.prefetch = c->chain_prefetch;
   c->last_chain_phases = c->chain_n;
   c->chain_n = 0;
   c->chain_mask = 0;
@@ -625,6 +628,7 @@ int enqueue_layer(Ctx* c, Model& M, int l, int m, const int32_t* d_tenant, const
   at.counters = c->counters.as<int32_t>() + kCounters / 2;
   at.err = c->err.as<uint32_t>();
   at.early_kv = 1;  // the step's descriptor and page tables precede the step's first kernel
+  at.group_rows = c->attn_group;
   if (c->gemv_dbg & 2) at.dbg_ts = c->attn_ts.as<unsigned long long>();
   RB_CUDA(attn_launch(at, c->num_sms, c->stream, c->pdl ? 1 : 0));
   if (launches) ++*launches;
@@ -925,6 +929,8 @@ int32_t rb_ctx_create(const rb_config* cfg, rb_ctx** out) {
   }
   if (const char* d = getenv("RB_NO_CHAIN")) c->chains = atoi(d) == 0;
   if (const char* d = getenv("RB_QGEMM")) c->qgemm = atoi(d) != 0;
+  if (const char* d = getenv("RB_CHAIN_PREFETCH")) c->chain_prefetch = atoi(d);
+  if (const char* d = getenv("RB_ATTN_GROUP")) c->attn_group = atoi(d) != 0;
   RB_CUDA(cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking));
   RB_CUDA(cudaEventCreate(&c->ev0));
   RB_CUDA(cudaEventCreate(&c->ev1));

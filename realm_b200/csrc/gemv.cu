@@ -742,7 +742,9 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const __grid_constant
           npend = 0;
           RB_TS(p, 6);
         };
+        const int pf = (ca.prefetch >= 0 && ca.prefetch < S) ? ca.prefetch : S;
         for (int i = 0; i < pr.n_units; ++i) {
+          if (!dep && npend >= pf) resolve();
           const int s = rp.s;
           if (issued >= (uint32_t)S) {
             ok = mbar_wait(&empty[s], (rp.round - 1) & 1, a.err, DEV_TIMEOUT_EMPTY);
@@ -762,7 +764,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const __grid_constant
           if (++x_sb == a.nsb) x_sb = 0;
           rp.next(S);
           ++issued;
-          if (!dep && (npend == S || i + 1 == pr.n_units)) resolve();
+          if (!dep && (npend >= pf || i + 1 == pr.n_units)) resolve();
         }
       }
       // drain: every issued copy must land before this CTA may exit

@@ -79,6 +79,9 @@ struct ChainArgs {
   uint32_t bar_mask = 0;
   unsigned long long* gbar = nullptr;  // [kMaxPhases] grid-barrier arrival counters (monotonic, start at 0)
   int32_t stages = 0, stage_bytes = 0;  // ring geometry, set by gemv_chain_launch
+  // weight units a producer may issue for a phase before the grid barrier that
+  // phase waits on has passed (< 0: the whole ring)
+  int32_t prefetch = -1;
 };
 
 // Scratch needed by one GEMV launch (partials in floats, counters in ints).

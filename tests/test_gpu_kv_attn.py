@@ -126,3 +126,43 @@ def test_attention_append_then_attend(ctx, oracle):
         assert np.abs(out[t] - exp).max() < 2e-5
         gk, gv = pool.gather(t, 0)
         assert np.array_equal(gk.view(np.uint32), rk.view(np.uint32))
+
+
+@pytest.mark.parametrize("n_heads,n_kv,hd,kv_dtype", [
+    (32, 32, 128, "f16"),  # MHA: 4 rows per pair
+    (16, 8, 64, "f16"),    # GQA 2: 2 rows per pair
+    (32, 8, 128, "f16"),   # GQA 4: one row per pair
+    (32, 4, 64, "f32"),    # fp32 pools: one row per pair
+])
+def test_prompt_chunk_rows_share_pages(ctx, oracle, n_heads, n_kv, hd, kv_dtype):
+    """Consecutive rows of one tenant (a prompt chunk) attend as a group: each row
+    still sees exactly positions [0, its own position] (per-column causal mask)."""
+    import realm_b200 as rb
+    O = oracle
+    rng = np.random.default_rng(n_kv * 13 + hd)
+    f16 = kv_dtype == "f16"
+    L = 300
+    pool = ctx.kv_pool(1, n_kv, hd, rb.F16 if f16 else rb.F32, n_pages=3 * (L // 16 + 2), max_tenants=3,
+                       max_seq=512)
+    pool.shuffle(5)
+    ks, vs = [], []
+    for t in range(3):
+        pool.create(t)
+        k = rng.normal(size=(L, n_kv, hd)).astype(np.float32)
+        v = rng.normal(size=(L, n_kv, hd)).astype(np.float32)
+        pool.append(t, 0, k, v)
+        r = O.KVCache(512, n_kv, hd, kv_fp16=f16)
+        r.append(k, v)
+        ks.append(r)
+    # tenant 0: 13 rows at positions 15..27 (a page edge inside), tenant 1: 6 rows
+    # ending at the last position, tenant 2: one row, then tenant 0 again (new group)
+    tenants = [0] * 13 + [1] * 6 + [2] + [0] * 3
+    positions = list(range(15, 28)) + list(range(L - 6, L)) + [7] + [100, 101, 103]
+    q = rng.normal(size=(len(tenants), n_heads * hd)).astype(np.float32)
+    out = pool.attention_forward(0, tenants, q, n_heads, 1 / np.sqrt(hd), positions=positions)
+    for i, (t, p) in enumerate(zip(tenants, positions)):
+        rk, rv = ks[t].current_data()
+        n = (p + 1) * n_kv * hd
+        exp = _oracle_attn(O, rk[:n], rv[:n], q[i], p, n_heads, n_kv, hd)
+        err = np.abs(out[i] - exp)
+        assert err.max() <= 2e-3 and np.all(err <= 1e-3 * np.abs(exp) + 2e-5), (i, t, p, err.max())

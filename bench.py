@@ -439,6 +439,29 @@ def run_case(args):
     if args.case == "load":
         run_load(rb, torch, ctx, dev)
         return
+    if args.case == "sample":
+        run_sample(rb, torch, ctx, dev)
+        return
+    if args.case == "qgemm":
+        # the tcgen05 dequant-GEMM (opt-in path): 8 launches of a 4096 x 4096 Q4_K
+        # weight over 8 copies (75 MB > L2), 64 rows
+        ctx.close()
+        os.environ["RB_QGEMM"] = "1"
+        qctx = rb.Context(0)
+        n, k, m = 4096, 4096, 64
+        ws = []
+        for i in range(8):
+            x = torch.randn(n, k, device=dev).mul_(0.02)
+            blk = torch.empty(n * k // 256 * 144, dtype=torch.uint8, device=dev)
+            qctx.quantize(rb.Q4_K, x.view(-1), blk)
+            ws.append(rb.Weight(qctx, rb.Q4_K, n, k, blk))
+        xs = torch.randn(m, k, device=dev)
+        y = torch.empty(m, n, device=dev)
+        for w in ws:
+            w.matmul(xs, m, out=y)
+        torch.cuda.synchronize(dev)
+        print("qgemm case done", flush=True)
+        return
     m = build_model(rb, torch, ctx, dev, TENANTS_PER_GPU)
     rng = np.random.default_rng(4)
     lens = rng.integers(128, 513, TENANTS_PER_GPU)
@@ -546,6 +569,44 @@ def run_load(rb, torch, ctx, dev):
           flush=True)
 
 
+def run_sample(rb, torch, ctx, dev, n_rows=64, vocab=32000):
+    """Fused sampling on the device: 64 logits rows of the Llama vocabulary,
+    top-k 40 + top-p 0.9 + temperature 0.8 + repetition penalty 1.1 over 64
+    previous tokens per row, timed with CUDA events over 50 launches on the
+    context stream (device pointers). Prints one JSON line."""
+    import ctypes as C
+    from realm_b200 import sampling as S
+    g = torch.Generator(device=dev)
+    g.manual_seed(7)
+    lg = torch.randn(n_rows, vocab, generator=g, device=dev).mul_(3.0)
+    params = S._params_array([rb.SamplingParams(0.8, 0.9, 40, 1.1)] * n_rows)
+    dparams = torch.frombuffer(bytearray(bytes(params)), dtype=torch.uint8).to(dev)
+    prev = torch.randint(0, vocab, (n_rows * 64,), generator=g, device=dev, dtype=torch.int32)
+    off = torch.arange(0, n_rows * 64 + 1, 64, device=dev, dtype=torch.int32)
+    uni = torch.rand(n_rows, generator=g, device=dev)
+    out = torch.empty(n_rows, device=dev, dtype=torch.int32)
+    stream = torch.cuda.ExternalStream(ctx.stream, device=dev)
+
+    def call():
+        r = rb.lib().rb_sample_logits(ctx.handle, lg.data_ptr(), vocab, n_rows, vocab, dparams.data_ptr(),
+                                      prev.data_ptr(), off.data_ptr(), uni.data_ptr(), out.data_ptr(), rb.PTR_DEVICE)
+        assert r == n_rows, rb.last_error()
+    for _ in range(5):
+        call()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize(dev)
+    ev0.record(stream)
+    for _ in range(50):
+        call()
+    ev1.record(stream)
+    torch.cuda.synchronize(dev)
+    us = ev0.elapsed_time(ev1) * 1e3 / 50
+    print(json.dumps({"metric": "sample_us_per_call", "value": round(us, 2), "unit": "us", "rows": n_rows,
+                      "vocab": vocab, "strategy": "T 0.8, top-k 40, top-p 0.9, penalty 1.1 over 64 tokens",
+                      "note": "each call includes its host synchronisation and the 256-byte token copy back"}),
+          flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -553,7 +614,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU-baseline leg")
-    ap.add_argument("--case", choices=["gemv", "decode", "attn", "serve", "load"],
+    ap.add_argument("--case", choices=["gemv", "decode", "attn", "serve", "load", "sample", "qgemm"],
                     help="profiling case for ncu: run a small workload of one kernel family and exit")
     args = ap.parse_args()
     if args.case:

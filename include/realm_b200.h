@@ -358,7 +358,7 @@ typedef struct rb_sampling {
   float repetition_penalty; /* 1.0: off */
 } rb_sampling;
 
-/* Samples one token per row of logits [n_rows][ld] (vocab <= 55296). prev_tokens /
+/* Samples one token per row of logits [n_rows][ld] (vocab <= 53248). prev_tokens /
  * prev_offsets: row r's previous tokens are prev_tokens[prev_offsets[r] ..
  * prev_offsets[r + 1]) (both NULL: none). uniforms: [n_rows] values in [0, 1).
  * With RB_PTR_DEVICE every pointer is device memory; otherwise all are host

@@ -7,7 +7,7 @@
 
 namespace rb {
 
-constexpr int kSampleMaxVocab = 55296;  // the row lives in shared memory (216 KB)
+constexpr int kSampleMaxVocab = 53248;  // the row lives in shared memory (217 KB with chunk padding)
 
 size_t sample_smem_bytes(int vocab);
 // logits [n_rows][ld] (device), params [n_rows], previous tokens prev[prev_off[r] ..

@@ -41,21 +41,23 @@ struct AttnCfg {
   static constexpr int STAGE = 2 * SBLK;
 };
 
-// Query columns per (row group, kv head) pair: the n_rep heads of up to
-// NC / n_rep consecutive rows of one tenant (a prefill chunk) share every K/V
-// page. fp16 pools only; 4 columns keep two CTAs per SM.
-template <int NREP, int F16>
+// Query columns per (row group, kv head) pair: in the grouped variant (GR) the
+// n_rep heads of up to NC / n_rep consecutive rows of one tenant (a prompt
+// chunk) share every K/V page. fp16 pools only; 4 columns keep two CTAs per SM.
+// Steps without such rows (decode) run the ungrouped variant and its smaller
+// shared-memory footprint.
+template <int NREP, int F16, int GR = 1>
 __host__ __device__ constexpr int attn_cols() {
-  return (F16 && NREP < 4) ? 4 : NREP;
+  return (GR && F16 && NREP < 4) ? 4 : NREP;
 }
 
-template <int HD, int NREP, int F16>
+template <int HD, int NREP, int F16, int GR>
 __host__ __device__ constexpr int attn_smem_bytes() {
   return 1024                                                           // ring alignment
          + kAttnWarps * AttnCfg<HD, F16>::NSW * AttnCfg<HD, F16>::STAGE  // rings
-         + attn_cols<NREP, F16>() * HD * 4                              // q
+         + attn_cols<NREP, F16, GR>() * HD * 4                              // q
          + kAttnWarps * (NREP > 8 ? NREP : 8) * 16 * 4                 // probabilities
-         + kAttnWarps * attn_cols<NREP, F16>() * (HD + 2) * 4           // warp merge
+         + kAttnWarps * attn_cols<NREP, F16, GR>() * (HD + 2) * 4           // warp merge
          + kAttnWarps * AttnCfg<HD, F16>::NSW * 8                      // mbarriers
          + kMaxRows * 8 + 64;                                          // row tables
 }
@@ -126,11 +128,11 @@ struct UnitInfo {
   bool valid;
 };
 
-template <int HD, int NREP, int F16>
+template <int HD, int NREP, int F16, int GR>
 __global__ void __launch_bounds__(kAttnWarps * 32) attn_kernel(const __grid_constant__ AttnArgs a) {
   using C = AttnCfg<HD, F16>;
   constexpr int NSW = C::NSW;
-  constexpr int NC = attn_cols<NREP, F16>(), RG = NC / NREP;  // query columns, rows per group
+  constexpr int NC = attn_cols<NREP, F16, GR>(), RG = NC / NREP;  // query columns, rows per group
   extern __shared__ __align__(128) uint8_t smem_raw[];
   // the swizzle pattern of TMA boxes follows shared-memory address bits: align to 1 KB
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -167,7 +169,7 @@ __global__ void __launch_bounds__(kAttnWarps * 32) attn_kernel(const __grid_cons
     int pmin = 0x7fffffff, ng = 0;
     for (int r = 0; r < a.n_rows;) {
       int n = 1;
-      while (n < (a.group_rows ? RG : 1) && r + n < a.n_rows && a.row_tenant[r + n] == a.row_tenant[r] &&
+      while (n < RG && r + n < a.n_rows && a.row_tenant[r + n] == a.row_tenant[r] &&
              a.row_pos[r + n] == a.row_pos[r + n - 1] + 1)
         ++n;
       g_row0[ng] = r;
@@ -647,10 +649,10 @@ __global__ void __launch_bounds__(kAttnWarps * 32) attn_kernel(const __grid_cons
       mbar_wait(&mybars[k % NSW], (k / NSW) & 1, a.err, DEV_TIMEOUT_DRAIN);
 }
 
-template <int HD, int NREP, int F16>
+template <int HD, int NREP, int F16, int GR>
 cudaError_t launch_attn_t(const AttnArgs& a, int num_sms, cudaStream_t s, int pdl) {
-  constexpr int smem = attn_smem_bytes<HD, NREP, F16>();
-  auto kern = attn_kernel<HD, NREP, F16>;
+  constexpr int smem = attn_smem_bytes<HD, NREP, F16, GR>();
+  auto kern = attn_kernel<HD, NREP, F16, GR>;
   static unsigned long long attr_set = 0;
   int dev = 0;
   cudaGetDevice(&dev);
@@ -678,11 +680,12 @@ cudaError_t launch_attn_t(const AttnArgs& a, int num_sms, cudaStream_t s, int pd
 
 template <int HD, int F16>
 cudaError_t launch_attn_hd(const AttnArgs& a, int nrep, int num_sms, cudaStream_t s, int pdl) {
+  const bool gr = F16 && a.group_rows;  // the grouped variant differs only for fp16 and n_rep < 4
   switch (nrep) {
-    case 1: return launch_attn_t<HD, 1, F16>(a, num_sms, s, pdl);
-    case 2: return launch_attn_t<HD, 2, F16>(a, num_sms, s, pdl);
-    case 4: return launch_attn_t<HD, 4, F16>(a, num_sms, s, pdl);
-    case 8: return launch_attn_t<HD, 8, F16>(a, num_sms, s, pdl);
+    case 1: return gr ? launch_attn_t<HD, 1, F16, 1>(a, num_sms, s, pdl) : launch_attn_t<HD, 1, F16, 0>(a, num_sms, s, pdl);
+    case 2: return gr ? launch_attn_t<HD, 2, F16, 1>(a, num_sms, s, pdl) : launch_attn_t<HD, 2, F16, 0>(a, num_sms, s, pdl);
+    case 4: return launch_attn_t<HD, 4, F16, 0>(a, num_sms, s, pdl);
+    case 8: return launch_attn_t<HD, 8, F16, 0>(a, num_sms, s, pdl);
   }
   return cudaErrorInvalidValue;
 }

@@ -34,7 +34,8 @@ struct AttnArgs {
   // pages may be read before it completes (the decode step); 0: wait first
   int32_t early_kv = 0;
   // 1: consecutive rows of one tenant at consecutive positions share K/V pages
-  // (up to 4 query columns per pair on fp16 pools); 0: one row per pair
+  // (the grouped kernel variant: up to 4 query columns per pair on fp16 pools);
+  // 0: one row per pair (decode steps, where no two rows share a tenant)
   int32_t group_rows = 1;
   unsigned long long* dbg_ts = nullptr;  // measurement hook: [cta][8] %globaltimer stamps (or null)
 };

@@ -266,7 +266,7 @@ struct Model {
   // activation fragments: q|k|v and LM-head input (a), o-proj (o), gate/up (f), down (d)
   FragBuf fa, fo, ff, fd;
   int max_rows = 0;
-  std::map<int, cudaGraphExec_t> graphs;  // by row count
+  std::map<int, cudaGraphExec_t> graphs;  // by 2 * row count + grouped attention
   std::map<int, int> graph_launches;
 };
 
@@ -301,6 +301,7 @@ struct Ctx {
   bool gemm_step = false;  // the step being enqueued runs its projections on the tcgen05 GEMM
   int chain_prefetch = -1;  // RB_CHAIN_PREFETCH: next-phase weight units issued ahead of a grid barrier
   int attn_group = 1;       // RB_ATTN_GROUP=0: one attention pair per row (no K/V sharing in prefill chunks)
+  bool step_grouped = false;  // the step has consecutive rows of one tenant (a prompt chunk)
   DevBuf qg_part;      // tcgen05 GEMM partial sums
 };
 
@@ -628,7 +629,7 @@ int enqueue_layer(Ctx* c, Model& M, int l, int m, const int32_t* d_tenant, const
   at.counters = c->counters.as<int32_t>() + kCounters / 2;
   at.err = c->err.as<uint32_t>();
   at.early_kv = 1;  // the step's descriptor and page tables precede the step's first kernel
-  at.group_rows = c->attn_group;
+  at.group_rows = c->attn_group && c->step_grouped;
   if (c->gemv_dbg & 2) at.dbg_ts = c->attn_ts.as<unsigned long long>();
   RB_CUDA(attn_launch(at, c->num_sms, c->stream, c->pdl ? 1 : 0));
   if (launches) ++*launches;
@@ -787,6 +788,14 @@ int plan_rows(KvPool& P, int n, const uint32_t* tenants, const uint32_t* tokens,
   return RB_OK;
 }
 
+// Whether some row continues the previous row's tenant at the next position:
+// such rows attend as a group (shared K/V pages).
+bool rows_grouped(const RowPlan& rp) {
+  for (size_t r = 1; r < rp.tenant.size(); ++r)
+    if (rp.tenant[r] == rp.tenant[r - 1] && rp.pos[r] == rp.pos[r - 1] + 1) return true;
+  return false;
+}
+
 int upload_desc(rb_ctx* c, const RowPlan& rp, int32_t* d_desc) {
   const int n = (int)rp.tenant.size(), nu = (int)rp.upd.size() / 3;
   const size_t ints = kDescUpd + 3 * (size_t)nu;
@@ -863,7 +872,8 @@ int run_forward(rb_ctx* c, Model& M, int m, bool use_graph) {
     if (int rc = ensure_qg_model(c, M)) return rc;
   RB_CUDA(cudaEventRecord(c->ev0, c->stream));
   if (use_graph) {
-    auto it = M.graphs.find(m);
+    const int key = 2 * m + (c->step_grouped ? 1 : 0);  // the attention variant is part of the graph
+    auto it = M.graphs.find(key);
     if (it == M.graphs.end()) {
       cudaGraph_t g = nullptr;
       RB_CUDA(cudaStreamBeginCapture(c->stream, cudaStreamCaptureModeThreadLocal));
@@ -878,11 +888,11 @@ int run_forward(rb_ctx* c, Model& M, int m, bool use_graph) {
       e = cudaGraphInstantiate(&ex, g, 0);
       cudaGraphDestroy(g);
       if (e != cudaSuccess) return fail(RB_ERR_CUDA, "graph instantiate: %s", cudaGetErrorString(e));
-      it = M.graphs.emplace(m, ex).first;
-      M.graph_launches[m] = launches;
+      it = M.graphs.emplace(key, ex).first;
+      M.graph_launches[key] = launches;
     }
     RB_CUDA(cudaGraphLaunch(it->second, c->stream));
-    launches = M.graph_launches[m];
+    launches = M.graph_launches[key];
   } else {
     if (int rc = enqueue_step(c, M, m, &launches)) return rc;
   }
@@ -1418,6 +1428,7 @@ int32_t rb_attention_forward(rb_ctx* c, int32_t pool, uint32_t layer, uint32_t n
   at.partials = c->attn_partials.as<float>();
   at.counters = c->counters.as<int32_t>() + kCounters / 2;
   at.err = c->err.as<uint32_t>();
+  at.group_rows = c->attn_group && rows_grouped(rp);
   RB_CUDA(cudaEventRecord(c->ev0, c->stream));
   RB_CUDA(attn_launch(at, c->num_sms, c->stream, 0));
   RB_CUDA(cudaEventRecord(c->ev1, c->stream));
@@ -1596,6 +1607,7 @@ int32_t rb_forward(rb_ctx* c, int32_t model, uint32_t n_rows, const uint32_t* te
   RowPlan rp;
   if (int rc = plan_rows(P, n_rows, tenants, tokens, positions, -1, rp)) return rc;
   if (int rc = upload_desc(c, rp, M->desc.as<int32_t>())) return rc;
+  c->step_grouped = rows_grouped(rp);
   if (int rc = run_forward(c, *M, n_rows, c->graphs)) return rc;
   // outputs
   std::vector<unsigned long long> keys(n_rows);
@@ -1743,6 +1755,7 @@ int32_t rb_forward_layer(rb_ctx* c, int32_t model, uint32_t t, uint32_t layer, c
                        M->fa.view(), M->ss.as<float>(), kMaxRowsAbi, c->stream));
   int launches = 2;
   c->gemm_step = c->qgemm && S >= (uint32_t)kQgemmMinRows;
+  c->step_grouped = S > 1;  // one tenant at consecutive positions
   if (c->gemm_step)
     if (int rc = ensure_qg_model(c, *M)) return rc;
   RB_CUDA(cudaEventRecord(c->ev0, c->stream));

@@ -436,6 +436,9 @@ def run_case(args):
     if args.case == "serve":
         run_serve(rb, torch, ctx, dev)
         return
+    if args.case == "serve_sampled":
+        run_serve(rb, torch, ctx, dev, sampling=rb.SamplingParams(0.8, 0.9, 40, 1.1))
+        return
     if args.case == "load":
         run_load(rb, torch, ctx, dev)
         return
@@ -477,7 +480,7 @@ def run_case(args):
         print("decode step", s, ctx.last_forward_launches(), "launches", flush=True)
 
 
-def run_serve(rb, torch, ctx, dev, n_req=96, max_batch=32, max_tokens=128):
+def run_serve(rb, torch, ctx, dev, n_req=96, max_batch=32, max_tokens=128, sampling=None):
     """Continuous batching through rb_scheduler on the bench model: n_req
     requests (prompts U[128, 512] from seed 5) all queued at t = 0, at most
     max_batch live, max_tokens each. Every step is one rb_forward over the live
@@ -501,7 +504,7 @@ def run_serve(rb, torch, ctx, dev, n_req=96, max_batch=32, max_tokens=128):
     s = rb.Scheduler(m, max_batch_size=max_batch)
     st0 = s.stats()
     for i in range(n_req):
-        s.submit(i, rng.integers(0, CFG["vocab"], int(lens[i])).tolist(), max_tokens)
+        s.submit(i, rng.integers(0, CFG["vocab"], int(lens[i])).tolist(), max_tokens, sampling=sampling, seed=i)
     torch.cuda.synchronize(dev)
     t0 = time.perf_counter()
     with Clocks(0) as clk:
@@ -513,7 +516,9 @@ def run_serve(rb, torch, ctx, dev, n_req=96, max_batch=32, max_tokens=128):
     dev_ms = st["device_ms"] - st0["device_ms"]
     assert gen == n_req * max_tokens and all(len(v) == max_tokens for v in out.values())
     line = {
-        "metric": "serve_generated_tok_per_s", "value": round(gen / wall, 1), "unit": "tok/s",
+        "metric": "serve_generated_tok_per_s" + ("_sampled" if sampling else ""), "value": round(gen / wall, 1),
+        "unit": "tok/s",
+        "sampling": None if sampling is None else vars(sampling),
         "device_tok_per_s": round(gen / (dev_ms * 1e-3), 1),
         "prompt_tok_per_s": round(int(lens.sum()) / wall, 1),
         "steps": steps, "rows_per_step": round((st["rows"] - st0["rows"]) / steps, 2),
@@ -614,7 +619,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU-baseline leg")
-    ap.add_argument("--case", choices=["gemv", "decode", "attn", "serve", "load", "sample", "qgemm"],
+    ap.add_argument("--case", choices=["gemv", "decode", "attn", "serve", "serve_sampled", "load", "sample", "qgemm"],
                     help="profiling case for ncu: run a small workload of one kernel family and exit")
     args = ap.parse_args()
     if args.case:

@@ -142,7 +142,7 @@ __global__ void __launch_bounds__(kAttnWarps * 32) attn_kernel(const __grid_cons
   float* mrg = pb + kAttnWarps * (NREP > 8 ? NREP : 8) * 16;
   uint64_t* bars = reinterpret_cast<uint64_t*>(mrg + kAttnWarps * NC * (HD + 2));
   long long* row_pages = reinterpret_cast<long long*>(bars + kAttnWarps * NSW);  // prefix of pages per row group
-  __shared__ int s_last, s_ng;
+  __shared__ int s_last, s_ng, s_whole;
   __shared__ int g_row0[kMaxRows], g_nr[kMaxRows];
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -183,6 +183,13 @@ __global__ void __launch_bounds__(kAttnWarps * 32) attn_kernel(const __grid_cons
     row_pages[ng] = acc;
     s_ng = ng;
     s_pos_min = pmin;
+    // Whole pairs: when every pair fits on a CTA of its own and the longest is at
+    // most twice the even share, CTA b takes pair b whole (no partials, no merge).
+    int longest = 0;
+    for (int gi = 0; gi < ng; ++gi)
+      longest = max(longest, (a.row_pos[g_row0[gi] + g_nr[gi] - 1] >> 4) + 1);
+    const long long n_pairs = (long long)ng * n_kv, share = (acc + G - 1) / G;
+    s_whole = a.whole_pairs && n_pairs <= G && longest <= 2 * share;
   }
   __syncthreads();
   const int pos_min = a.early_kv ? s_pos_min : -1;
@@ -190,8 +197,19 @@ __global__ void __launch_bounds__(kAttnWarps * 32) attn_kernel(const __grid_cons
   const long long P = row_pages[n_groups];
   // only the first Gp = min(G, P) CTAs take pages, so that none of them is empty
   const long long Gp = P < G ? P : G;
-  const long long P0 = (long long)blockIdx.x < Gp ? P * blockIdx.x / Gp : P;
-  const long long P1 = (long long)blockIdx.x < Gp ? P * (blockIdx.x + 1) / Gp : P;
+  long long P0 = (long long)blockIdx.x < Gp ? P * blockIdx.x / Gp : P;
+  long long P1 = (long long)blockIdx.x < Gp ? P * (blockIdx.x + 1) / Gp : P;
+  if (s_whole) {
+    // pair b = (group b / n_kv, kv head b % n_kv): its pages within the group's block
+    const long long b = blockIdx.x;
+    P0 = P1 = P;
+    if (b < (long long)n_groups * n_kv) {
+      const int gi = (int)(b / n_kv), kvh = (int)(b % n_kv);
+      const long long np = (row_pages[gi + 1] - row_pages[gi]) / n_kv;
+      P0 = row_pages[gi] + kvh * np;
+      P1 = P0 + np;
+    }
+  }
   auto cta_start = [&](long long cc) { return P * cc / Gp; };
 
   auto seg_at = [&](long long x) -> UnitInfo {

@@ -37,6 +37,9 @@ struct AttnArgs {
   // (the grouped kernel variant: up to 4 query columns per pair on fp16 pools);
   // 0: one row per pair (decode steps, where no two rows share a tenant)
   int32_t group_rows = 1;
+  // 1: when the pairs are few and even enough, each CTA takes one (row, kv head)
+  // pair whole instead of an even share of all pages (no cross-CTA merge)
+  int32_t whole_pairs = 1;
   unsigned long long* dbg_ts = nullptr;  // measurement hook: [cta][8] %globaltimer stamps (or null)
 };
 

@@ -302,6 +302,7 @@ struct Ctx {
   int chain_prefetch = -1;  // RB_CHAIN_PREFETCH: next-phase weight units issued ahead of a grid barrier
   int attn_group = 1;       // RB_ATTN_GROUP=0: one attention pair per row (no K/V sharing in prefill chunks)
   bool step_grouped = false;  // the step has consecutive rows of one tenant (a prompt chunk)
+  int attn_whole = 1;         // RB_ATTN_WHOLE=0: always split attention pages evenly over the CTAs
   DevBuf qg_part;      // tcgen05 GEMM partial sums
 };
 
@@ -630,6 +631,7 @@ int enqueue_layer(Ctx* c, Model& M, int l, int m, const int32_t* d_tenant, const
   at.err = c->err.as<uint32_t>();
   at.early_kv = 1;  // the step's descriptor and page tables precede the step's first kernel
   at.group_rows = c->attn_group && c->step_grouped;
+  at.whole_pairs = c->attn_whole;
   if (c->gemv_dbg & 2) at.dbg_ts = c->attn_ts.as<unsigned long long>();
   RB_CUDA(attn_launch(at, c->num_sms, c->stream, c->pdl ? 1 : 0));
   if (launches) ++*launches;
@@ -941,6 +943,7 @@ int32_t rb_ctx_create(const rb_config* cfg, rb_ctx** out) {
   if (const char* d = getenv("RB_QGEMM")) c->qgemm = atoi(d) != 0;
   if (const char* d = getenv("RB_CHAIN_PREFETCH")) c->chain_prefetch = atoi(d);
   if (const char* d = getenv("RB_ATTN_GROUP")) c->attn_group = atoi(d) != 0;
+  if (const char* d = getenv("RB_ATTN_WHOLE")) c->attn_whole = atoi(d) != 0;
   RB_CUDA(cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking));
   RB_CUDA(cudaEventCreate(&c->ev0));
   RB_CUDA(cudaEventCreate(&c->ev1));

@@ -183,13 +183,14 @@ __global__ void __launch_bounds__(kAttnWarps * 32) attn_kernel(const __grid_cons
     row_pages[ng] = acc;
     s_ng = ng;
     s_pos_min = pmin;
-    // Whole pairs: when every pair fits on a CTA of its own and the longest is at
-    // most twice the even share, CTA b takes pair b whole (no partials, no merge).
+    // Whole pairs: CTA b takes pairs [b n / G, (b + 1) n / G) whole (no partials,
+    // no merge) when even the worst CTA (ceil(n / G) pairs of the longest length)
+    // stays within twice the even page share; every CTA computes the same answer.
     int longest = 0;
     for (int gi = 0; gi < ng; ++gi)
       longest = max(longest, (a.row_pos[g_row0[gi] + g_nr[gi] - 1] >> 4) + 1);
     const long long n_pairs = (long long)ng * n_kv, share = (acc + G - 1) / G;
-    s_whole = a.whole_pairs && n_pairs <= G && longest <= 2 * share;
+    s_whole = a.whole_pairs && (long long)longest * ((n_pairs + G - 1) / G) <= 2 * share;
   }
   __syncthreads();
   const int pos_min = a.early_kv ? s_pos_min : -1;
@@ -200,15 +201,15 @@ __global__ void __launch_bounds__(kAttnWarps * 32) attn_kernel(const __grid_cons
   long long P0 = (long long)blockIdx.x < Gp ? P * blockIdx.x / Gp : P;
   long long P1 = (long long)blockIdx.x < Gp ? P * (blockIdx.x + 1) / Gp : P;
   if (s_whole) {
-    // pair b = (group b / n_kv, kv head b % n_kv): its pages within the group's block
-    const long long b = blockIdx.x;
-    P0 = P1 = P;
-    if (b < (long long)n_groups * n_kv) {
-      const int gi = (int)(b / n_kv), kvh = (int)(b % n_kv);
-      const long long np = (row_pages[gi + 1] - row_pages[gi]) / n_kv;
-      P0 = row_pages[gi] + kvh * np;
-      P1 = P0 + np;
-    }
+    // pair q = (group q / n_kv, kv head q % n_kv) starts at page row_pages[group] + kv head * np
+    const long long n_pairs = (long long)n_groups * n_kv;
+    auto pair_start = [&](long long q) -> long long {
+      if (q >= n_pairs) return P;
+      const int gi = (int)(q / n_kv), kvh = (int)(q % n_kv);
+      return row_pages[gi] + kvh * ((row_pages[gi + 1] - row_pages[gi]) / n_kv);
+    };
+    P0 = pair_start(n_pairs * blockIdx.x / G);
+    P1 = pair_start(n_pairs * (blockIdx.x + 1) / G);
   }
   auto cta_start = [&](long long cc) { return P * cc / Gp; };
 

@@ -82,6 +82,19 @@ int32_t rb_sync(rb_ctx* ctx);
 /* The context's cudaStream_t, for callers that enqueue their own copies. */
 void* rb_stream(rb_ctx* ctx);
 int32_t rb_num_sms(rb_ctx* ctx);
+/* Test hook: the architecture the library's kernels were compiled for, as the
+ * CUDA runtime reports it for the loaded module (cudaFuncAttributes::binaryVersion,
+ * 100 for sm_100a), written to *version. */
+int32_t rb_kernel_binary_version(rb_ctx* ctx, int32_t* version);
+/* Failure-detection test hook: the next multi-phase GEMV launch on this context
+ * (the next rb_forward runs it outside any cached CUDA graph) gets its first
+ * grid barrier's target out of reach, and every grid-barrier wait in it gives
+ * up after spin_polls polls. The waits report through the device error word,
+ * the kernel finishes, and the call returns RB_ERR_TIMEOUT (the reference's
+ * host functions map such failures to a negative status as well,
+ * crates/realm-runtime/src/host_functions.rs:145-155); the context stays usable.
+ * Cache lengths are not advanced by the failed step. */
+int32_t rb_test_fail_next_grid_barrier(rb_ctx* ctx, uint32_t spin_polls);
 
 /* ---- quantised blocks ----
  * rb_dequantize: bit-exact dequantize_q4_k / q6_k / q8_0
@@ -117,10 +130,14 @@ int32_t rb_weight_matmul(rb_ctx* ctx, int32_t handle, const float* input, float*
  * returns without waiting), and all other working memory is one fixed
  * 3,434,496-byte device array in the library, held on every GPU that loads it
  * until the process exits. Limits: batch <= 8, K <= 16384, N <= 131072, at most
- * 160 GEMV CTAs; larger calls fail with RB_ERR_INVALID. Every call on a device
+ * 160 GEMV CTAs; larger calls fail with RB_ERR_INVALID. A Q8_0 weight whose K
+ * is not a multiple of 256 (rows zero-padded at upload) is refused with
+ * RB_ERR_UNSUPPORTED; rb_weight_matmul takes it. Every call on a device
  * shares the array (it keeps the last call's contents), so calls whose GPU
  * work overlaps race: order them on one stream. The first call on a device
- * looks up the array's address; make it before any stream capture there.
+ * looks up the array's address and caches it for the device's primary
+ * context: make that call before any stream capture there, and do not call
+ * again after the context was torn down (cudaDeviceReset) in this process.
  * Returns batch * n. */
 int32_t rb_weight_matmul_noalloc(rb_ctx* ctx, int32_t handle, const float* input, float* output, uint32_t batch,
                                  uint32_t flags);
@@ -250,6 +267,17 @@ int32_t rb_compute_logits(rb_ctx* ctx, int32_t model, const float* hidden, uint3
  * weight bytes (wq, wk, wv, wo, w_gate, w_up, w_down in that order) to dst.
  * Returns bytes, RB_ERR_NOT_FOUND (no such layer) or RB_ERR_INVALID (max_size too small). */
 int32_t rb_memory64_load_layer(rb_ctx* ctx, int32_t model, uint32_t layer_id, void* dst, uint32_t max_size);
+/* memory64_read (memory64_host.rs:767-825): copies `size` bytes at `offset` of the
+ * model's Memory64 image into the caller's linear memory `mem` (mem_size bytes,
+ * the WASM memory's extent) at `mem_offset`. The image is the layers' weight
+ * bytes back to back, each layer laid out as rb_memory64_load_layer returns it.
+ * Returns size, or the reference's codes: -4 (mem_offset + size overflows),
+ * -5 (beyond mem_size), -2 (offset + size beyond the image). `mem` is host
+ * memory unless flags has RB_PTR_DEVICE. */
+int32_t rb_memory64_read(rb_ctx* ctx, int32_t model, uint64_t offset, void* mem, uint32_t mem_size,
+                         uint32_t mem_offset, uint32_t size, uint32_t flags);
+/* Total bytes of the model's Memory64 image (sum of every layer's weight bytes). */
+int32_t rb_memory64_size(rb_ctx* ctx, int32_t model, uint64_t* size);
 
 /* ---- GGUF files ----
  * rb_gguf is GGUFParser (crates/realm-core/src/formats/gguf.rs:100-479) over a

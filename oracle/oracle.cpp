@@ -422,6 +422,74 @@ int or_dequant_matmul(int dtype, const void* blocks, size_t nblocks, const float
   const size_t be = or_block_elems(dtype);
   if (be == 0 || k % be || nblocks != n * (k / be)) return -3;
   threads = set_threads(threads);
+  // Each y[b, o] is the sequential sum s += w[i] * x[i] over i = 0..k-1 (product
+  // and sum rounded separately). Eight output rows are carried side by side in
+  // one vector (w transposed to [k][8]) and four tokens at a time, which only
+  // interleaves independent sums: every element gets exactly the scalar result.
+  const long NG = (long)((n + 7) / 8);
+#pragma omp parallel num_threads(threads) if (threads > 1)
+  {
+    std::vector<float> w(8 * k), wt(8 * k);
+#pragma omp for schedule(static)
+    for (long gi = 0; gi < NG; ++gi) {
+      const size_t o0 = (size_t)gi * 8, nr = std::min<size_t>(8, n - o0);
+      for (size_t r = 0; r < 8; ++r) {
+        if (r < nr) dequant_row(dtype, blocks, o0 + r, k, w.data() + r * k);
+        else std::fill(w.begin() + r * k, w.begin() + (r + 1) * k, 0.f);
+      }
+      for (size_t i = 0; i < k; ++i)
+        for (size_t r = 0; r < 8; ++r) wt[i * 8 + r] = w[r * k + i];
+      size_t b = 0;
+#ifdef OR_HAVE_AVX2
+      for (; b + 4 <= m; b += 4) {
+        __m256 s0 = _mm256_setzero_ps(), s1 = s0, s2 = s0, s3 = s0;
+        const float *x0 = x + b * k, *x1 = x0 + k, *x2 = x1 + k, *x3 = x2 + k;
+        for (size_t i = 0; i < k; ++i) {
+          const __m256 wv = _mm256_loadu_ps(wt.data() + i * 8);
+          s0 = _mm256_add_ps(s0, _mm256_mul_ps(wv, _mm256_set1_ps(x0[i])));
+          s1 = _mm256_add_ps(s1, _mm256_mul_ps(wv, _mm256_set1_ps(x1[i])));
+          s2 = _mm256_add_ps(s2, _mm256_mul_ps(wv, _mm256_set1_ps(x2[i])));
+          s3 = _mm256_add_ps(s3, _mm256_mul_ps(wv, _mm256_set1_ps(x3[i])));
+        }
+        float o[4][8];
+        _mm256_storeu_ps(o[0], s0);
+        _mm256_storeu_ps(o[1], s1);
+        _mm256_storeu_ps(o[2], s2);
+        _mm256_storeu_ps(o[3], s3);
+        for (size_t t = 0; t < 4; ++t)
+          for (size_t r = 0; r < nr; ++r) y[(b + t) * n + o0 + r] = o[t][r];
+      }
+      for (; b < m; ++b) {
+        __m256 s = _mm256_setzero_ps();
+        const float* xr = x + b * k;
+        for (size_t i = 0; i < k; ++i)
+          s = _mm256_add_ps(s, _mm256_mul_ps(_mm256_loadu_ps(wt.data() + i * 8), _mm256_set1_ps(xr[i])));
+        float o[8];
+        _mm256_storeu_ps(o, s);
+        for (size_t r = 0; r < nr; ++r) y[b * n + o0 + r] = o[r];
+      }
+#else
+      for (; b < m; ++b) {
+        const float* xr = x + b * k;
+        for (size_t r = 0; r < nr; ++r) {
+          float s = 0.f;
+          for (size_t i = 0; i < k; ++i) s += wt[i * 8 + r] * xr[i];
+          y[b * n + o0 + r] = s;
+        }
+      }
+#endif
+    }
+  }
+  return (int)(m * n);
+}
+
+// The plain row-at-a-time form of or_dequant_matmul (one sequential sum per
+// output element); kept to check that the vectorised form gives the same bits.
+int or_dequant_matmul_scalar(int dtype, const void* blocks, size_t nblocks, const float* x, float* y,
+                             size_t m, size_t n, size_t k, int threads) {
+  const size_t be = or_block_elems(dtype);
+  if (be == 0 || k % be || nblocks != n * (k / be)) return -3;
+  threads = set_threads(threads);
   const long N = (long)n;
 #pragma omp parallel num_threads(threads) if (threads > 1)
   {

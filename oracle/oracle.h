@@ -48,6 +48,9 @@ int or_fused_matmul(int dtype, const void* blocks, size_t nblocks, const float* 
 // dequantise then an fp32 GEMM; here with a sequential fp32 sum per output.
 int or_dequant_matmul(int dtype, const void* blocks, size_t nblocks, const float* x,
                       float* y, size_t m, size_t n, size_t k, int threads);
+// The same sums computed one output element at a time (bit-identical check).
+int or_dequant_matmul_scalar(int dtype, const void* blocks, size_t nblocks, const float* x,
+                             float* y, size_t m, size_t n, size_t k, int threads);
 // Same, accumulated in double (error-bound shadow for tolerance checks).
 int or_dequant_matmul_f64(int dtype, const void* blocks, size_t nblocks, const float* x,
                           double* y, size_t m, size_t n, size_t k, int threads);

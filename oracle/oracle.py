@@ -43,6 +43,7 @@ def lib():
         L.or_quantize.argtypes = [i32, vp, sz, vp]
         L.or_fused_matmul.argtypes = [i32, vp, sz, vp, vp, sz, sz, sz, i32]
         L.or_dequant_matmul.argtypes = [i32, vp, sz, vp, vp, sz, sz, sz, i32]
+        L.or_dequant_matmul_scalar.argtypes = [i32, vp, sz, vp, vp, sz, sz, sz, i32]
         L.or_dequant_matmul_f64.argtypes = [i32, vp, sz, vp, vp, sz, sz, sz, i32]
         L.or_rms_norm.argtypes = [vp, vp, C.c_float, sz, sz, vp]
         L.or_rope.argtypes = [vp, sz, sz, sz, sz, C.c_float]
@@ -116,11 +117,12 @@ def fused_matmul(dtype, blocks, x, m, n, k, threads=1, nblocks_override=None):
     return rc, y
 
 
-def dequant_matmul(dtype, blocks, x, m, n, k, threads=0, f64=False):
+def dequant_matmul(dtype, blocks, x, m, n, k, threads=0, f64=False, scalar=False):
     blocks = np.ascontiguousarray(blocks, dtype=np.uint8)
     x = np.ascontiguousarray(x, dtype=np.float32)
     y = np.zeros((m, n), np.float64 if f64 else np.float32)
-    fn = lib().or_dequant_matmul_f64 if f64 else lib().or_dequant_matmul
+    fn = (lib().or_dequant_matmul_f64 if f64 else
+          lib().or_dequant_matmul_scalar if scalar else lib().or_dequant_matmul)
     rc = fn(dtype, _p(blocks), nblocks(dtype, blocks.nbytes), _p(x), _p(y), m, n, k, threads)
     assert rc >= 0, rc
     return y

@@ -77,6 +77,8 @@ _sig("rb_last_error", [C.c_char_p, _sz])
 _sig("rb_sync", [_vp])
 _sig("rb_stream", [_vp], _vp)
 _sig("rb_num_sms", [_vp])
+_sig("rb_kernel_binary_version", [_vp, _I32P])
+_sig("rb_test_fail_next_grid_barrier", [_vp, _u32])
 _sig("rb_dequantize", [_vp, _i32, _vp, _sz, _vp, _u32])
 _sig("rb_quantize", [_vp, _i32, _vp, _sz, _vp, _u32])
 _sig("rb_fused_dequant_matmul", [_vp, _i32, _vp, _sz, _vp, _vp, _u32, _u32, _u32, _u32])
@@ -111,6 +113,8 @@ _sig("rb_embed_tokens", [_vp, _i32, _vp, _u32, _vp, _u32])
 _sig("rb_forward_layer", [_vp, _i32, _u32, _u32, _vp, _u32, _u32, _vp, _u32])
 _sig("rb_compute_logits", [_vp, _i32, _vp, _u32, _vp, _u32])
 _sig("rb_memory64_load_layer", [_vp, _i32, _u32, _vp, _u32])
+_sig("rb_memory64_read", [_vp, _i32, C.c_uint64, _vp, _u32, _u32, _u32, _u32])
+_sig("rb_memory64_size", [_vp, _i32, C.POINTER(C.c_uint64)])
 _sig("rb_last_forward_ms", [_vp], C.c_float)
 _sig("rb_last_forward_launches", [_vp])
 
@@ -535,6 +539,18 @@ class Model:
         buf = np.empty(max_size, np.uint8)
         n = _check(_lib.rb_memory64_load_layer(self.ctx.handle, self.handle, layer_id, _ptr(buf), max_size))
         return buf[:n]
+
+    def memory64_size(self) -> int:
+        n = C.c_uint64()
+        _check(_lib.rb_memory64_size(self.ctx.handle, self.handle, C.byref(n)))
+        return n.value
+
+    def memory64_read(self, offset: int, mem, mem_offset: int, size: int) -> int:
+        """memory64_read: `size` bytes at `offset` of the Memory64 image into the
+        caller's linear memory `mem` (a uint8 array or CUDA tensor) at mem_offset."""
+        nbytes = (mem.numel() * mem.element_size()) if _is_dev(mem) else mem.nbytes
+        return _check(_lib.rb_memory64_read(self.ctx.handle, self.handle, offset, _ptr(mem), nbytes, mem_offset,
+                                            size, _flags(mem)))
 
     def close(self):
         if self.handle >= 0:

@@ -672,14 +672,9 @@ template <int HD, int NREP, int F16, int GR>
 cudaError_t launch_attn_t(const AttnArgs& a, int num_sms, cudaStream_t s, int pdl) {
   constexpr int smem = attn_smem_bytes<HD, NREP, F16, GR>();
   auto kern = attn_kernel<HD, NREP, F16, GR>;
-  static unsigned long long attr_set = 0;
   int dev = 0;
   cudaGetDevice(&dev);
-  if (!(attr_set & (1ull << dev))) {
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-    if (e != cudaSuccess) return e;
-    attr_set |= 1ull << dev;
-  }
+  if (cudaError_t e = ensure_smem_attr(kern, smem, dev)) return e;
   static_assert(smem <= 227 * 1024, "shared memory of one CTA");
   // two CTAs per SM when they fit (228 KB per SM, 1 KB reserved per CTA); never
   // more CTAs than attn_grid() allows for

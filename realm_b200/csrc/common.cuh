@@ -8,7 +8,27 @@
 #error "compile with nvcc"
 #endif
 
+#include <mutex>
+#include <set>
+#include <utility>
+
 namespace rb {
+
+// Raises a kernel's dynamic shared-memory limit once per (kernel, device).
+// Thread-safe: contexts on different host threads may launch concurrently.
+inline cudaError_t ensure_smem_attr_impl(const void* kern, int bytes, int dev) {
+  static std::mutex mu;
+  static std::set<std::pair<const void*, int>> done;
+  std::lock_guard<std::mutex> lock(mu);
+  if (done.count({kern, dev})) return cudaSuccess;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  if (e == cudaSuccess) done.insert({kern, dev});
+  return e;
+}
+template <class K>
+inline cudaError_t ensure_smem_attr(K kern, int bytes, int dev) {
+  return ensure_smem_attr_impl(reinterpret_cast<const void*>(kern), bytes, dev);
+}
 
 // ---- device error word (bounded waits report here instead of hanging) ----
 enum DevErr : uint32_t {
@@ -119,13 +139,15 @@ __device__ __forceinline__ unsigned long long atom_add_release_u64(unsigned long
   return old;
 }
 
-// Waits until *ctr >= target (bounded: ~0.5 s, then reports and returns false).
+// Waits until *ctr >= target (bounded, then reports and returns false).
 // On a timeout the first reporter also leaves err[1..3] = target, the counter
 // it last saw (low 32 bits each) and `who` (caller-defined) for the host.
+// `limit` polls at most (0: the default 2^22, about half a second).
 __device__ __forceinline__ bool grid_wait(const unsigned long long* ctr, unsigned long long target, uint32_t* err,
-                                          uint32_t who) {
+                                          uint32_t who, uint32_t limit = 0) {
   unsigned long long v = 0;
-  for (uint32_t i = 0; i < (1u << 22); ++i) {
+  const uint32_t n = limit ? limit : (1u << 22);
+  for (uint32_t i = 0; i < n; ++i) {
     v = ld_acquire_u64(ctr);
     if (v >= target) return true;
     if (i > 64) __nanosleep(100);

@@ -304,6 +304,10 @@ struct Ctx {
   bool step_grouped = false;  // the step has consecutive rows of one tenant (a prompt chunk)
   int attn_whole = 1;         // RB_ATTN_WHOLE=0: always split attention pages evenly over the CTAs
   DevBuf qg_part;      // tcgen05 GEMM partial sums
+  // failure-detection test hook (rb_test_fail_next_grid_barrier): when nonzero,
+  // the next multi-phase GEMV launch with a grid barrier gets its first
+  // barrier's target out of reach and this poll limit for every barrier wait
+  uint32_t test_fail_spin = 0;
 };
 
 // With RB_QGEMM=1, batches of at least this many rows take the tcgen05 dequant-GEMM.
@@ -534,6 +538,13 @@ int chain_flush(Ctx* c, int* launches) {
   ca.bar_mask = c->chain_mask;
   ca.gbar = c->gbar.as<unsigned long long>();
   ca.prefetch = c->chain_prefetch;
+  if (c->test_fail_spin && c->chain_mask) {
+    int b = 1;
+    while (!((c->chain_mask >> b) & 1u)) ++b;
+    ca.fail_bar = b;
+    ca.grid_spin = c->test_fail_spin;
+    c->test_fail_spin = 0;
+  }
   c->last_chain_phases = c->chain_n;
   c->chain_n = 0;
   c->chain_mask = 0;
@@ -870,6 +881,7 @@ int ensure_qg_model(Ctx* c, Model& M) {
 
 int run_forward(rb_ctx* c, Model& M, int m, bool use_graph) {
   int launches = 0;
+  if (c->test_fail_spin) use_graph = false;  // the armed hook must not be baked into a cached graph
   if (c->qgemm && m >= kQgemmMinRows)
     if (int rc = ensure_qg_model(c, M)) return rc;
   RB_CUDA(cudaEventRecord(c->ev0, c->stream));
@@ -989,6 +1001,22 @@ int32_t rb_sync(rb_ctx* c) {
 }
 void* rb_stream(rb_ctx* c) { return c ? (void*)c->stream : nullptr; }
 int32_t rb_num_sms(rb_ctx* c) { return c ? c->num_sms : fail(RB_ERR_BAD_HANDLE, "null context"); }
+
+int32_t rb_test_fail_next_grid_barrier(rb_ctx* c, uint32_t spin_polls) {
+  if (!c) return fail(RB_ERR_BAD_HANDLE, "null context");
+  c->test_fail_spin = spin_polls ? spin_polls : 1;
+  return RB_OK;
+}
+
+int32_t rb_kernel_binary_version(rb_ctx* c, int32_t* version) {
+  if (!c) return fail(RB_ERR_BAD_HANDLE, "null context");
+  if (!version) return fail(RB_ERR_INVALID, "null output");
+  RB_CUDA(cudaSetDevice(c->device));
+  cudaFuncAttributes fa{};
+  RB_CUDA(cudaFuncGetAttributes(&fa, embed_kernel));
+  *version = fa.binaryVersion;
+  return RB_OK;
+}
 
 int32_t rb_dequantize(rb_ctx* c, int32_t dtype, const void* blocks, size_t nblocks, float* out, uint32_t flags) {
   if (!c) return fail(RB_ERR_BAD_HANDLE, "null context");
@@ -1432,6 +1460,7 @@ int32_t rb_attention_forward(rb_ctx* c, int32_t pool, uint32_t layer, uint32_t n
   at.counters = c->counters.as<int32_t>() + kCounters / 2;
   at.err = c->err.as<uint32_t>();
   at.group_rows = c->attn_group && rows_grouped(rp);
+  at.whole_pairs = c->attn_whole;
   RB_CUDA(cudaEventRecord(c->ev0, c->stream));
   RB_CUDA(attn_launch(at, c->num_sms, c->stream, 0));
   RB_CUDA(cudaEventRecord(c->ev1, c->stream));
@@ -1816,6 +1845,57 @@ int32_t rb_memory64_load_layer(rb_ctx* c, int32_t model, uint32_t layer_id, void
   return (int32_t)total;
 }
 
+// The Memory64 image: layer 0's wq, wk, wv, wo, w_gate, w_up, w_down bytes, then
+// layer 1's, ... (the order rb_memory64_load_layer copies one layer in).
+static const int kMem64Order[7] = {1, 2, 3, 4, 6, 7, 8};
+
+int32_t rb_memory64_size(rb_ctx* c, int32_t model, uint64_t* size) {
+  Model* M = get_model(c, model);
+  if (!M) return fail(RB_ERR_BAD_HANDLE, "model %d", model);
+  if (!size) return fail(RB_ERR_INVALID, "null size");
+  uint64_t total = 0;
+  for (const LayerW& L : M->layers)
+    for (int i : kMem64Order) total += L.raw[i].bytes;
+  *size = total;
+  return RB_OK;
+}
+
+int32_t rb_memory64_read(rb_ctx* c, int32_t model, uint64_t offset, void* mem, uint32_t mem_size,
+                         uint32_t mem_offset, uint32_t size, uint32_t flags) {
+  Model* M = get_model(c, model);
+  if (!M) return fail(RB_ERR_BAD_HANDLE, "model %d", model);
+  // memory64_host.rs:785-805: destination overflow (-4), then bounds (-5)
+  const uint64_t end_ptr = (uint64_t)mem_offset + size;
+  if (end_ptr > 0xffffffffull) return fail(RB_ERR_IO, "memory pointer overflow: %u + %u", mem_offset, size);
+  if (end_ptr > mem_size)
+    return fail(RB_ERR_NO_MEMORY, "memory pointer out of bounds: %u + %u > %u", mem_offset, size, mem_size);
+  if (size > 0x7fffffffu) return fail(RB_ERR_PTR_OVERFLOW, "read larger than 2 GiB");
+  // memory64_host.rs:808-813 / 298-330: the read must lie inside the image (-2)
+  uint64_t total = 0;
+  for (const LayerW& L : M->layers)
+    for (int i : kMem64Order) total += L.raw[i].bytes;
+  if (offset > total || size > total - offset)
+    return fail(RB_ERR_NOT_FOUND, "memory64_read failed at offset %llu: %u bytes exceed the %llu-byte image",
+                (unsigned long long)offset, size, (unsigned long long)total);
+  if (size && !mem) return fail(RB_ERR_INVALID, "null destination");
+  const cudaMemcpyKind kind = (flags & RB_PTR_DEVICE) ? cudaMemcpyDeviceToDevice : cudaMemcpyDeviceToHost;
+  uint64_t base = 0, done = 0;
+  for (const LayerW& L : M->layers)
+    for (int i : kMem64Order) {
+      const RawTensor& t = L.raw[i];
+      const uint64_t lo = base, hi = base + t.bytes;
+      base = hi;
+      if (done == size || hi <= offset + done || t.bytes == 0) continue;
+      if (!t.d.p) return fail(RB_ERR_NOT_FOUND, "weight bytes of the image are not resident");
+      const uint64_t from = offset + done - lo;
+      const uint64_t n = std::min<uint64_t>(t.bytes - from, size - done);
+      RB_CUDA(cudaMemcpyAsync((uint8_t*)mem + mem_offset + done, (const uint8_t*)t.d.p + from, n, kind, c->stream));
+      done += n;
+    }
+  if (int rc = sync_ctx(c)) return rc;
+  return (int32_t)size;
+}
+
 float rb_last_forward_ms(rb_ctx* c) { return c ? c->last_ms : -1.f; }
 int32_t rb_last_forward_launches(rb_ctx* c) { return c ? c->last_launches : fail(RB_ERR_BAD_HANDLE, "null context"); }
 
@@ -1837,7 +1917,9 @@ int32_t rb_last_forward_launches(rb_ctx* c) { return c ? c->last_launches : fail
 // Limits (calls beyond them fail with RB_ERR_INVALID and a message naming the
 // limit): batch <= 8 rows, K <= 16384, N <= 131072 (512 groups of 256 rows),
 // and at most 160 GEMV CTAs (the device's SM count when the weight has that
-// many 256-row x 256-column units). The array is 3,434,496 bytes.
+// many 256-row x 256-column units). The array is 3,434,496 bytes. Q8_0 weights
+// whose K is not a multiple of 256 (zero-padded at upload) are refused with
+// RB_ERR_UNSUPPORTED.
 //
 // The array is shared by every call on a device, from every context, and keeps
 // the contents of the last call; the counters are cleared on the stream at the
@@ -1847,7 +1929,9 @@ int32_t rb_last_forward_launches(rb_ctx* c) { return c ? c->last_launches : fail
 //
 // The first call on a device looks up the array's device address with
 // cudaGetSymbolAddress (with that device current) and caches it; make that
-// first call before any stream capture on the device.
+// first call before any stream capture on the device. The cached address
+// belongs to the device's primary context: after cudaDeviceReset in this
+// process it is stale, so no call may follow a reset.
 // ---------------------------------------------------------------------------
 namespace {
 

@@ -21,6 +21,10 @@
 //  * Row groups split across CTAs are reduced by the last-arriving CTA in a
 //    fixed order (deterministic; no spin waits), then the fused epilogue runs.
 #include "gemv.cuh"
+
+#include <mutex>
+#include <set>
+#include <utility>
 #include "quant.cuh"
 #include "xfrag.cuh"
 
@@ -588,7 +592,7 @@ __device__ __forceinline__ void consume_phase(const GemvArgs& a, int p, int n_ph
                                               float* T, RingPos& rp, bool& alive,
                                               const unsigned long long* gbar /* this barrier's counter */,
                                               bool wait_grid,
-                                              unsigned long long bar_target) {
+                                              unsigned long long bar_target, uint32_t grid_spin) {
   constexpr int UB = unit_bytes(DT);
   constexpr int TB = tile_bytes(DT);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -597,7 +601,7 @@ __device__ __forceinline__ void consume_phase(const GemvArgs& a, int p, int n_ph
   if (pr.n_units == 0) return;
   if (wait_grid) {  // uniform over the CTA; only thread 0 reads the target
     // everything the phases before wrote is visible once all CTAs arrived
-    if (tid == 0) grid_wait(gbar, bar_target, a.err, (blockIdx.x << 8) | ((uint32_t)p << 1));
+    if (tid == 0) grid_wait(gbar, bar_target, a.err, (blockIdx.x << 8) | ((uint32_t)p << 1), grid_spin);
     named_bar(1, 32 * kConsumerWarps);
   }
   if (tid == 0) RB_TS(p, 1);
@@ -734,7 +738,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const __grid_constant
             }
             const unsigned long long tgt = s_tgt[need - 1];
             if (tgt == 0ull) report_error(a.err, DEV_TIMEOUT_SMEM);
-            else grid_wait(ca.gbar + need, tgt, a.err, (blockIdx.x << 8) | ((uint32_t)p << 1) | 1u);
+            else grid_wait(ca.gbar + need, tgt, a.err, (blockIdx.x << 8) | ((uint32_t)p << 1) | 1u, ca.grid_spin);
             passed = need;
           }
           dep = true;
@@ -789,11 +793,11 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const __grid_constant
     if (wg) passed = need;
     switch (a.dtype) {
       case DT_Q4_K: consume_phase<DT_Q4_K, NT>(a, p, ca.n_phases, pr, ring, S, SB, full, empty, inv_rms, red, T, rp, alive,
-                                         ca.gbar + need, wg, my_target); break;
+                                         ca.gbar + need, wg, my_target, ca.grid_spin); break;
       case DT_Q6_K: consume_phase<DT_Q6_K, NT>(a, p, ca.n_phases, pr, ring, S, SB, full, empty, inv_rms, red, T, rp, alive,
-                                         ca.gbar + need, wg, my_target); break;
+                                         ca.gbar + need, wg, my_target, ca.grid_spin); break;
       default: consume_phase<DT_Q8_0, NT>(a, p, ca.n_phases, pr, ring, S, SB, full, empty, inv_rms, red, T, rp, alive,
-                                         ca.gbar + need, wg, my_target); break;
+                                         ca.gbar + need, wg, my_target, ca.grid_spin); break;
     }
     if (p + 1 < ca.n_phases && ((ca.bar_mask >> (p + 1)) & 1u)) {
       // this CTA is done with phase p (epilogue writes included): arrive
@@ -802,7 +806,8 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const __grid_constant
         // one counter per barrier slot: every CTA arrives at each slot exactly
         // once per launch, so a ticket always lies in its own launch's window
         const unsigned long long t = atom_add_release_u64(ca.gbar + (p + 1), 1ull);
-        s_tgt[p] = (t / gridDim.x + 1) * gridDim.x;
+        // (the failure-detection hook moves one barrier's target a grid beyond reach)
+        s_tgt[p] = (t / gridDim.x + 1 + (ca.fail_bar == p + 1 ? 1 : 0)) * gridDim.x;
       }
     }
   }
@@ -1110,13 +1115,21 @@ cudaError_t launch_chain_t(ChainArgs ca, int num_sms, cudaStream_t s, int pdl) {
   int smem = chain_smem(ca.stages, sb, NT).total;
   if (ca.n_phases > 1 && smem < kChainMinSmem) smem = kChainMinSmem;  // one CTA per SM
   auto kern = gemv_kernel<NT>;
-  static unsigned long long attr_set = 0;  // per instantiation, one bit per device
   int dev = 0;
   cudaGetDevice(&dev);
-  if (!(attr_set & (1ull << dev))) {
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBudget + 8192);
-    if (e != cudaSuccess) return e;
-    attr_set |= 1ull << dev;
+  if (cudaError_t e = ensure_smem_attr(kern, kSmemBudget + 8192, dev)) return e;
+  if (ca.n_phases > 1) {
+    // grid barriers need every CTA resident at once: one CTA per SM must fit
+    // (checked once per device and footprint)
+    static std::mutex mu;
+    static std::set<std::pair<int, int>> ok;
+    std::lock_guard<std::mutex> lock(mu);
+    if (!ok.count({dev, smem})) {
+      int per_sm = 0;
+      if (cudaError_t e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kThreads, smem)) return e;
+      if (per_sm < 1) return cudaErrorCooperativeLaunchTooLarge;
+      ok.insert({dev, smem});
+    }
   }
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(ca.n_phases == 1 ? gemv_ctas(num_sms, ca.ph[0].n_rg, ca.ph[0].nsb) : num_sms);
@@ -1727,14 +1740,9 @@ template <int NT>
 cudaError_t launch_qgemm_epi_t(const GemvArgs& a, const QgemmTail& q, cudaStream_t s, int pdl) {
   const int smem = (kConsumerWarps * kMaxTokens + kMaxTokens + tile_floats(NT)) * 4;
   auto kern = qgemm_epi_kernel<NT>;
-  static unsigned long long attr_set = 0;
   int dev = 0;
   cudaGetDevice(&dev);
-  if (!(attr_set & (1ull << dev))) {
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-    if (e != cudaSuccess) return e;
-    attr_set |= 1ull << dev;
-  }
+  if (cudaError_t e = ensure_smem_attr(kern, smem, dev)) return e;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(a.n_rg);
   cfg.blockDim = dim3(kConsumerWarps * 32);
@@ -1751,14 +1759,9 @@ cudaError_t launch_qgemm_epi_t(const GemvArgs& a, const QgemmTail& q, cudaStream
 template <int DT>
 cudaError_t launch_qgemm_t(const QgemmArgs& q, int G, cudaStream_t s, int pdl) {
   auto kern = qgemm_kernel<DT>;
-  static unsigned long long attr_set = 0;
   int dev = 0;
   cudaGetDevice(&dev);
-  if (!(attr_set & (1ull << dev))) {
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kQgSmem);
-    if (e != cudaSuccess) return e;
-    attr_set |= 1ull << dev;
-  }
+  if (cudaError_t e = ensure_smem_attr(kern, kQgSmem, dev)) return e;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(G);
   cfg.blockDim = dim3(kQgThreads);

@@ -82,6 +82,10 @@ struct ChainArgs {
   // weight units a producer may issue for a phase before the grid barrier that
   // phase waits on has passed (< 0: the whole ring)
   int32_t prefetch = -1;
+  // failure-detection test hook: barrier slot whose target is moved out of
+  // reach (0: none), and the poll limit of every grid-barrier wait (0: default)
+  int32_t fail_bar = 0;
+  uint32_t grid_spin = 0;
 };
 
 // Scratch needed by one GEMV launch (partials in floats, counters in ints).

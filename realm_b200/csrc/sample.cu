@@ -399,15 +399,9 @@ cudaError_t sample_launch(const float* logits, int ld, int n_rows, int vocab, co
                           const uint32_t* prev, const uint32_t* prev_off, const float* uniforms, uint32_t* out,
                           cudaStream_t s) {
   if (n_rows < 1 || vocab < 1 || vocab > kSampleMaxVocab || ld < vocab) return cudaErrorInvalidValue;
-  static unsigned long long attr_set = 0;
   int dev = 0;
   cudaGetDevice(&dev);
-  if (!(attr_set & (1ull << dev))) {
-    cudaError_t e = cudaFuncSetAttribute(sample_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         (int)sample_smem_bytes(kSampleMaxVocab));
-    if (e != cudaSuccess) return e;
-    attr_set |= 1ull << dev;
-  }
+  if (cudaError_t e = ensure_smem_attr(sample_kernel, (int)sample_smem_bytes(kSampleMaxVocab), dev)) return e;
   sample_kernel<<<n_rows, kST, sample_smem_bytes(vocab), s>>>(logits, ld, vocab, params, prev, prev_off, uniforms, out);
   return cudaGetLastError();
 }

@@ -176,3 +176,32 @@ def test_chain_kernel_matches_single_gemv_launches(ctx, small):
     finally:
         c2.close()
     assert np.array_equal(chained.view(np.uint32), single.view(np.uint32))
+
+
+def test_memory64_read(ctx, oracle, small):
+    """memory64_read (memory64_host.rs:767-825): a byte range of the model's
+    Memory64 image (layers back to back, each as memory64_load_layer lays it
+    out) into caller memory, with the reference's error codes."""
+    import realm_b200 as rb
+    O = oracle
+    cfg, W = small
+    m = _build(ctx, cfg, W, True, max_tenants=1)
+    order = (O.W_Q, O.W_K, O.W_V, O.W_O, O.W_GATE, O.W_UP, O.W_DOWN)
+    image = b"".join(W[(w, l)][1].tobytes() for l in range(cfg["n_layers"]) for w in order)
+    assert m.memory64_size() == len(image)
+    mem = np.zeros(1 << 20, np.uint8)
+    rng = np.random.default_rng(3)
+    layer0 = sum(W[(w, 0)][1].nbytes for w in order)
+    # ranges inside one tensor, across tensors, across the layer boundary, the tail
+    for off, size in [(0, 1000), (W[(O.W_Q, 0)][1].nbytes - 7, 5000), (layer0 - 300, 700),
+                      (len(image) - 513, 513), (int(rng.integers(0, len(image) - 9000)), 9000)]:
+        at = int(rng.integers(0, 1000))
+        assert m.memory64_read(off, mem, at, size) == size
+        assert mem[at:at + size].tobytes() == image[off:off + size]
+    for args, code in [((0, mem, 2**32 - 10, 20), -4),           # destination pointer overflow
+                       ((0, mem, mem.nbytes - 10, 20), -5),      # beyond the caller's memory
+                       ((len(image) - 10, mem, 0, 20), -2)]:     # beyond the image
+        with pytest.raises(rb.RealmError) as e:
+            m.memory64_read(*args)
+        assert e.value.code == code, (args, e.value.code)
+    m.close()

@@ -1,10 +1,20 @@
 """rb_weight_matmul_noalloc: the GEMV entry point that allocates nothing.
 
-Checked against rb_weight_matmul (the allocating entry point) on device
-buffers, through the C ABI, on two calls in a row with different inputs (the
-second call reuses the shared scratch the first left behind). Tolerance as the
-GEMV parity tests: relative to sum_k |W[n,k] x[k]|, 3e-5 for Q4_K and 1e-5 for
-Q6_K / Q8_0. Collected last so it also runs after every other test.
+Some callers cannot allocate device memory when they run a matmul (a host that
+hands the library a fixed memory budget, an allocator owned by another
+runtime, or a serving loop where cudaMalloc/cudaFree and their device-wide
+synchronisation are not allowed). This entry point keeps its working memory in
+one fixed device array inside the library.
+
+Checked through the C ABI on device buffers, on two calls in a row with
+different inputs (the second call reuses the shared scratch the first left
+behind):
+- against the oracle's dequant + GEMM accumulated in double, at the GEMV parity
+  tests' tolerance (relative to sum_k |W[n,k] x[k]|: 3e-5 for Q4_K, 1e-5 for
+  Q6_K / Q8_0);
+- against rb_weight_matmul (the allocating entry point), within the same bound;
+- free device memory is unchanged across a warm call (no allocation).
+Collected last so that it also runs after every other test.
 """
 import numpy as np
 import pytest
@@ -23,7 +33,7 @@ def _rel_err(got, ref, w, x):
     ("q6k", 1024, 4096, 5),
     ("q80", 300, 512, 3),      # ragged last row group
 ])
-def test_noalloc_matches_weight_matmul(ctx, oracle, fmt, n, k, m):
+def test_noalloc_matches_oracle(ctx, oracle, fmt, n, k, m):
     import torch
     import realm_b200 as rb
     O = oracle
@@ -37,16 +47,45 @@ def test_noalloc_matches_weight_matmul(ctx, oracle, fmt, n, k, m):
     dev = torch.device("cuda", 0)
     try:
         for call in range(2):
-            x = torch.from_numpy(rng.normal(0, 1, size=(m, k)).astype(np.float32)).to(dev)
-            ref = torch.empty(m, n, device=dev)
+            xh = rng.normal(0, 1, size=(m, k)).astype(np.float32)
+            x = torch.from_numpy(xh).to(dev)
             got = torch.full((m, n), float("nan"), device=dev)
-            w.matmul(x, m, out=ref)
+            via_alloc = torch.empty(m, n, device=dev)
             w.matmul_noalloc(x, got, m)
+            w.matmul(x, m, out=via_alloc)
             ctx.sync()
-            g, r = got.cpu().numpy(), ref.cpu().numpy()
+            g = got.cpu().numpy()
             assert np.all(np.isfinite(g)), call
-            err = _rel_err(g, r, wdq, x.cpu().numpy())
-            assert err < tol, (call, err)
+            ref = O.dequant_matmul(dt, blocks, xh, m, n, k, f64=True)
+            err = _rel_err(g, ref, wdq, xh)
+            assert err < tol, ("vs oracle", call, err)
+            err2 = _rel_err(g, via_alloc.cpu().numpy(), wdq, xh)
+            assert err2 < tol, ("vs rb_weight_matmul", call, err2)
+    finally:
+        w.free()
+
+
+def test_noalloc_allocates_no_device_memory(ctx, oracle):
+    import torch
+    import realm_b200 as rb
+    O = oracle
+    rng = np.random.default_rng(17)
+    n, k, m = 11008, 4096, 8
+    blocks = O.quantize(O.Q4K, rng.normal(0, 0.02, size=(n, k)).astype(np.float32))
+    w = rb.Weight(ctx, O.Q4K, n, k, blocks)
+    dev = torch.device("cuda", 0)
+    try:
+        x = torch.randn(m, k, device=dev)
+        y = torch.empty(m, n, device=dev)
+        w.matmul_noalloc(x, y, m)  # first call: looks up the scratch array's address
+        ctx.sync()
+        torch.cuda.synchronize(dev)
+        free0, _ = torch.cuda.mem_get_info(dev)
+        for _ in range(3):
+            w.matmul_noalloc(x, y, m)
+        ctx.sync()
+        free1, _ = torch.cuda.mem_get_info(dev)
+        assert free1 == free0, (free0, free1)
     finally:
         w.free()
 
@@ -76,3 +115,12 @@ def test_noalloc_rejects_beyond_limits(ctx, oracle):
         assert e.value.code == -3 and "16384" in str(e.value)
     finally:
         big.free()
+    # Q8_0 rows whose K is not a multiple of 256 are zero-padded at upload:
+    # refused here (the allocating entry point takes them)
+    pad = rb.Weight(ctx, O.Q80, 40, 96, O.quantize(O.Q80, rng.normal(0, 0.02, size=(40, 96)).astype(np.float32)))
+    try:
+        with pytest.raises(rb.RealmError) as e:
+            pad.matmul_noalloc(torch.zeros(1, 96, device=dev), torch.zeros(1, 40, device=dev), 1)
+        assert e.value.code == -23 and "256" in str(e.value)
+    finally:
+        pad.free()

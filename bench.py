@@ -32,7 +32,8 @@ sys.path.insert(0, ROOT)
 
 CFG = dict(n_layers=32, hidden=4096, n_heads=32, n_kv_heads=32, head_dim=128, ffn=11008, vocab=32000,
            max_seq=1024, rms_eps=1e-5, layer_eps=1e-5, rope_theta=10000.0)
-TENANTS_PER_GPU = 8
+TENANTS_PER_GPU = 8       # configs[3] on one GPU
+TOTAL_TENANTS_MULTI = 64  # configs[3] at 2/4/8 GPUs: 32/16/8 per GPU
 METRIC = "aggregate decode tok/s, 8 tenants Llama-7B Q4_K; paged-KV attn HBM GB/s vs peak"
 Q4K_BPW, Q6K_BPW = 144 / 256, 210 / 256
 # dram__bytes_read.sum + dram__bytes_write.sum of one gate|up GEMV launch (22016 x 4096
@@ -110,15 +111,16 @@ class Clocks:
 # ---------------------------------------------------------------------------
 # our arm
 # ---------------------------------------------------------------------------
-def build_model(rb, torch, ctx, dev, n_tenants, host_copy=None):
+def build_model(rb, torch, ctx, dev, n_tenants, host_copy=None, base=None):
     """Random-init Q4_K_M weights generated and quantised on the device. If
     host_copy is a dict, the GGUF bytes of every tensor are also copied into it
     (for the CPU baseline on identical weights)."""
-    cfg = dict(CFG, kv_dtype=rb.F16, max_tenants=n_tenants, kv_pages=n_tenants * (CFG["max_seq"] // 16))
+    base = base or CFG
+    cfg = dict(base, kv_dtype=rb.F16, max_tenants=n_tenants, kv_pages=n_tenants * (base["max_seq"] // 16))
     m = rb.Model(ctx, cfg)
     g = torch.Generator(device=dev)
-    H, Q, KV, F, V = CFG["hidden"], CFG["n_heads"] * CFG["head_dim"], CFG["n_kv_heads"] * CFG["head_dim"], \
-        CFG["ffn"], CFG["vocab"]
+    H, Q, KV, F, V = base["hidden"], base["n_heads"] * base["head_dim"], base["n_kv_heads"] * base["head_dim"], \
+        base["ffn"], base["vocab"]
     seed = [3]
 
     def qt(dt, rows, cols):
@@ -141,7 +143,7 @@ def build_model(rb, torch, ctx, dev, n_tenants, host_copy=None):
     put(rb.W_OUTPUT, -1, rb.Q6_K, qt(rb.Q6_K, V, H))
     shapes = [(rb.W_Q, Q, H, rb.Q4_K), (rb.W_K, KV, H, rb.Q4_K), (rb.W_V, KV, H, rb.Q6_K), (rb.W_O, H, Q, rb.Q4_K),
               (rb.W_GATE, F, H, rb.Q4_K), (rb.W_UP, F, H, rb.Q4_K), (rb.W_DOWN, H, F, rb.Q4_K)]
-    for l in range(CFG["n_layers"]):
+    for l in range(base["n_layers"]):
         put(rb.W_ATTN_NORM, l, rb.F32, ones)
         put(rb.W_FFN_NORM, l, rb.F32, ones)
         for which, r, c, dt in shapes:
@@ -218,6 +220,95 @@ def attention_roofline(rb, torch, ctx, dev, hbm_peak, peak_kind):
             "avg_launch_us": round(avg * 1e3, 2)}
 
 
+def decode_step_line(step_bytes, step_ms, prof_ms, hbm_peak, nt):
+    """Per-GPU decode-step roofline, plus the GEMV chains' figure inside the
+    step: their share of a kernel-by-kernel run of one step (no overlap),
+    applied to the graph-replayed step time, against the weight bytes they
+    stream."""
+    tot = sum(prof_ms.values())
+    share = prof_ms["gemv"] / tot if tot > 0 else None
+    wb = weight_bytes(CFG)
+    line = {"tenants_per_gpu": nt, "bytes_per_step": int(step_bytes),
+            "achieved_GBps": round(step_bytes / (step_ms * 1e-3) / 1e9, 1),
+            "frac": round(step_bytes / (step_ms * 1e-3) / 1e9 / hbm_peak, 4),
+            "kernel_ms_serialised": {k: round(v, 4) for k, v in prof_ms.items()}}
+    if share:
+        chain_ms = step_ms * share
+        line["chain"] = {"share": round(share, 4), "ms_in_step": round(chain_ms, 4), "weight_bytes": int(wb),
+                         "GBps": round(wb / (chain_ms * 1e-3) / 1e9, 1),
+                         "frac": round(wb / (chain_ms * 1e-3) / 1e9 / hbm_peak, 4)}
+    return line
+
+
+SWEEP_SHAPES = [(4096, 4096, "q4k"), (11008, 4096, "q4k"), (4096, 11008, "q4k"), (32000, 4096, "q6k")]
+SWEEP_M = (1, 8, 16, 64)
+
+
+def gemv_sweep(rb, torch, ctx, dev, hbm_peak, peak_kind):
+    """the fused dequant GEMV/GEMM at Llama-7B shapes, weights
+    N(0, 0.02) quantised on the device (seed 3 per shape), M = 1, 8, 16, 64.
+    Device time per launch from a CUDA graph of 48 launches rotating weight
+    copies that together exceed the 126 MB L2 (each launch streams from HBM)."""
+    out = []
+    g = torch.Generator(device=dev)
+    for n, k, fmt in SWEEP_SHAPES:
+        dt = rb.Q4_K if fmt == "q4k" else rb.Q6_K
+        bpw = Q4K_BPW if fmt == "q4k" else Q6K_BPW
+        wbytes = n * k * bpw
+        copies = max(2, int(np.ceil(300e6 / wbytes)))
+        g.manual_seed(3)
+        x = torch.randn(n, k, generator=g, device=dev).mul_(0.02)
+        blk = torch.empty(int(wbytes), dtype=torch.uint8, device=dev)
+        ctx.quantize(dt, x.view(-1), blk)
+        del x
+        ws = [rb.Weight(ctx, dt, n, k, blk) for _ in range(copies)]
+        for m in SWEEP_M:
+            us = ctx.gemv_timing(ws, m, iters=48, reps=3)
+            alg = wbytes + 4 * m * k + 4 * m * n
+            gbps = alg / (us * 1e-6) / 1e9
+            out.append({"n": n, "k": k, "fmt": fmt, "m": m, "us": round(us, 2), "GBps": round(gbps, 1),
+                        "frac": round(gbps / hbm_peak, 4), "path": "tcgen05" if ctx.uses_tcgen05(m) else "mma.sync"})
+        for w in ws:
+            w.free()
+        del blk
+    return {"workload": "configs[2]: N x K weights N(0,0.02) seed 3, fp32 activations, M rows", "peak": hbm_peak,
+            "peak_kind": peak_kind, "points": out}
+
+
+def cpu_sweep(threads, budget_s=1.0):
+    """configs[2] on the host cores, timed on a row sample of each weight (the
+    cost per output row is constant, so time x N / rows sampled is the full
+    call). B1: the reference's fused kernel restated (fused.rs:229-374 /
+    1128-1259) on one thread; B2: the same on every thread; B3: dequantise then
+    an fp32 GEMM (CandleCpuBackend semantics, candle_cpu_backend.rs:92-114) on
+    every thread."""
+    from oracle import oracle as O
+    rng = np.random.default_rng(3)
+    pts = []
+    for n, k, fmt in SWEEP_SHAPES:
+        dt = O.Q4K if fmt == "q4k" else O.Q6K
+        rows = 256
+        blocks = O.quantize(dt, rng.normal(0, 0.02, size=(rows, k)).astype(np.float32))
+        wbytes = n * k * O.BLOCK_BYTES[dt] / 256
+        for m in SWEEP_M:
+            x = rng.normal(0, 1, size=(m, k)).astype(np.float32)
+            rec = {"n": n, "k": k, "fmt": fmt, "m": m, "rows_sampled": rows}
+            for name, fn in (("B1", lambda: O.fused_matmul(dt, blocks, x, m, rows, k, threads=1)),
+                             ("B2", lambda: O.fused_matmul(dt, blocks, x, m, rows, k, threads=threads)),
+                             ("B3", lambda: O.dequant_matmul(dt, blocks, x, m, rows, k, threads=threads))):
+                fn()
+                t0, reps = time.perf_counter(), 0
+                while True:
+                    fn()
+                    reps += 1
+                    if time.perf_counter() - t0 > budget_s / 8 or reps >= 50:
+                        break
+                per_call = (time.perf_counter() - t0) / reps * (n / rows)
+                rec[name] = {"us": round(per_call * 1e6, 1), "GBps": round(wbytes / per_call / 1e9, 3)}
+            pts.append(rec)
+    return {"threads": threads, "points": pts}
+
+
 def cpu_baseline(weights, threads, max_s=20.0):
     """The oracle (C++ restatement of the reference CPU path, all host threads)
     on a bounded sample: single-token decode forwards of one tenant at context
@@ -253,16 +344,29 @@ def run_ours(args):
         dist.init_process_group("nccl", device_id=dev)
     hbm_peak, peak_kind = peaks()
     ctx = rb.Context(local)
-    nt = TENANTS_PER_GPU
+    ledger = None
+    if dist:
+        from realm_b200.sharding import StepLedger
+        ledger = StepLedger.from_default_group("bench")
+    # 8 tenants on one GPU; 64 tenants sharded over 2/4/8 GPUs by
+    # LPT on prompt length (equal counts, so every rank runs the same row count)
+    rng = np.random.default_rng(4)
+    n_total = TENANTS_PER_GPU if world == 1 else TOTAL_TENANTS_MULTI
+    all_lens = rng.integers(128, 513, n_total)
+    all_ids = [rng.integers(0, CFG["vocab"], int(n)).astype(np.uint32) for n in all_lens]
+    if world == 1:
+        mine = list(range(n_total))
+    else:
+        from realm_b200.sharding import lpt_shard
+        mine = lpt_shard([int(x) for x in all_lens], world, equal_counts=True)[rank]
+    nt = len(mine)
+    lens = all_lens[mine]
     host_w = {} if (world == 1 and not args.no_cpu) else None
     m = build_model(rb, torch, ctx, dev, nt, host_w)
-    # prompts: U[128, 512] ids U[0, 32000) from seed 4 (per rank offset)
-    rng = np.random.default_rng(4 + rank)
-    lens = rng.integers(128, 513, nt)
     last = []
-    for t in range(nt):
+    for t, g in enumerate(mine):
         m.tenant_create(t)
-        ids = rng.integers(0, CFG["vocab"], int(lens[t])).astype(np.uint32)
+        ids = all_ids[g]
         for cs in range(0, len(ids), 64):
             chunk = ids[cs:cs + 64]
             _, am = m.forward_rows([t] * len(chunk), chunk, want_logits=False)
@@ -271,6 +375,9 @@ def run_ours(args):
     tok = np.array(last, np.uint32)
     for _ in range(args.warmup):
         _, tok = m.forward_rows(tenants, tok, want_logits=False)
+    if ledger:  # every rank is alive and warmed up before anyone times
+        ledger.done(1)
+        ledger.wait_peers(1, timeout_s=600)
     stream = torch.cuda.ExternalStream(ctx.stream, device=dev)
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     if dist:
@@ -287,12 +394,17 @@ def run_ours(args):
         ev1.record(stream)
         torch.cuda.synchronize(dev)
     e2e_ms = ev0.elapsed_time(ev1)
+    # one more step run kernel by kernel: the shares of the step's device time
+    prof_ms, _ = m.forward_profile(tenants, tok)
+    if ledger:
+        ledger.done(2)
+        ledger.wait_peers(2, timeout_s=600)
     if dist:
         t = torch.tensor([dev_ms, e2e_ms], device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         dev_ms, e2e_ms = float(t[0]), float(t[1])
         dist.barrier()
-    tokens = nt * world * args.steps
+    tokens = nt * world * args.steps  # equal tenant counts per rank
     value = tokens / (dev_ms * 1e-3)
     e2e = tokens / (e2e_ms * 1e-3)
     if rank != 0:
@@ -301,6 +413,7 @@ def run_ours(args):
         return
     roof = gemv_roofline(rb, torch, ctx, dev, hbm_peak, peak_kind)
     attn = attention_roofline(rb, torch, ctx, dev, hbm_peak, peak_kind)
+    sweep = gemv_sweep(rb, torch, ctx, dev, hbm_peak, peak_kind) if world == 1 else None
     # decode-step roofline: weights once + KV of every tenant per step
     mean_ctx = float(np.mean(lens)) + args.warmup + args.steps / 2
     step_bytes = weight_bytes(CFG) + nt * mean_ctx * CFG["n_layers"] * 2 * CFG["n_kv_heads"] * CFG["head_dim"] * 2
@@ -311,16 +424,20 @@ def run_ours(args):
         "vs_baseline": None, "dtype": "f32 (Q4_K/Q6_K weights exact in fp16 tensor-core operands, fp16 hi/lo "
                                       "activations, fp32 accumulate)",
         "data": "synthetic: random-init N(0,0.02) weights quantised on device, prompts U[128,512] seed 4",
-        "config": {"workload": "Llama-2-7B Q4_K_M decode (configs[3]), 8 tenants per GPU, fp16 paged KV",
-                   "tenants": nt * world, "prompt_lens": [int(x) for x in lens], "parallelism": f"tenant-sharded x{world}",
+        "config": {"workload": ("Llama-2-7B Q4_K_M decode (configs[3]), 8 tenants on 1 GPU" if world == 1 else
+                                f"Llama-2-7B Q4_K_M decode (configs[3]), 64 tenants sharded over {world} GPUs "
+                                f"(LPT by prompt length), weights replicated") + ", fp16 paged KV",
+                   "tenants": nt * world, "tenants_per_gpu": nt,
+                   "prompt_lens": [int(x) for x in lens] if world == 1 else None,
+                   "parallelism": f"tenant-sharded x{world}",
                    "l2": "weights 3.9 GB per step > 126 MB L2 (no flush needed)"},
         "e2e": {"value": round(e2e, 1), "unit": "tok/s", "h2d_bytes_per_step": 4 * (2 + 3 * 64),
                 "d2h_bytes_per_step": 8 * nt},
         "gpu_launches": launches,
         "roofline": roof,
         "attention": attn,
-        "decode_step": {"bytes_per_step": int(step_bytes), "achieved_GBps": round(step_bytes / (step_ms * 1e-3) / 1e9, 1),
-                        "frac": round(step_bytes / (step_ms * 1e-3) / 1e9 / hbm_peak, 4)},
+        "gemv_sweep": sweep,
+        "decode_step": decode_step_line(step_bytes, step_ms, prof_ms, hbm_peak, nt),
         "clocks": clk.summary(),
     }
     if host_w is not None:
@@ -328,6 +445,10 @@ def run_ours(args):
             line["cpu_baseline"] = cpu_baseline(host_w, os.cpu_count() or 1)
         except Exception as e:  # a baseline failure must not hide the GPU number
             line["cpu_baseline"] = {"error": str(e)[:200]}
+        try:
+            line["cpu_sweep"] = cpu_sweep(os.cpu_count() or 1)
+        except Exception as e:
+            line["cpu_sweep"] = {"error": str(e)[:200]}
     print(json.dumps(line), flush=True)
     if dist:
         dist.destroy_process_group()
@@ -445,6 +566,9 @@ def run_case(args):
     if args.case == "sample":
         run_sample(rb, torch, ctx, dev)
         return
+    if args.case == "llama70b":
+        run_llama70b(rb, torch, ctx, dev, args)
+        return
     if args.case == "qgemm":
         # the tcgen05 dequant-GEMM (opt-in path): 8 launches of a 4096 x 4096 Q4_K
         # weight over 8 copies (75 MB > L2), 64 rows
@@ -478,6 +602,70 @@ def run_case(args):
     for s in range(3):
         _, tok = m.forward_rows(tenants, tok, want_logits=False)
         print("decode step", s, ctx.last_forward_launches(), "launches", flush=True)
+
+
+CFG70B = dict(n_layers=80, hidden=8192, n_heads=64, n_kv_heads=8, head_dim=128, ffn=28672, vocab=32000,
+              max_seq=4096, rms_eps=1e-5, layer_eps=1e-5, rope_theta=10000.0)
+
+
+def run_llama70b(rb, torch, ctx, dev, args):
+    """Llama-2-70B shape (80 layers, hidden 8192, 64 q / 8 kv heads
+    of 128, FFN 28672, vocab 32000), random-init N(0, 0.02) weights quantised
+    to Q4_K_M on the device (about 40 GB), 16 tenants with fp16 paged KV.
+    Decode: every tenant's cache holds 3840 random entries (the prompt's K/V
+    stand-in), then 16-row decode steps are timed (CUDA events over the graph
+    replays). Prefill: one tenant's 3840-token prompt in 64-row steps, timed.
+    Prints one JSON line."""
+    hbm_peak, peak_kind = peaks()
+    nt, prompt = 16, 3840
+    m = build_model(rb, torch, ctx, dev, nt, base=CFG70B)
+    kvw = CFG70B["n_kv_heads"] * CFG70B["head_dim"]
+    g = torch.Generator(device=dev)
+    g.manual_seed(5)
+    for t in range(nt):
+        m.tenant_create(t)
+        for l in range(CFG70B["n_layers"]):
+            m.kv.append(t, l, torch.randn(prompt, kvw, generator=g, device=dev),
+                        torch.randn(prompt, kvw, generator=g, device=dev))
+    tenants = np.arange(nt, dtype=np.uint32)
+    tok = np.random.default_rng(5).integers(0, CFG70B["vocab"], nt).astype(np.uint32)
+    for _ in range(3):
+        _, tok = m.forward_rows(tenants, tok, want_logits=False)
+    steps = max(4, min(args.steps, 32))
+    dev_ms = 0.0
+    with Clocks(0) as clk:
+        for _ in range(steps):
+            _, tok = m.forward_rows(tenants, tok, want_logits=False)
+            dev_ms += ctx.last_forward_ms()
+    step_ms = dev_ms / steps
+    prof_ms, _ = m.forward_profile(tenants, tok)
+    ctx_mean = prompt + 3 + steps / 2
+    wb = weight_bytes(CFG70B)
+    kvb = nt * ctx_mean * CFG70B["n_layers"] * 2 * kvw * 2
+    # prefill: one more tenant-sized prompt through 64-row steps (the cache of
+    # tenant 0 is reset and refilled by the prompt itself)
+    m.tenant_reset(0)
+    ids = np.random.default_rng(55).integers(0, CFG70B["vocab"], prompt).astype(np.uint32)
+    torch.cuda.synchronize(dev)
+    pre_ms = 0.0
+    for cs in range(0, prompt, 64):
+        m.forward_rows([0] * 64, ids[cs:cs + 64], want_logits=False)
+        pre_ms += ctx.last_forward_ms()
+    line = {"metric": "configs[4] Llama-2-70B Q4_K_M decode tok/s (16 tenants, ctx 3840+)", "unit": "tok/s",
+            "value": round(nt / (step_ms * 1e-3), 1), "ms_per_step": round(step_ms, 3), "steps": steps,
+            "decode_step": {"bytes_per_step": int(wb + kvb), "weight_bytes": int(wb), "kv_bytes": int(kvb),
+                            "achieved_GBps": round((wb + kvb) / (step_ms * 1e-3) / 1e9, 1),
+                            "frac": round((wb + kvb) / (step_ms * 1e-3) / 1e9 / hbm_peak, 4),
+                            "peak": hbm_peak, "peak_kind": peak_kind,
+                            "kernel_ms_serialised": {k: round(v, 3) for k, v in prof_ms.items()}},
+            "prefill": {"tokens": prompt, "rows_per_step": 64, "ms": round(pre_ms, 1),
+                        "tok_per_s": round(prompt / (pre_ms * 1e-3), 1),
+                        "path": "tcgen05" if ctx.uses_tcgen05(64) else "mma.sync"},
+            "config": {"workload": "Llama-2-70B shape, random-init Q4_K_M (attn_v, output Q6_K), 16 tenants, "
+                                   "fp16 paged KV, caches of 3840 N(0,1) entries; prefill of a 3840-token prompt",
+                       "weights_GB": round(wb / 1e9, 2)},
+            "clocks": clk.summary()}
+    print(json.dumps(line), flush=True)
 
 
 def run_serve(rb, torch, ctx, dev, n_req=96, max_batch=32, max_tokens=128, sampling=None):
@@ -619,7 +807,8 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU-baseline leg")
-    ap.add_argument("--case", choices=["gemv", "decode", "attn", "serve", "serve_sampled", "load", "sample", "qgemm"],
+    ap.add_argument("--case", choices=["gemv", "decode", "attn", "serve", "serve_sampled", "load", "sample", "qgemm",
+                             "llama70b"],
                     help="profiling case for ncu: run a small workload of one kernel family and exit")
     args = ap.parse_args()
     if args.case:

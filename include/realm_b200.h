@@ -128,7 +128,7 @@ int32_t rb_weight_matmul(rb_ctx* ctx, int32_t handle, const float* input, float*
  * synchronisation are not allowed): input [batch][k] and output [batch][n] are
  * caller-owned device buffers (flags must contain RB_PTR_DEVICE; RB_ASYNC
  * returns without waiting), and all other working memory is one fixed
- * 3,434,496-byte device array in the library, held on every GPU that loads it
+ * 3,565,568-byte device array in the library, held on every GPU that loads it
  * until the process exits. Limits: batch <= 8, K <= 16384, N <= 131072, at most
  * 160 GEMV CTAs; larger calls fail with RB_ERR_INVALID. A Q8_0 weight whose K
  * is not a multiple of 256 (rows zero-padded at upload) is refused with
@@ -148,6 +148,9 @@ int32_t rb_weight_matmul_noalloc(rb_ctx* ctx, int32_t handle, const float* input
  * the mean is returned in *avg_us. */
 int32_t rb_weight_matmul_timing(rb_ctx* ctx, const int32_t* handles, uint32_t n_handles, uint32_t batch, uint32_t iters,
                                 uint32_t reps, float* avg_us);
+/* 1 when rb_weight_matmul of `batch` rows runs on the tcgen05 dequant-GEMM,
+ * 0 when it runs on the mma.sync GEMV. */
+int32_t rb_weight_matmul_path(rb_ctx* ctx, uint32_t batch);
 /* Test hook: the resident tiled bytes converted back to GGUF layout (Q4_K). */
 int32_t rb_weight_export(rb_ctx* ctx, int32_t handle, void* out_blocks, size_t nbytes, uint32_t flags);
 
@@ -250,6 +253,15 @@ int32_t rb_tenant_reset(rb_ctx* ctx, int32_t model, uint32_t tenant);
  * Returns n_rows. */
 int32_t rb_forward(rb_ctx* ctx, int32_t model, uint32_t n_rows, const uint32_t* tenants, const uint32_t* tokens,
                    const uint32_t* positions, float* logits, uint32_t* argmax, uint32_t flags);
+
+/* Measurement hook: one decode step as rb_forward (positions = cache lengths,
+ * no outputs), run without graph replay or programmatic dependent launch and
+ * with an event after every kernel, so each interval is one kernel's device
+ * time. kind_ms[4] receives the summed milliseconds of the embedding, GEMV
+ * (multi-phase chain), attention and tcgen05 GEMM launches. Returns the
+ * number of launches. */
+int32_t rb_forward_profile(rb_ctx* ctx, int32_t model, uint32_t n_rows, const uint32_t* tenants,
+                           const uint32_t* tokens, float* kind_ms);
 
 /* realm_embed_tokens (crates/realm-runtime/src/memory64_host.rs:2483-2613): out [n][hidden]. Returns bytes. */
 int32_t rb_embed_tokens(rb_ctx* ctx, int32_t model, const uint32_t* token_ids, uint32_t n, float* out,

@@ -88,6 +88,7 @@ _sig("rb_weight_matmul", [_vp, _i32, _vp, _vp, _u32, _u32])
 _sig("rb_weight_export", [_vp, _i32, _vp, _sz, _u32])
 _sig("rb_weight_matmul_noalloc", [_vp, _i32, _vp, _vp, _u32, _u32])
 _sig("rb_weight_matmul_timing", [_vp, _vp, _u32, _u32, _u32, _u32, C.POINTER(C.c_float)])
+_sig("rb_weight_matmul_path", [_vp, _u32])
 _sig("rb_candle_matmul", [_vp, _vp, _vp, _vp, _u32, _u32, _u32, _u32])
 _sig("rb_candle_matmul_transposed", [_vp, _vp, _vp, _vp, _u32, _u32, _u32, _u32])
 _sig("rb_kv_pool_create", [_vp, _u32, _u32, _u32, _i32, _u32, _u32, _u32, _I32P])
@@ -109,6 +110,7 @@ _sig("rb_model_kv_pool", [_vp, _i32])
 _sig("rb_tenant_create", [_vp, _i32, _u32])
 _sig("rb_tenant_reset", [_vp, _i32, _u32])
 _sig("rb_forward", [_vp, _i32, _u32, _vp, _vp, _vp, _vp, _vp, _u32])
+_sig("rb_forward_profile", [_vp, _i32, _u32, _vp, _vp, _vp])
 _sig("rb_embed_tokens", [_vp, _i32, _vp, _u32, _vp, _u32])
 _sig("rb_forward_layer", [_vp, _i32, _u32, _u32, _vp, _u32, _u32, _vp, _u32])
 _sig("rb_compute_logits", [_vp, _i32, _vp, _u32, _vp, _u32])
@@ -280,6 +282,10 @@ class Context:
         _check(_lib.rb_weight_matmul_timing(self._h, h.ctypes.data_as(C.c_void_p), len(h), batch, iters, reps,
                                             C.byref(out)))
         return float(out.value)
+
+    def uses_tcgen05(self, batch: int) -> bool:
+        """Whether a matmul of `batch` rows runs on the tcgen05 dequant-GEMM."""
+        return bool(_lib.rb_weight_matmul_path(self._h, batch))
 
     def upload_weight(self, dtype: int, n: int, k: int, blocks) -> "Weight":
         return Weight(self, dtype, n, k, blocks)
@@ -492,6 +498,16 @@ class Model:
         _check(_lib.rb_forward(self.ctx.handle, self.handle, n, _ptr(t), _ptr(tok), _ptr(p), _ptr(logits), _ptr(am),
                                PTR_HOST))
         return logits, am
+
+    def forward_profile(self, tenants, tokens):
+        """One decode step run kernel by kernel (no graph, no overlap): summed
+        device ms of the embedding, GEMV chain, attention and tcgen05 GEMM
+        launches, and the launch count."""
+        t = _u32arr(tenants)
+        tok = _u32arr(tokens)
+        ms = np.zeros(4, np.float32)
+        n = _check(_lib.rb_forward_profile(self.ctx.handle, self.handle, len(t), _ptr(t), _ptr(tok), _ptr(ms)))
+        return dict(zip(("embed", "gemv", "attention", "qgemm"), ms.tolist())), n
 
     def forward(self, token_ids, position: int, tenant: int = 0):
         """Model::forward (model.rs:572-625): logits of the last token."""

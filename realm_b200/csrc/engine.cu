@@ -188,11 +188,12 @@ struct Weight {
 
 // Device storage for one GEMV input's activation fragments (xfrag.cuh).
 struct FragBuf {
-  DevBuf f, i, c, s;
+  DevBuf f, i, i3, c, s;
   cudaError_t alloc(int k, int nt) {
     cudaError_t e;
     if ((e = f.alloc(xf_bytes(k, nt))) != cudaSuccess) return e;
     if ((e = i.alloc(xi_bytes(k, nt))) != cudaSuccess) return e;
+    if ((e = i3.alloc(x3_bytes(k, nt))) != cudaSuccess) return e;
     if ((e = c.alloc(xc_bytes(k, nt))) != cudaSuccess) return e;
     return s.alloc(xs_bytes(k, nt));
   }
@@ -200,6 +201,7 @@ struct FragBuf {
     XFrags v;
     v.xf = f.as<uint4>();
     v.xi = i.as<uint4>();
+    v.x3 = i3.as<uint2>();
     v.xc = c.as<float>();
     v.xs = s.as<uint32_t>();
     return v;
@@ -210,7 +212,7 @@ struct FragBuf {
   XFrags view_for(int consumer_dtype) const {
     XFrags v = view();
     if (consumer_dtype == DT_Q4_K) v.xf = nullptr;
-    else v.xi = nullptr, v.xc = nullptr;
+    else v.xi = nullptr, v.x3 = nullptr, v.xc = nullptr;
     return v;
   }
 };
@@ -308,7 +310,20 @@ struct Ctx {
   // the next multi-phase GEMV launch with a grid barrier gets its first
   // barrier's target out of reach and this poll limit for every barrier wait
   uint32_t test_fail_spin = 0;
+  // measurement hook (rb_forward_profile): when set, an event is recorded
+  // after every launch of the step, tagged with the launch's kind
+  std::vector<std::pair<int, cudaEvent_t>>* prof = nullptr;
 };
+
+enum ProfKind { PROF_EMBED = 0, PROF_GEMV = 1, PROF_ATTN = 2, PROF_QGEMM = 3, PROF_KINDS = 4 };
+
+void prof_mark(Ctx* c, int kind) {
+  if (!c->prof) return;
+  cudaEvent_t e = nullptr;
+  if (cudaEventCreate(&e) != cudaSuccess) return;
+  cudaEventRecord(e, c->stream);
+  c->prof->push_back({kind, e});
+}
 
 // With RB_QGEMM=1, batches of at least this many rows take the tcgen05 dequant-GEMM.
 constexpr int kQgemmMinRows = 16;
@@ -428,6 +443,7 @@ GemvArgs base_args(Ctx* c, const Weight& w, int m) {
 
 int launch_gemv(Ctx* c, const GemvArgs& a, int* launches) {
   RB_CUDA(gemv_launch(a, c->num_sms, c->stream, c->pdl ? 1 : 0));
+  prof_mark(c, PROF_GEMV);
   if (launches) ++*launches;
   return RB_OK;
 }
@@ -449,6 +465,7 @@ int launch_qgemm(Ctx* c, const GemvArgs& a, int* launches) {
   const QgemmPlan p = qgemm_plan(c->num_sms, a.n_rg, a.nsb);
   if (c->qg_part.n < qgemm_part_floats(p) * 4) return fail(RB_ERR_INVALID, "GEMM scratch not sized for this weight");
   RB_CUDA(qgemm_launch(a, c->qg_part.as<float>(), p, c->stream, c->pdl ? 1 : 0));
+  prof_mark(c, PROF_QGEMM);
   if (launches) *launches += 2;
   return RB_OK;
 }
@@ -458,21 +475,22 @@ int launch_qgemm(Ctx* c, const GemvArgs& a, int* launches) {
 // first stamp) of the most recent GEMV launch.
 void dump_stamps(Ctx* c, int n_phases) {
   const int G = c->num_sms;
-  std::vector<unsigned long long> ts((size_t)G * kMaxPhases * 16);
+  std::vector<unsigned long long> ts((size_t)G * kMaxPhases * kStampSlots);
   if (cudaMemcpy(ts.data(), c->dbg_ts.p, ts.size() * 8, cudaMemcpyDeviceToHost) != cudaSuccess) return;
   unsigned long long t0 = ~0ull;
   for (unsigned long long v : ts)
     if (v) t0 = std::min(t0, v);
-  const char* names[16] = {"cons_start", "cons_dep_ok", "cons_first_full", "cons_last_unit",
-                           "cons_done", "prod_first_w", "prod_x_released", "prod_last_w",
-                           "seg_begin", "seg_deposited", "seg_ticket", "seg_summed",
-                           "seg_epi_done", "resid_elems", "resid_ss", "resid_frags"};
+  const char* names[kStampSlots] = {"cons_start", "cons_dep_ok", "cons_first_full", "cons_last_unit",
+                                    "cons_done", "prod_first_w", "prod_x_released", "prod_last_w",
+                                    "seg_begin", "seg_deposited", "seg_ticket", "seg_summed",
+                                    "seg_epi_done", "resid_elems", "resid_ss", "resid_frags",
+                                    "seg_fenced", "grid_arrived", "s18", "s19", "s20", "s21", "s22", "s23"};
   for (int p = 0; p < n_phases; ++p)
-    for (int k = 0; k < 16; ++k) {
+    for (int k = 0; k < kStampSlots; ++k) {
       double mn = 1e30, mx = 0, sum = 0;
       int n = 0;
       for (int b = 0; b < G; ++b) {
-        const unsigned long long v = ts[((size_t)b * kMaxPhases + p) * 16 + k];
+        const unsigned long long v = ts[((size_t)b * kMaxPhases + p) * kStampSlots + k];
         if (!v) continue;
         const double d = (double)(v - t0) / 1000.0;
         mn = std::min(mn, d);
@@ -487,15 +505,15 @@ void dump_stamps(Ctx* c, int n_phases) {
   for (int p = 0; p < n_phases; ++p) {
     std::vector<std::pair<double, int>> tails;
     for (int b = 0; b < G; ++b) {
-      const unsigned long long* t = &ts[((size_t)b * kMaxPhases + p) * 16];
+      const unsigned long long* t = &ts[((size_t)b * kMaxPhases + p) * kStampSlots];
       if (t[3] && t[4]) tails.push_back({(double)(t[4] - t[3]) / 1000.0, b});
     }
     std::sort(tails.rbegin(), tails.rend());
     for (size_t i = 0; i < tails.size() && i < 3; ++i) {
       const int b = tails[i].second;
-      const unsigned long long* t = &ts[((size_t)b * kMaxPhases + p) * 16];
+      const unsigned long long* t = &ts[((size_t)b * kMaxPhases + p) * kStampSlots];
       fprintf(stderr, "[gemv phase %d] slow cta %3d tail %6.2f us:", p, b, tails[i].first);
-      for (int k = 8; k < 16; ++k)
+      for (int k = 8; k < kStampSlots; ++k)
         if (t[k]) fprintf(stderr, " %s %+.2f", names[k], ((double)t[k] - (double)t[3]) / 1000.0);
       fprintf(stderr, "\n");
     }
@@ -549,6 +567,7 @@ int chain_flush(Ctx* c, int* launches) {
   c->chain_n = 0;
   c->chain_mask = 0;
   RB_CUDA(gemv_chain_launch(ca, c->num_sms, c->stream, c->pdl ? 1 : 0));
+  prof_mark(c, PROF_GEMV);
   if (launches) ++*launches;
   return RB_OK;
 }
@@ -645,6 +664,7 @@ int enqueue_layer(Ctx* c, Model& M, int l, int m, const int32_t* d_tenant, const
   at.whole_pairs = c->attn_whole;
   if (c->gemv_dbg & 2) at.dbg_ts = c->attn_ts.as<unsigned long long>();
   RB_CUDA(attn_launch(at, c->num_sms, c->stream, c->pdl ? 1 : 0));
+  prof_mark(c, PROF_ATTN);
   if (launches) ++*launches;
   // o-proj + residual; writes fragments of x * ffn_norm
   GemvArgs ao = base_args(c, L.o, m);
@@ -713,6 +733,7 @@ int enqueue_step(Ctx* c, Model& M, int m, int* launches) {
                                          kMaxRowsAbi, M.argmax.as<unsigned long long>(),
                                          M.layers[0].raw[0].d.as<float>(), gemv_nt_for(m), M.fa.view());
   RB_CUDA(cudaGetLastError());
+  prof_mark(c, PROF_EMBED);
   if (launches) ++*launches;
   for (int l = 0; l < (int)cf.n_layers; ++l)
     if (int rc = enqueue_layer(c, M, l, m, desc + kDescTenant, desc + kDescPos, launches)) return rc;
@@ -946,8 +967,8 @@ int32_t rb_ctx_create(const rb_config* cfg, rb_ctx** out) {
   c->graphs = cfg->use_graphs != 0;
   if (const char* d = getenv("RB_GEMV_DBG")) c->gemv_dbg = atoi(d);
   if (c->gemv_dbg & 2) {
-    RB_CUDA(c->dbg_ts.alloc((size_t)c->num_sms * kMaxPhases * 16 * 8));
-    RB_CUDA(cudaMemset(c->dbg_ts.p, 0, (size_t)c->num_sms * kMaxPhases * 16 * 8));
+    RB_CUDA(c->dbg_ts.alloc((size_t)c->num_sms * kMaxPhases * kStampSlots * 8));
+    RB_CUDA(cudaMemset(c->dbg_ts.p, 0, (size_t)c->num_sms * kMaxPhases * kStampSlots * 8));
     RB_CUDA(c->attn_ts.alloc((size_t)attn_grid(c->num_sms) * 8 * 8));
     RB_CUDA(cudaMemset(c->attn_ts.p, 0, (size_t)attn_grid(c->num_sms) * 8 * 8));
   }
@@ -1194,6 +1215,11 @@ int32_t rb_weight_matmul_timing(rb_ctx* c, const int32_t* handles, uint32_t n_ha
   *avg_us = ms * 1000.f / (float)(reps * iters);
   if ((c->gemv_dbg & 2) && c->dbg_ts.p) dump_stamps(c, 1);
   return RB_OK;
+}
+
+int32_t rb_weight_matmul_path(rb_ctx* c, uint32_t batch) {
+  if (!c) return fail(RB_ERR_BAD_HANDLE, "null context");
+  return (c->qgemm && (int)batch >= kQgemmMinRows) ? 1 : 0;
 }
 
 int32_t rb_weight_export(rb_ctx* c, int32_t h, void* out_blocks, size_t nbytes, uint32_t flags) {
@@ -1666,6 +1692,49 @@ int32_t rb_forward(rb_ctx* c, int32_t model, uint32_t n_rows, const uint32_t* te
   return (int32_t)n_rows;
 }
 
+int32_t rb_forward_profile(rb_ctx* c, int32_t model, uint32_t n_rows, const uint32_t* tenants,
+                           const uint32_t* tokens, float* kind_ms) {
+  Model* M = get_model(c, model);
+  if (!M) return fail(RB_ERR_BAD_HANDLE, "model %d", model);
+  if (!M->finalized) return fail(RB_ERR_INVALID, "model not finalized");
+  if (!kind_ms) return fail(RB_ERR_INVALID, "null output");
+  if (n_rows == 0 || n_rows > (uint32_t)c->max_rows) return fail(RB_ERR_INVALID, "n_rows %u not in [1, %d]", n_rows, c->max_rows);
+  for (uint32_t r = 0; r < n_rows; ++r)
+    if (tokens[r] >= M->cfg.vocab) return fail(RB_ERR_INVALID, "token %u >= vocab", tokens[r]);
+  KvPool& P = *c->pools[M->pool];
+  RowPlan rp;
+  if (int rc = plan_rows(P, n_rows, tenants, tokens, nullptr, -1, rp)) return rc;
+  if (int rc = upload_desc(c, rp, M->desc.as<int32_t>())) return rc;
+  c->step_grouped = rows_grouped(rp);
+  std::vector<std::pair<int, cudaEvent_t>> marks;
+  cudaEvent_t start = nullptr;
+  RB_CUDA(cudaEventCreate(&start));
+  const bool pdl = c->pdl;
+  c->pdl = false;  // serialised launches: each interval is one kernel
+  RB_CUDA(cudaEventRecord(start, c->stream));
+  c->prof = &marks;
+  int rc = run_forward(c, *M, (int)n_rows, false);
+  c->prof = nullptr;
+  c->pdl = pdl;
+  if (!rc) rc = sync_ctx(c);
+  for (int k = 0; k < PROF_KINDS; ++k) kind_ms[k] = 0.f;
+  cudaEvent_t prev = start;
+  for (auto& mk : marks) {
+    float ms = 0.f;
+    if (!rc) cudaEventElapsedTime(&ms, prev, mk.second);
+    kind_ms[mk.first] += ms;
+    prev = mk.second;
+  }
+  for (auto& mk : marks) cudaEventDestroy(mk.second);
+  cudaEventDestroy(start);
+  if (rc) return rc;
+  for (uint32_t r = 0; r < n_rows; ++r) {
+    KvTenant& T = P.tenants[rp.tenant[r]];
+    for (auto& l : T.len) l = std::max(l, rp.pos[r] + 1);
+  }
+  return (int32_t)marks.size();
+}
+
 static int sample_rows(rb_ctx* c, const float* d_logits, uint32_t ld, uint32_t n_rows, uint32_t vocab,
                        const rb_sampling* params, const uint32_t* prev, const uint32_t* prev_off,
                        const float* uniforms, uint32_t* out, uint32_t flags) {
@@ -1917,7 +1986,7 @@ int32_t rb_last_forward_launches(rb_ctx* c) { return c ? c->last_launches : fail
 // Limits (calls beyond them fail with RB_ERR_INVALID and a message naming the
 // limit): batch <= 8 rows, K <= 16384, N <= 131072 (512 groups of 256 rows),
 // and at most 160 GEMV CTAs (the device's SM count when the weight has that
-// many 256-row x 256-column units). The array is 3,434,496 bytes. Q8_0 weights
+// many 256-row x 256-column units). The array is 3,565,568 bytes. Q8_0 weights
 // whose K is not a multiple of 256 (zero-padded at upload) are refused with
 // RB_ERR_UNSUPPORTED.
 //
@@ -1942,15 +2011,18 @@ constexpr int kNaMaxCtas = 160;
 constexpr int kNaMaxDevices = 64;
 constexpr size_t kNaXf = (size_t)(kNaMaxK / 256) * kXfSbBytes;   // NT = 1
 constexpr size_t kNaXi = (size_t)(kNaMaxK / 256) * kXiSbBytes;
+constexpr size_t kNaX3 = (size_t)(kNaMaxK / 256) * kX3SbBytes;
 constexpr size_t kNaXc = (size_t)(kNaMaxK / 256) * kXcSbBytes;
 constexpr size_t kNaXs = (size_t)(kNaMaxK / 256) * kXsSbBytes;
 constexpr size_t kNaPartials = (size_t)kNaMaxCtas * 2 * 16 * 128 * 4;  // gemv_partials_floats(160, 1) floats
 constexpr size_t kNaCounters = (size_t)kNaMaxRowGroups * 4;
-constexpr size_t kNaOffXi = kNaXf, kNaOffXc = kNaOffXi + kNaXi, kNaOffXs = kNaOffXc + kNaXc,
-                 kNaOffPart = kNaOffXs + kNaXs, kNaOffCnt = kNaOffPart + kNaPartials, kNaBytes = kNaOffCnt + kNaCounters;
-static_assert(kNaOffXi % 256 == 0 && kNaOffXc % 256 == 0 && kNaOffXs % 256 == 0 && kNaOffPart % 256 == 0 &&
-                  kNaOffCnt % 256 == 0,
+constexpr size_t kNaOffXi = kNaXf, kNaOffX3 = kNaOffXi + kNaXi, kNaOffXc = kNaOffX3 + kNaX3,
+                 kNaOffXs = kNaOffXc + kNaXc, kNaOffPart = kNaOffXs + kNaXs, kNaOffCnt = kNaOffPart + kNaPartials,
+                 kNaBytes = kNaOffCnt + kNaCounters;
+static_assert(kNaOffXi % 256 == 0 && kNaOffX3 % 256 == 0 && kNaOffXc % 256 == 0 && kNaOffXs % 256 == 0 &&
+                  kNaOffPart % 256 == 0 && kNaOffCnt % 256 == 0,
               "scratch sections must stay 256-byte aligned");
+static_assert(kNaBytes == 3565568, "the documented size of the no-alloc scratch array");
 
 // Host code sees only a stand-in for this symbol; its device address comes from
 // cudaGetSymbolAddress.
@@ -2002,6 +2074,7 @@ extern "C" int32_t rb_weight_matmul_noalloc(rb_ctx* c, int32_t h, const float* i
   XFrags xf;
   xf.xf = reinterpret_cast<uint4*>(base);
   xf.xi = reinterpret_cast<uint4*>(base + kNaOffXi);
+  xf.x3 = reinterpret_cast<uint2*>(base + kNaOffX3);
   xf.xc = reinterpret_cast<float*>(base + kNaOffXc);
   xf.xs = reinterpret_cast<uint32_t*>(base + kNaOffXs);
   int32_t* counters = reinterpret_cast<int32_t*>(base + kNaOffCnt);

@@ -10,7 +10,7 @@
 //  * One producer lane streams 256-row x 256-column units (37-70 KB) with the
 //    bulk-copy engine (cp.async.bulk, no multicast) into a shared-memory ring.
 //  * The activations arrive as pre-built B fragments (xfrag.cuh, written once
-//    by the producing kernel): int8 two-limb for Q4_K, fp16 hi/lo (~22 bits)
+//    by the producing kernel): int8 three-limb for Q4_K, fp16 hi/lo (~22 bits)
 //    for Q6_K and Q8_0. They are bulk-copied next to each weight unit, so the
 //    tensor cores see exact integer weights and no conversion work happens here.
 //  * Sixteen consumer warps (one 16-row tile each) turn the quantised values
@@ -41,7 +41,7 @@ constexpr int kSmemBudget = 200 * 1024;
 // activation bytes staged per unit: Q4_K reads int8 limbs + scales + sums, the
 // others fp16 hi/lo fragments + sums
 __host__ __device__ constexpr int x_stage_bytes(int dtype, int nt) {
-  return dtype == DT_Q4_K ? nt * (kXiSbBytes + kXcSbBytes + kXsSbBytes) : nt * (kXfSbBytes + kXsSbBytes);
+  return dtype == DT_Q4_K ? nt * (kXiSbBytes + kX3SbBytes + kXcSbBytes + kXsSbBytes) : nt * (kXfSbBytes + kXsSbBytes);
 }
 __host__ __device__ constexpr int stage_bytes(int dtype, int nt) { return unit_bytes(dtype) + x_stage_bytes(dtype, nt); }
 // epilogue tile: token-major, a row of kRowGroup + 1 floats per token (the
@@ -63,10 +63,10 @@ __device__ __forceinline__ unsigned long long gtimer() {
   asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
   return t;
 }
-// measurement stamps (dbg bit 1): [cta][phase][16] %globaltimer values
+// measurement stamps (dbg bit 1): [cta][phase][kStampSlots] %globaltimer values
 #define RB_TS(p, slot)                                                                                    \
   do {                                                                                                    \
-    if ((a.dbg & 2) && a.dbg_ts) a.dbg_ts[((size_t)blockIdx.x * kMaxPhases + (p)) * 16 + (slot)] = gtimer(); \
+    if ((a.dbg & 2) && a.dbg_ts) a.dbg_ts[((size_t)blockIdx.x * kMaxPhases + (p)) * kStampSlots + (slot)] = gtimer(); \
   } while (0)
 
 __device__ __forceinline__ float4 ldcg4(const float* p) { return __ldcg(reinterpret_cast<const float4*>(p)); }
@@ -89,14 +89,15 @@ __device__ __forceinline__ void mma_s8_16832(int d[4], const uint32_t a[4], uint
 }
 
 // Q4_K on the int8 tensor path. Per 32-column sub-block j the MMA gives exact
-// integer dot products C1 (limb 1) and C2 (limb 2) of the 4-bit quants with
-// the activation limbs; sc_j * (256*C1 + C2) accumulates exactly in int32 over
-// a 64-column group (|.| < 2^31 by construction), then scales by the group's
-// activation scale. Per row: y = d/256 * sum_g s_g * S_g - dmin * sum_j m_j * xsum_j
+// integer dot products C1, C2, C3 of the 4-bit quants with the three activation
+// limbs; sc_j * (256*C1 + C2) accumulates exactly in int32 over a 64-column
+// group (|.| < 2^31 by construction), sc_j * C3 in a second int32, and the pair
+// is scaled by the group's activation scale: s * (S12 + S3 / 256) / 256.
+// Per row: y = d/256 * sum_g s_g * (S12_g + S3_g / 256) - dmin * sum_j m_j * xsum_j
 // (dequantize_q4_k, quant.rs:160-182: q*d*sc - dmin*m, regrouped).
 template <int NT>
-__device__ __forceinline__ void tile_q4k(const uint8_t* tile, const uint8_t* xi, const uint8_t* xc, const uint8_t* xsb,
-                                         int lane, float acc[NT][4]) {
+__device__ __forceinline__ void tile_q4k(const uint8_t* tile, const uint8_t* xi, const uint8_t* x3, const uint8_t* xc,
+                                         const uint8_t* xsb, int lane, float acc[NT][4]) {
   const int g = lane >> 2, c = lane & 3;
   const uint4 hA = lds128(tile + g * 16);
   const uint4 hB = lds128(tile + (g + 8) * 16);
@@ -122,9 +123,11 @@ __device__ __forceinline__ void tile_q4k(const uint8_t* tile, const uint8_t* xi,
 #pragma unroll
   for (int grp = 0; grp < 4; ++grp) {  // 64-column group = sub-blocks 2grp, 2grp+1
     const uint4 q = lds128(qs + grp * 512 + lane * 16);
-    int S[NT][4];
+    int S[NT][4], S3[NT][4];
 #pragma unroll
-    for (int nt = 0; nt < NT; ++nt) S[nt][0] = S[nt][1] = S[nt][2] = S[nt][3] = 0;
+    for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+      for (int r = 0; r < 4; ++r) S[nt][r] = S3[nt][r] = 0;
 #pragma unroll
     for (int h = 0; h < 2; ++h) {
       const int j = 2 * grp + h;
@@ -139,36 +142,43 @@ __device__ __forceinline__ void tile_q4k(const uint8_t* tile, const uint8_t* xi,
 #pragma unroll
       for (int nt = 0; nt < NT; ++nt) {
         const uint4 b = lds128(xi + nt * kXiSbBytes + (j * 32 + lane) * 16);
-        int c1[4], c2[4];
+        const uint2 b3 = lds64(x3 + nt * kX3SbBytes + (j * 32 + lane) * 8);
+        int c1[4], c2[4], c3[4];
         mma_s8_16832(c1, af, b.x, b.y);
         mma_s8_16832(c2, af, b.z, b.w);
+        mma_s8_16832(c3, af, b3.x, b3.y);
         S[nt][0] += sa * (c1[0] * 256 + c2[0]);
         S[nt][1] += sa * (c1[1] * 256 + c2[1]);
         S[nt][2] += sbv * (c1[2] * 256 + c2[2]);
         S[nt][3] += sbv * (c1[3] * 256 + c2[3]);
+        S3[nt][0] += sa * c3[0];
+        S3[nt][1] += sa * c3[1];
+        S3[nt][2] += sbv * c3[2];
+        S3[nt][3] += sbv * c3[3];
       }
     }
 #pragma unroll
     for (int nt = 0; nt < NT; ++nt) {
       const float2 sv = *reinterpret_cast<const float2*>(xc + nt * kXcSbBytes + (grp * 8 + 2 * c) * 4);
-      u[nt][0] = fmaf(sv.x, (float)S[nt][0], u[nt][0]);
-      u[nt][1] = fmaf(sv.y, (float)S[nt][1], u[nt][1]);
-      u[nt][2] = fmaf(sv.x, (float)S[nt][2], u[nt][2]);
-      u[nt][3] = fmaf(sv.y, (float)S[nt][3], u[nt][3]);
+      u[nt][0] = fmaf(sv.x, fmaf((float)S3[nt][0], 1.0f / 256.0f, (float)S[nt][0]), u[nt][0]);
+      u[nt][1] = fmaf(sv.y, fmaf((float)S3[nt][1], 1.0f / 256.0f, (float)S[nt][1]), u[nt][1]);
+      u[nt][2] = fmaf(sv.x, fmaf((float)S3[nt][2], 1.0f / 256.0f, (float)S[nt][2]), u[nt][2]);
+      u[nt][3] = fmaf(sv.y, fmaf((float)S3[nt][3], 1.0f / 256.0f, (float)S[nt][3]), u[nt][3]);
     }
   }
   const float dA8 = dA * (1.0f / 256.0f), dB8 = dB * (1.0f / 256.0f);
+  const float mA8 = mA * 256.0f, mB8 = mB * 256.0f;  // the hi parts of the sums hold sum / 256
 #pragma unroll
   for (int nt = 0; nt < NT; ++nt) {
     const uint2 sw = lds64(xsb + nt * kXsSbBytes + (g * 8 + 2 * c) * 4);
     const uint32_t bm_hi = prmt(sw.x, sw.y, 0x5410u), bm_lo = prmt(sw.x, sw.y, 0x7632u);
-    float cm[4] = {0.f, 0.f, 0.f, 0.f};
-    mma_1688(cm, am0, am1, bm_hi);
-    mma_1688(cm, am0, am1, bm_lo);
-    acc[nt][0] = fmaf(-mA, cm[0], fmaf(dA8, u[nt][0], acc[nt][0]));
-    acc[nt][1] = fmaf(-mA, cm[1], fmaf(dA8, u[nt][1], acc[nt][1]));
-    acc[nt][2] = fmaf(-mB, cm[2], fmaf(dB8, u[nt][2], acc[nt][2]));
-    acc[nt][3] = fmaf(-mB, cm[3], fmaf(dB8, u[nt][3], acc[nt][3]));
+    float ch[4] = {0.f, 0.f, 0.f, 0.f}, cl[4] = {0.f, 0.f, 0.f, 0.f};
+    mma_1688(ch, am0, am1, bm_hi);
+    mma_1688(cl, am0, am1, bm_lo);
+    acc[nt][0] = fmaf(-mA, cl[0], fmaf(-mA8, ch[0], fmaf(dA8, u[nt][0], acc[nt][0])));
+    acc[nt][1] = fmaf(-mA, cl[1], fmaf(-mA8, ch[1], fmaf(dA8, u[nt][1], acc[nt][1])));
+    acc[nt][2] = fmaf(-mB, cl[2], fmaf(-mB8, ch[2], fmaf(dB8, u[nt][2], acc[nt][2])));
+    acc[nt][3] = fmaf(-mB, cl[3], fmaf(-mB8, ch[3], fmaf(dB8, u[nt][3], acc[nt][3])));
   }
 }
 
@@ -207,16 +217,17 @@ __device__ __forceinline__ void tile_q6k(const uint8_t* tile, const uint8_t* xb,
         af[3] = hsub2_u(lop3_and_or(word >> 12, 0x000F000Fu, 0x64006400u) | ((X >> 2) & 0x00300030u), 0x64206420u);
         const float fa = dA * (float)(int8_t)(sAs[ks >> 2] >> (8 * (ks & 3)));
         const float fb = dB * (float)(int8_t)(sBs[ks >> 2] >> (8 * (ks & 3)));
+        const float fa8 = fa * 256.0f, fb8 = fb * 256.0f;  // hi activation parts hold x / 256
 #pragma unroll
         for (int nt = 0; nt < NT; ++nt) {
           const uint4 b = lds128(xb + nt * kXfSbBytes + (ks * 32 + lane) * 16);
           float ch_[4] = {0.f, 0.f, 0.f, 0.f}, cl_[4] = {0.f, 0.f, 0.f, 0.f};
           mma_16816(ch_, af, b.x, b.y);
           mma_16816(cl_, af, b.z, b.w);
-          acc[nt][0] = fmaf(fa, ch_[0] + cl_[0], acc[nt][0]);
-          acc[nt][1] = fmaf(fa, ch_[1] + cl_[1], acc[nt][1]);
-          acc[nt][2] = fmaf(fb, ch_[2] + cl_[2], acc[nt][2]);
-          acc[nt][3] = fmaf(fb, ch_[3] + cl_[3], acc[nt][3]);
+          acc[nt][0] = fmaf(fa, cl_[0], fmaf(fa8, ch_[0], acc[nt][0]));
+          acc[nt][1] = fmaf(fa, cl_[1], fmaf(fa8, ch_[1], acc[nt][1]));
+          acc[nt][2] = fmaf(fb, cl_[2], fmaf(fb8, ch_[2], acc[nt][2]));
+          acc[nt][3] = fmaf(fb, cl_[3], fmaf(fb8, ch_[3], acc[nt][3]));
         }
       }
     }
@@ -236,6 +247,7 @@ __device__ __forceinline__ void tile_q80(const uint8_t* tile, const uint8_t* xb,
     const uint4 q = lds128(qs + ch * 512 + lane * 16);
     const float da = half_bits_to_float(dAs[ch >> 1] >> ((ch & 1) * 16));
     const float db = half_bits_to_float(dBs[ch >> 1] >> ((ch & 1) * 16));
+    const float da8 = da * 256.0f, db8 = db * 256.0f;  // hi activation parts hold x / 256
     float ct[2][NT][4];
 #pragma unroll
     for (int hl = 0; hl < 2; ++hl)
@@ -259,10 +271,10 @@ __device__ __forceinline__ void tile_q80(const uint8_t* tile, const uint8_t* xb,
     }
 #pragma unroll
     for (int nt = 0; nt < NT; ++nt) {
-      acc[nt][0] = fmaf(da, ct[0][nt][0] + ct[1][nt][0], acc[nt][0]);
-      acc[nt][1] = fmaf(da, ct[0][nt][1] + ct[1][nt][1], acc[nt][1]);
-      acc[nt][2] = fmaf(db, ct[0][nt][2] + ct[1][nt][2], acc[nt][2]);
-      acc[nt][3] = fmaf(db, ct[0][nt][3] + ct[1][nt][3], acc[nt][3]);
+      acc[nt][0] = fmaf(da, ct[1][nt][0], fmaf(da8, ct[0][nt][0], acc[nt][0]));
+      acc[nt][1] = fmaf(da, ct[1][nt][1], fmaf(da8, ct[0][nt][1], acc[nt][1]));
+      acc[nt][2] = fmaf(db, ct[1][nt][2], fmaf(db8, ct[0][nt][2], acc[nt][2]));
+      acc[nt][3] = fmaf(db, ct[1][nt][3], fmaf(db8, ct[0][nt][3], acc[nt][3]));
     }
   }
 }
@@ -279,9 +291,25 @@ __device__ __forceinline__ void kv_store(const KvView& kv, int layer, int which,
   else reinterpret_cast<float*>(kv.pool)[off] = v;
 }
 
+// RESID rows x[t][row] of this thread's accumulator elements, read through L2
+// (written by another CTA earlier in the launch); issued early by callers so
+// the load overlaps other L2 round trips.
+template <int NT>
+__device__ __forceinline__ void load_resid(const GemvArgs& a, int rg, int warp, int lane, float xv[NT][4]) {
+  const int g = lane >> 2, c = lane & 3;
+  const int row0 = rg * kRowGroup + warp * kTileRows + g;
+#pragma unroll
+  for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+    for (int r = 0; r < 4; ++r) {
+      const int t = nt * 8 + 2 * c + (r & 1), row = row0 + ((r & 2) ? 8 : 0);
+      xv[nt][r] = (t < a.m && row < a.n) ? __ldcg(a.resid + (size_t)t * a.ldr + row) : 0.f;
+    }
+}
+
 template <int NT>
 __device__ void epilogue(const GemvArgs& a, int p, int rg, int warp, int lane, float acc[NT][4],
-                         const float* inv_rms, float* red, float* T) {
+                         const float* inv_rms, float* red, float* T, const float (*xpre)[4] = nullptr) {
   constexpr int LD = 8 * NT;
   const int g = lane >> 2, c = lane & 3;
   const int tid = warp * 32 + lane;
@@ -324,16 +352,18 @@ __device__ void epilogue(const GemvArgs& a, int p, int rg, int warp, int lane, f
     frags_write(T, 1, kTLd, kRowGroup / 2, LD, rg * (kRowGroup / 2), 0, nullptr, a.xout, NT, red, tid,
                 32 * kConsumerWarps, [] { named_bar(2, 32 * kConsumerWarps); });
   } else if (a.epi == EPI_RESID) {
-    // x rows were written by another CTA earlier in this launch: read them
-    // through L2, all before the first store (one round trip)
+    // x rows were written by another CTA earlier in this launch: read through
+    // L2, all before the first store (one round trip), unless the caller
+    // already issued the loads
     float xv[NT][4];
+    if (xpre) {
 #pragma unroll
-    for (int nt = 0; nt < NT; ++nt)
+      for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
-      for (int r = 0; r < 4; ++r) {
-        const int t = nt * 8 + 2 * c + (r & 1), row = row0 + ((r & 2) ? 8 : 0);
-        xv[nt][r] = (t < a.m && row < a.n) ? __ldcg(a.resid + (size_t)t * a.ldr + row) : 0.f;
-      }
+        for (int r = 0; r < 4; ++r) xv[nt][r] = xpre[nt][r];
+    } else {
+      load_resid<NT>(a, rg, warp, lane, xv);
+    }
     float sq[NT][2];
 #pragma unroll
     for (int nt = 0; nt < NT; ++nt) {
@@ -548,11 +578,20 @@ __device__ __forceinline__ void finish_segment(const GemvArgs& a, int p, int n_p
     while (cl > 0 && U * cl / Gp > ub) --cl;
     const int ncontrib = (int)(cl - cf + 1);
     if (threadIdx.x == 0) {
-      s_last = (atom_add_acq_rel(a.counters + rg, 1) == ncontrib - 1);
+      // release: every partial store of the CTA (ordered by the barrier above)
+      // is visible before the ticket; acquire: the other contributors' are
+      // visible to the reads below when this CTA is last
+      fence_acq_rel_gpu();
+      RB_TS(p, 16);
+      s_last = (atom_add_relaxed(a.counters + rg, 1) == ncontrib - 1);
+      fence_acq_rel_gpu();
       RB_TS(p, 10);
     }
     named_bar(1, 32 * kConsumerWarps);
     if (s_last) {
+      float xv[NT][4];
+      const bool resid = a.epi == EPI_RESID;
+      if (resid) load_resid<NT>(a, rg, warp, lane, xv);
 #pragma unroll
       for (int nt = 0; nt < NT; ++nt) acc[nt][0] = acc[nt][1] = acc[nt][2] = acc[nt][3] = 0.f;
       // contributor cc deposited into slot 0 iff rg is its first row group:
@@ -562,22 +601,34 @@ __device__ __forceinline__ void finish_segment(const GemvArgs& a, int p, int n_p
         const int sl = cc == cf ? sl_cf : slot_base;
         return a.partials + ((((size_t)cc * nslots + sl) * kConsumerWarps + warp) * NT) * 128 + lane * 4;
       };
-      // summed in contributor order (deterministic)
-      for (long long cc = cf; cc <= cl; ++cc) {
-        const float* src = src_of(cc);
+      // summed in contributor order (deterministic); the loads of a batch of
+      // contributors are all in flight before the first add
+      constexpr int kB = 1;  // more batching spills registers (96 per thread at 17 warps)
+      for (long long c0 = cf; c0 <= cl; c0 += kB) {
+        float4 q[kB][NT];
 #pragma unroll
-        for (int nt = 0; nt < NT; ++nt) {
-          const float4 q = ldcg4(src + nt * 128);
-          acc[nt][0] += q.x;
-          acc[nt][1] += q.y;
-          acc[nt][2] += q.z;
-          acc[nt][3] += q.w;
-        }
+        for (int b = 0; b < kB; ++b)
+          if (c0 + b <= cl) {
+            const float* src = src_of(c0 + b);
+#pragma unroll
+            for (int nt = 0; nt < NT; ++nt) q[b][nt] = ldcg4(src + nt * 128);
+          }
+#pragma unroll
+        for (int b = 0; b < kB; ++b)
+          if (c0 + b <= cl) {
+#pragma unroll
+            for (int nt = 0; nt < NT; ++nt) {
+              acc[nt][0] += q[b][nt].x;
+              acc[nt][1] += q[b][nt].y;
+              acc[nt][2] += q[b][nt].z;
+              acc[nt][3] += q[b][nt].w;
+            }
+          }
       }
       if (stamp) RB_TS(p, 11);
       // the epilogue runs even after a timed-out wait (error already reported):
       // its named barriers must be reached by every consumer warp
-      epilogue<NT>(a, p, rg, warp, lane, acc, irms, red, T);
+      epilogue<NT>(a, p, rg, warp, lane, acc, irms, red, T, resid ? xv : nullptr);
       if (threadIdx.x == 0) a.counters[rg] = 0;
       if (stamp) RB_TS(p, 12);
     }
@@ -639,7 +690,8 @@ __device__ __forceinline__ void consume_phase(const GemvArgs& a, int p, int n_ph
       const uint8_t* tile = st + warp * TB;
       const uint8_t* xb = st + UB;
       if (DT == DT_Q4_K)
-        tile_q4k<NT>(tile, xb, xb + NT * kXiSbBytes, xb + NT * (kXiSbBytes + kXcSbBytes), lane, acc);
+        tile_q4k<NT>(tile, xb, xb + NT * kXiSbBytes, xb + NT * (kXiSbBytes + kX3SbBytes),
+                     xb + NT * (kXiSbBytes + kX3SbBytes + kXcSbBytes), lane, acc);
       else if (DT == DT_Q6_K) tile_q6k<NT>(tile, xb, lane, acc);
       else tile_q80<NT>(tile, xb, lane, acc);
     }
@@ -715,6 +767,9 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const __grid_constant
             bulk_g2s(st, reinterpret_cast<const uint8_t*>(a.xin.xi) + (size_t)sb * NT * kXiSbBytes, NT * kXiSbBytes,
                      bar);
             st += NT * kXiSbBytes;
+            bulk_g2s(st, reinterpret_cast<const uint8_t*>(a.xin.x3) + (size_t)sb * NT * kX3SbBytes, NT * kX3SbBytes,
+                     bar);
+            st += NT * kX3SbBytes;
             bulk_g2s(st, reinterpret_cast<const uint8_t*>(a.xin.xc) + (size_t)sb * NT * kXcSbBytes, NT * kXcSbBytes,
                      bar);
             st += NT * kXcSbBytes;
@@ -806,6 +861,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const __grid_constant
         // one counter per barrier slot: every CTA arrives at each slot exactly
         // once per launch, so a ticket always lies in its own launch's window
         const unsigned long long t = atom_add_release_u64(ca.gbar + (p + 1), 1ull);
+        RB_TS(p, 17);
         // (the failure-detection hook moves one barrier's target a grid beyond reach)
         s_tgt[p] = (t / gridDim.x + 1 + (ca.fail_bar == p + 1 ? 1 : 0)) * gridDim.x;
       }
@@ -1406,10 +1462,17 @@ __device__ __forceinline__ void qg_store_b(int ntn, uint32_t sB, int tid, const 
     if (e < n_items) {
       const int ksl = e / per_ks, rem = e - ksl * per_ks, nt = rem >> 5, l = rem & 31;
       const int t = nt * 8 + (l >> 2), col = 16 * ksl + 2 * (l & 3);
-      sts32(sB + qg_boff(t, col), bv[i].x);
-      sts32(sB + qg_boff(t, col + 8), bv[i].y);
-      sts32(sB + kQgBPlane + qg_boff(t, col), bv[i].z);
-      sts32(sB + kQgBPlane + qg_boff(t, col + 8), bv[i].w);
+      // the fragments hold x ~= 256 hi + lo; the GEMM's planes take x ~= hi + lo
+      uint32_t w[4] = {bv[i].x, bv[i].y, bv[i].z, bv[i].w};
+#pragma unroll
+      for (int q = 0; q < 2; ++q) {
+        const float2 h = __half22float2(u32_as_h2(w[q])), lo = __half22float2(u32_as_h2(w[q + 2]));
+        hilo2(fmaf(256.0f, h.x, lo.x), fmaf(256.0f, h.y, lo.y), w[q], w[q + 2]);
+      }
+      sts32(sB + qg_boff(t, col), w[0]);
+      sts32(sB + qg_boff(t, col + 8), w[1]);
+      sts32(sB + kQgBPlane + qg_boff(t, col), w[2]);
+      sts32(sB + kQgBPlane + qg_boff(t, col + 8), w[3]);
     }
   }
 }

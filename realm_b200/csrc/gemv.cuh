@@ -73,6 +73,7 @@ struct GemvArgs {
 // phase p wrote when bit p + 1 of bar_mask is set: a grid barrier separates
 // them). A single GEMV is a chain of one phase.
 constexpr int kMaxPhases = 6;
+constexpr int kStampSlots = 24;  // %globaltimer stamps per CTA and phase (measurement hook)
 struct ChainArgs {
   GemvArgs ph[kMaxPhases];
   int32_t n_phases = 0;

@@ -36,6 +36,7 @@ ATOL, RTOL = 2e-3, 1e-3
 
 
 def _assert_close(got, ref, what):
+    assert np.all(np.isfinite(got)) and np.all(np.isfinite(ref)), (what, "non-finite values")
     err = np.abs(np.asarray(got, np.float64) - np.asarray(ref, np.float64))
     bound = ATOL + RTOL * np.abs(np.asarray(ref, np.float64))
     bad = err > bound
@@ -213,7 +214,7 @@ def _outlier_rows(rng, m, k, n_out=4):
 @pytest.mark.parametrize("fmt", ["q4k", "q6k", "q80"])
 @pytest.mark.parametrize("m", [1, 8, 16, 64])
 def test_gemv_outlier_activations_absolute_bound(ctx, oracle, fmt, m):
-    """Rows with a few channels 100-1000x the median: the int8 two-limb (Q4_K)
+    """Rows with a few channels 100-1000x the median: the int8 three-limb (Q4_K)
     and fp16 hi/lo (Q6_K, Q8_0) activations still meet the absolute bound
     2e-3 + 1e-3 |y| against the oracle's dequant + GEMM in double."""
     O = oracle
@@ -258,4 +259,58 @@ def test_model_outlier_channels_teacher_forced(ctx, oracle):
         _assert_close(lg[-1], ref_logits[g], ("step", g))
         agree += int(am[-1] == toks[g])
     assert agree / len(toks) >= 0.99
+    m.close()
+
+
+# ---------------------------------------------------------------------------
+# Llama-2-70B geometry
+# ---------------------------------------------------------------------------
+LLAMA70B = dict(n_layers=80, hidden=8192, n_heads=64, n_kv_heads=8, head_dim=128, ffn=28672, vocab=32000,
+                max_seq=4096, rms_eps=1e-5, layer_eps=1e-5, rope_theta=10000.0)
+
+
+def test_config5_geometry_one_layer_teacher_forced(ctx, oracle):
+    """The 70B layer geometry (hidden 8192, 64 q / 8 kv heads of 128, FFN 28672 =
+    112 super-blocks, GQA 8 in the model path, fp16 KV) with 1 of its 80 layers:
+    4 tenants with prompts prefilled in 64-row steps, then 8 batched decode
+    steps teacher-forced on the oracle's greedy tokens."""
+    import realm_b200 as rb
+    O = oracle
+    cfg = dict(LLAMA70B, n_layers=1, max_seq=512)
+    W = synth.make_weights(cfg, seed=5)
+    rng = np.random.default_rng(5)
+    lens = rng.integers(60, 200, 4)
+    prompts = [rng.integers(0, cfg["vocab"], int(n)).astype(np.uint32) for n in lens]
+    n_dec = 8
+    ref_tok, ref_lg = [], []
+    for p in prompts:
+        om = O.Model(dict(cfg, kv_fp16=1), W)
+        for cs in range(0, len(p), 64):
+            lg = om.forward(p[cs:cs + 64], cs)
+        toks, lgs = [O.argmax(lg)], [lg.copy()]
+        pos = len(p)
+        for _ in range(n_dec - 1):
+            lg = om.forward([toks[-1]], pos)
+            pos += 1
+            toks.append(O.argmax(lg))
+            lgs.append(lg.copy())
+        ref_tok.append(toks)
+        ref_lg.append(np.stack(lgs))
+        del om
+    m = rb.Model(ctx, dict(cfg, kv_dtype=rb.F16, max_tenants=4))
+    m.set_weights(W)
+    del W
+    for t, p in enumerate(prompts):
+        m.tenant_create(t)
+        for cs in range(0, len(p), 64):
+            lg, am = m.forward_rows([t] * len(p[cs:cs + 64]), p[cs:cs + 64])
+        _assert_close(lg[-1], ref_lg[t][0], ("prompt", t))
+    agree, total = 0, 0
+    for g in range(1, n_dec):
+        lg, am = m.forward_rows(list(range(4)), [ref_tok[t][g - 1] for t in range(4)])
+        for t in range(4):
+            _assert_close(lg[t], ref_lg[t][g], ("decode", g, t))
+            agree += int(am[t] == ref_tok[t][g])
+            total += 1
+    assert agree / total >= 0.99, (agree, total)
     m.close()

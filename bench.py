@@ -267,7 +267,7 @@ def gemv_sweep(rb, torch, ctx, dev, hbm_peak, peak_kind):
             alg = wbytes + 4 * m * k + 4 * m * n
             gbps = alg / (us * 1e-6) / 1e9
             out.append({"n": n, "k": k, "fmt": fmt, "m": m, "us": round(us, 2), "GBps": round(gbps, 1),
-                        "frac": round(gbps / hbm_peak, 4), "path": "tcgen05" if ctx.uses_tcgen05(m) else "mma.sync"})
+                        "frac": round(gbps / hbm_peak, 4), "path": "tcgen05" if (fmt == "q4k" and ctx.uses_tcgen05(m)) else "mma.sync"})
         for w in ws:
             w.free()
         del blk
@@ -589,13 +589,14 @@ def run_case(args):
         torch.cuda.synchronize(dev)
         print("qgemm case done", flush=True)
         return
-    m = build_model(rb, torch, ctx, dev, TENANTS_PER_GPU)
+    base = dict(CFG, n_layers=args.layers) if args.layers else CFG
+    m = build_model(rb, torch, ctx, dev, TENANTS_PER_GPU, base=base)
     rng = np.random.default_rng(4)
     lens = rng.integers(128, 513, TENANTS_PER_GPU)
     kvw = CFG["n_kv_heads"] * CFG["head_dim"]
     for t in range(TENANTS_PER_GPU):  # caches filled directly (K/V ~ N(0,1)) instead of a prefill
         m.tenant_create(t)
-        for l in range(CFG["n_layers"]):
+        for l in range(base["n_layers"]):
             m.kv.append(t, l, torch.randn(int(lens[t]), kvw, device=dev), torch.randn(int(lens[t]), kvw, device=dev))
     tenants = np.arange(TENANTS_PER_GPU, dtype=np.uint32)
     tok = tenants.copy()
@@ -807,6 +808,8 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU-baseline leg")
+    ap.add_argument("--layers", type=int, default=0,
+                    help="decode case only: build the 7B model with this many layers (small ncu captures)")
     ap.add_argument("--case", choices=["gemv", "decode", "attn", "serve", "serve_sampled", "load", "sample", "qgemm",
                              "llama70b"],
                     help="profiling case for ncu: run a small workload of one kernel family and exit")

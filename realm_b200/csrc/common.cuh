@@ -206,6 +206,9 @@ __device__ __forceinline__ __half2 u32_as_h2(uint32_t u) { return *reinterpret_c
 __device__ __forceinline__ uint32_t hfma2_u(uint32_t a, uint32_t b, uint32_t c) {
   return h2_as_u32(__hfma2(u32_as_h2(a), u32_as_h2(b), u32_as_h2(c)));
 }
+__device__ __forceinline__ uint32_t h2_u32_mul(uint32_t a, uint32_t b) {
+  return h2_as_u32(__hmul2(u32_as_h2(a), u32_as_h2(b)));
+}
 __device__ __forceinline__ uint32_t hsub2_u(uint32_t a, uint32_t b) {
   return h2_as_u32(__hsub2(u32_as_h2(a), u32_as_h2(b)));
 }

@@ -299,13 +299,17 @@ struct Ctx {
   bool chains = true;  // RB_NO_CHAIN=1 launches every GEMV on its own
   DevBuf gbar;         // grid-barrier arrival counters (one per barrier slot) of multi-phase launches
   int last_chain_phases = 1;
-  bool qgemm = false;  // RB_QGEMM=1 sends batches of 16+ rows to the tcgen05 GEMM (measured slower than the GEMV)
+  // tcgen05 GEMM routing (RB_QGEMM): 0 never; 1 every format from 16 rows (test
+  // and measurement mode); 2 (default) Q4_K from 33 rows, where the
+  // exact-weight GEMM beats the mma.sync GEMV on B200 (16-32 rows stay on the GEMV)
+  int qgemm = 2;
   bool gemm_step = false;  // the step being enqueued runs its projections on the tcgen05 GEMM
   int chain_prefetch = -1;  // RB_CHAIN_PREFETCH: next-phase weight units issued ahead of a grid barrier
   int attn_group = 1;       // RB_ATTN_GROUP=0: one attention pair per row (no K/V sharing in prefill chunks)
   bool step_grouped = false;  // the step has consecutive rows of one tenant (a prompt chunk)
   int attn_whole = 1;         // RB_ATTN_WHOLE=0: always split attention pages evenly over the CTAs
   DevBuf qg_part;      // tcgen05 GEMM partial sums
+  DevBuf qg_bprep;     // tcgen05 exact-weight GEMM: activation planes
   // failure-detection test hook (rb_test_fail_next_grid_barrier): when nonzero,
   // the next multi-phase GEMV launch with a grid barrier gets its first
   // barrier's target out of reach and this poll limit for every barrier wait
@@ -327,6 +331,12 @@ void prof_mark(Ctx* c, int kind) {
 
 // With RB_QGEMM=1, batches of at least this many rows take the tcgen05 dequant-GEMM.
 constexpr int kQgemmMinRows = 16;
+constexpr int kQgemmAutoMinRows = 33;
+// whether a batch of m rows runs its matmuls on the tcgen05 GEMM (Q4_K in the default mode)
+bool gemm_rows(const Ctx* c, int m) {
+  return (c->qgemm == 1 && m >= kQgemmMinRows) || (c->qgemm == 2 && m >= kQgemmAutoMinRows);
+}
+bool gemm_for(const Ctx* c, int m, int dtype) { return gemm_rows(c, m) && (c->qgemm == 1 || dtype == DT_Q4_K); }
 
 constexpr int kMaxRowsAbi = 64;
 constexpr int kCounters = 1 << 16;
@@ -456,6 +466,11 @@ int ensure_qg_part(Ctx* c, int n_rg, int nsb) {
     if (c->qg_part.p) RB_CUDA(cudaStreamSynchronize(c->stream));  // earlier launches may still read it
     RB_CUDA(c->qg_part.alloc(need));
   }
+  const size_t bneed = qgemm_bprep_bytes(nsb);
+  if (c->qg_bprep.n < bneed) {
+    if (c->qg_bprep.p) RB_CUDA(cudaStreamSynchronize(c->stream));
+    RB_CUDA(c->qg_bprep.alloc(bneed));
+  }
   return RB_OK;
 }
 
@@ -463,10 +478,11 @@ int ensure_qg_part(Ctx* c, int n_rg, int nsb) {
 // the GEMM, then the partial sums and the fused epilogue (two launches).
 int launch_qgemm(Ctx* c, const GemvArgs& a, int* launches) {
   const QgemmPlan p = qgemm_plan(c->num_sms, a.n_rg, a.nsb);
-  if (c->qg_part.n < qgemm_part_floats(p) * 4) return fail(RB_ERR_INVALID, "GEMM scratch not sized for this weight");
-  RB_CUDA(qgemm_launch(a, c->qg_part.as<float>(), p, c->stream, c->pdl ? 1 : 0));
+  if (c->qg_part.n < qgemm_part_floats(p) * 4 || c->qg_bprep.n < qgemm_bprep_bytes(a.nsb))
+    return fail(RB_ERR_INVALID, "GEMM scratch not sized for this weight");
+  RB_CUDA(qgemm_launch(a, c->qg_part.as<float>(), c->qg_bprep.as<uint8_t>(), p, c->stream, c->pdl ? 1 : 0));
   prof_mark(c, PROF_QGEMM);
-  if (launches) *launches += 2;
+  if (launches) *launches += a.dtype == DT_Q4_K ? 3 : 2;
   return RB_OK;
 }
 
@@ -573,7 +589,7 @@ int chain_flush(Ctx* c, int* launches) {
 }
 
 int chain_add(Ctx* c, GemvArgs a, bool reads_previous, int* launches) {
-  if (c->gemm_step) {  // 16+ rows: every phase is its own tcgen05 GEMM + epilogue
+  if (c->gemm_step && a.dtype == DT_Q4_K) {  // 16+ rows: Q4_K phases run the tcgen05 GEMM + epilogue
     if (int rc = chain_flush(c, launches)) return rc;
     return launch_qgemm(c, a, launches);
   }
@@ -724,7 +740,7 @@ constexpr int kDescTenant = 2, kDescPos = 2 + 64, kDescTok = 2 + 128, kDescUpd =
 
 int enqueue_step(Ctx* c, Model& M, int m, int* launches) {
   const rb_model_config& cf = M.cfg;
-  c->gemm_step = c->qgemm && m >= kQgemmMinRows;
+  c->gemm_step = gemm_rows(c, m);
   KvPool& P = *c->pools[M.pool];
   int32_t* desc = M.desc.as<int32_t>();
   embed_kernel<<<dim3(m, (cf.hidden + 255) / 256), 128, 0, c->stream>>>(
@@ -903,7 +919,7 @@ int ensure_qg_model(Ctx* c, Model& M) {
 int run_forward(rb_ctx* c, Model& M, int m, bool use_graph) {
   int launches = 0;
   if (c->test_fail_spin) use_graph = false;  // the armed hook must not be baked into a cached graph
-  if (c->qgemm && m >= kQgemmMinRows)
+  if (gemm_rows(c, m))
     if (int rc = ensure_qg_model(c, M)) return rc;
   RB_CUDA(cudaEventRecord(c->ev0, c->stream));
   if (use_graph) {
@@ -973,7 +989,7 @@ int32_t rb_ctx_create(const rb_config* cfg, rb_ctx** out) {
     RB_CUDA(cudaMemset(c->attn_ts.p, 0, (size_t)attn_grid(c->num_sms) * 8 * 8));
   }
   if (const char* d = getenv("RB_NO_CHAIN")) c->chains = atoi(d) == 0;
-  if (const char* d = getenv("RB_QGEMM")) c->qgemm = atoi(d) != 0;
+  if (const char* d = getenv("RB_QGEMM")) c->qgemm = atoi(d);
   if (const char* d = getenv("RB_CHAIN_PREFETCH")) c->chain_prefetch = atoi(d);
   if (const char* d = getenv("RB_ATTN_GROUP")) c->attn_group = atoi(d) != 0;
   if (const char* d = getenv("RB_ATTN_WHOLE")) c->attn_whole = atoi(d) != 0;
@@ -1129,7 +1145,7 @@ static int weight_matmul_dev(rb_ctx* c, const Weight& w, const float* din, float
     a.epi = EPI_STORE;
     a.y = dout + (size_t)b0 * w.n;
     a.ldy = w.n;
-    if (c->qgemm && m >= kQgemmMinRows) {
+    if (gemm_for(c, m, w.dtype)) {
       if (int rc = ensure_qg_part(c, w.n_rg, w.k / kSuperK)) return rc;
       if (int rc = launch_qgemm(c, a, nullptr)) return rc;
     } else if (int rc = launch_gemv(c, a, nullptr)) {
@@ -1191,7 +1207,7 @@ int32_t rb_weight_matmul_timing(rb_ctx* c, const int32_t* handles, uint32_t n_ha
     a.epi = EPI_STORE;
     a.y = y.as<float>();
     a.ldy = w.n;
-    rc = (c->qgemm && m >= kQgemmMinRows) ? launch_qgemm(c, a, nullptr) : launch_gemv(c, a, nullptr);
+    rc = gemm_for(c, m, w.dtype) ? launch_qgemm(c, a, nullptr) : launch_gemv(c, a, nullptr);
   }
   cudaError_t e = cudaStreamEndCapture(c->stream, &g);
   if (rc) {
@@ -1219,7 +1235,7 @@ int32_t rb_weight_matmul_timing(rb_ctx* c, const int32_t* handles, uint32_t n_ha
 
 int32_t rb_weight_matmul_path(rb_ctx* c, uint32_t batch) {
   if (!c) return fail(RB_ERR_BAD_HANDLE, "null context");
-  return (c->qgemm && (int)batch >= kQgemmMinRows) ? 1 : 0;
+  return gemm_for(c, (int)batch, DT_Q4_K) ? 1 : 0;
 }
 
 int32_t rb_weight_export(rb_ctx* c, int32_t h, void* out_blocks, size_t nbytes, uint32_t flags) {
@@ -1855,7 +1871,7 @@ int32_t rb_forward_layer(rb_ctx* c, int32_t model, uint32_t t, uint32_t layer, c
   RB_CUDA(xfrag_launch(M->x.as<float>(), H, M->layers[layer].raw[0].d.as<float>(), (int)S, H, gemv_nt_for((int)S),
                        M->fa.view(), M->ss.as<float>(), kMaxRowsAbi, c->stream));
   int launches = 2;
-  c->gemm_step = c->qgemm && S >= (uint32_t)kQgemmMinRows;
+  c->gemm_step = gemm_rows(c, (int)S);
   c->step_grouped = S > 1;  // one tenant at consecutive positions
   if (c->gemm_step)
     if (int rc = ensure_qg_model(c, *M)) return rc;

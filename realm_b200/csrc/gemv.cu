@@ -1308,6 +1308,8 @@ struct QgemmArgs {
   const uint8_t* w = nullptr;
   int32_t dtype = 0, n_rg = 0, nsb = 0, m = 0, nt_x = 0;
   const uint4* xf = nullptr;  // fp16 hi/lo fragments, n-tile stride nt_x
+  const uint32_t* xs = nullptr;  // sub-block sums (Q4_K min term of the exact-weight GEMM)
+  const uint8_t* bprep = nullptr;  // exact-weight GEMM: prepared activation planes (q2_bprep_kernel)
   const int8_t* rexp = nullptr;
   float* part = nullptr;      // [n_rt][slots][64 tokens][128 rows]
   int32_t slots = 0;
@@ -1755,7 +1757,8 @@ __global__ void __launch_bounds__(kConsumerWarps * 32) qgemm_epi_kernel(const __
       }
   }
   const int row0 = rg * kRowGroup + warp * kTileRows + g;
-  const float sA = pow2f(-(int)q.rexp[row0]), sB = pow2f(-(int)q.rexp[row0 + 8]);
+  // the per-row 2^e of the hi/lo-weight GEMM (none for the exact-weight GEMM)
+  const float sA = q.rexp ? pow2f(-(int)q.rexp[row0]) : 1.f, sB = q.rexp ? pow2f(-(int)q.rexp[row0 + 8]) : 1.f;
 #pragma unroll
   for (int nt = 0; nt < NT; ++nt) {
     acc[nt][0] *= sA;
@@ -1797,6 +1800,443 @@ __global__ void rowexp_kernel(const uint8_t* w, int dtype, int n_rg, int nsb, in
     e = min(max(14 - x, -100), 100);
   }
   out[row] = (int8_t)e;
+}
+
+// ===========================================================================
+// Exact-weight tcgen05 GEMM for Q4_K, 16..64 rows (prefill chunks, large
+// scheduler steps).
+//
+// y = sum_sb d_sb * (sum_k sc_j q_k x_k) - dmin_sb * (sum_j m_j xsum_j) per row.
+// The products sc_j * q_k are integers below 2^10, exact in fp16, so the A
+// operand needs no hi/lo split: eight producer warps turn the 4-bit quants of
+// a 128-row x 64-column slice into sc * q with two bit operations and one
+// half2 fused multiply-add per pair. The activations come as fp16 hi/lo
+// (x ~= 256 hi + lo, xfrag.cuh) stacked along N: N = 2 Np (hi rows, then lo
+// rows), so one MMA per 16-column step accumulates both. The min term is a
+// second MMA per slice with K = 16 (two live columns: the slice's two
+// sub-blocks' mins times their activation sums). Each (128-row tile,
+// super-block) run accumulates in its own TMEM pair (D, Dm; two pairs
+// alternate) and four drain warps fold it into per-row registers with the
+// super-block's d and dmin: y += d (256 D_hi + D_lo) - dmin (256 Dm_hi + Dm_lo).
+// Work split, partial slots and the epilogue kernel are those of the hi/lo GEMM.
+// Every mbarrier wait is bounded.
+// ===========================================================================
+constexpr int kQ2MaxStages = 6;
+constexpr int kQ2SmemUse = 216 * 1024;
+constexpr int kQ2Drain = 4;                     // warps 0-3: TMEM lanes 0-127
+constexpr int kQ2Prod = 8;                      // warps 4-11: one 16-row tile each
+constexpr int kQ2LoadWarp = kQ2Drain + kQ2Prod;  // 12: weight ring
+constexpr int kQ2MmaWarp = kQ2LoadWarp + 1;      // 13
+constexpr int kQ2BWarp = kQ2MmaWarp + 1;         // 14: activation planes
+constexpr int kQ2Threads = 32 * (kQ2BWarp + 1);
+constexpr int kQ2APlane = kQgRows * kQgKc * 2;   // 16 KB: 128 rows x 64 k fp16
+constexpr int kQ2BPlane = 128 * kQgKc * 2;       // 16 KB: up to 128 N rows (hi, lo) x 64 k
+constexpr int kQ2MPlane = 128 * 16 * 2;          // 4 KB: 128 rows x 16 k (min-term operands)
+// stage: A plane | A min plane | B plane (N2 rows) | B min plane (N2 rows)
+__host__ __device__ constexpr int q2_stage_bytes(int n2) { return kQ2APlane + kQ2MPlane + n2 * 64 * 2 + n2 * 16 * 2; }
+constexpr int kQ2QStages = 3;  // weight ring: 18 KB per (128-row tile, super-block) run
+__host__ __device__ constexpr int q2_stages(int n2) {
+  return (kQ2SmemUse - kQ2QStages * 8 * 2304) / q2_stage_bytes(n2) > kQ2MaxStages
+             ? kQ2MaxStages
+             : (kQ2SmemUse - kQ2QStages * 8 * 2304) / q2_stage_bytes(n2);
+}
+constexpr int kQ2Lbo = 128 * 16;                 // bytes between 8-column chunks (all planes: 128 rows)
+constexpr int kQ2Smem = kQ2SmemUse + 1024;
+
+__device__ __forceinline__ uint32_t q2_off(int row, int col) {
+  return (uint32_t)((col >> 3) * kQ2Lbo + (row >> 3) * 128 + (row & 7) * 16 + (col & 7) * 2);
+}
+// activation planes hold N2 = 2 Np rows: 8-column chunks N2 * 16 bytes apart
+__host__ __device__ __forceinline__ uint32_t q2b_off(int n2, int row, int col) {
+  return (uint32_t)((col >> 3) * n2 * 16 + (row >> 3) * 128 + (row & 7) * 16 + (col & 7) * 2);
+}
+// per 64-column slice, in global memory: the B plane (N2 x 64 fp16) then the
+// min-term plane (N2 x 16 fp16), laid out as they sit in shared memory
+__host__ __device__ constexpr int q2_bslice_bytes(int n2) { return n2 * 64 * 2 + n2 * 16 * 2; }
+// half2 {v, v} of a small non-negative integer v (< 1024), exactly
+__device__ __forceinline__ uint32_t h2_int(uint32_t v) {
+  const uint32_t b = 0x6400u | v;  // fp16 1024 + v
+  return hsub2_u(b | (b << 16), 0x64006400u);
+}
+// issues one 32-lane x 8-column load; tcgen05.wait::ld makes the registers valid
+__device__ __forceinline__ void tmem_ld8_async(uint32_t taddr, uint32_t r[8]) {
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0, %1, %2, %3, %4, %5, %6, %7}, [%8];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7])
+               : "r"(taddr)
+               : "memory");
+}
+__device__ __forceinline__ void tmem_ld8(uint32_t taddr, float v[8]) {
+  uint32_t r[8];
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0, %1, %2, %3, %4, %5, %6, %7}, [%8];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7])
+               : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+  for (int i = 0; i < 8; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+// One 64-column slice (sub-blocks 2 grp, 2 grp + 1) of this warp's 16-row
+// tile: A = sc * q at rows tw*16 + g, + 8; the mins of both sub-blocks into
+// columns 0, 1 of the min plane; d, dmin into dd when `first` (run start).
+__device__ __forceinline__ void q2_produce_a(const uint8_t* tile, int tw, int grp, int lane, uint32_t sA, uint32_t sAm,
+                                             float2* dd, bool first) {
+  const int g = lane >> 2, c = lane & 3;
+  const uint4 hA = lds128(tile + g * 16);
+  const uint4 hB = lds128(tile + (g + 8) * 16);
+  const uint32_t scA_lo = hA.y & 0x3F3F3F3Fu, scA_hi = (hA.w & 0x0F0F0F0Fu) | ((hA.y >> 2) & 0x30303030u);
+  const uint32_t mnA_lo = hA.z & 0x3F3F3F3Fu, mnA_hi = ((hA.w >> 4) & 0x0F0F0F0Fu) | ((hA.z >> 2) & 0x30303030u);
+  const uint32_t scB_lo = hB.y & 0x3F3F3F3Fu, scB_hi = (hB.w & 0x0F0F0F0Fu) | ((hB.y >> 2) & 0x30303030u);
+  const uint32_t mnB_lo = hB.z & 0x3F3F3F3Fu, mnB_hi = ((hB.w >> 4) & 0x0F0F0F0Fu) | ((hB.z >> 2) & 0x30303030u);
+  const int rA = tw * 16 + g, rB = rA + 8;
+  const uint4 q = lds128(tile + 256 + grp * 512 + lane * 16);
+  const uint32_t wd[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+  for (int h = 0; h < 2; ++h) {
+    const int j = 2 * grp + h;
+    const uint32_t sa = ((j < 4 ? scA_lo : scA_hi) >> (8 * (j & 3))) & 0xffu;
+    const uint32_t sb = ((j < 4 ? scB_lo : scB_hi) >> (8 * (j & 3))) & 0xffu;
+    const uint32_t ka = h2_int(sa), kb = h2_int(sb);
+    const uint32_t na = h2_int(sa << 4) ^ 0x80008000u;     // -16 sc (x 64 below)
+    const uint32_t nb = h2_int(sb << 4) ^ 0x80008000u;
+    const uint32_t oa = h2_u32_mul(na, 0x54005400u);        // -16 sc * 64 = -1024 sc
+    const uint32_t ob = h2_u32_mul(nb, 0x54005400u);
+#pragma unroll
+    for (int half = 0; half < 2; ++half) {
+      const uint32_t w = wd[2 * h + half];
+      const int col = 32 * h + 16 * half + 4 * c;
+      const uint32_t w01 = prmt(w, 0u, 0x4140u), w23 = prmt(w, 0u, 0x4342u);
+      const uint32_t s01 = w01 >> 4, s23 = w23 >> 4;
+      // low nibbles: row g; high nibbles: row g + 8; (1024 + q) sc - 1024 sc = sc q
+      const uint32_t a01 = hfma2_u(lop3_and_or(w01, 0x000F000Fu, 0x64006400u), ka, oa);
+      const uint32_t a23 = hfma2_u(lop3_and_or(w23, 0x000F000Fu, 0x64006400u), ka, oa);
+      const uint32_t b01 = hfma2_u(lop3_and_or(s01, 0x000F000Fu, 0x64006400u), kb, ob);
+      const uint32_t b23 = hfma2_u(lop3_and_or(s23, 0x000F000Fu, 0x64006400u), kb, ob);
+      sts64(sA + q2_off(rA, col), a01, a23);
+      sts64(sA + q2_off(rB, col), b01, b23);
+    }
+  }
+  if (c == 0) {
+    // min plane: column 0 = m_{2 grp}, column 1 = m_{2 grp + 1} (the rest stays zero)
+    const int j0 = 2 * grp, j1 = j0 + 1;
+    const uint32_t ma0 = ((j0 < 4 ? mnA_lo : mnA_hi) >> (8 * (j0 & 3))) & 0xffu;
+    const uint32_t ma1 = ((j1 < 4 ? mnA_lo : mnA_hi) >> (8 * (j1 & 3))) & 0xffu;
+    const uint32_t mb0 = ((j0 < 4 ? mnB_lo : mnB_hi) >> (8 * (j0 & 3))) & 0xffu;
+    const uint32_t mb1 = ((j1 < 4 ? mnB_lo : mnB_hi) >> (8 * (j1 & 3))) & 0xffu;
+    sts32(sAm + q2_off(rA, 0), prmt(h2_int(ma0), h2_int(ma1), 0x5410u));
+    sts32(sAm + q2_off(rB, 0), prmt(h2_int(mb0), h2_int(mb1), 0x5410u));
+    if (first) {
+      dd[rA] = make_float2(guard_scale(half_bits_to_float(hA.x), 0.00000006f),
+                           guard_scale(half_bits_to_float(hA.x >> 16), 0.00000024f));
+      dd[rB] = make_float2(guard_scale(half_bits_to_float(hB.x), 0.00000006f),
+                           guard_scale(half_bits_to_float(hB.x >> 16), 0.00000024f));
+    }
+  }
+}
+
+// The activation planes of every 64-column slice, written once per GEMM from
+// the fp16 hi/lo fragments: B rows [0, Np) the hi parts of tokens 0..Np-1,
+// rows [Np, 2 Np) the lo parts (tokens >= m zero); the min-term plane holds the
+// sums of the slice's two sub-blocks in columns 0, 1 (hi, lo rows likewise)
+// and zeros in columns 2..15. One CTA per slice.
+template <int NT>
+__global__ void __launch_bounds__(256) q2_bprep_kernel(const uint4* xf, const uint32_t* xs, int m, int nt_x,
+                                                       uint8_t* out) {
+  constexpr int Np = 8 * NT, N2 = 2 * Np;
+  const int kg = blockIdx.x, sb = kg >> 2, ks0 = (kg & 3) * 4;
+  uint8_t* B = out + (size_t)kg * q2_bslice_bytes(N2);
+  uint8_t* Bm = B + N2 * 64 * 2;
+  pdl_wait();
+  pdl_launch_dependents();
+  for (int e = threadIdx.x; e < 4 * NT * 32; e += blockDim.x) {
+    const int ksl = e / (NT * 32), rem = e % (NT * 32), nt = rem >> 5, l = rem & 31;
+    const int t = nt * 8 + (l >> 2), col = 16 * ksl + 2 * (l & 3);
+    uint4 v = make_uint4(0u, 0u, 0u, 0u);
+    if (t < m) v = __ldg(xf + (((size_t)sb * nt_x + nt) * 16 + ks0 + ksl) * 32 + l);
+    *reinterpret_cast<uint32_t*>(B + q2b_off(N2, t, col)) = v.x;
+    *reinterpret_cast<uint32_t*>(B + q2b_off(N2, t, col + 8)) = v.y;
+    *reinterpret_cast<uint32_t*>(B + q2b_off(N2, Np + t, col)) = v.z;
+    *reinterpret_cast<uint32_t*>(B + q2b_off(N2, Np + t, col + 8)) = v.w;
+  }
+  for (int e = threadIdx.x; e < N2 * 8; e += blockDim.x) {  // (row, pair of columns)
+    const int row = e >> 3, cp = (e & 7) * 2;
+    uint32_t w = 0u;
+    if (cp == 0) {
+      const int t = row < Np ? row : row - Np;
+      if (t < m) {
+        const uint32_t* src = xs + (((size_t)sb * nt_x + (t >> 3)) * 8 + (t & 7)) * 8 + 2 * (kg & 3);
+        const uint32_t s0 = __ldg(src), s1 = __ldg(src + 1);
+        w = row < Np ? prmt(s0, s1, 0x5410u) : prmt(s0, s1, 0x7632u);
+      }
+    }
+    *reinterpret_cast<uint32_t*>(Bm + q2b_off(N2, row, cp)) = w;
+  }
+}
+
+template <int NT>
+__global__ void __launch_bounds__(kQ2Threads, 1) qgemm2_kernel(const __grid_constant__ QgemmArgs a) {
+  constexpr int Np = 8 * NT, N2 = 2 * Np;
+  constexpr int TB = tile_bytes(DT_Q4_K), HU = 8 * TB;
+  constexpr int QS = kQ2QStages;
+  constexpr int kQ2Stages = q2_stages(N2), kQ2Stage = q2_stage_bytes(N2);
+  constexpr int kOffAm = kQ2APlane, kOffB = kQ2APlane + kQ2MPlane, kOffBm = kOffB + N2 * 64 * 2;
+  constexpr uint32_t kCols = 8 * Np <= 32 ? 32 : (8 * Np <= 64 ? 64 : (8 * Np <= 128 ? 128 : (8 * Np <= 256 ? 256 : 512)));
+  static_assert(QS >= 2, "weight ring");
+  extern __shared__ __align__(1024) uint8_t q2_smem_raw[];
+  __shared__ uint64_t sfull[kQ2MaxStages], sfree[kQ2MaxStages];
+  __shared__ uint64_t qfull[kQ2QStages], qempty[kQ2QStages];
+  __shared__ uint64_t accfull[2], accempty[2], ddfull[2], bfull[kQ2MaxStages];
+  __shared__ float2 dd[2][kQgRows];
+  __shared__ uint32_t tmem_slot;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(q2_smem_raw) + 1023) & ~(uintptr_t)1023);
+  const uint32_t sbase = smem_u32(smem);
+  uint8_t* qring = smem + kQ2Stages * kQ2Stage;
+  const int n_rt = 2 * a.n_rg, kG = 4 * a.nsb;
+  const long long U = (long long)n_rt * kG;
+  const int G = gridDim.x, cta = blockIdx.x;
+  const long long u0 = U * cta / G, u1 = U * (cta + 1) / G;
+  if (warp == 0) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&tmem_slot)),
+                 "r"(kCols)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  // the A min plane's unused columns 2..15 stay zero for the whole launch
+  for (int i = tid; i < kQ2Stages * kQ2MPlane / 16; i += blockDim.x) {
+    const int st = i / (kQ2MPlane / 16), r = i % (kQ2MPlane / 16);
+    *reinterpret_cast<uint4*>(smem + st * kQ2Stage + kOffAm + r * 16) = make_uint4(0u, 0u, 0u, 0u);
+  }
+  if (tid == 0) {
+    for (int i = 0; i < kQ2Stages; ++i) {
+      mbar_init(&sfull[i], kQ2Prod);
+      mbar_init(&sfree[i], 1);
+      mbar_init(&bfull[i], 1);
+    }
+    for (int i = 0; i < QS; ++i) {
+      mbar_init(&qfull[i], 1);
+      mbar_init(&qempty[i], kQ2Prod);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&accfull[i], 1);
+      mbar_init(&accempty[i], kQ2Drain);
+      mbar_init(&ddfull[i], kQ2Prod);
+    }
+    fence_barrier_init();
+  }
+  fence_async_smem();
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = tmem_slot;
+  // a run: a maximal stretch of slices inside one (128-row tile, super-block)
+  auto run_end = [&](long long u) { return min(u1, (u / 4 + 1) * 4); };
+
+  if (warp == kQ2LoadWarp) {
+    // ---- loader: the eight 16-row tiles of each (tile, super-block) run ----
+    if (lane == 0) {
+      long long iq = 0;
+      bool ok = true;
+      for (long long u = u0; ok && u < u1; u = run_end(u)) {
+        const int rt = (int)(u / kG), sb = (int)((u - (long long)rt * kG) >> 2);
+        const int rg = rt >> 1, half = rt & 1;
+        const int q = (int)(iq % QS);
+        if (iq >= QS && !mbar_wait(&qempty[q], (uint32_t)((iq / QS - 1) & 1), a.err, DEV_TIMEOUT_SMEM)) {
+          ok = false;
+          break;
+        }
+        mbar_arrive_expect_tx(&qfull[q], HU);
+        bulk_g2s(qring + (size_t)q * HU, a.w + ((size_t)rg * a.nsb + sb) * unit_bytes(DT_Q4_K) + (size_t)half * 8 * TB,
+                 HU, &qfull[q]);
+        ++iq;
+      }
+      for (long long j = iq > QS ? iq - QS : 0; j < iq; ++j)
+        mbar_wait(&qfull[j % QS], (uint32_t)((j / QS) & 1), nullptr, 0);
+    }
+    __syncwarp();
+  } else if (warp == kQ2BWarp) {
+    // ---- activation planes of every slice, copied from the prepared buffer ----
+    if (lane == 0) {
+      pdl_wait();
+      constexpr uint32_t BB = N2 * 64 * 2, BM = N2 * 16 * 2;
+      long long it = 0;
+      for (long long u = u0; u < u1; ++u, ++it) {
+        const int s = (int)(it % kQ2Stages);
+        if (it >= kQ2Stages && !mbar_wait(&sfree[s], (uint32_t)((it / kQ2Stages - 1) & 1), a.err, DEV_TIMEOUT_EMPTY))
+          break;
+        // the planes sit back to back in the prepared buffer and in the stage
+        const uint8_t* src = a.bprep + (size_t)(u % kG) * q2_bslice_bytes(N2);
+        mbar_arrive_expect_tx(&bfull[s], BB + BM);
+        bulk_g2s(smem + s * kQ2Stage + kOffB, src, BB + BM, &bfull[s]);
+      }
+      for (long long j = it > kQ2Stages ? it - kQ2Stages : 0; j < it; ++j)
+        mbar_wait(&bfull[j % kQ2Stages], (uint32_t)((j / kQ2Stages) & 1), nullptr, 0);
+    }
+    __syncwarp();
+  } else if (warp == kQ2MmaWarp) {
+    // ---- MMA issuer ----
+    if (lane == 0) {
+      const uint32_t idesc = umma_idesc_f16(kQgRows, N2);
+      long long it = 0, gi = 0;
+      bool ok = true;
+      for (long long u = u0; ok && u < u1; ++gi) {
+        const long long ue = run_end(u);
+        const int b = (int)(gi & 1);
+        if (gi >= 2 && !mbar_wait(&accempty[b], (uint32_t)((gi / 2 - 1) & 1), a.err, DEV_TIMEOUT_DRAIN)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t dmain = tmem + (uint32_t)(b * 2 * N2), dmin = dmain + (uint32_t)N2;
+        for (bool first = true; u < ue; ++u, ++it, first = false) {
+          const int s = (int)(it % kQ2Stages);
+          if (!mbar_wait(&sfull[s], (uint32_t)((it / kQ2Stages) & 1), a.err, DEV_TIMEOUT_FULL) ||
+              !mbar_wait(&bfull[s], (uint32_t)((it / kQ2Stages) & 1), a.err, DEV_TIMEOUT_FULL)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t st = sbase + s * kQ2Stage;
+          if (!(a.dbg & 2)) {
+            constexpr uint32_t kBLbo = N2 * 16;
+#pragma unroll
+            for (int ks = 0; ks < kQgKc / 16; ++ks)
+              umma_f16(dmain, umma_desc(st + ks * 2 * kQ2Lbo, kQ2Lbo, 128),
+                       umma_desc(st + kOffB + ks * 2 * kBLbo, kBLbo, 128), idesc, (first && ks == 0) ? 0u : 1u);
+            umma_f16(dmin, umma_desc(st + kOffAm, kQ2Lbo, 128), umma_desc(st + kOffBm, kBLbo, 128), idesc,
+                     first ? 0u : 1u);
+          }
+          umma_commit(&sfree[s]);
+        }
+        if (!ok) break;
+        umma_commit(&accfull[b]);
+      }
+      if (it > 0) {
+        const long long last = it - 1;
+        mbar_wait(&sfree[last % kQ2Stages], (uint32_t)((last / kQ2Stages) & 1), nullptr, 0);
+      }
+    }
+    __syncwarp();
+  } else if (warp >= kQ2Drain) {
+    // ---- producers (warps 4-11): A = sc * q, min plane, d / dmin, activations ----
+    const int pw = warp - kQ2Drain;
+    bool alive = true;
+    long long it = 0, iq = 0, gi = 0;
+    for (long long u = u0; alive && u < u1; ++gi) {
+      const long long ue = run_end(u);
+      const int b = (int)(gi & 1);
+      const int q = (int)(iq % QS);
+      alive = mbar_wait(&qfull[q], (uint32_t)((iq / QS) & 1), a.err, DEV_TIMEOUT_FULL);
+      // dd[b] was last read by the drain of run gi - 2
+      if (alive && gi >= 2) alive = mbar_wait(&accempty[b], (uint32_t)((gi / 2 - 1) & 1), a.err, DEV_TIMEOUT_DRAIN);
+      for (bool first = true; alive && u < ue; ++u, ++it) {
+        const int kg = (int)(u % kG);
+        const int s = (int)(it % kQ2Stages);
+        if (it >= kQ2Stages)
+          alive = mbar_wait(&sfree[s], (uint32_t)((it / kQ2Stages - 1) & 1), a.err, DEV_TIMEOUT_EMPTY);
+        if (!alive) break;
+        const uint32_t st = sbase + s * kQ2Stage;
+        if (!(a.dbg & 1))
+          q2_produce_a(qring + (size_t)q * HU + pw * TB, pw, kg & 3, lane, st, st + kOffAm, dd[b], first);
+        fence_async_smem();
+        __syncwarp();
+        if (lane == 0) {
+          if (first) mbar_arrive(&ddfull[b]);
+          mbar_arrive(&sfull[s]);
+          if (u + 1 == ue) mbar_arrive(&qempty[q]);
+        }
+        __syncwarp();
+        first = false;
+      }
+      ++iq;
+    }
+  } else {
+    // ---- drain (warps 0-3): row 32 warp + lane of the 128-row tile ----
+    const int row = 32 * warp + lane;
+    float y[Np];
+#pragma unroll
+    for (int t = 0; t < Np; ++t) y[t] = 0.f;
+    bool alive = true;
+    long long gi = 0;
+    for (long long u = u0; alive && u < u1; ++gi) {
+      const long long ue = run_end(u);
+      const int rt = (int)(u / kG);
+      const int b = (int)(gi & 1);
+      alive = mbar_wait(&accfull[b], (uint32_t)((gi / 2) & 1), a.err, DEV_TIMEOUT_DRAIN) &&
+              mbar_wait(&ddfull[b], (uint32_t)((gi / 2) & 1), a.err, DEV_TIMEOUT_DRAIN);
+      __syncwarp();
+      if (!alive) break;
+      tc_fence_after();
+      const float d = dd[b][row].x, dm = dd[b][row].y;
+      const uint32_t tl = tmem + ((uint32_t)(32 * warp) << 16) + (uint32_t)(b * 2 * N2);
+#pragma unroll
+      for (int t0 = 0; t0 < Np; t0 += 8) {
+        uint32_t dh[8], dl[8], mh[8], ml[8];
+        tmem_ld8_async(tl + t0, dh);
+        tmem_ld8_async(tl + Np + t0, dl);
+        tmem_ld8_async(tl + N2 + t0, mh);
+        tmem_ld8_async(tl + N2 + Np + t0, ml);
+        asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+        for (int i = 0; i < 8; ++i)
+          y[t0 + i] = fmaf(-dm, fmaf(256.0f, __uint_as_float(mh[i]), __uint_as_float(ml[i])),
+                           fmaf(d, fmaf(256.0f, __uint_as_float(dh[i]), __uint_as_float(dl[i])), y[t0 + i]));
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&accempty[b]);
+      u = ue;
+      if (u == u1 || u % kG == 0) {
+        // segment end: this CTA's share of tile rt into its partial slot
+        const int slot = cta - qg_owner((long long)rt * kG, U, G);
+        float* dst = a.part + ((size_t)rt * a.slots + slot) * kMaxTokens * kQgRows + row;
+#pragma unroll
+        for (int t = 0; t < Np; ++t) {
+          if (t < a.m) dst[(size_t)t * kQgRows] = y[t];
+          y[t] = 0.f;
+        }
+      }
+    }
+  }
+  pdl_launch_dependents();
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kCols) : "memory");
+  }
+}
+
+template <int NT>
+cudaError_t launch_q2_bprep_t(const QgemmArgs& q, uint8_t* out, cudaStream_t s, int pdl) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(4 * q.nsb);
+  cfg.blockDim = dim3(256);
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, q2_bprep_kernel<NT>, q.xf, q.xs, q.m, q.nt_x, out);
+}
+
+template <int NT>
+cudaError_t launch_qgemm2_t(const QgemmArgs& q, int G, cudaStream_t s, int pdl) {
+  auto kern = qgemm2_kernel<NT>;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (cudaError_t e = ensure_smem_attr(kern, kQ2Smem, dev)) return e;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(G);
+  cfg.blockDim = dim3(kQ2Threads);
+  cfg.dynamicSmemBytes = kQ2Smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, kern, q);
 }
 
 template <int NT>
@@ -1945,11 +2385,15 @@ cudaError_t rowexp_launch(const uint8_t* tiled, int dtype, int n_rg, int nsb, in
   return cudaGetLastError();
 }
 
-cudaError_t qgemm_launch(const GemvArgs& a, float* part, const QgemmPlan& p, cudaStream_t s, int pdl) {
+size_t qgemm_bprep_bytes(int nsb) { return (size_t)4 * nsb * q2_bslice_bytes(2 * kMaxTokens); }
+
+cudaError_t qgemm_launch(const GemvArgs& a, float* part, uint8_t* bprep, const QgemmPlan& p, cudaStream_t s,
+                         int pdl) {
   const int8_t* rexp = a.rexp;
   if (a.m < 16 || a.m > kMaxTokens || !a.xin.xf || !rexp || !part || p.G < 1) return cudaErrorInvalidValue;
   QgemmArgs q;
   q.w = a.w;
+  q.xs = a.xin.xs;
   q.dtype = a.dtype;
   q.n_rg = a.n_rg;
   q.nsb = a.nsb;
@@ -1962,7 +2406,25 @@ cudaError_t qgemm_launch(const GemvArgs& a, float* part, const QgemmPlan& p, cud
   q.dbg = a.dbg >> 4;
   q.err = a.err;
   cudaError_t e;
-  switch (a.dtype) {
+  const bool exact = a.dtype == DT_Q4_K && a.xin.xs && bprep && !(a.dbg & 0x100);  // exact-weight GEMM for Q4_K
+  q.bprep = bprep;
+  switch (exact ? -1 : a.dtype) {
+    case -1:
+      switch (gemv_nt_for(a.m)) {
+        case 2:
+          e = launch_q2_bprep_t<2>(q, bprep, s, pdl);
+          if (e == cudaSuccess) e = launch_qgemm2_t<2>(q, p.G, s, pdl);
+          break;
+        case 4:
+          e = launch_q2_bprep_t<4>(q, bprep, s, pdl);
+          if (e == cudaSuccess) e = launch_qgemm2_t<4>(q, p.G, s, pdl);
+          break;
+        default:
+          e = launch_q2_bprep_t<8>(q, bprep, s, pdl);
+          if (e == cudaSuccess) e = launch_qgemm2_t<8>(q, p.G, s, pdl);
+          break;
+      }
+      break;
     case DT_Q4_K: e = launch_qgemm_t<DT_Q4_K>(q, p.G, s, pdl); break;
     case DT_Q6_K: e = launch_qgemm_t<DT_Q6_K>(q, p.G, s, pdl); break;
     case DT_Q8_0: e = launch_qgemm_t<DT_Q8_0>(q, p.G, s, pdl); break;
@@ -1971,7 +2433,7 @@ cudaError_t qgemm_launch(const GemvArgs& a, float* part, const QgemmPlan& p, cud
   if (e != cudaSuccess) return e;
   QgemmTail t;
   t.part = part;
-  t.rexp = rexp;
+  t.rexp = exact ? nullptr : rexp;
   t.slots = p.slots;
   t.G = p.G;
   t.kG = p.kG;

@@ -110,7 +110,11 @@ struct QgemmPlan {
 QgemmPlan qgemm_plan(int num_sms, int n_rg, int nsb);
 size_t qgemm_part_floats(const QgemmPlan& p);
 cudaError_t rowexp_launch(const uint8_t* tiled, int dtype, int n_rg, int nsb, int8_t* out, cudaStream_t s);
-cudaError_t qgemm_launch(const GemvArgs& a, float* part, const QgemmPlan& p, cudaStream_t s, int pdl);
+// Q4_K runs the exact-weight GEMM, which also needs bprep: qgemm_bprep_bytes(nsb)
+// bytes of scratch for its activation planes (null: the hi/lo-weight GEMM).
+size_t qgemm_bprep_bytes(int nsb);
+cudaError_t qgemm_launch(const GemvArgs& a, float* part, uint8_t* bprep, const QgemmPlan& p, cudaStream_t s,
+                         int pdl);
 
 // Repack GGUF blocks into the tiled layout. Source rows come from up to two
 // matrices: mode 0 plain (rows of a), 1 concat (a then b), 2 interleave-8

@@ -160,6 +160,13 @@ __global__ void __launch_bounds__(kAttnWarps * 32) attn_kernel(const __grid_cons
   // new tokens that the previous kernel appends: pages wholly below the
   // smallest position of this launch's rows are streamed before waiting for it.
   __shared__ int s_pos_min;
+  // the rows' tenants and positions, read once (coalesced) into shared memory
+  __shared__ int s_rt[kMaxRows], s_rp[kMaxRows];
+  for (int i = threadIdx.x; i < a.n_rows; i += blockDim.x) {
+    s_rt[i] = a.row_tenant[i];
+    s_rp[i] = a.row_pos[i];
+  }
+  __syncthreads();
   // Rows group by tenant: up to RG consecutive rows of one tenant at
   // consecutive positions share a pair (the last has the largest position).
   // Stream-K over pages: the pages of all (row group, kv head) pairs form one
@@ -169,14 +176,13 @@ __global__ void __launch_bounds__(kAttnWarps * 32) attn_kernel(const __grid_cons
     int pmin = 0x7fffffff, ng = 0;
     for (int r = 0; r < a.n_rows;) {
       int n = 1;
-      while (n < RG && r + n < a.n_rows && a.row_tenant[r + n] == a.row_tenant[r] &&
-             a.row_pos[r + n] == a.row_pos[r + n - 1] + 1)
+      while (n < RG && r + n < a.n_rows && s_rt[r + n] == s_rt[r] && s_rp[r + n] == s_rp[r + n - 1] + 1)
         ++n;
       g_row0[ng] = r;
       g_nr[ng] = n;
       row_pages[ng] = acc;
-      acc += (long long)n_kv * ((a.row_pos[r + n - 1] >> 4) + 1);
-      for (int i = 0; i < n; ++i) pmin = min(pmin, a.row_pos[r + i]);
+      acc += (long long)n_kv * ((s_rp[r + n - 1] >> 4) + 1);
+      for (int i = 0; i < n; ++i) pmin = min(pmin, s_rp[r + i]);
       ++ng;
       r += n;
     }
@@ -188,7 +194,7 @@ __global__ void __launch_bounds__(kAttnWarps * 32) attn_kernel(const __grid_cons
     // stays within twice the even page share; every CTA computes the same answer.
     int longest = 0;
     for (int gi = 0; gi < ng; ++gi)
-      longest = max(longest, (a.row_pos[g_row0[gi] + g_nr[gi] - 1] >> 4) + 1);
+      longest = max(longest, (s_rp[g_row0[gi] + g_nr[gi] - 1] >> 4) + 1);
     const long long n_pairs = (long long)ng * n_kv, share = (acc + G - 1) / G;
     s_whole = a.whole_pairs && (long long)longest * ((n_pairs + G - 1) / G) <= 2 * share;
   }
@@ -219,7 +225,7 @@ __global__ void __launch_bounds__(kAttnWarps * 32) attn_kernel(const __grid_cons
     if (!ui.valid) return ui;
     int r = 0;
     while (r + 1 < n_groups && row_pages[r + 1] <= x) ++r;
-    const int last_pos = a.row_pos[g_row0[r] + g_nr[r] - 1];
+    const int last_pos = s_rp[g_row0[r] + g_nr[r] - 1];
     const int np = (last_pos >> 4) + 1;
     const long long local = x - row_pages[r];
     ui.row = g_row0[r];
@@ -238,8 +244,7 @@ __global__ void __launch_bounds__(kAttnWarps * 32) attn_kernel(const __grid_cons
   uint8_t* myring = rings + warp * NSW * C::STAGE;
   uint64_t* mybars = bars + warp * NSW;
   const size_t kv_head_stride = (size_t)16 * HD;  // elements
-  auto block_ptr = [&](int tenant, int p, int which, int kvh) -> const uint8_t* {
-    const int page = a.kv.ptab[(size_t)tenant * a.kv.ptab_stride + p];
+  auto block_ptr = [&](int page, int which, int kvh) -> const uint8_t* {
     const size_t el = ((((size_t)page * a.kv.n_layers + a.layer) * 2 + which) * n_kv + kvh) * kv_head_stride;
     return reinterpret_cast<const uint8_t*>(a.kv.pool) + el * C::ESZ;
   };
@@ -261,14 +266,28 @@ __global__ void __launch_bounds__(kAttnWarps * 32) attn_kernel(const __grid_cons
     pp = pu.valid ? pu.p_begin + warp : -1;
   }
   int issued = 0, consumed = 0;
+  // Page-table cache of this warp (uniform use): lane i holds the physical page
+  // of page pc_base + 4 i of tenant pc_tenant, refilled with one coalesced load
+  // per 32 of the warp's pages instead of one dependent load per page.
+  int pc_tenant = -1, pc_base = 0, pc_val = 0;
+  auto page_of = [&](int tenant, int p) -> int {
+    if (tenant != pc_tenant || p < pc_base || ((p - pc_base) & (kAttnWarps - 1)) ||
+        p >= pc_base + kAttnWarps * 32) {
+      pc_tenant = tenant;
+      pc_base = p;
+      const int q = p + kAttnWarps * lane;
+      pc_val = q < a.kv.ptab_stride ? a.kv.ptab[(size_t)tenant * a.kv.ptab_stride + q] : 0;
+    }
+    return __shfl_sync(0xffffffffu, pc_val, (p - pc_base) / kAttnWarps);
+  };
   auto issue_upto = [&](int limit, bool old_only = false) {
     while (issued < limit && pu.valid && (!old_only || (pp + 1) * 16 <= pos_min)) {
       const int s = issued % NSW;
+      const int page = page_of(s_rt[pu.row], pp);
       if (lane == 0) mbar_arrive_expect_tx(&mybars[s], 2 * C::BLK);
       if constexpr (F16) {
         // TMA boxes: K then V of (page, layer, kv head), HD / 64 boxes each
         if (lane == 0) {
-          const int page = a.kv.ptab[(size_t)a.row_tenant[pu.row] * a.kv.ptab_stride + pp];
           const int yk = ((((page * a.kv.n_layers + a.layer) * 2) * n_kv + pu.kvh) * 16);
 #pragma unroll
           for (int which = 0; which < 2; ++which)
@@ -278,9 +297,8 @@ __global__ void __launch_bounds__(kAttnWarps * 32) attn_kernel(const __grid_cons
                           &mybars[s]);
         }
       } else if (lane == 0) {
-        const int tenant = a.row_tenant[pu.row];
-        bulk_g2s(myring + s * C::STAGE, block_ptr(tenant, pp, 0, pu.kvh), C::BLK, &mybars[s]);
-        bulk_g2s(myring + s * C::STAGE + C::SBLK, block_ptr(tenant, pp, 1, pu.kvh), C::BLK, &mybars[s]);
+        bulk_g2s(myring + s * C::STAGE, block_ptr(page, 0, pu.kvh), C::BLK, &mybars[s]);
+        bulk_g2s(myring + s * C::STAGE + C::SBLK, block_ptr(page, 1, pu.kvh), C::BLK, &mybars[s]);
       }
       ++issued;
       prod_advance();
@@ -329,7 +347,7 @@ __global__ void __launch_bounds__(kAttnWarps * 32) attn_kernel(const __grid_cons
       // causal limit of columns 2c, 2c+1: their row's position + 1
       int lim[2];
 #pragma unroll
-      for (int h = 0; h < 2; ++h) lim[h] = 2 * c + h < nc ? a.row_pos[ui.row + (2 * c + h) / NREP] + 1 : 0;
+      for (int h = 0; h < 2; ++h) lim[h] = 2 * c + h < nc ? s_rp[ui.row + (2 * c + h) / NREP] + 1 : 0;
       float ot[KS][4];
 #pragma unroll
       for (int mt = 0; mt < KS; ++mt) ot[mt][0] = ot[mt][1] = ot[mt][2] = ot[mt][3] = 0.f;

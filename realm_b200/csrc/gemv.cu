@@ -70,6 +70,19 @@ __device__ __forceinline__ unsigned long long gtimer() {
   } while (0)
 
 __device__ __forceinline__ float4 ldcg4(const float* p) { return __ldcg(reinterpret_cast<const float4*>(p)); }
+// L2 loads issued where they stand in the program (volatile): the tail of a
+// split row group requests the residual rows before the partial sums, so both
+// round trips overlap
+__device__ __forceinline__ float ldcg_issue(const float* p) {
+  float v;
+  asm volatile("ld.global.cg.f32 %0, [%1];" : "=f"(v) : "l"(p));
+  return v;
+}
+__device__ __forceinline__ float4 ldcg4_issue(const float* p) {
+  float4 v;
+  asm volatile("ld.global.cg.v4.f32 {%0, %1, %2, %3}, [%4];" : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w) : "l"(p));
+  return v;
+}
 
 __device__ __forceinline__ float guard_scale(float v, float repl) {
   // fused.rs:276-285 / 1171-1175: NaN or Inf super-scales are replaced
@@ -303,7 +316,7 @@ __device__ __forceinline__ void load_resid(const GemvArgs& a, int rg, int warp, 
 #pragma unroll
     for (int r = 0; r < 4; ++r) {
       const int t = nt * 8 + 2 * c + (r & 1), row = row0 + ((r & 2) ? 8 : 0);
-      xv[nt][r] = (t < a.m && row < a.n) ? __ldcg(a.resid + (size_t)t * a.ldr + row) : 0.f;
+      xv[nt][r] = (t < a.m && row < a.n) ? ldcg_issue(a.resid + (size_t)t * a.ldr + row) : 0.f;
     }
 }
 
@@ -611,7 +624,7 @@ __device__ __forceinline__ void finish_segment(const GemvArgs& a, int p, int n_p
           if (c0 + b <= cl) {
             const float* src = src_of(c0 + b);
 #pragma unroll
-            for (int nt = 0; nt < NT; ++nt) q[b][nt] = ldcg4(src + nt * 128);
+            for (int nt = 0; nt < NT; ++nt) q[b][nt] = ldcg4_issue(src + nt * 128);
           }
 #pragma unroll
         for (int b = 0; b < kB; ++b)

@@ -104,12 +104,20 @@ __device__ __forceinline__ void ldsm_x4_trans(uint32_t r[4], const void* p) {
                : "r"(smem_u32(p)));
 }
 // two fp32 values -> packed fp16 hi and lo parts (x ~= hi + lo, ~22 bits)
+// (paired conversions: hi = RN(x), lo = RN(x - hi), two values per instruction)
 __device__ __forceinline__ void pack_hilo(float x0, float x1, uint32_t& hi, uint32_t& lo) {
-  __half h0, l0, h1, l1;
-  split_hilo(x0, h0, l0);
-  split_hilo(x1, h1, l1);
-  hi = (uint32_t)__half_as_ushort(h0) | ((uint32_t)__half_as_ushort(h1) << 16);
-  lo = (uint32_t)__half_as_ushort(l0) | ((uint32_t)__half_as_ushort(l1) << 16);
+  const __half2 h = __floats2half2_rn(x0, x1);
+  const float2 f = __half22float2(h);
+  const __half2 l = __floats2half2_rn(x0 - f.x, x1 - f.y);
+  hi = *reinterpret_cast<const uint32_t*>(&h);
+  lo = *reinterpret_cast<const uint32_t*>(&l);
+}
+// 2^x by the hardware approximation (relative error below 2^-22; flushes
+// subnormal results to zero, which the softmax weights absorb)
+__device__ __forceinline__ float exp2_fast(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
 }
 
 // A segment: this CTA's share of one (row, kv head) pair, pages [p_begin, p_end)
@@ -353,6 +361,13 @@ __global__ void __launch_bounds__(kAttnWarps * 32) attn_kernel(const __grid_cons
       for (int mt = 0; mt < KS; ++mt) ot[mt][0] = ot[mt][1] = ot[mt][2] = ot[mt][3] = 0.f;
       float* pt = pb + warp * 16 * 8;  // [16 tokens][8 heads] transpose buffer
       const int mi = lane >> 3, rr = lane & 7;
+      // this lane's ldmatrix addresses in a K block and a V block, per k-step
+      int koff[KS], voff[KS];
+#pragma unroll
+      for (int ks = 0; ks < KS; ++ks) {
+        koff[ks] = swz(rr + (mi & 1) * 8, ks * 2 + (mi >> 1));
+        voff[ks] = swz(rr + (mi >> 1) * 8, ks * 2 + (mi & 1));
+      }
       for (int p = ui.p_begin + warp; p < ui.p_end; p += kAttnWarps) {
         issue_upto(consumed + NSW);
         const int s = consumed % NSW;
@@ -368,7 +383,7 @@ __global__ void __launch_bounds__(kAttnWarps * 32) attn_kernel(const __grid_cons
 #pragma unroll
         for (int ks = 0; ks < KS; ++ks) {
           uint32_t af[4];
-          ldsm_x4(af, kb + swz(rr + (mi & 1) * 8, ks * 2 + (mi >> 1)));
+          ldsm_x4(af, kb + koff[ks]);
           mma_16816(sa[(ks & 1) * 2], af, qb[ks][0][0], qb[ks][0][1]);
           mma_16816(sa[(ks & 1) * 2 + 1], af, qb[ks][1][0], qb[ks][1][1]);
         }
@@ -402,7 +417,7 @@ __global__ void __launch_bounds__(kAttnWarps * 32) attn_kernel(const __grid_cons
             mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 8));
             mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 16));
             const float mn = fmaxf(mh[h], mx);
-            alpha[h] = mh[h] == -INFINITY ? 0.f : exp2f(mh[h] - mn);
+            alpha[h] = mh[h] == -INFINITY ? 0.f : exp2_fast(mh[h] - mn);
             lh[h] *= alpha[h];
             mh[h] = mn;
           }
@@ -416,8 +431,8 @@ __global__ void __launch_bounds__(kAttnWarps * 32) attn_kernel(const __grid_cons
         }
 #pragma unroll
         for (int h = 0; h < 2; ++h) {
-          pr[h] = v0h[h] ? exp2f(s0[h] - mh[h]) : 0.f;
-          pr[2 + h] = v1h[h] ? exp2f(s1[h] - mh[h]) : 0.f;
+          pr[h] = v0h[h] ? exp2_fast(s0[h] - mh[h]) : 0.f;
+          pr[2 + h] = v1h[h] ? exp2_fast(s1[h] - mh[h]) : 0.f;
           lh[h] += pr[h] + pr[2 + h];
         }
         // P^T as the B operand: lane (g, c) needs heads g, tokens 2c, 2c+1, 2c+8, 2c+9
@@ -433,7 +448,7 @@ __global__ void __launch_bounds__(kAttnWarps * 32) attn_kernel(const __grid_cons
 #pragma unroll
         for (int mt = 0; mt < KS; ++mt) {
           uint32_t af[4];
-          ldsm_x4_trans(af, vb + swz(rr + (mi >> 1) * 8, mt * 2 + (mi & 1)));
+          ldsm_x4_trans(af, vb + voff[mt]);
           mma_16816(ot[mt], af, pbh0, pbh1);
           mma_16816(ot[mt], af, pbl0, pbl1);
         }

@@ -362,7 +362,8 @@ __device__ void epilogue(const GemvArgs& a, int p, int rg, int warp, int lane, f
       }
     }
     named_bar(2, 32 * kConsumerWarps);
-    frags_write(T, 1, kTLd, kRowGroup / 2, LD, rg * (kRowGroup / 2), 0, nullptr, a.xout, NT, red, tid,
+    frags_write(T, 1, kTLd, kRowGroup / 2, LD, rg * (kRowGroup / 2), a.xout_t0, nullptr, a.xout,
+                a.xout_nt ? a.xout_nt : NT, red, tid,
                 32 * kConsumerWarps, [] { named_bar(2, 32 * kConsumerWarps); });
   } else if (a.epi == EPI_RESID) {
     // x rows were written by another CTA earlier in this launch: read through
@@ -417,7 +418,8 @@ __device__ void epilogue(const GemvArgs& a, int p, int rg, int warp, int lane, f
     named_bar(2, 32 * kConsumerWarps);  // red is reused as frags_write scratch below
     if (tid == 0) RB_TS(p, 14);
     if (a.xout.xs)
-      frags_write(T, 1, kTLd, kRowGroup, LD, rg * kRowGroup, 0, nullptr, a.xout, NT, red, tid, 32 * kConsumerWarps,
+      frags_write(T, 1, kTLd, kRowGroup, LD, rg * kRowGroup, a.xout_t0, nullptr, a.xout, a.xout_nt ? a.xout_nt : NT,
+                  red, tid, 32 * kConsumerWarps,
                   [] { named_bar(2, 32 * kConsumerWarps); });
     if (tid == 0) RB_TS(p, 15);
   } else if (a.epi == EPI_LOGITS) {
@@ -1725,18 +1727,33 @@ struct QgemmTail {
 
 // Sums each 256-row group's partial slots (CTA order), undoes 2^e_row and runs
 // the GEMV epilogue (same fragment mapping: warp = 16-row tile of the group).
-template <int NT>
-__global__ void __launch_bounds__(kConsumerWarps * 32) qgemm_epi_kernel(const __grid_constant__ GemvArgs a,
+// One CTA per (256-row group, 8-token n-tile): the tokens of an epilogue are
+// independent, so splitting them gives NT times the CTAs.
+__global__ void __launch_bounds__(kConsumerWarps * 32) qgemm_epi_kernel(const __grid_constant__ GemvArgs ga,
                                                                         const __grid_constant__ QgemmTail q) {
   extern __shared__ __align__(16) float qe_smem[];
   float* red = qe_smem;                              // kConsumerWarps * kMaxTokens
   float* inv_rms = red + kConsumerWarps * kMaxTokens;  // kMaxTokens
-  float* T = inv_rms + kMaxTokens;                   // tile_floats(NT)
+  float* T = inv_rms + kMaxTokens;                   // tile_floats(1)
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int g = lane >> 2, c = lane & 3;
-  const int rg = blockIdx.x;
+  const int rg = blockIdx.x, t0 = 8 * blockIdx.y;
   pdl_wait();
   pdl_launch_dependents();
+  if (t0 >= ga.m) return;
+  // this CTA's tokens t0 .. t0 + 7 as tokens 0..7 of a narrower launch
+  GemvArgs a = ga;
+  a.m = min(8, ga.m - t0);
+  a.xout_nt = ga.m <= 8 ? 1 : ga.m <= 16 ? 2 : ga.m <= 32 ? 4 : 8;  // gemv_nt_for
+  a.xout_t0 = t0;
+  if (a.y) a.y += (size_t)t0 * a.ldy;
+  if (a.resid) a.resid += (size_t)t0 * a.ldr;
+  if (a.q_out) a.q_out += (size_t)t0 * a.ldq;
+  if (a.ss_out) a.ss_out += t0;
+  if (a.ss_part) a.ss_part += t0;
+  if (a.argmax) a.argmax += t0;
+  if (a.row_pos) a.row_pos += t0;
+  if (a.row_tenant) a.row_tenant += t0;
   if (a.ss_part) {  // as consume_phase: eight strided partial sums per token, added in a fixed order
     const int t = tid & 63, r = tid >> 6;
     if (t < a.m) {
@@ -1756,30 +1773,23 @@ __global__ void __launch_bounds__(kConsumerWarps * 32) qgemm_epi_kernel(const __
   const int rt = rg * 2 + (warp >> 3);
   const int rl = (warp & 7) * 16 + g;  // row within the 128-row tile (and rl + 8)
   const int c0 = qg_owner((long long)rt * q.kG, q.U, q.G), c1 = qg_owner((long long)rt * q.kG + q.kG - 1, q.U, q.G);
-  float acc[NT][4];
-#pragma unroll
-  for (int nt = 0; nt < NT; ++nt) acc[nt][0] = acc[nt][1] = acc[nt][2] = acc[nt][3] = 0.f;
+  float acc[1][4] = {{0.f, 0.f, 0.f, 0.f}};
   for (int cc = c0; cc <= c1; ++cc) {
     const float* base = q.part + ((size_t)rt * q.slots + (cc - c0)) * kMaxTokens * kQgRows;
 #pragma unroll
-    for (int nt = 0; nt < NT; ++nt)
-#pragma unroll
-      for (int r = 0; r < 4; ++r) {
-        const int t = nt * 8 + 2 * c + (r & 1);
-        if (t < a.m) acc[nt][r] += __ldcg(base + (size_t)t * kQgRows + rl + ((r & 2) ? 8 : 0));
-      }
+    for (int r = 0; r < 4; ++r) {
+      const int t = 2 * c + (r & 1);
+      if (t < a.m) acc[0][r] += __ldcg(base + (size_t)(t0 + t) * kQgRows + rl + ((r & 2) ? 8 : 0));
+    }
   }
   const int row0 = rg * kRowGroup + warp * kTileRows + g;
   // the per-row 2^e of the hi/lo-weight GEMM (none for the exact-weight GEMM)
   const float sA = q.rexp ? pow2f(-(int)q.rexp[row0]) : 1.f, sB = q.rexp ? pow2f(-(int)q.rexp[row0 + 8]) : 1.f;
-#pragma unroll
-  for (int nt = 0; nt < NT; ++nt) {
-    acc[nt][0] *= sA;
-    acc[nt][1] *= sA;
-    acc[nt][2] *= sB;
-    acc[nt][3] *= sB;
-  }
-  epilogue<NT>(a, 0, rg, warp, lane, acc, a.ss_part ? inv_rms : nullptr, red, T);
+  acc[0][0] *= sA;
+  acc[0][1] *= sA;
+  acc[0][2] *= sB;
+  acc[0][3] *= sB;
+  epilogue<1>(a, 0, rg, warp, lane, acc, a.ss_part ? inv_rms : nullptr, red, T);
 }
 
 // Per-row exponent e with (bound of |w| over the row) * 2^e < 2^14, from the
@@ -1997,8 +2007,11 @@ __global__ void __launch_bounds__(kQ2Threads, 1) qgemm2_kernel(const __grid_cons
   extern __shared__ __align__(1024) uint8_t q2_smem_raw[];
   __shared__ uint64_t sfull[kQ2MaxStages], sfree[kQ2MaxStages];
   __shared__ uint64_t qfull[kQ2QStages], qempty[kQ2QStages];
-  __shared__ uint64_t accfull[2], accempty[2], ddfull[2], bfull[kQ2MaxStages];
-  __shared__ float2 dd[2][kQgRows];
+  // d, dmin of each run's rows: four slots, so producers run up to four runs
+  // ahead of the drain (the TMEM pairs alternate between two)
+  constexpr int kDd = 4;
+  __shared__ uint64_t accfull[2], accempty[2], ddfull[kDd], ddempty[kDd], bfull[kQ2MaxStages];
+  __shared__ float2 dd[kDd][kQgRows];
   __shared__ uint32_t tmem_slot;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(q2_smem_raw) + 1023) & ~(uintptr_t)1023);
@@ -2032,8 +2045,10 @@ __global__ void __launch_bounds__(kQ2Threads, 1) qgemm2_kernel(const __grid_cons
     for (int i = 0; i < 2; ++i) {
       mbar_init(&accfull[i], 1);
       mbar_init(&accempty[i], kQ2Drain);
-      mbar_init(&ddfull[i], kQ2Prod);
     }
+    for (int i = 0; i < kDd; ++i) {
+      mbar_init(&ddfull[i], kQ2Prod);
+      mbar_init(&ddempty[i], kQ2Drain);    }
     fence_barrier_init();
   }
   fence_async_smem();
@@ -2139,8 +2154,10 @@ __global__ void __launch_bounds__(kQ2Threads, 1) qgemm2_kernel(const __grid_cons
       const int b = (int)(gi & 1);
       const int q = (int)(iq % QS);
       alive = mbar_wait(&qfull[q], (uint32_t)((iq / QS) & 1), a.err, DEV_TIMEOUT_FULL);
-      // dd[b] was last read by the drain of run gi - 2
-      if (alive && gi >= 2) alive = mbar_wait(&accempty[b], (uint32_t)((gi / 2 - 1) & 1), a.err, DEV_TIMEOUT_DRAIN);
+      // dd slot gi % kDd was last read by the drain of run gi - kDd
+      const int ds = (int)(gi % kDd);
+      if (alive && gi >= kDd)
+        alive = mbar_wait(&ddempty[ds], (uint32_t)((gi / kDd - 1) & 1), a.err, DEV_TIMEOUT_DRAIN);
       for (bool first = true; alive && u < ue; ++u, ++it) {
         const int kg = (int)(u % kG);
         const int s = (int)(it % kQ2Stages);
@@ -2149,11 +2166,11 @@ __global__ void __launch_bounds__(kQ2Threads, 1) qgemm2_kernel(const __grid_cons
         if (!alive) break;
         const uint32_t st = sbase + s * kQ2Stage;
         if (!(a.dbg & 1))
-          q2_produce_a(qring + (size_t)q * HU + pw * TB, pw, kg & 3, lane, st, st + kOffAm, dd[b], first);
+          q2_produce_a(qring + (size_t)q * HU + pw * TB, pw, kg & 3, lane, st, st + kOffAm, dd[ds], first);
         fence_async_smem();
         __syncwarp();
         if (lane == 0) {
-          if (first) mbar_arrive(&ddfull[b]);
+          if (first) mbar_arrive(&ddfull[ds]);
           mbar_arrive(&sfull[s]);
           if (u + 1 == ue) mbar_arrive(&qempty[q]);
         }
@@ -2175,11 +2192,13 @@ __global__ void __launch_bounds__(kQ2Threads, 1) qgemm2_kernel(const __grid_cons
       const int rt = (int)(u / kG);
       const int b = (int)(gi & 1);
       alive = mbar_wait(&accfull[b], (uint32_t)((gi / 2) & 1), a.err, DEV_TIMEOUT_DRAIN) &&
-              mbar_wait(&ddfull[b], (uint32_t)((gi / 2) & 1), a.err, DEV_TIMEOUT_DRAIN);
+              mbar_wait(&ddfull[gi % kDd], (uint32_t)((gi / kDd) & 1), a.err, DEV_TIMEOUT_DRAIN);
       __syncwarp();
       if (!alive) break;
       tc_fence_after();
-      const float d = dd[b][row].x, dm = dd[b][row].y;
+      const float d = dd[gi % kDd][row].x, dm = dd[gi % kDd][row].y;
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&ddempty[gi % kDd]);
       const uint32_t tl = tmem + ((uint32_t)(32 * warp) << 16) + (uint32_t)(b * 2 * N2);
 #pragma unroll
       for (int t0 = 0; t0 < Np; t0 += 8) {
@@ -2252,15 +2271,13 @@ cudaError_t launch_qgemm2_t(const QgemmArgs& q, int G, cudaStream_t s, int pdl) 
   return cudaLaunchKernelEx(&cfg, kern, q);
 }
 
-template <int NT>
-cudaError_t launch_qgemm_epi_t(const GemvArgs& a, const QgemmTail& q, cudaStream_t s, int pdl) {
-  const int smem = (kConsumerWarps * kMaxTokens + kMaxTokens + tile_floats(NT)) * 4;
-  auto kern = qgemm_epi_kernel<NT>;
+cudaError_t launch_qgemm_epi(const GemvArgs& a, const QgemmTail& q, cudaStream_t s, int pdl) {
+  const int smem = (kConsumerWarps * kMaxTokens + kMaxTokens + tile_floats(1)) * 4;
   int dev = 0;
   cudaGetDevice(&dev);
-  if (cudaError_t e = ensure_smem_attr(kern, smem, dev)) return e;
+  if (cudaError_t e = ensure_smem_attr(qgemm_epi_kernel, smem, dev)) return e;
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(a.n_rg);
+  cfg.gridDim = dim3(a.n_rg, gemv_nt_for(a.m));
   cfg.blockDim = dim3(kConsumerWarps * 32);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = s;
@@ -2269,7 +2286,7 @@ cudaError_t launch_qgemm_epi_t(const GemvArgs& a, const QgemmTail& q, cudaStream
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = pdl ? 1 : 0;
-  return cudaLaunchKernelEx(&cfg, kern, a, q);
+  return cudaLaunchKernelEx(&cfg, qgemm_epi_kernel, a, q);
 }
 
 template <int DT>
@@ -2451,11 +2468,7 @@ cudaError_t qgemm_launch(const GemvArgs& a, float* part, uint8_t* bprep, const Q
   t.G = p.G;
   t.kG = p.kG;
   t.U = p.U;
-  switch (gemv_nt_for(a.m)) {
-    case 2: return launch_qgemm_epi_t<2>(a, t, s, pdl);
-    case 4: return launch_qgemm_epi_t<4>(a, t, s, pdl);
-    default: return launch_qgemm_epi_t<8>(a, t, s, pdl);
-  }
+  return launch_qgemm_epi(a, t, s, pdl);
 }
 
 }  // namespace rb

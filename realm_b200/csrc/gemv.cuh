@@ -48,6 +48,8 @@ struct GemvArgs {
   int32_t ldr = 0;
   float* ss_out = nullptr;  // RESID: [n_rg][ld_ss]
   XFrags xout;              // RESID / SWIGLU: fragments of the next GEMV's input
+  int32_t xout_nt = 0;      //   their n-tile count (0: the kernel's own) and the
+  int32_t xout_t0 = 0;      //   token of this launch's row 0 (token-split epilogues)
   const float* xf_norm = nullptr;  // RESID: norm weight the next GEMV fuses
   unsigned long long* argmax = nullptr;  // LOGITS: per token key
   // QKV

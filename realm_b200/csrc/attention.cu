@@ -338,24 +338,39 @@ __global__ void __launch_bounds__(kAttnWarps * 32) attn_kernel(const __grid_cons
       // fp32, then O^T += V^T P^T (A = V tile by ldmatrix.trans, B = P as
       // fp16 hi + lo). Lane (g = lane/4, c = lane%4) owns heads 2c, 2c+1.
       constexpr int KS = HD / 16;
+      // PK: at most 4 query columns, so the MMA's 8 columns carry the hi parts
+      // (columns 0-3) and the lo parts (4-7) of the same heads: one MMA per
+      // step instead of two. Lanes c and c ^ 2 then hold the two halves of the
+      // same heads, summed by one shuffle; every lane works on heads
+      // hb + 0, hb + 1 (hb = 2 (c & 1) packed, 2 c otherwise).
+      constexpr bool PK = NC <= 4;
       const int g = lane >> 2, c = lane & 3;
+      const int hb = PK ? 2 * (c & 1) : 2 * c;
       const float qscale = a.scale * 1.4426950408889634f;
-      uint32_t qb[KS][2][2];  // [k-step][hi, lo][b0, b1]
+      uint32_t qb[KS][2][2];  // [k-step][hi, lo][b0, b1] (packed: [k-step][0][b0, b1])
 #pragma unroll
       for (int ks = 0; ks < KS; ++ks)
 #pragma unroll
         for (int b = 0; b < 2; ++b) {
           const int d = ks * 16 + 2 * c + 8 * b;
+          const int hq = PK ? (g & 3) : g;
           // scores in base-2 units: scale * log2(e) folded into q
-          const float x0 = g < nc ? qs[g * HD + d] * qscale : 0.f;
-          const float x1 = g < nc ? qs[g * HD + d + 1] * qscale : 0.f;
-          pack_hilo(x0, x1, qb[ks][0][b], qb[ks][1][b]);
+          const float x0 = hq < nc ? qs[hq * HD + d] * qscale : 0.f;
+          const float x1 = hq < nc ? qs[hq * HD + d + 1] * qscale : 0.f;
+          uint32_t hi, lo;
+          pack_hilo(x0, x1, hi, lo);
+          if (PK) {
+            qb[ks][0][b] = g < 4 ? hi : lo;
+          } else {
+            qb[ks][0][b] = hi;
+            qb[ks][1][b] = lo;
+          }
         }
       float mh[2] = {-INFINITY, -INFINITY}, lh[2] = {0.f, 0.f};
-      // causal limit of columns 2c, 2c+1: their row's position + 1
+      // causal limit of columns hb, hb + 1: their row's position + 1
       int lim[2];
 #pragma unroll
-      for (int h = 0; h < 2; ++h) lim[h] = 2 * c + h < nc ? s_rp[ui.row + (2 * c + h) / NREP] + 1 : 0;
+      for (int h = 0; h < 2; ++h) lim[h] = hb + h < nc ? s_rp[ui.row + (hb + h) / NREP] + 1 : 0;
       float ot[KS][4];
 #pragma unroll
       for (int mt = 0; mt < KS; ++mt) ot[mt][0] = ot[mt][1] = ot[mt][2] = ot[mt][3] = 0.f;
@@ -384,12 +399,20 @@ __global__ void __launch_bounds__(kAttnWarps * 32) attn_kernel(const __grid_cons
         for (int ks = 0; ks < KS; ++ks) {
           uint32_t af[4];
           ldsm_x4(af, kb + koff[ks]);
-          mma_16816(sa[(ks & 1) * 2], af, qb[ks][0][0], qb[ks][0][1]);
-          mma_16816(sa[(ks & 1) * 2 + 1], af, qb[ks][1][0], qb[ks][1][1]);
+          if (PK) {
+            mma_16816(sa[ks & 3], af, qb[ks][0][0], qb[ks][0][1]);
+          } else {
+            mma_16816(sa[(ks & 1) * 2], af, qb[ks][0][0], qb[ks][0][1]);
+            mma_16816(sa[(ks & 1) * 2 + 1], af, qb[ks][1][0], qb[ks][1][1]);
+          }
         }
-        float sc[4];  // (tok g, head 2c), (g, 2c+1), (g+8, 2c), (g+8, 2c+1)
+        float sc[4];  // (tok g, head hb), (g, hb+1), (g+8, hb), (g+8, hb+1)
 #pragma unroll
-        for (int e = 0; e < 4; ++e) sc[e] = (sa[0][e] + sa[2][e]) + (sa[1][e] + sa[3][e]);
+        for (int e = 0; e < 4; ++e) {
+          sc[e] = (sa[0][e] + sa[2][e]) + (sa[1][e] + sa[3][e]);
+          // packed: hi-part sums in lanes c < 2, lo-part sums in c >= 2
+          if (PK) sc[e] += __shfl_xor_sync(0xffffffffu, sc[e], 2);
+        }
         bool v0h[2], v1h[2];
 #pragma unroll
         for (int h = 0; h < 2; ++h) {
@@ -436,31 +459,43 @@ __global__ void __launch_bounds__(kAttnWarps * 32) attn_kernel(const __grid_cons
           lh[h] += pr[h] + pr[2 + h];
         }
         // P^T as the B operand: lane (g, c) needs heads g, tokens 2c, 2c+1, 2c+8, 2c+9
-        pt[g * 8 + 2 * c] = pr[0];
-        pt[g * 8 + 2 * c + 1] = pr[1];
-        pt[(g + 8) * 8 + 2 * c] = pr[2];
-        pt[(g + 8) * 8 + 2 * c + 1] = pr[3];
+        if (!PK || c < 2) {
+          pt[g * 8 + hb] = pr[0];
+          pt[g * 8 + hb + 1] = pr[1];
+          pt[(g + 8) * 8 + hb] = pr[2];
+          pt[(g + 8) * 8 + hb + 1] = pr[3];
+        }
         __syncwarp();
+        const int hp = PK ? (g & 3) : g;
         uint32_t pbh0, pbl0, pbh1, pbl1;
-        pack_hilo(pt[(2 * c) * 8 + g], pt[(2 * c + 1) * 8 + g], pbh0, pbl0);
-        pack_hilo(pt[(2 * c + 8) * 8 + g], pt[(2 * c + 9) * 8 + g], pbh1, pbl1);
+        pack_hilo(pt[(2 * c) * 8 + hp], pt[(2 * c + 1) * 8 + hp], pbh0, pbl0);
+        pack_hilo(pt[(2 * c + 8) * 8 + hp], pt[(2 * c + 9) * 8 + hp], pbh1, pbl1);
         __syncwarp();
+        if (PK) {  // columns 0-3: the hi parts of P, 4-7: the lo parts
+          if (g >= 4) {
+            pbh0 = pbl0;
+            pbh1 = pbl1;
+          }
+        }
 #pragma unroll
         for (int mt = 0; mt < KS; ++mt) {
           uint32_t af[4];
           ldsm_x4_trans(af, vb + voff[mt]);
           mma_16816(ot[mt], af, pbh0, pbh1);
-          mma_16816(ot[mt], af, pbl0, pbl1);
+          if (!PK) mma_16816(ot[mt], af, pbl0, pbl1);
         }
         ++consumed;
       }
       // this warp's partial: O^T fragments -> mrg[head][dim], then m, l per head
+      // (packed: the hi- and lo-weighted halves of a head sit in lanes c, c ^ 2)
 #pragma unroll
       for (int mt = 0; mt < KS; ++mt)
 #pragma unroll
         for (int q = 0; q < 4; ++q) {
-          const int head = 2 * c + (q & 1), dim = mt * 16 + g + ((q & 2) ? 8 : 0);
-          if (head < nc) mrg[(warp * NC + head) * (HD + 2) + dim] = ot[mt][q];
+          float v = ot[mt][q];
+          if (PK) v += __shfl_xor_sync(0xffffffffu, v, 2);
+          const int head = hb + (q & 1), dim = mt * 16 + g + ((q & 2) ? 8 : 0);
+          if (head < nc && (!PK || c < 2)) mrg[(warp * NC + head) * (HD + 2) + dim] = v;
         }
       // the per-lane partial sums of each head, then (m, l) in natural-log units
 #pragma unroll
@@ -469,12 +504,12 @@ __global__ void __launch_bounds__(kAttnWarps * 32) attn_kernel(const __grid_cons
         lh[h] += __shfl_xor_sync(0xffffffffu, lh[h], 8);
         lh[h] += __shfl_xor_sync(0xffffffffu, lh[h], 16);
       }
-      if (g == 0)
+      if (g == 0 && (!PK || c < 2))
 #pragma unroll
         for (int h = 0; h < 2; ++h)
-          if (2 * c + h < nc) {
-            mrg[(warp * NC + 2 * c + h) * (HD + 2) + HD] = mh[h] * 0.6931471805599453f;
-            mrg[(warp * NC + 2 * c + h) * (HD + 2) + HD + 1] = lh[h];
+          if (hb + h < nc) {
+            mrg[(warp * NC + hb + h) * (HD + 2) + HD] = mh[h] * 0.6931471805599453f;
+            mrg[(warp * NC + hb + h) * (HD + 2) + HD + 1] = lh[h];
           }
     } else {
       float m[NREP], l[NREP], o[NREP][DPL];

@@ -589,6 +589,9 @@ def run_case(args):
         torch.cuda.synchronize(dev)
         print("attn case done", flush=True)
         return
+    if args.case == "chunk":
+        run_chunk_attn(rb, torch, dev)
+        return
     if args.case == "gemv":
         n, k, m = 2 * CFG["ffn"], CFG["hidden"], TENANTS_PER_GPU
         ws = []
@@ -656,6 +659,47 @@ def run_case(args):
         print("decode step", s, ctx.last_forward_launches(), "launches", flush=True)
 
 
+def run_chunk_attn(rb, torch, dev, ctx_len=4032, rows=64, reps=7):
+    """Prompt-chunk attention: one tenant whose fp16 cache holds ctx_len
+    N(0,1) entries, a rows-long chunk at the next positions (GQA 8, hd 128, the
+    configs[4] heads), through rb_attention_forward on device buffers. Median
+    device us of the prompt-chunk kernel (grouped rows) against one decode pair
+    per row (RB_ATTN_GROUP=0), and the K/V bytes each requests (the per-row
+    pairs of one tenant mostly hit L2). Prints one JSON line."""
+    out = {}
+    for n_heads, n_kv in ((64, 8),):
+        hd = 128
+        res = {}
+        for grouped in (1, 0):
+            os.environ["RB_ATTN_GROUP"] = str(grouped)
+            ctx = rb.Context(0)
+            del os.environ["RB_ATTN_GROUP"]
+            n_pages = (ctx_len + rows) // 16 + 2
+            pool = ctx.kv_pool(1, n_kv, hd, rb.F16, n_pages=n_pages, max_tenants=1, max_seq=ctx_len + rows)
+            pool.shuffle(3)
+            pool.create(0)
+            g = torch.Generator(device=dev)
+            g.manual_seed(7)
+            pool.append(0, 0, torch.randn(ctx_len + rows, n_kv * hd, generator=g, device=dev),
+                        torch.randn(ctx_len + rows, n_kv * hd, generator=g, device=dev))
+            q = torch.randn(rows, n_heads * hd, generator=g, device=dev)
+            o = torch.empty(rows, n_heads * hd, device=dev)
+            pos = list(range(ctx_len, ctx_len + rows))
+            ms = []
+            for _ in range(reps):
+                pool.attention_forward(0, [0] * rows, q, n_heads, 1 / np.sqrt(hd), positions=pos, out=o)
+                ms.append(ctx.last_forward_ms())
+            res["chunk_kernel" if grouped else "per_row_pairs"] = round(float(np.median(ms[2:])) * 1e3, 1)
+            ctx.close()
+        pages = (ctx_len + rows) // 16
+        out[f"gqa{n_heads // n_kv}"] = {
+            "us": res, "kv_MB_per_kv_head_tile": round(pages * 16 * hd * 2 * 2 / 1e6, 2),
+            "kv_MB_read": {"chunk_kernel": round(n_kv * (rows * n_heads // n_kv // 64) * pages * 8192 / 1e6, 1),
+                           "per_row_pairs": round(n_kv * rows * pages * 8192 / 1e6, 1)}}
+    print(json.dumps({"case": "chunk_attention", "ctx": ctx_len, "rows": rows, "hd": 128, "results": out}),
+          flush=True)
+
+
 CFG70B = dict(n_layers=80, hidden=8192, n_heads=64, n_kv_heads=8, head_dim=128, ffn=28672, vocab=32000,
               max_seq=4096, rms_eps=1e-5, layer_eps=1e-5, rope_theta=10000.0)
 
@@ -703,6 +747,8 @@ def run_llama70b(rb, torch, ctx, dev, args):
     for cs in range(0, prompt, 64):
         m.forward_rows([0] * 64, ids[cs:cs + 64], want_logits=False)
         pre_ms += ctx.last_forward_ms()
+    # one more 64-row chunk (positions 3840..3903) run kernel by kernel: where a deep chunk's time goes
+    pre_prof, _ = m.forward_profile([0] * 64, np.random.default_rng(56).integers(0, CFG70B["vocab"], 64).astype(np.uint32))
     line = {"metric": "configs[4] Llama-2-70B Q4_K_M decode tok/s (16 tenants, ctx 3840+)", "unit": "tok/s",
             "value": round(nt / (step_ms * 1e-3), 1), "ms_per_step": round(step_ms, 3), "steps": steps,
             "decode_step": {"bytes_per_step": int(wb + kvb), "weight_bytes": int(wb), "kv_bytes": int(kvb),
@@ -712,7 +758,8 @@ def run_llama70b(rb, torch, ctx, dev, args):
                             "kernel_ms_serialised": {k: round(v, 3) for k, v in prof_ms.items()}},
             "prefill": {"tokens": prompt, "rows_per_step": 64, "ms": round(pre_ms, 1),
                         "tok_per_s": round(prompt / (pre_ms * 1e-3), 1),
-                        "path": "tcgen05" if ctx.uses_tcgen05(64) else "mma.sync"},
+                        "path": "tcgen05" if ctx.uses_tcgen05(64) else "mma.sync",
+                        "chunk_ms_serialised": {k: round(v, 3) for k, v in pre_prof.items()}},
             "config": {"workload": "Llama-2-70B shape, random-init Q4_K_M (attn_v, output Q6_K), 16 tenants, "
                                    "fp16 paged KV, caches of 3840 N(0,1) entries; prefill of a 3840-token prompt",
                        "weights_GB": round(wb / 1e9, 2)},
@@ -861,7 +908,7 @@ def main():
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU-baseline leg")
     ap.add_argument("--layers", type=int, default=0,
                     help="decode case only: build the 7B model with this many layers (small ncu captures)")
-    ap.add_argument("--case", choices=["gemv", "decode", "attn", "serve", "serve_sampled", "load", "sample", "qgemm",
+    ap.add_argument("--case", choices=["gemv", "decode", "attn", "chunk", "serve", "serve_sampled", "load", "sample", "qgemm",
                              "llama70b"],
                     help="profiling case for ncu: run a small workload of one kernel family and exit")
     args = ap.parse_args()

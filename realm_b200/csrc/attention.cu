@@ -27,6 +27,12 @@ namespace {
 constexpr int kAttnWarps = 4;
 constexpr int kMaxRows = 64;
 
+// Scratch of the decode kernel on num_ctas CTAs: two pair partials per CTA
+// (query columns: attn_cols).
+__host__ __device__ constexpr size_t decode_partials_floats(int num_ctas, int n_rep, int hd) {
+  return (size_t)num_ctas * 2 * (n_rep < 4 ? 4 : n_rep) * (hd + 2);
+}
+
 // ring stages per warp: two CTAs of 4 warps per SM keep ~190 KB of fp16 K/V in flight per SM
 __host__ __device__ constexpr int attn_ring(int hd, int f16) { return hd == 128 ? (f16 ? 3 : 1) : 3; }
 
@@ -93,6 +99,9 @@ __device__ __forceinline__ void tma_load_2d(void* smem_dst, const CUtensorMap* m
       : "memory");
 }
 
+__device__ __forceinline__ void named_bar_sync(int id, int threads) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
+}
 __device__ __forceinline__ void ldsm_x4(uint32_t r[4], const void* p) {
   asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
                : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
@@ -128,6 +137,13 @@ __device__ __forceinline__ void attn_stamp(const AttnArgs& a, int slot) {
     asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
     a.dbg_ts[(size_t)blockIdx.x * 8 + slot] = t;
   }
+}
+
+// Row r belongs to a prompt chunk: a run of consecutive rows of one tenant at
+// consecutive positions, at least two rows long.
+__device__ __forceinline__ bool row_in_chunk(const int* rt, const int* rp, int n, int r) {
+  return (r > 0 && rt[r - 1] == rt[r] && rp[r - 1] + 1 == rp[r]) ||
+         (r + 1 < n && rt[r + 1] == rt[r] && rp[r] + 1 == rp[r + 1]);
 }
 
 struct UnitInfo {
@@ -183,6 +199,10 @@ __global__ void __launch_bounds__(kAttnWarps * 32) attn_kernel(const __grid_cons
     long long acc = 0;
     int pmin = 0x7fffffff, ng = 0;
     for (int r = 0; r < a.n_rows;) {
+      if (a.skip_chunked && row_in_chunk(s_rt, s_rp, a.n_rows, r)) {  // the prompt-chunk kernel's row
+        ++r;
+        continue;
+      }
       int n = 1;
       while (n < RG && r + n < a.n_rows && s_rt[r + n] == s_rt[r] && s_rp[r + n] == s_rp[r + n - 1] + 1)
         ++n;
@@ -736,6 +756,411 @@ __global__ void __launch_bounds__(kAttnWarps * 32) attn_kernel(const __grid_cons
       mbar_wait(&mybars[k % NSW], (k / NSW) & 1, a.err, DEV_TIMEOUT_DRAIN);
 }
 
+// ---------------------------------------------------------------------------
+// Prompt-chunk attention (fp16 pools, n_rep 8). The rows of a chunk (a
+// run of consecutive positions of one tenant, as a prefill step or a prompt
+// chunk in a mixed step has) share their tenant's K/V pages, so the query
+// vectors (row, head) of one kv head become the M dimension of the MMAs:
+// 16 per warp, 64 per item (chunk, kv head, 64-vector tile). An item's pages
+// (up to its last row's position) are cut into segments of SEG pages, SEG
+// chosen per launch so that there are about two units (item, segment) per
+// CTA; a unit streams its pages once through a shared ring (TMA boxes,
+// 128-byte swizzle, a producer warp) for all 64 vectors:
+//   S = Q K^T   mma m16n8k16, A = Q as fp16 hi + lo (~22 bits, scale and
+//               log2 e folded in), B = K straight from the ldmatrix fragments;
+//   online softmax per vector in fp32 (row maxima over the quad, raised
+//               lazily by warp vote), causal limit = the vector's position;
+//   O += P V    A = P from the S accumulators (hi + lo), B = V by
+//               ldmatrix.trans.
+// A single-segment item is written out directly; otherwise each unit leaves
+// (O, m, l) in its slot and the last unit of the item to finish merges the
+// slots in segment order (deterministic). Results go out as fp32 rows and / or
+// the o-proj's activation fragments. At n_rep 8 a 64-row chunk reads each kv
+// head's pages 8 times instead of 64.
+// ---------------------------------------------------------------------------
+constexpr int kChunkWarps = 4;                // consumers; warp kChunkWarps streams the pages
+constexpr int kChunkVecs = 16 * kChunkWarps;  // query vectors per item
+constexpr int kChunkStages = 6;
+constexpr int kChunkCounterOff = 16384;       // item counters, past the decode kernel's pair counters
+
+// Items of one launch for n_kv kv heads: per chunk n_kv x ceil(rows * n_rep / 64),
+// at most n_kv x (64 * 8 / 64 + 32) over the <= 32 chunks of <= 64 rows.
+__host__ __device__ constexpr int chunk_max_items(int n_kv) { return n_kv * (kMaxRows * 8 / kChunkVecs + kMaxRows / 2); }
+
+template <int HD>
+__host__ __device__ constexpr int chunk_smem_bytes() {
+  return 1024                                // ring alignment (128-byte swizzle pattern)
+         + kChunkStages * 2 * 16 * HD * 2    // ring: K and V of one page per stage
+         + kChunkVecs * HD * 4               // results of one item
+         + kChunkStages * 2 * 8;             // full / empty barriers
+}
+
+template <int HD, int NREP>
+__global__ void __launch_bounds__((kChunkWarps + 1) * 32, 2) attn_chunk_kernel(const __grid_constant__ AttnArgs a) {
+  constexpr int BLK = 16 * HD * 2, STAGE = 2 * BLK, NS = kChunkStages, KS = HD / 16;
+  extern __shared__ __align__(128) uint8_t smem_raw[];
+  uint8_t* ring = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  float* ofin = reinterpret_cast<float*>(ring + NS * STAGE);
+  uint64_t* full = reinterpret_cast<uint64_t*>(ofin + kChunkVecs * HD);
+  uint64_t* empty = full + NS;
+  constexpr int kTiles = kMaxRows * NREP / kChunkVecs;  // tiles of a chunk of at most kMaxRows rows
+  __shared__ int s_rt[kMaxRows], s_rp[kMaxRows], c_row0[kMaxRows / 2], c_nr[kMaxRows / 2];
+  // units: chunk-major, then kv head, then tile, then segment. c_u0: units before
+  // the chunk; c_hu: units of one kv head of it; t_u0: units before tile t within
+  // one kv head; t_np: the tile's pages
+  __shared__ int c_u0[kMaxRows / 2 + 1], c_hu[kMaxRows / 2], c_nt[kMaxRows / 2];
+  __shared__ int t_u0[kMaxRows / 2][kTiles + 1], t_np[kMaxRows / 2][kTiles];
+  __shared__ int s_nc, s_seg, s_last;
+  __shared__ float frag_scratch[16];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int n_kv = a.kv.n_kv;
+  const int G = gridDim.x;
+  float* partials = a.partials + decode_partials_floats(G, NREP, HD);  // past the decode kernel's
+  int32_t* counters = a.counters + kChunkCounterOff;
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < NS; ++i) {
+      mbar_init(&full[i], 1);
+      mbar_init(&empty[i], kChunkWarps);
+    }
+    fence_barrier_init();
+  }
+  pdl_launch_dependents();
+  // rows, queries and the chunk's own K/V come from the kernels before this one
+  pdl_wait();
+  for (int i = threadIdx.x; i < a.n_rows; i += blockDim.x) {
+    s_rt[i] = a.row_tenant[i];
+    s_rp[i] = a.row_pos[i];
+  }
+  __syncthreads();
+  struct Item {
+    int row0, tenant, kvh, v0, nv, npages;  // vectors v0 .. v0 + nv of the chunk (v = row * NREP + rep)
+  };
+  if (threadIdx.x == 0) {
+    int nc = 0;
+    long long total = 0;
+    for (int r = 0; r < a.n_rows;) {
+      if (!row_in_chunk(s_rt, s_rp, a.n_rows, r)) {
+        ++r;
+        continue;
+      }
+      int n = 1;
+      while (r + n < a.n_rows && s_rt[r + n] == s_rt[r] && s_rp[r + n] == s_rp[r + n - 1] + 1) ++n;
+      c_row0[nc] = r;
+      c_nr[nc] = n;
+      c_nt[nc] = (n * NREP + kChunkVecs - 1) / kChunkVecs;
+      for (int t = 0; t < c_nt[nc]; ++t) {
+        const int vl = min((t + 1) * kChunkVecs, n * NREP) - 1;  // the tile's last vector
+        t_np[nc][t] = (s_rp[r + vl / NREP] >> 4) + 1;
+        total += (long long)n_kv * t_np[nc][t];
+      }
+      ++nc;
+      r += n;
+    }
+    // segment length: about two units per CTA, at least 4 pages
+    const int seg = max(4, (int)((total + 2LL * G - 1) / (2LL * G)));
+    int u = 0;
+    for (int ci = 0; ci < nc; ++ci) {
+      c_u0[ci] = u;
+      int hu = 0;
+      for (int t = 0; t < c_nt[ci]; ++t) {
+        t_u0[ci][t] = hu;
+        hu += (t_np[ci][t] + seg - 1) / seg;
+      }
+      t_u0[ci][c_nt[ci]] = hu;
+      c_hu[ci] = hu;
+      u += n_kv * hu;
+    }
+    c_u0[nc] = u;
+    s_nc = nc;
+    s_seg = seg;
+  }
+  __syncthreads();
+  const int n_chunks = s_nc, seg = s_seg, n_units = c_u0[n_chunks];
+  // unit -> item, its id (for the merge counter), segments, first and end page
+  auto unit_at = [&](int u, Item& I, int& item_id, int& nseg, int& seg0, int& p0, int& p1) {
+    int ci = 0;
+    while (ci + 1 < n_chunks && c_u0[ci + 1] <= u) ++ci;
+    const int local = u - c_u0[ci], hu = c_hu[ci];
+    I.kvh = local / hu;
+    const int r = local % hu;
+    int t = 0;
+    while (t + 1 < c_nt[ci] && t_u0[ci][t + 1] <= r) ++t;
+    I.row0 = c_row0[ci];
+    I.tenant = s_rt[I.row0];
+    I.v0 = t * kChunkVecs;
+    I.nv = min(kChunkVecs, c_nr[ci] * NREP - I.v0);
+    I.npages = t_np[ci][t];
+    seg0 = c_u0[ci] + I.kvh * hu + t_u0[ci][t];  // the item's first unit
+    nseg = t_u0[ci][t + 1] - t_u0[ci][t];
+    item_id = (ci * n_kv + I.kvh) * kTiles + t;  // < 32 * n_kv * 8 <= 16384 counters (n_kv <= 64)
+    p0 = (u - seg0) * seg;
+    p1 = min(I.npages, p0 + seg);
+  };
+
+  if (warp == kChunkWarps) {
+    // ---- producer: the pages of this CTA's units, in order, through the ring
+    if (lane == 0) {
+      uint32_t issued = 0;
+      bool ok = true;
+      for (int u = blockIdx.x; u < n_units && ok; u += G) {
+        Item I;
+        int item_id, nseg, seg0, p0, p1;
+        unit_at(u, I, item_id, nseg, seg0, p0, p1);
+        const int32_t* pt = a.kv.ptab + (size_t)I.tenant * a.kv.ptab_stride;
+        for (int p = p0; p < p1; ++p) {
+          const int s = issued % NS;
+          if (issued >= (uint32_t)NS) {
+            ok = mbar_wait(&empty[s], ((issued / NS) - 1) & 1, a.err, DEV_TIMEOUT_EMPTY);
+            if (!ok) break;
+          }
+          const int page = pt[p];
+          mbar_arrive_expect_tx(&full[s], 2 * BLK);
+          const int yk = (((page * a.kv.n_layers + a.layer) * 2) * n_kv + I.kvh) * 16;
+#pragma unroll
+          for (int which = 0; which < 2; ++which)
+#pragma unroll
+            for (int b = 0; b < HD / 64; ++b)
+              tma_load_2d(ring + s * STAGE + which * BLK + b * 2048, &a.kv_tmap, b * 64, yk + which * n_kv * 16,
+                          &full[s]);
+          ++issued;
+        }
+      }
+      // every issued copy lands before the CTA may exit (the consumers may have stopped early)
+      const uint32_t first = issued > (uint32_t)NS ? issued - NS : 0u;
+      for (uint32_t j = first; j < issued; ++j) mbar_wait(&full[j % NS], (j / NS) & 1, a.err, DEV_TIMEOUT_DRAIN);
+    }
+    return;
+  }
+
+  // ---- consumers
+  constexpr int NTH = kChunkWarps * 32;
+  const int g = lane >> 2, c = lane & 3;
+  const int tid = threadIdx.x;
+  const float qscale = a.scale * 1.4426950408889634f;  // scores in base-2 units
+  // this lane's ldmatrix rows in a K block and a V block (addresses formed per use)
+  const int mi = lane >> 3, rk = (lane & 7) + (mi & 1) * 8, rv = (lane & 7) + (mi >> 1) * 8;
+  bool alive = true;
+  uint32_t consumed = 0;
+  for (int u = blockIdx.x; u < n_units; u += G) {
+    Item I;
+    int item_id, nseg, seg0, p0, p1;
+    unit_at(u, I, item_id, nseg, seg0, p0, p1);
+    // this thread's two query vectors: rows g and g + 8 of the warp's 16
+    const int vA = warp * 16 + g, vB = vA + 8;
+    const bool okA = vA < I.nv, okB = vB < I.nv;
+    const int rowA = I.row0 + (I.v0 + vA) / NREP, rowB = I.row0 + (I.v0 + vB) / NREP;
+    const int headA = I.kvh * NREP + (I.v0 + vA) % NREP, headB = I.kvh * NREP + (I.v0 + vB) % NREP;
+    const float* qA = a.q + (size_t)rowA * a.ldq + (size_t)headA * HD;
+    const float* qB = a.q + (size_t)rowB * a.ldq + (size_t)headB * HD;
+    uint32_t qh[KS][4], ql[KS][4];  // A fragments of Q (hi, lo)
+#pragma unroll
+    for (int ks = 0; ks < KS; ++ks)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int d = ks * 16 + 2 * c + ((e & 2) ? 8 : 0);
+        const bool ok = (e & 1) ? okB : okA;
+        const float* qp = (e & 1) ? qB : qA;
+        const float2 v = ok ? *reinterpret_cast<const float2*>(qp + d) : make_float2(0.f, 0.f);
+        pack_hilo(v.x * qscale, v.y * qscale, qh[ks][e], ql[ks][e]);
+      }
+    const int limA = okA ? s_rp[rowA] + 1 : 0, limB = okB ? s_rp[rowB] + 1 : 0;
+    float mA = -INFINITY, mB = -INFINITY, lA = 0.f, lB = 0.f;
+    float o[2 * KS][4];
+#pragma unroll
+    for (int j = 0; j < 2 * KS; ++j) o[j][0] = o[j][1] = o[j][2] = o[j][3] = 0.f;
+    for (int p = p0; p < p1; ++p, ++consumed) {
+      const int s = consumed % NS;
+      if (alive) alive = mbar_wait(&full[s], (consumed / NS) & 1, a.err, DEV_TIMEOUT_FULL);
+      const uint8_t* kb = ring + s * STAGE;
+      const uint8_t* vb = kb + BLK;
+      // S: n-tile t = tokens 8t..8t+7 of the page; hi and lo parts apart
+      float sh[2][4], sl[2][4];
+#pragma unroll
+      for (int t = 0; t < 2; ++t)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) sh[t][e] = sl[t][e] = 0.f;
+#pragma unroll
+      for (int ks = 0; ks < KS; ++ks) {
+        uint32_t kf[4];  // K as an A fragment (tokens x dims) = B fragments of both n-tiles
+        ldsm_x4(kf, kb + swz(rk, ks * 2 + (mi >> 1)));
+        mma_16816(sh[0], qh[ks], kf[0], kf[2]);
+        mma_16816(sl[0], ql[ks], kf[0], kf[2]);
+        mma_16816(sh[1], qh[ks], kf[1], kf[3]);
+        mma_16816(sl[1], ql[ks], kf[1], kf[3]);
+      }
+      // sc[t][e]: vector A (e < 2) or B, token 16p + 8t + 2c + (e & 1)
+      float sc[2][4];
+#pragma unroll
+      for (int t = 0; t < 2; ++t)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const int tok = p * 16 + t * 8 + 2 * c + (e & 1);
+          sc[t][e] = tok < ((e & 2) ? limB : limA) ? sh[t][e] + sl[t][e] : -INFINITY;
+        }
+      float xA = fmaxf(fmaxf(sc[0][0], sc[0][1]), fmaxf(sc[1][0], sc[1][1]));
+      float xB = fmaxf(fmaxf(sc[0][2], sc[0][3]), fmaxf(sc[1][2], sc[1][3]));
+      xA = fmaxf(xA, __shfl_xor_sync(0xffffffffu, xA, 1));
+      xA = fmaxf(xA, __shfl_xor_sync(0xffffffffu, xA, 2));
+      xB = fmaxf(xB, __shfl_xor_sync(0xffffffffu, xB, 1));
+      xB = fmaxf(xB, __shfl_xor_sync(0xffffffffu, xB, 2));
+      if (__any_sync(0xffffffffu, xA > mA || xB > mB)) {
+        const float nA = fmaxf(mA, xA), nB = fmaxf(mB, xB);
+        const float alA = mA == -INFINITY ? 0.f : exp2_fast(mA - nA);
+        const float alB = mB == -INFINITY ? 0.f : exp2_fast(mB - nB);
+        mA = nA;
+        mB = nB;
+        lA *= alA;
+        lB *= alB;
+#pragma unroll
+        for (int j = 0; j < 2 * KS; ++j) {
+          o[j][0] *= alA;
+          o[j][1] *= alA;
+          o[j][2] *= alB;
+          o[j][3] *= alB;
+        }
+      }
+      float pr[2][4];
+#pragma unroll
+      for (int t = 0; t < 2; ++t)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const float m = (e & 2) ? mB : mA;
+          pr[t][e] = sc[t][e] == -INFINITY ? 0.f : exp2_fast(sc[t][e] - m);
+        }
+      lA += (pr[0][0] + pr[0][1]) + (pr[1][0] + pr[1][1]);
+      lB += (pr[0][2] + pr[0][3]) + (pr[1][2] + pr[1][3]);
+      // P as the A fragment (vectors x tokens) of the P V step
+      uint32_t ph[4], pl[4];
+      pack_hilo(pr[0][0], pr[0][1], ph[0], pl[0]);
+      pack_hilo(pr[0][2], pr[0][3], ph[1], pl[1]);
+      pack_hilo(pr[1][0], pr[1][1], ph[2], pl[2]);
+      pack_hilo(pr[1][2], pr[1][3], ph[3], pl[3]);
+#pragma unroll
+      for (int mt = 0; mt < KS; ++mt) {
+        uint32_t vf[4];  // V^T as an A fragment (dims x tokens) = B fragments of two 8-dim n-tiles
+        ldsm_x4_trans(vf, vb + swz(rv, mt * 2 + (mi & 1)));
+        mma_16816(o[2 * mt], ph, vf[0], vf[2]);
+        mma_16816(o[2 * mt], pl, vf[0], vf[2]);
+        mma_16816(o[2 * mt + 1], ph, vf[1], vf[3]);
+        mma_16816(o[2 * mt + 1], pl, vf[1], vf[3]);
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty[s]);
+    }
+    lA += __shfl_xor_sync(0xffffffffu, lA, 1);
+    lA += __shfl_xor_sync(0xffffffffu, lA, 2);
+    lB += __shfl_xor_sync(0xffffffffu, lB, 1);
+    lB += __shfl_xor_sync(0xffffffffu, lB, 2);
+    named_bar_sync(1, NTH);  // the previous unit's results are written out
+    if (nseg == 1) {
+      const float iA = lA > 0.f ? 1.0f / lA : 0.f, iB = lB > 0.f ? 1.0f / lB : 0.f;
+#pragma unroll
+      for (int j = 0; j < 2 * KS; ++j) {
+        const int d = j * 8 + 2 * c;
+        *reinterpret_cast<float2*>(ofin + vA * HD + d) = make_float2(o[j][0] * iA, o[j][1] * iA);
+        *reinterpret_cast<float2*>(ofin + vB * HD + d) = make_float2(o[j][2] * iB, o[j][3] * iB);
+      }
+    } else {
+      // this unit's (O, m, l) per vector into its slot; the item's last unit merges
+      float* slot = partials + (size_t)u * kChunkVecs * (HD + 2);
+#pragma unroll
+      for (int j = 0; j < 2 * KS; ++j) {
+        const int d = j * 8 + 2 * c;
+        __stcg(reinterpret_cast<float2*>(slot + vA * (HD + 2) + d), make_float2(o[j][0], o[j][1]));
+        __stcg(reinterpret_cast<float2*>(slot + vB * (HD + 2) + d), make_float2(o[j][2], o[j][3]));
+      }
+      if (c == 0) {
+        __stcg(reinterpret_cast<float2*>(slot + vA * (HD + 2) + HD), make_float2(mA, lA));
+        __stcg(reinterpret_cast<float2*>(slot + vB * (HD + 2) + HD), make_float2(mB, lB));
+      }
+      named_bar_sync(1, NTH);  // the slot's stores before thread 0's release
+      if (tid == 0) s_last = atom_add_acq_rel(counters + item_id, 1) == nseg - 1;
+      named_bar_sync(1, NTH);
+      if (!s_last) continue;
+      // merge the item's slots in segment order, each thread on its own fragment
+      // positions: per segment one batch of independent L2 loads, then
+      // (M, L, O) <- (M, L, O) and (m, l, o) rescaled to the larger maximum
+      const float* first = partials + (size_t)seg0 * kChunkVecs * (HD + 2);
+      constexpr int JH = KS;  // 8-dim n-tiles per half of the head dimension
+#pragma unroll 1
+      for (int h = 0; h < 2; ++h) {
+        float MA = -INFINITY, MB = -INFINITY, LA = 0.f, LB = 0.f;
+        float acc[JH][4];
+#pragma unroll
+        for (int j = 0; j < JH; ++j) acc[j][0] = acc[j][1] = acc[j][2] = acc[j][3] = 0.f;
+        for (int q = 0; q < nseg; ++q) {
+          const float* sq = first + (size_t)q * kChunkVecs * (HD + 2);
+          const float2 mlA = __ldcg(reinterpret_cast<const float2*>(sq + vA * (HD + 2) + HD));
+          const float2 mlB = __ldcg(reinterpret_cast<const float2*>(sq + vB * (HD + 2) + HD));
+          float2 oa[JH], ob[JH];
+#pragma unroll
+          for (int j = 0; j < JH; ++j) {
+            const int d = (h * JH + j) * 8 + 2 * c;
+            oa[j] = __ldcg(reinterpret_cast<const float2*>(sq + vA * (HD + 2) + d));
+            ob[j] = __ldcg(reinterpret_cast<const float2*>(sq + vB * (HD + 2) + d));
+          }
+          const float nA = fmaxf(MA, mlA.x), nB = fmaxf(MB, mlB.x);
+          const float fA = MA == -INFINITY ? 0.f : exp2_fast(MA - nA), gA = mlA.x == -INFINITY ? 0.f : exp2_fast(mlA.x - nA);
+          const float fB = MB == -INFINITY ? 0.f : exp2_fast(MB - nB), gB = mlB.x == -INFINITY ? 0.f : exp2_fast(mlB.x - nB);
+          MA = nA;
+          MB = nB;
+          LA = LA * fA + mlA.y * gA;
+          LB = LB * fB + mlB.y * gB;
+#pragma unroll
+          for (int j = 0; j < JH; ++j) {
+            acc[j][0] = acc[j][0] * fA + oa[j].x * gA;
+            acc[j][1] = acc[j][1] * fA + oa[j].y * gA;
+            acc[j][2] = acc[j][2] * fB + ob[j].x * gB;
+            acc[j][3] = acc[j][3] * fB + ob[j].y * gB;
+          }
+        }
+        const float iA = LA > 0.f ? 1.0f / LA : 0.f, iB = LB > 0.f ? 1.0f / LB : 0.f;
+#pragma unroll
+        for (int j = 0; j < JH; ++j) {
+          const int d = (h * JH + j) * 8 + 2 * c;
+          *reinterpret_cast<float2*>(ofin + vA * HD + d) = make_float2(acc[j][0] * iA, acc[j][1] * iA);
+          *reinterpret_cast<float2*>(ofin + vB * HD + d) = make_float2(acc[j][2] * iB, acc[j][3] * iB);
+        }
+      }
+      if (tid == 0) counters[item_id] = 0;
+    }
+    named_bar_sync(1, NTH);
+    // whole rows: the tile starts at a multiple of 64 vectors, a multiple of n_rep
+    const int r0 = I.row0 + I.v0 / NREP, nrows = I.nv / NREP;
+    if (a.out)
+      for (int i = tid; i < I.nv * HD; i += NTH) {
+        const int v = I.v0 + i / HD;
+        a.out[(size_t)(I.row0 + v / NREP) * a.ldo + (size_t)(I.kvh * NREP + v % NREP) * HD + i % HD] = ofin[i];
+      }
+    if (a.xout.xi || a.xout.xf)
+      for (int rl = 0; rl < nrows; ++rl)
+        frags_write(ofin + rl * NREP * HD, 1, 0, NREP * HD, 1, I.kvh * NREP * HD, r0 + rl, nullptr, a.xout, a.xf_nt,
+                    frag_scratch, tid, NTH, [] { named_bar_sync(1, kChunkWarps * 32); });
+  }
+}
+
+template <int HD, int NREP>
+cudaError_t launch_chunk_t(const AttnArgs& a, int num_sms, cudaStream_t s, int pdl) {
+  constexpr int smem = chunk_smem_bytes<HD>();
+  static_assert(2 * (smem + 1024) <= 228 * 1024, "two CTAs per SM");
+  auto kern = attn_chunk_kernel<HD, NREP>;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (cudaError_t e = ensure_smem_attr(kern, smem, dev)) return e;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(attn_grid(num_sms));
+  cfg.blockDim = dim3((kChunkWarps + 1) * 32);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, kern, a);
+}
+
 template <int HD, int NREP, int F16, int GR>
 cudaError_t launch_attn_t(const AttnArgs& a, int num_sms, cudaStream_t s, int pdl) {
   constexpr int smem = attn_smem_bytes<HD, NREP, F16, GR>();
@@ -837,13 +1262,28 @@ cudaError_t kv_tensor_map(const KvView& kv, size_t n_pages, CUtensorMap* out) {
   return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
 }
 
-size_t attn_partials_floats(int num_ctas, int n_rep, int hd) {
-  return (size_t)num_ctas * 2 * (n_rep < 4 ? 4 : n_rep) * (hd + 2);  // query columns: attn_cols
+size_t attn_partials_floats(int num_ctas, int n_rep, int hd, int n_kv) {
+  // + the prompt-chunk kernel's unit slots: at most 2 per CTA plus one per item
+  return decode_partials_floats(num_ctas, n_rep, hd) +
+         (size_t)(2 * num_ctas + chunk_max_items(n_kv)) * kChunkVecs * (hd + 2);
 }
 
-cudaError_t attn_launch(const AttnArgs& a, int num_sms, cudaStream_t s, int pdl) {
-  if (a.n_rows < 1 || a.n_rows > kMaxRows) return cudaErrorInvalidValue;
-  const int nrep = a.n_heads / a.kv.n_kv;
+cudaError_t attn_launch(const AttnArgs& a_in, int num_sms, cudaStream_t s, int pdl, int* launches) {
+  if (a_in.n_rows < 1 || a_in.n_rows > kMaxRows) return cudaErrorInvalidValue;
+  const int nrep = a_in.n_heads / a_in.kv.n_kv;
+  AttnArgs a = a_in;
+  // n_rep 8 only: at n_rep 4 the decode kernel packs a row's hi and lo query
+  // parts into one MMA, so both need the same MMAs per page and the rows of a
+  // chunk already share the pages through L2 (bench.py --case chunk)
+  if (a.group_rows && a.kv.f16 && nrep == 8 && (a.kv.hd == 64 || a.kv.hd == 128) &&
+      a.kv.n_kv <= 64) {
+    // prompt chunks on their own kernel; the decode kernel takes the other rows
+    cudaError_t e = a.kv.hd == 128 ? launch_chunk_t<128, 8>(a, num_sms, s, pdl) : launch_chunk_t<64, 8>(a, num_sms, s, pdl);
+    if (e != cudaSuccess) return e;
+    if (launches) ++*launches;
+    a.skip_chunked = 1;
+  }
+  if (launches) ++*launches;
   if (a.kv.hd == 128) {
     return a.kv.f16 ? launch_attn_hd<128, 1>(a, nrep, num_sms, s, pdl) : launch_attn_hd<128, 0>(a, nrep, num_sms, s, pdl);
   } else if (a.kv.hd == 64) {

@@ -40,13 +40,21 @@ struct AttnArgs {
   // 1: when the pairs are few and even enough, each CTA takes one (row, kv head)
   // pair whole instead of an even share of all pages (no cross-CTA merge)
   int32_t whole_pairs = 1;
+  // set by attn_launch when a prompt-chunk kernel takes the rows that belong to
+  // runs of consecutive positions of one tenant: the decode kernel skips them
+  int32_t skip_chunked = 0;
   unsigned long long* dbg_ts = nullptr;  // measurement hook: [cta][8] %globaltimer stamps (or null)
 };
 
-// Partial-result scratch for a launch on num_ctas CTAs (attn_grid).
-size_t attn_partials_floats(int num_ctas, int n_rep, int hd);
+// Partial-result scratch for a launch on num_ctas CTAs (attn_grid) over a pool
+// of n_kv kv heads.
+size_t attn_partials_floats(int num_ctas, int n_rep, int hd, int n_kv);
 int attn_grid(int num_sms);
-cudaError_t attn_launch(const AttnArgs& a, int num_sms, cudaStream_t s, int pdl);
+// Enqueues the attention of a step: one kernel, or (fp16 pools, n_rep 4 or 8,
+// group_rows) the prompt-chunk kernel for runs of consecutive rows of one
+// tenant followed by the decode kernel for the other rows. *launches (if
+// given) is increased by the number of kernels enqueued.
+cudaError_t attn_launch(const AttnArgs& a, int num_sms, cudaStream_t s, int pdl, int* launches = nullptr);
 
 // Standalone append of k/v rows ([n_rows][n_kv*hd] fp32) at (tenant, pos).
 cudaError_t kv_append_launch(const KvView& kv, int layer, int n_rows, const int32_t* row_tenant,

@@ -679,9 +679,8 @@ int enqueue_layer(Ctx* c, Model& M, int l, int m, const int32_t* d_tenant, const
   at.group_rows = c->attn_group && c->step_grouped;
   at.whole_pairs = c->attn_whole;
   if (c->gemv_dbg & 2) at.dbg_ts = c->attn_ts.as<unsigned long long>();
-  RB_CUDA(attn_launch(at, c->num_sms, c->stream, c->pdl ? 1 : 0));
+  RB_CUDA(attn_launch(at, c->num_sms, c->stream, c->pdl ? 1 : 0, launches));
   prof_mark(c, PROF_ATTN);
-  if (launches) ++*launches;
   // o-proj + residual; writes fragments of x * ffn_norm
   GemvArgs ao = base_args(c, L.o, m);
   ao.xin = M.fo.view();
@@ -895,7 +894,7 @@ int pool_create(rb_ctx* c, int n_layers, int n_kv, int hd, int kv_dtype, int n_p
   for (int i = n_pages - 1; i >= 0; --i) P->free_list.push_back(i);
   P->tenants.resize(max_tenants);
   const int n_rep_max = 8;
-  if (int rc = ensure_attn_partials(c, attn_partials_floats(attn_grid(c->num_sms), n_rep_max, hd))) return rc;
+  if (int rc = ensure_attn_partials(c, attn_partials_floats(attn_grid(c->num_sms), n_rep_max, hd, n_kv))) return rc;
   c->pools.push_back(std::move(P));
   return (int)c->pools.size() - 1;
 }
@@ -1504,16 +1503,17 @@ int32_t rb_attention_forward(rb_ctx* c, int32_t pool, uint32_t layer, uint32_t n
   at.group_rows = c->attn_group && rows_grouped(rp);
   at.whole_pairs = c->attn_whole;
   RB_CUDA(cudaEventRecord(c->ev0, c->stream));
-  RB_CUDA(attn_launch(at, c->num_sms, c->stream, 0));
+  int n_launch = 0;
+  RB_CUDA(attn_launch(at, c->num_sms, c->stream, 0, &n_launch));
   RB_CUDA(cudaEventRecord(c->ev1, c->stream));
   if (!(flags & RB_PTR_DEVICE)) RB_CUDA(cudaMemcpyAsync(out, dout, qbytes, cudaMemcpyDeviceToHost, c->stream));
   if ((flags & RB_PTR_DEVICE) && (flags & RB_ASYNC)) {
-    c->last_launches = 1;
+    c->last_launches = n_launch;
     return (int32_t)(n_rows * n_heads * P->hd);
   }
   if (int rc = sync_ctx(c)) return rc;
   cudaEventElapsedTime(&c->last_ms, c->ev0, c->ev1);
-  c->last_launches = 1;
+  c->last_launches = n_launch;
   return (int32_t)(n_rows * n_heads * P->hd);
 }
 

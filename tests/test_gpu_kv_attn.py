@@ -131,7 +131,9 @@ def test_attention_append_then_attend(ctx, oracle):
 @pytest.mark.parametrize("n_heads,n_kv,hd,kv_dtype", [
     (32, 32, 128, "f16"),  # MHA: 4 rows per pair
     (16, 8, 64, "f16"),    # GQA 2: 2 rows per pair
-    (32, 8, 128, "f16"),   # GQA 4: one row per pair
+    (32, 8, 128, "f16"),   # GQA 4: one row per pair (hi and lo query parts packed)
+    (32, 4, 64, "f16"),    # GQA 8, hd 64: the prompt-chunk kernel
+    (64, 8, 128, "f16"),   # GQA 8, hd 128 (configs[4] heads): the prompt-chunk kernel
     (32, 4, 64, "f32"),    # fp32 pools: one row per pair
 ])
 def test_prompt_chunk_rows_share_pages(ctx, oracle, n_heads, n_kv, hd, kv_dtype):
@@ -160,6 +162,41 @@ def test_prompt_chunk_rows_share_pages(ctx, oracle, n_heads, n_kv, hd, kv_dtype)
     positions = list(range(15, 28)) + list(range(L - 6, L)) + [7] + [100, 101, 103]
     q = rng.normal(size=(len(tenants), n_heads * hd)).astype(np.float32)
     out = pool.attention_forward(0, tenants, q, n_heads, 1 / np.sqrt(hd), positions=positions)
+    for i, (t, p) in enumerate(zip(tenants, positions)):
+        rk, rv = ks[t].current_data()
+        n = (p + 1) * n_kv * hd
+        exp = _oracle_attn(O, rk[:n], rv[:n], q[i], p, n_heads, n_kv, hd)
+        err = np.abs(out[i] - exp)
+        assert err.max() <= 2e-3 and np.all(err <= 1e-3 * np.abs(exp) + 2e-5), (i, t, p, err.max())
+
+
+@pytest.mark.parametrize("n_heads,n_kv,hd", [(32, 8, 128), (64, 8, 128), (32, 4, 64)])
+def test_prompt_chunk_kernel_long_chunk(ctx, oracle, n_heads, n_kv, hd):
+    """A 61-row prompt chunk deep into a long context (several 64-vector tiles
+    per kv head, ~60 pages, split into segments over CTAs and merged) beside
+    decode rows of other tenants in one call: at GQA 8 the chunk rows run on the
+    prompt-chunk kernel and the others on the decode kernel; every row against
+    the oracle at the attention bound."""
+    import realm_b200 as rb
+    O = oracle
+    rng = np.random.default_rng(hd + n_heads)
+    L = 1000
+    pool = ctx.kv_pool(1, n_kv, hd, rb.F16, n_pages=3 * (L // 16 + 2), max_tenants=3, max_seq=1024)
+    pool.shuffle(9)
+    ks = []
+    for t in range(3):
+        pool.create(t)
+        k = rng.normal(size=(L, n_kv, hd)).astype(np.float32)
+        v = rng.normal(size=(L, n_kv, hd)).astype(np.float32)
+        pool.append(t, 0, k, v)
+        r = O.KVCache(1024, n_kv, hd, kv_fp16=True)
+        r.append(k, v)
+        ks.append(r)
+    tenants = [1] + [0] * 61 + [2, 1]
+    positions = [500] + list(range(L - 61, L)) + [L - 1, 17]
+    q = rng.normal(size=(len(tenants), n_heads * hd)).astype(np.float32)
+    out = pool.attention_forward(0, tenants, q, n_heads, 1 / np.sqrt(hd), positions=positions)
+    assert ctx.last_forward_launches() == (2 if n_heads // n_kv == 8 else 1)
     for i, (t, p) in enumerate(zip(tenants, positions)):
         rk, rv = ks[t].current_data()
         n = (p + 1) * n_kv * hd

@@ -33,14 +33,21 @@ __host__ __device__ constexpr size_t decode_partials_floats(int num_ctas, int n_
   return (size_t)num_ctas * 2 * (n_rep < 4 ? 4 : n_rep) * (hd + 2);
 }
 
-// ring stages per warp: two CTAs of 4 warps per SM keep ~190 KB of fp16 K/V in flight per SM
-__host__ __device__ constexpr int attn_ring(int hd, int f16) { return hd == 128 ? (f16 ? 3 : 1) : 3; }
+// ring stages per warp: ~190 KB of fp16 K/V in flight per SM. At hd 128 with at
+// most 2 query heads per kv head, three CTAs of 4 warps fit per SM with two
+// stages each (the same bytes as two CTAs with three stages, with half as many
+// warps again to hide latency); with 4-8 heads the larger merge buffers leave
+// room for two CTAs, with three stages each.
+__host__ __device__ constexpr int attn_ring(int hd, int f16, int nrep) {
+  return hd == 128 ? (f16 ? (nrep <= 2 ? 2 : 3) : 1) : 3;
+}
 
-template <int HD, int F16>
+
+template <int HD, int F16, int NREP = 1>
 struct AttnCfg {
   static constexpr int ESZ = F16 ? 2 : 4;
   static constexpr int BLK = 16 * HD * ESZ;  // one page of one kv head (K or V), bytes
-  static constexpr int NSW = attn_ring(HD, F16);
+  static constexpr int NSW = attn_ring(HD, F16, NREP);
   // fp16 blocks arrive by TMA as HD / 64 boxes of 16 rows x 128 bytes with
   // 128-byte swizzle (each box 1024-byte aligned), fp32 blocks by a plain bulk copy
   static constexpr int SBLK = BLK;
@@ -60,11 +67,11 @@ __host__ __device__ constexpr int attn_cols() {
 template <int HD, int NREP, int F16, int GR>
 __host__ __device__ constexpr int attn_smem_bytes() {
   return 1024                                                           // ring alignment
-         + kAttnWarps * AttnCfg<HD, F16>::NSW * AttnCfg<HD, F16>::STAGE  // rings
+         + kAttnWarps * AttnCfg<HD, F16, NREP>::NSW * AttnCfg<HD, F16, NREP>::STAGE  // rings
          + attn_cols<NREP, F16, GR>() * HD * 4                              // q
          + kAttnWarps * (NREP > 8 ? NREP : 8) * 16 * 4                 // probabilities
          + kAttnWarps * attn_cols<NREP, F16, GR>() * (HD + 2) * 4           // warp merge
-         + kAttnWarps * AttnCfg<HD, F16>::NSW * 8                      // mbarriers
+         + kAttnWarps * AttnCfg<HD, F16, NREP>::NSW * 8                // mbarriers
          + kMaxRows * 8 + 64;                                          // row tables
 }
 
@@ -153,8 +160,8 @@ struct UnitInfo {
 };
 
 template <int HD, int NREP, int F16, int GR>
-__global__ void __launch_bounds__(kAttnWarps * 32) attn_kernel(const __grid_constant__ AttnArgs a) {
-  using C = AttnCfg<HD, F16>;
+__global__ void __launch_bounds__(kAttnWarps * 32, 3) attn_kernel(const __grid_constant__ AttnArgs a) {
+  using C = AttnCfg<HD, F16, NREP>;
   constexpr int NSW = C::NSW;
   constexpr int NC = attn_cols<NREP, F16, GR>(), RG = NC / NREP;  // query columns, rows per group
   extern __shared__ __align__(128) uint8_t smem_raw[];
@@ -1149,7 +1156,7 @@ cudaError_t launch_chunk_t(const AttnArgs& a, int num_sms, cudaStream_t s, int p
   cudaGetDevice(&dev);
   if (cudaError_t e = ensure_smem_attr(kern, smem, dev)) return e;
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(attn_grid(num_sms));
+  cfg.gridDim = dim3(2 * num_sms);
   cfg.blockDim = dim3((kChunkWarps + 1) * 32);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = s;
@@ -1169,9 +1176,15 @@ cudaError_t launch_attn_t(const AttnArgs& a, int num_sms, cudaStream_t s, int pd
   cudaGetDevice(&dev);
   if (cudaError_t e = ensure_smem_attr(kern, smem, dev)) return e;
   static_assert(smem <= 227 * 1024, "shared memory of one CTA");
-  // two CTAs per SM when they fit (228 KB per SM, 1 KB reserved per CTA); never
-  // more CTAs than attn_grid() allows for
-  const int per_sm = 2 * (smem + 1024) <= 228 * 1024 ? 2 : 1;
+  // as many CTAs per SM as are resident at once (static shared memory and
+  // registers included), at most attn_grid() / num_sms
+  static int per_sm_cache[64] = {};
+  int per_sm = dev < 64 ? per_sm_cache[dev] : 0;
+  if (per_sm == 0) {
+    if (cudaError_t e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kAttnWarps * 32, smem)) return e;
+    per_sm = per_sm < 1 ? 1 : per_sm > 3 ? 3 : per_sm;
+    if (dev < 64) per_sm_cache[dev] = per_sm;
+  }
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(num_sms * per_sm);
   cfg.blockDim = dim3(kAttnWarps * 32);
@@ -1235,7 +1248,7 @@ __global__ void kv_gather_kernel(const KvView kv, int layer, int tenant, int len
 
 }  // namespace
 
-int attn_grid(int num_sms) { return 2 * num_sms; }  // upper bound on the attention grid
+int attn_grid(int num_sms) { return 3 * num_sms; }  // upper bound on the attention grids
 
 cudaError_t kv_tensor_map(const KvView& kv, size_t n_pages, CUtensorMap* out) {
   using EncodeFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,

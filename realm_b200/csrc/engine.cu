@@ -308,6 +308,7 @@ struct Ctx {
   int attn_group = 1;       // RB_ATTN_GROUP=0: one attention pair per row (no K/V sharing in prefill chunks)
   bool step_grouped = false;  // the step has consecutive rows of one tenant (a prompt chunk)
   int attn_whole = 1;         // RB_ATTN_WHOLE=0: always split attention pages evenly over the CTAs
+  bool merge_v = true;        // RB_MERGE_V=0: v runs as a phase of its own after q|k
   DevBuf qg_part;      // tcgen05 GEMM partial sums
   DevBuf qg_bprep;     // tcgen05 exact-weight GEMM: activation planes
   // failure-detection test hook (rb_test_fail_next_grid_barrier): when nonzero,
@@ -645,8 +646,19 @@ int enqueue_layer(Ctx* c, Model& M, int l, int m, const int32_t* d_tenant, const
   a.row_tenant = d_tenant;
   a.row_pos = d_pos;
   a.kv = P.view();
+  // v joins the q|k phase as its second weight (one stream-K split, one tail)
+  // unless the step runs its Q4_K projections on the tcgen05 GEMM
+  const bool merge_v = c->merge_v && !L.v_fused && !c->gemm_step && L.v.k == L.qk.k &&
+                       (L.v.dtype == L.qk.dtype || (L.qk.dtype == DT_Q4_K && L.v.dtype == DT_Q6_K));
+  if (merge_v) {
+    a.w2 = L.v.tiled.as<uint8_t>();
+    a.dtype2 = L.v.dtype;
+    a.n2 = L.v.n;
+    a.n_rg2 = L.v.n_rg;
+    a.qkv_row0_2 = (Hq + Hkv) * hd;
+  }
   if (int rc = chain_add(c, a, true, launches)) return rc;
-  if (!L.v_fused) {
+  if (!L.v_fused && !merge_v) {
     GemvArgs av = a;
     av.w = L.v.tiled.as<uint8_t>();
     av.dtype = L.v.dtype;
@@ -992,6 +1004,7 @@ int32_t rb_ctx_create(const rb_config* cfg, rb_ctx** out) {
   if (const char* d = getenv("RB_CHAIN_PREFETCH")) c->chain_prefetch = atoi(d);
   if (const char* d = getenv("RB_ATTN_GROUP")) c->attn_group = atoi(d) != 0;
   if (const char* d = getenv("RB_ATTN_WHOLE")) c->attn_whole = atoi(d) != 0;
+  if (const char* d = getenv("RB_MERGE_V")) c->merge_v = atoi(d) != 0;
   RB_CUDA(cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking));
   RB_CUDA(cudaEventCreate(&c->ev0));
   RB_CUDA(cudaEventCreate(&c->ev1));

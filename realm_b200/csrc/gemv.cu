@@ -320,10 +320,15 @@ __device__ __forceinline__ void load_resid(const GemvArgs& a, int rg, int warp, 
     }
 }
 
+// rg: row group within the phase's unit space; rows of a second weight
+// (rg >= a.n_rg, QKV only) are numbered from its own first row.
 template <int NT>
-__device__ void epilogue(const GemvArgs& a, int p, int rg, int warp, int lane, float acc[NT][4],
+__device__ void epilogue(const GemvArgs& a, int p, int rg_u, int warp, int lane, float acc[NT][4],
                          const float* inv_rms, float* red, float* T, const float (*xpre)[4] = nullptr) {
   constexpr int LD = 8 * NT;
+  const bool part2 = rg_u >= a.n_rg;
+  const int rg = part2 ? rg_u - a.n_rg : rg_u;
+  const int a_n = part2 ? a.n2 : a.n;
   const int g = lane >> 2, c = lane & 3;
   const int tid = warp * 32 + lane;
   const int row0 = rg * kRowGroup + warp * kTileRows + g;  // rows row0 and row0+8
@@ -342,7 +347,7 @@ __device__ void epilogue(const GemvArgs& a, int p, int rg, int warp, int lane, f
 #pragma unroll
       for (int r = 0; r < 4; ++r) {
         const int t = nt * 8 + 2 * c + (r & 1), row = row0 + ((r & 2) ? 8 : 0);
-        if (t < a.m && row < a.n) a.y[(size_t)t * a.ldy + row] = acc[nt][r];
+        if (t < a.m && row < a_n) a.y[(size_t)t * a.ldy + row] = acc[nt][r];
       }
     }
   } else if (a.epi == EPI_SWIGLU) {
@@ -356,7 +361,7 @@ __device__ void epilogue(const GemvArgs& a, int p, int rg, int warp, int lane, f
         const float gt = acc[nt][r], up = acc[nt][r + 2];
         const float sig = 1.0f / (1.0f + expf(-gt));
         const float h = (gt * sig) * up;
-        const bool ok = t < a.m && 2 * (rg * (kRowGroup / 2) + ol) < a.n;
+        const bool ok = t < a.m && 2 * (rg * (kRowGroup / 2) + ol) < a_n;
         T[t * kTLd + ol] = ok ? h : 0.f;
         if (ok && a.y) a.y[(size_t)t * a.ldy + rg * (kRowGroup / 2) + ol] = h;
       }
@@ -387,7 +392,7 @@ __device__ void epilogue(const GemvArgs& a, int p, int rg, int warp, int lane, f
         const int t = nt * 8 + 2 * c + (r & 1), row = row0 + ((r & 2) ? 8 : 0);
         const int rl = row - rg * kRowGroup;
         float tv = 0.f;
-        if (t < a.m && row < a.n) {
+        if (t < a.m && row < a_n) {
           const float v = xv[nt][r] + acc[nt][r];
           a.resid[(size_t)t * a.ldr + row] = v;
           sq[nt][r & 1] += v * v;
@@ -429,7 +434,7 @@ __device__ void epilogue(const GemvArgs& a, int p, int rg, int warp, int lane, f
 #pragma unroll
       for (int r = 0; r < 4; ++r) {
         const int t = nt * 8 + 2 * c + (r & 1), row = row0 + ((r & 2) ? 8 : 0);
-        if (t < a.m && row < a.n) {
+        if (t < a.m && row < a_n) {
           if (a.y) a.y[(size_t)t * a.ldy + row] = acc[nt][r];
           const unsigned long long key =
               ((unsigned long long)float_order_key(acc[nt][r]) << 32) | (unsigned long long)row;
@@ -457,10 +462,10 @@ __device__ void epilogue(const GemvArgs& a, int p, int rg, int warp, int lane, f
       for (int r = 0; r < 4; ++r) {
         const int t = nt * 8 + 2 * c + (r & 1);
         const int row = row0 + ((r & 2) ? 8 : 0);
-        const int grow = a.qkv_row0 + row;
+        const int grow = (part2 ? a.qkv_row0_2 : a.qkv_row0) + row;
         const bool is_v = grow >= a.n_q_rows + a.n_k_rows;
         const float partner = __shfl_xor_sync(0xffffffffu, acc[nt][r], 4);
-        const bool valid = t < a.m && row < a.n;
+        const bool valid = t < a.m && row < a_n;
         if (!valid) continue;
         const int pos = a.row_pos[t];
         float v = acc[nt][r];
@@ -527,7 +532,7 @@ struct PhaseRange {
 };
 __device__ __forceinline__ PhaseRange phase_range(const GemvArgs& a) {
   PhaseRange r;
-  r.U = (long long)a.n_rg * a.nsb;
+  r.U = (long long)(a.n_rg + a.n_rg2) * a.nsb;
   r.Gp = r.U < (long long)gridDim.x ? (int)r.U : (int)gridDim.x;
   if ((int)blockIdx.x < r.Gp) {
     r.u0 = r.U * blockIdx.x / r.Gp;
@@ -653,14 +658,26 @@ __device__ __forceinline__ void finish_segment(const GemvArgs& a, int p, int n_p
 }
 
 template <int DT, int NT>
+__device__ __forceinline__ void tile_dt(const uint8_t* st, int warp, int lane, float (&acc)[NT][4]) {
+  constexpr int UB = unit_bytes(DT), TB = tile_bytes(DT);
+  const uint8_t* tile = st + warp * TB;
+  const uint8_t* xb = st + UB;
+  if (DT == DT_Q4_K)
+    tile_q4k<NT>(tile, xb, xb + NT * kXiSbBytes, xb + NT * (kXiSbBytes + kX3SbBytes),
+                 xb + NT * (kXiSbBytes + kX3SbBytes + kXcSbBytes), lane, acc);
+  else if (DT == DT_Q6_K) tile_q6k<NT>(tile, xb, lane, acc);
+  else tile_q80<NT>(tile, xb, lane, acc);
+}
+
+// DT: format of the phase's weight; DT2: of its second weight (row groups
+// from a.n_rg on), DT2 == DT when there is none.
+template <int DT, int DT2, int NT>
 __device__ __forceinline__ void consume_phase(const GemvArgs& a, int p, int n_phases, const PhaseRange& pr, uint8_t* ring, int S,
                                               int SB, uint64_t* full, uint64_t* empty, float* inv_rms, float* red,
                                               float* T, RingPos& rp, bool& alive,
                                               const unsigned long long* gbar /* this barrier's counter */,
                                               bool wait_grid,
                                               unsigned long long bar_target, uint32_t grid_spin) {
-  constexpr int UB = unit_bytes(DT);
-  constexpr int TB = tile_bytes(DT);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int tid = threadIdx.x;
   if (tid == 0) RB_TS(p, 0);
@@ -702,13 +719,8 @@ __device__ __forceinline__ void consume_phase(const GemvArgs& a, int p, int n_ph
     if (i == 0 && tid == 0) RB_TS(p, 2);
     if (alive && !(a.dbg & 1)) {
       const uint8_t* st = ring + (size_t)s * SB;
-      const uint8_t* tile = st + warp * TB;
-      const uint8_t* xb = st + UB;
-      if (DT == DT_Q4_K)
-        tile_q4k<NT>(tile, xb, xb + NT * kXiSbBytes, xb + NT * (kXiSbBytes + kX3SbBytes),
-                     xb + NT * (kXiSbBytes + kX3SbBytes + kXcSbBytes), lane, acc);
-      else if (DT == DT_Q6_K) tile_q6k<NT>(tile, xb, lane, acc);
-      else tile_q80<NT>(tile, xb, lane, acc);
+      if (DT2 != DT && rg >= a.n_rg) tile_dt<DT2, NT>(st, warp, lane, acc);
+      else tile_dt<DT, NT>(st, warp, lane, acc);
     }
     __syncwarp();
     if (lane == 0) mbar_arrive(&empty[s]);
@@ -768,17 +780,18 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const __grid_constant
       for (int p = 0; p < ca.n_phases && ok; ++p) {
         const GemvArgs& a = ca.ph[p];
         const PhaseRange pr = phase_range(a);
-        const int UB = unit_bytes(a.dtype), XB = x_stage_bytes(a.dtype, NT);
+        const long long U1 = (long long)a.n_rg * a.nsb;  // units of the first weight
         // the phase's activations depend on the latest grid barrier at or before it
         const int need = last_barrier(ca.bar_mask, p);
         bool dep = pdl_done && need <= passed;
         int npend = 0;
         int x_sb = pr.n_units ? (int)(pr.u0 % a.nsb) : 0;
+        int pend_dt[kMaxStages];
         // activation bytes for super-block sb: Q4_K {int8 limbs, scales, sums}, else {fp16 hi/lo, sums}
-        auto issue_x = [&](int s, int sb) {
-          uint8_t* st = ring + (size_t)s * SB + UB;
+        auto issue_x = [&](int s, int sb, int dt) {
+          uint8_t* st = ring + (size_t)s * SB + unit_bytes(dt);
           uint64_t* bar = &full[s];
-          if (a.dtype == DT_Q4_K) {
+          if (dt == DT_Q4_K) {
             bulk_g2s(st, reinterpret_cast<const uint8_t*>(a.xin.xi) + (size_t)sb * NT * kXiSbBytes, NT * kXiSbBytes,
                      bar);
             st += NT * kXiSbBytes;
@@ -812,7 +825,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const __grid_constant
             passed = need;
           }
           dep = true;
-          for (int j = 0; j < npend; ++j) issue_x(pend_s[j], pend_sb[j]);
+          for (int j = 0; j < npend; ++j) issue_x(pend_s[j], pend_sb[j], pend_dt[j]);
           npend = 0;
           RB_TS(p, 6);
         };
@@ -824,15 +837,20 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const __grid_constant
             ok = mbar_wait(&empty[s], (rp.round - 1) & 1, a.err, DEV_TIMEOUT_EMPTY);
             if (!ok) break;
           }
-          mbar_arrive_expect_tx(&full[s], UB + XB);
-          bulk_g2s_evict_first(ring + (size_t)s * SB, a.w + (pr.u0 + i) * (long long)UB, UB, &full[s], pol);
+          const long long u = pr.u0 + i;
+          const int dt = u < U1 ? a.dtype : a.dtype2;
+          const int UB = unit_bytes(dt);
+          mbar_arrive_expect_tx(&full[s], UB + x_stage_bytes(dt, NT));
+          const uint8_t* wsrc = u < U1 ? a.w + u * (long long)UB : a.w2 + (u - U1) * (long long)UB;
+          bulk_g2s_evict_first(ring + (size_t)s * SB, wsrc, UB, &full[s], pol);
           if (i == 0) RB_TS(p, 5);
           if (i + 1 == pr.n_units) RB_TS(p, 7);
           if (dep) {
-            issue_x(s, x_sb);
+            issue_x(s, x_sb, dt);
           } else {
             pend_s[npend] = s;
             pend_sb[npend] = x_sb;
+            pend_dt[npend] = dt;
             ++npend;
           }
           if (++x_sb == a.nsb) x_sb = 0;
@@ -862,11 +880,17 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const __grid_constant
     const unsigned long long my_target = wg ? s_tgt[need - 1] : 0ull;
     if (wg) passed = need;
     switch (a.dtype) {
-      case DT_Q4_K: consume_phase<DT_Q4_K, NT>(a, p, ca.n_phases, pr, ring, S, SB, full, empty, inv_rms, red, T, rp, alive,
+      case DT_Q4_K:
+        if (a.n_rg2 && a.dtype2 == DT_Q6_K)
+          consume_phase<DT_Q4_K, DT_Q6_K, NT>(a, p, ca.n_phases, pr, ring, S, SB, full, empty, inv_rms, red, T, rp,
+                                              alive, ca.gbar + need, wg, my_target, ca.grid_spin);
+        else
+          consume_phase<DT_Q4_K, DT_Q4_K, NT>(a, p, ca.n_phases, pr, ring, S, SB, full, empty, inv_rms, red, T, rp,
+                                              alive, ca.gbar + need, wg, my_target, ca.grid_spin);
+        break;
+      case DT_Q6_K: consume_phase<DT_Q6_K, DT_Q6_K, NT>(a, p, ca.n_phases, pr, ring, S, SB, full, empty, inv_rms, red, T, rp, alive,
                                          ca.gbar + need, wg, my_target, ca.grid_spin); break;
-      case DT_Q6_K: consume_phase<DT_Q6_K, NT>(a, p, ca.n_phases, pr, ring, S, SB, full, empty, inv_rms, red, T, rp, alive,
-                                         ca.gbar + need, wg, my_target, ca.grid_spin); break;
-      default: consume_phase<DT_Q8_0, NT>(a, p, ca.n_phases, pr, ring, S, SB, full, empty, inv_rms, red, T, rp, alive,
+      default: consume_phase<DT_Q8_0, DT_Q8_0, NT>(a, p, ca.n_phases, pr, ring, S, SB, full, empty, inv_rms, red, T, rp, alive,
                                          ca.gbar + need, wg, my_target, ca.grid_spin); break;
     }
     if (p + 1 < ca.n_phases && ((ca.bar_mask >> (p + 1)) & 1u)) {
@@ -1178,7 +1202,10 @@ __global__ void quantize_kernel(int dtype, const float* x, size_t nblocks, uint8
 template <int NT>
 cudaError_t launch_chain_t(ChainArgs ca, int num_sms, cudaStream_t s, int pdl) {
   int sb = 0;
-  for (int p = 0; p < ca.n_phases; ++p) sb = max(sb, stage_bytes(ca.ph[p].dtype, NT));
+  for (int p = 0; p < ca.n_phases; ++p) {
+    sb = max(sb, stage_bytes(ca.ph[p].dtype, NT));
+    if (ca.ph[p].n_rg2) sb = max(sb, stage_bytes(ca.ph[p].dtype2, NT));
+  }
   sb = (sb + 127) & ~127;
   const int fit = (kSmemBudget - 4 * tile_floats(NT) - 4096) / sb;
   ca.stages = fit > kMaxStages ? kMaxStages : fit < 1 ? 1 : fit;
@@ -1203,7 +1230,7 @@ cudaError_t launch_chain_t(ChainArgs ca, int num_sms, cudaStream_t s, int pdl) {
     }
   }
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(ca.n_phases == 1 ? gemv_ctas(num_sms, ca.ph[0].n_rg, ca.ph[0].nsb) : num_sms);
+  cfg.gridDim = dim3(ca.n_phases == 1 ? gemv_ctas(num_sms, ca.ph[0].n_rg + ca.ph[0].n_rg2, ca.ph[0].nsb) : num_sms);
   cfg.blockDim = dim3(kThreads);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = s;
@@ -2330,6 +2357,9 @@ cudaError_t gemv_chain_launch(const ChainArgs& c, int num_sms, cudaStream_t s, i
     const GemvArgs& a = c.ph[p];
     if (a.m != m || a.m < 1 || a.m > kMaxTokens) return cudaErrorInvalidValue;
     if (a.dtype != DT_Q4_K && a.dtype != DT_Q6_K && a.dtype != DT_Q8_0) return cudaErrorInvalidValue;
+    // a second weight: same format, or Q6_K after Q4_K, in a QKV epilogue
+    if (a.n_rg2 && (!a.w2 || a.epi != EPI_QKV || !(a.dtype2 == a.dtype || (a.dtype == DT_Q4_K && a.dtype2 == DT_Q6_K))))
+      return cudaErrorInvalidValue;
   }
   switch (gemv_nt_for(m)) {
     case 1: return launch_chain_t<1>(c, num_sms, s, pdl);
@@ -2420,7 +2450,7 @@ size_t qgemm_bprep_bytes(int nsb) { return (size_t)4 * nsb * q2_bslice_bytes(2 *
 cudaError_t qgemm_launch(const GemvArgs& a, float* part, uint8_t* bprep, const QgemmPlan& p, cudaStream_t s,
                          int pdl) {
   const int8_t* rexp = a.rexp;
-  if (a.m < 16 || a.m > kMaxTokens || !a.xin.xf || !rexp || !part || p.G < 1) return cudaErrorInvalidValue;
+  if (a.m < 16 || a.m > kMaxTokens || !a.xin.xf || !rexp || !part || p.G < 1 || a.n_rg2) return cudaErrorInvalidValue;
   QgemmArgs q;
   q.w = a.w;
   q.xs = a.xin.xs;

@@ -36,8 +36,8 @@ struct GemvArgs {
   // optional second weight of the same K in the same phase (GEMV kernel only):
   // its row groups follow the first's in the unit space, so both share one
   // stream-K split and one tail (a QKV phase runs q|k and v together); its
-  // rows start at qkv_row0_2 in the QKV epilogue. dtype2 is dtype or Q6_K
-  // after Q4_K.
+  // rows start at qkv_row0_2 in the QKV epilogue. dtype2 is dtype, or Q6_K
+  // after Q4_K in steps of at most 8 rows.
   const uint8_t* w2 = nullptr;
   int32_t dtype2 = 0, n2 = 0, n_rg2 = 0, qkv_row0_2 = 0;
   int32_t m = 0;      // tokens (x rows)

@@ -307,7 +307,7 @@ struct Ctx {
   int chain_prefetch = -1;  // RB_CHAIN_PREFETCH: next-phase weight units issued ahead of a grid barrier
   int attn_group = 1;       // RB_ATTN_GROUP=0: one attention pair per row (no K/V sharing in prefill chunks)
   bool step_grouped = false;  // the step has consecutive rows of one tenant (a prompt chunk)
-  int attn_whole = 1;         // RB_ATTN_WHOLE=0: always split attention pages evenly over the CTAs
+  int attn_whole = 1;         // RB_ATTN_WHOLE: 0 always split attention pages evenly over the CTAs; k > 1 whole pairs within k x the even share (1: 3x)
   bool merge_v = true;        // RB_MERGE_V=0: v runs as a phase of its own after q|k
   DevBuf qg_part;      // tcgen05 GEMM partial sums
   DevBuf qg_bprep;     // tcgen05 exact-weight GEMM: activation planes
@@ -1003,7 +1003,7 @@ int32_t rb_ctx_create(const rb_config* cfg, rb_ctx** out) {
   if (const char* d = getenv("RB_QGEMM")) c->qgemm = atoi(d);
   if (const char* d = getenv("RB_CHAIN_PREFETCH")) c->chain_prefetch = atoi(d);
   if (const char* d = getenv("RB_ATTN_GROUP")) c->attn_group = atoi(d) != 0;
-  if (const char* d = getenv("RB_ATTN_WHOLE")) c->attn_whole = atoi(d) != 0;
+  if (const char* d = getenv("RB_ATTN_WHOLE")) c->attn_whole = atoi(d);
   if (const char* d = getenv("RB_MERGE_V")) c->merge_v = atoi(d) != 0;
   RB_CUDA(cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking));
   RB_CUDA(cudaEventCreate(&c->ev0));

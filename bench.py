@@ -534,7 +534,7 @@ def run_reference(args):
     om = O.Model(dict(CFG, kv_fp16=1), W, threads=threads)
     om.kv_fill(448, seed=0)
     pos = 448
-    for _ in range(min(args.warmup, 1)):
+    for _ in range(min(args.warmup, 3)):
         om.forward([1], pos)
         pos += 1
     k = max(1, min(args.steps, 4))
@@ -548,7 +548,7 @@ def run_reference(args):
               f"path: dequant + fp32 GEMV, {threads} threads); the reference serves tenants one token at a time, so "
               f"aggregate tok/s over tenants equals this rate")
     print(json.dumps({"impl": "reference", "metric": METRIC, "value": round(v, 4), "unit": "tok/s",
-                      "n_gpus": int(os.environ.get("WORLD_SIZE", "1")), "steps": k, "warmup": min(args.warmup, 1),
+                      "n_gpus": int(os.environ.get("WORLD_SIZE", "1")), "steps": k, "warmup": min(args.warmup, 3),
                       "ms_per_step": round(dt / k * 1e3, 2), "higher_is_better": True, "scaling": "weak",
                       "vs_baseline": None, "dtype": "f32", "data": "synthetic (numpy N(0,0.02), seed 3)",
                       "config": {"workload": "Llama-2-7B Q4_K_M decode (configs[3]), one tenant-token per sample"},

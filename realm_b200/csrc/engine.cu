@@ -649,7 +649,8 @@ int enqueue_layer(Ctx* c, Model& M, int l, int m, const int32_t* d_tenant, const
   // v joins the q|k phase as its second weight (one stream-K split, one tail)
   // unless the step runs its Q4_K projections on the tcgen05 GEMM
   const bool merge_v = c->merge_v && !L.v_fused && !c->gemm_step && L.v.k == L.qk.k &&
-                       (L.v.dtype == L.qk.dtype || (L.qk.dtype == DT_Q4_K && L.v.dtype == DT_Q6_K && m <= 8));
+                       (m <= 8 ? (L.qk.dtype == DT_Q4_K ? L.v.dtype == DT_Q6_K : L.v.dtype == L.qk.dtype)
+                               : L.v.dtype == L.qk.dtype);
   if (merge_v) {
     a.w2 = L.v.tiled.as<uint8_t>();
     a.dtype2 = L.v.dtype;

@@ -880,8 +880,10 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const __grid_constant
     if (wg) passed = need;
     switch (a.dtype) {
       case DT_Q4_K:
-        if (NT == 1 && a.n_rg2 && a.dtype2 == DT_Q6_K)  // mixed formats: 8-row steps only (register budget)
-          consume_phase<DT_Q4_K, (NT == 1 ? DT_Q6_K : DT_Q4_K), NT>(a, p, ca.n_phases, pr, ring, S, SB, full, empty, inv_rms, red, T, rp,
+        // 8-row steps: every Q4_K phase runs the mixed loop (a phase without a
+        // second weight never reaches its Q6_K part), one inlined copy fewer
+        if constexpr (NT == 1)
+          consume_phase<DT_Q4_K, DT_Q6_K, NT>(a, p, ca.n_phases, pr, ring, S, SB, full, empty, inv_rms, red, T, rp,
                                               alive, ca.gbar + need, wg, my_target, ca.grid_spin);
         else
           consume_phase<DT_Q4_K, DT_Q4_K, NT>(a, p, ca.n_phases, pr, ring, S, SB, full, empty, inv_rms, red, T, rp,
@@ -2358,7 +2360,8 @@ cudaError_t gemv_chain_launch(const ChainArgs& c, int num_sms, cudaStream_t s, i
     if (a.dtype != DT_Q4_K && a.dtype != DT_Q6_K && a.dtype != DT_Q8_0) return cudaErrorInvalidValue;
     // a second weight: same format, or Q6_K after Q4_K, in a QKV epilogue
     if (a.n_rg2 && (!a.w2 || a.epi != EPI_QKV ||
-                    !(a.dtype2 == a.dtype || (a.dtype == DT_Q4_K && a.dtype2 == DT_Q6_K && gemv_nt_for(a.m) == 1))))
+                    !(gemv_nt_for(a.m) == 1 ? (a.dtype == DT_Q4_K ? a.dtype2 == DT_Q6_K : a.dtype2 == a.dtype)
+                                             : a.dtype2 == a.dtype)))
       return cudaErrorInvalidValue;
   }
   switch (gemv_nt_for(m)) {
